@@ -1,0 +1,210 @@
+/* ssd_b200.h - C ABI of the B200 (sm_100a) kernels behind one SSD
+ * speculative-decoding round: tree draft through a subset of the target's
+ * layers plus bridges, tree attention over the shared KV cache, one-pass
+ * target verification, and KV compaction.
+ *
+ * The reference (yotamabramson/subnetwork-speculative-decoding) is pure
+ * Python/PyTorch and has no FFI. Each entry point below names the reference
+ * code (path:line inside that project) whose computation it replaces; the
+ * Python host package calls these through ctypes.
+ *
+ * Conventions
+ *  - Every function returns an int status (SSD_OK == 0). On failure
+ *    ssd_last_error() returns a message for the calling host thread.
+ *  - Pointers are device pointers unless a parameter says otherwise. Sizes
+ *    are int64. `stream` is a cudaStream_t passed as void*.
+ *  - No function allocates device memory. Functions that need scratch take a
+ *    caller-owned `workspace` of `workspace_bytes` bytes which must be zeroed
+ *    once before its first use (its counters reset themselves afterwards);
+ *    one workspace must not be shared by calls that run concurrently.
+ *  - dtype SSD_F32 selects the fp32 CUDA-core path (the exact-parity tier);
+ *    SSD_BF16 selects the tcgen05 tensor-core path (bf16 operands, fp32
+ *    accumulation). Activations passed to a GEMM use the weights' dtype.
+ *  - The residual stream is always fp32 [T, d] row-major.
+ */
+#ifndef SSD_B200_H
+#define SSD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  SSD_OK = 0,
+  SSD_ERR_INVALID = 1,     /* bad argument (maps to Python ValueError) */
+  SSD_ERR_UNSUPPORTED = 2, /* shape/dtype this build does not handle */
+  SSD_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  SSD_ERR_OVERFLOW = 4,    /* cache or buffer capacity exceeded (RuntimeError) */
+  SSD_ERR_WORKSPACE = 5    /* workspace too small */
+};
+
+enum { SSD_F32 = 0, SSD_BF16 = 1 };
+enum { SSD_ACT_NONE = 0, SSD_ACT_SILU = 1, SSD_ACT_GELU = 2, SSD_ACT_RELU = 3 };
+
+/* Output-feature layout of a multi-segment GEMM. CONCAT: segment outputs are
+ * concatenated (q|k|v). PAIRS: two segments (gate, up) of equal size
+ * processed 64 features at a time so a SwiGLU epilogue sees both halves. */
+enum { SSD_SEG_CONCAT = 0, SSD_SEG_PAIRS = 1 };
+
+int ssd_version(void);
+const char* ssd_last_error(void);
+int ssd_device_sm_count(int device);
+
+/* Workspace bytes the GEMM / attention / head entry points need for up to
+ * `max_rows` rows and vocab size `vocab` (rows = tokens of one forward). */
+int64_t ssd_workspace_bytes(int64_t max_rows, int64_t vocab);
+
+/* Embedding gather: resid[t, :] = table[ids[t], :] (fp32 out).
+ * Replaces base.embed_tokens(input_ids), ssd/models/subnetwork_draft.py:290-291. */
+int ssd_embed(const int32_t* ids, int64_t T, const void* table, int64_t vocab, int64_t d, int dtype,
+              float* resid, uint32_t* status, void* stream);
+
+/* RMSNorm of the fp32 residual stream into the GEMM activation dtype:
+ * out = weight * (x * rsqrt(mean(x^2) + eps)).
+ * Replaces LlamaRMSNorm (subnetwork_draft.py:216,245,344) and the bridge
+ * RMSNorm (ssd/models/bridges.py:33-37). */
+int ssd_rmsnorm(const float* x, int64_t T, int64_t d, int64_t ldx, const void* weight, float eps, void* out,
+                int64_t ldo, int dtype, void* stream);
+
+/* y = x @ W^T (+ bias) with a fused epilogue, W given as up to 3 row
+ * segments w[i] of shape [rows[i], K] (row-major, K contiguous).
+ *   epilogue SSD_EPI_STORE:    out[t, n] = act(acc + bias)        (dtype)
+ *   epilogue SSD_EPI_RESIDUAL: resid[t, n] += acc + bias          (fp32)
+ *   epilogue SSD_EPI_SWIGLU:   out[t, f] = silu(acc_g + b_g) * (acc_u + b_u)
+ *                              (segments gate, up; layout SSD_SEG_PAIRS)
+ *   epilogue SSD_EPI_STORE_F32: out[t, n] = acc + bias as fp32 (logits)
+ * Replaces F.linear sites: o_proj + residual (subnetwork_draft.py:243), the
+ * SwiGLU MLP + residual (:245), bridge MLPs (ssd/models/bridges.py:53-54,
+ * 64-65, 131-135) and the lm_head (subnetwork_draft.py:347-349). */
+enum { SSD_EPI_STORE = 0, SSD_EPI_RESIDUAL = 1, SSD_EPI_SWIGLU = 2, SSD_EPI_STORE_F32 = 3 };
+int ssd_linear(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, const void* const* w,
+               const int64_t* rows, const void* const* bias, int seg_layout, int epilogue, int act, void* out,
+               int64_t ldo, float* resid, int64_t ldr, int dtype, void* workspace, int64_t workspace_bytes,
+               uint32_t* status, void* stream);
+
+/* Fused QKV projection + rotate-half RoPE + KV-cache write:
+ * q_out[t] = rope(x[t] @ Wq^T, pos[t]); k/v rows of token t are written to
+ * cache slot slots[t] of this layer (k rotated). rope_cos/rope_sin are fp32
+ * tables [max_pos, head_dim/2]. Cache layout per layer: [n_kv, max_slots,
+ * head_dim] with head stride `cache_head_stride` elements.
+ * Replaces q/k/v_proj + RoPE + KVCache.update (subnetwork_draft.py:209-222,
+ * ssd/engine/kv_cache.py:32-43). */
+int ssd_qkv_rope(const void* x, int64_t ldx, int64_t T, int64_t K, const void* wq, const void* wk, const void* wv,
+                 int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, const float* rope_cos, const float* rope_sin,
+                 int64_t max_pos, const int32_t* positions, const int32_t* slots, void* k_cache, void* v_cache,
+                 int64_t cache_head_stride, int64_t max_slots, void* q_out, int64_t ldq, int dtype, void* workspace,
+                 int64_t workspace_bytes, uint32_t* status, void* stream);
+
+/* Tree attention over the shared cache (split-KV, GQA). Row t attends cache
+ * slots [0, prefix_len[t]) and, if spec_mask is given, slot spec_base[0] + j
+ * for every set bit j of spec_mask[t * mask_words + j / 64]. Scores use
+ * scale = 1/sqrt(head_dim). q: [T, n_heads*head_dim]; out the same.
+ * Replaces SDPA with the bool tree mask (subnetwork_draft.py:165-191,
+ * 236-242; tree_drafter.py:192-196; ssd/engine/verify.py:37-41). */
+int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t n_heads, int64_t n_kv_heads,
+                       int64_t head_dim, const void* k_cache, const void* v_cache, int64_t cache_head_stride,
+                       int64_t max_slots, const int32_t* prefix_len, const int32_t* spec_base,
+                       const uint64_t* spec_mask, int64_t mask_words, int64_t kv_bound, void* out, int64_t ldo,
+                       int dtype, void* workspace, int64_t workspace_bytes, uint32_t* status, void* stream);
+
+/* Verify head: full-vocab lm_head fused with a per-row argmax (first index
+ * of the maximum, as torch.argmax). Also writes the top-2 gap per row.
+ * Replaces lm_head + argmax (subnetwork_draft.py:349, ssd/engine/verify.py:47,
+ * ssd/engine/speculative.py:81-84). */
+int ssd_head_argmax(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w, int64_t vocab,
+                    int32_t* out_idx, float* out_max, float* out_gap, int dtype, void* workspace,
+                    int64_t workspace_bytes, uint32_t* status, void* stream);
+
+/* Draft head: (sub-vocab) lm_head fused with log_softmax + per-row top-k
+ * (k <= 16). Column j of W is token vocab_ids[j] (identity if NULL).
+ * Outputs tokens [T, k] and fp32 log-probs [T, k], best first.
+ * Replaces lm_head/_sub_head + log_softmax().topk() (subnetwork_draft.py:
+ * 347-349, tree_drafter.py:128-133). */
+int ssd_head_topk(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w, int64_t vocab,
+                  const int64_t* vocab_ids, int64_t k, int32_t* out_tok, float* out_logprob, int dtype,
+                  void* workspace, int64_t workspace_bytes, uint32_t* status, void* stream);
+
+/* ---------------------------------------------------------------- tree ops
+ * The tree lives in device arrays: tokens[i], parents[i] (-1 = root),
+ * depths[i] (1..D), ranks[i], scores[i] (fp64 cumulative log-prob) and
+ * draft_pos[i]. All tree kernels are single-CTA and deterministic. */
+
+/* One drafting level. The frontier (node indices, -1 for the root) proposes
+ * k children each from topk_tok / topk_lp [n_frontier, k] (tokens < 0 or
+ * -inf log-probs are missing candidates). Candidates are ordered by
+ * descending cumulative score (fp64, ties keep frontier order then rank) and
+ * the first `width` (all if width <= 0) are appended at index *n_nodes,
+ * which is advanced; their indices go to next_frontier. If `fed`, the level
+ * is the input of the next draft forward and its ids / positions
+ * (root_pos + level + 1) / cache slots (root_pos + 1 + level_slot_offset + j)
+ * / prefix length (root_pos + 1) / ancestor bitmask over spec slots starting
+ * at root_pos + 1 are written to the fwd_* buffers.
+ * Replaces TreeDrafter.build's level step (tree_drafter.py:165-200). */
+int ssd_level_prune(const int32_t* topk_tok, const float* topk_lp, int64_t n_frontier, int64_t k, int64_t width,
+                    int64_t level, const int32_t* frontier, int32_t* next_frontier, int32_t* n_nodes,
+                    int32_t* tokens, int32_t* parents, int32_t* depths, int32_t* ranks, double* scores,
+                    int32_t* draft_pos, int64_t cap, const int32_t* root_pos, int fed, int64_t level_slot_offset,
+                    int32_t* fwd_ids, int32_t* fwd_pos, int32_t* fwd_slots, int32_t* fwd_plen,
+                    int32_t* fwd_spec_base, uint64_t* fwd_mask, int64_t mask_words, uint32_t* status,
+                    void* stream);
+
+/* Final max_nodes pruning: keep the best max_nodes nodes by (-score, depth),
+ * close the set under ancestors and compact it in index order with parents
+ * remapped (max_nodes <= 0: only drop empty slots). *n_nodes is updated.
+ * Replaces tree_drafter.py:202-207 and DraftTree.subset (:80-95). */
+int ssd_tree_prune(int32_t* n_nodes, int64_t max_nodes, int32_t* tokens, int32_t* parents, int32_t* depths,
+                   int32_t* ranks, double* scores, int32_t* draft_pos, int64_t cap, void* stream);
+
+/* Verify inputs for root + tree over rows_cap static rows: ids, positions
+ * root_pos + depth, cache slots root_pos + row, prefix length root_pos + 1
+ * and each node row's ancestor bitmask (bit i = node i at slot
+ * root_pos + 1 + i); rows past the tree are inert padding.
+ * Replaces verify_inputs (ssd/engine/verify.py:32-42). */
+int ssd_verify_prep(const int32_t* n_nodes, int64_t rows_cap, const int32_t* root_token, const int32_t* root_pos,
+                    const int32_t* tokens, const int32_t* parents, const int32_t* depths, int32_t* ids,
+                    int32_t* positions, int32_t* slots, int32_t* prefix_len, int32_t* spec_base, uint64_t* mask,
+                    int64_t mask_words, uint32_t* status, void* stream);
+
+/* Greedy tree walk: from the root follow the child (lowest rank first) whose
+ * token equals the row's argmax; the argmax at the last accepted node is the
+ * bonus token. Writes accepted node indices, their count, the bonus and the
+ * compaction source slots [root_pos, root_pos + 1 + a0, ...] (n_keep = 1 +
+ * accepted). Replaces greedy_verify (ssd/engine/verify.py:45-57) and the
+ * position list of ssd/engine/speculative.py:167. */
+int ssd_tree_walk_greedy(const int32_t* n_nodes, int64_t max_nodes, const int32_t* argmax, const int32_t* tokens,
+                         const int32_t* parents, const int32_t* ranks, const int32_t* root_pos, int32_t* accepted,
+                         int32_t* n_accepted, int32_t* bonus, int32_t* keep_slots, int32_t* n_keep, void* stream);
+
+/* In-place KV compaction over every layer: for j < *n_keep, cache slot
+ * keep_slots[j] moves to slot start[0] + j. Each thread owns one 16-byte
+ * group of one (layer, K/V, head) row across all kept slots and reads them
+ * all before writing, so overlapping source/destination slots are safe.
+ * Strides are in elements. Replaces KVCache.keep_positions
+ * (ssd/engine/kv_cache.py:54-70). */
+int ssd_kv_compact(void* cache, int64_t n_layers, int64_t layer_stride, int64_t kv_stride, int64_t n_kv_heads,
+                   int64_t head_stride, int64_t head_dim, const int32_t* start, const int32_t* keep_slots,
+                   const int32_t* n_keep, int64_t max_keep, int dtype, void* stream);
+
+/* Commit one round: append the accepted tokens + bonus to out_tokens at
+ * *n_out, advance *seq_len by 1 + accepted, make the bonus the new root and
+ * log the committed count in round_log (round_log[0] = rounds so far).
+ * Replaces the bookkeeping of ssd/engine/speculative.py:167-172. */
+int ssd_round_commit(const int32_t* n_accepted, const int32_t* accepted, const int32_t* tokens,
+                     const int32_t* bonus, int32_t* seq_len, int32_t* root_token, int32_t* out_tokens,
+                     int32_t* n_out, int64_t out_cap, int32_t* round_log, uint32_t* status, void* stream);
+
+/* Causal forward inputs for T rows starting at cache length *base: positions
+ * and cache slots base + r, prefix length base + r + 1; ids copied from
+ * src_ids if given. Replaces the default position_ids / causal mask of
+ * subnetwork_draft.py:296-297,179-191. */
+int ssd_causal_prep(const int32_t* base, int64_t T, const int32_t* src_ids, int32_t* ids, int32_t* positions,
+                    int32_t* slots, int32_t* prefix_len, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SSD_B200_H */

@@ -1,0 +1,421 @@
+// Mainloops and host launcher of the skinny GEMM family (see gemm.cuh).
+#include <mutex>
+#include <unordered_map>
+
+#include "gemm.cuh"
+#include "host.cuh"
+
+namespace ssd {
+
+// --------------------------------------------------------------- tcgen05 path
+// Warp roles (192 threads): warp 0 issues TMA, warp 1 owns TMEM and issues the
+// MMAs (one lane), warps 2..5 drain the accumulator and run the epilogue.
+// Pipeline: full[s] = TMA bytes of stage s landed; empty[s] = the MMAs that
+// read stage s retired (tcgen05.commit arrives on it).
+struct TcMaps {
+  CUtensorMap w[3];  // weight segments [rows, K], box {64, 32}
+  CUtensorMap x;     // activations [T, K], box {64, BN}
+};
+
+constexpr int kTcThreads = 192;
+constexpr int kABytes = kTileM * kChunkK * 2;  // 16 KB of weights per stage
+
+__host__ __device__ inline int tc_stage_bytes(int BN) { return kABytes + BN * kChunkK * 2; }
+__host__ __device__ inline int tc_region_bytes(int BN, int stages) {
+  const int ring = stages * tc_stage_bytes(BN);
+  const int epi = BN * kTileM * 4;
+  return ring > epi ? ring : epi;
+}
+__host__ __device__ inline int tc_smem_bytes(int BN, int stages) {
+  return 1024 /*alignment slack*/ + tc_region_bytes(BN, stages) + 256 /*barriers, flags*/;
+}
+__host__ __device__ inline uint32_t tc_tmem_cols(int BN) {
+  return BN <= 32 ? 32u : (BN <= 64 ? 64u : (BN <= 128 ? 128u : 256u));
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ TcMaps maps, const GemmShape g, const EpiArgs e) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stage_bytes = tc_stage_bytes(g.BN);
+  uint8_t* bar_base = smem + tc_region_bytes(g.BN, g.stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_base);
+  uint64_t* empty = full + g.stages;
+  uint64_t* accum = empty + g.stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  int* flag = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abort_flag = flag + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile_m = blockIdx.x / g.splits, split = blockIdx.x % g.splits;
+  const int tile_n = blockIdx.y;
+  const int kc0 = (int)((int64_t)split * g.kchunks / g.splits);
+  const int kc1 = (int)((int64_t)(split + 1) * g.kchunks / g.splits);
+  const int nk = kc1 - kc0;
+  const uint32_t ncols_alloc = tc_tmem_cols(g.BN);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < g.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, ncols_alloc);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < g.n_seg; ++i) tma_prefetch_desc(&maps.w[i]);
+      tma_prefetch_desc(&maps.x);
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      const uint32_t tx = kABytes + g.BN * kChunkK * 2;
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % g.stages;
+        if (i >= g.stages && !mbar_wait(&empty[s], ((i / g.stages) - 1) & 1)) {
+          report_error(g.status, kErrWaitTimeout);
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        uint8_t* a = smem + s * stage_bytes;
+        uint8_t* b = a + kABytes;
+        mbar_arrive_expect_tx(&full[s], tx);
+        const int kx = (kc0 + i) * kChunkK;
+#pragma unroll
+        for (int grp = 0; grp < 4; ++grp) {
+          int seg, row;
+          if (g.layout == SSD_SEG_PAIRS) {
+            seg = grp >> 1;
+            row = tile_m * 64 + (grp & 1) * 32;
+          } else {
+            const int n = tile_m * kTileM + grp * 32;
+            seg = 0;
+            for (int q = 1; q < g.n_seg; ++q)
+              if (n >= g.seg_start[q]) seg = q;
+            row = n - g.seg_start[seg];  // rows past the segment end are zero-filled by TMA
+          }
+          tma_load_2d(a + grp * 32 * 128, &maps.w[seg], &full[s], kx, row, pol_w);
+        }
+        tma_load_2d(b, &maps.x, &full[s], kx, tile_n * g.BN, pol_x);
+        ++issued;
+      }
+      // On abort, wait (bounded) for the copies already in flight to land so
+      // no TMA write targets shared memory after the CTA exits.
+      if (*abort_flag) {
+        for (int i = (issued > g.stages ? issued - g.stages : 0); i < issued; ++i)
+          (void)mbar_wait(&full[i % g.stages], (i / g.stages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kTileM, g.BN);
+      bool ok = true;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % g.stages;
+        if (!mbar_wait(&full[s], (i / g.stages) & 1)) {
+          report_error(g.status, kErrWaitTimeout);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + s * stage_bytes);
+        const uint32_t b = a + kABytes;
+#pragma unroll
+        for (int kk = 0; kk < kChunkK / 16; ++kk)
+          umma_bf16(tmem, sdesc_k_sw128(a + kk * 32), sdesc_k_sw128(b + kk * 32), idesc, (i | kk) != 0 ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      if (!ok) *abort_flag = 1;
+      // Arrives once every MMA above has retired (also on abort, so the
+      // epilogue never waits on MMAs still in flight). Waiting here too keeps
+      // TMEM allocated until the tensor core is done with it.
+      umma_commit(accum);
+      if (!mbar_wait(accum, 0)) report_error(g.status, kErrWaitTimeout);
+    }
+  } else {
+    // Epilogue warps 2..5. A warp may only touch TMEM lanes 32*(warp%4)..+31.
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    float* stage = reinterpret_cast<float*>(smem);
+    bool ok = mbar_wait(accum, 0);
+    if (!ok) report_error(g.status, kErrWaitTimeout);
+    tc_fence_after();
+    const int ncols = min(g.BN, g.T - tile_n * g.BN);
+    named_bar_sync(1, 128);  // all four warps past the wait before the ring is reused
+    ok = ok && (*abort_flag == 0);
+    if (ok) {
+      for (int c0 = 0; c0 < g.BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (c0 + i < ncols) stage[(c0 + i) * kTileM + r] = (nk > 0) ? v[i] : 0.f;
+      }
+    }
+    named_bar_sync(1, 128);
+    if (ok) finish_tile<bf16>(stage, flag, tile_m, tile_n, split, g, e, r, 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, ncols_alloc);
+  }
+}
+
+// ------------------------------------------------------------------ SIMT path
+// CUDA-core mainloop for the fp32 parity tier: 256 threads = 8 warps x 16
+// feature rows; lanes stride K (coalesced weight rows), 4 tokens per tile.
+constexpr int kSimtBN = 4;
+constexpr int kSimtKC = 512;
+
+struct SimtSegs {
+  const void* p[3];
+  int rows[3];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) simt_gemm_kernel(const T* __restrict__ x, int64_t ldx, const SimtSegs segs,
+                                                         const GemmShape g, const EpiArgs e) {
+  __shared__ float xs[kSimtBN][kSimtKC];
+  __shared__ float stage[kSimtBN * kTileM];
+  __shared__ int flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile_m = blockIdx.x / g.splits, split = blockIdx.x % g.splits;
+  const int tile_n = blockIdx.y;
+  const int t0 = tile_n * kSimtBN;
+  const int ncols = min(kSimtBN, g.T - t0);
+  const int k_begin = (int)((int64_t)split * g.kchunks / g.splits) * kChunkK;
+  const int k_end = min(g.K, (int)((int64_t)(split + 1) * g.kchunks / g.splits) * kChunkK);
+
+  const T* wrow[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int rr = warp * 16 + i;
+    int seg, row;
+    if (g.layout == SSD_SEG_PAIRS) {
+      seg = rr >> 6;
+      row = tile_m * 64 + (rr & 63);
+    } else {
+      const int n = tile_m * kTileM + rr;
+      seg = 0;
+      for (int q = 1; q < g.n_seg; ++q)
+        if (n >= g.seg_start[q]) seg = q;
+      row = n - g.seg_start[seg];
+    }
+    wrow[i] = (row < segs.rows[seg]) ? static_cast<const T*>(segs.p[seg]) + (int64_t)row * g.K : nullptr;
+  }
+  float acc[16][kSimtBN];
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+#pragma unroll
+    for (int c = 0; c < kSimtBN; ++c) acc[i][c] = 0.f;
+
+  for (int k0 = k_begin; k0 < k_end; k0 += kSimtKC) {
+    const int kn = min(kSimtKC, k_end - k0);
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < kSimtBN * kSimtKC; idx += 256) {
+      const int c = idx / kSimtKC, kk = idx % kSimtKC;
+      xs[c][kk] = (c < ncols && kk < kn) ? to_f32<T>(x[(int64_t)(t0 + c) * ldx + k0 + kk]) : 0.f;
+    }
+    __syncthreads();
+    for (int kk = lane; kk < kn; kk += 32) {
+      float xv[kSimtBN];
+#pragma unroll
+      for (int c = 0; c < kSimtBN; ++c) xv[c] = xs[c][kk];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float wv = wrow[i] ? to_f32<T>(wrow[i][k0 + kk]) : 0.f;
+#pragma unroll
+        for (int c = 0; c < kSimtBN; ++c) acc[i][c] = fmaf(wv, xv[c], acc[i][c]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+#pragma unroll
+    for (int c = 0; c < kSimtBN; ++c) {
+      const float v = warp_sum(acc[i][c]);
+      if (lane == 0) stage[c * kTileM + warp * 16 + i] = v;
+    }
+  __syncthreads();
+  if (threadIdx.x < 128) finish_tile<T>(stage, &flag, tile_m, tile_n, split, g, e, threadIdx.x, 1);
+}
+
+// ------------------------------------------------------------------- host side
+namespace {
+
+struct MapKey {
+  const void* p;
+  uint64_t inner, outer, stride;
+  uint32_t box_outer;
+  bool operator==(const MapKey& o) const {
+    return p == o.p && inner == o.inner && outer == o.outer && stride == o.stride && box_outer == o.box_outer;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = reinterpret_cast<uintptr_t>(k.p);
+    h = h * 0x9E3779B97F4A7C15ull ^ k.inner;
+    h = h * 0x9E3779B97F4A7C15ull ^ k.outer;
+    h = h * 0x9E3779B97F4A7C15ull ^ k.stride;
+    h = h * 0x9E3779B97F4A7C15ull ^ k.box_outer;
+    return static_cast<size_t>(h);
+  }
+};
+
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// bf16 2-D tensor map, box {64 elements (128 B), box_outer rows}, 128 B swizzle.
+int get_map(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_outer,
+            CUtensorMap* out) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_stride_bytes & 15))
+    return fail(SSD_ERR_INVALID, "bf16 GEMM operands need 16-byte aligned bases and row strides");
+  MapKey key{base, inner, outer, row_stride_bytes, box_outer};
+  {
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return SSD_OK;
+    }
+  }
+  TensorMapEncodeFn encode = tensor_map_encoder();
+  if (!encode) return fail(SSD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {64u, box_outer};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUtensorMap m;
+  CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SSD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  if (g_maps.size() > 8192) g_maps.clear();
+  g_maps.emplace(key, m);
+  *out = m;
+  return SSD_OK;
+}
+
+int round_bn(int64_t T) {
+  if (T > 256) return 128;
+  const int bn = (int)((T + 15) / 16) * 16;
+  return bn < 16 ? 16 : bn;
+}
+
+// K-split count from the weight shape only (never from T), so a token's
+// result is bit-identical whatever batch it is computed in.
+int choose_splits(int tiles_m, int kchunks, int cta_slots) {
+  if (tiles_m * 2 >= cta_slots) return 1;
+  int s = cta_slots / tiles_m;
+  const int max_s = kchunks / 4;
+  if (s > max_s) s = max_s;
+  return s < 1 ? 1 : s;
+}
+
+}  // namespace
+
+int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, const void* const* w,
+                const int64_t* rows, int layout, const EpiArgs& e, int dtype, void* workspace,
+                int64_t workspace_bytes, uint32_t* status, cudaStream_t stream, int64_t partial_offset_bytes) {
+  if (T <= 0 || K <= 0 || n_seg < 1 || n_seg > 3 || !x) return fail(SSD_ERR_INVALID, "bad GEMM arguments");
+  for (int i = 0; i < n_seg; ++i)
+    if (!w[i] || rows[i] <= 0) return fail(SSD_ERR_INVALID, "GEMM weight segment %d is empty", i);
+  if (T > (1 << 20) || K > (1 << 20)) return fail(SSD_ERR_UNSUPPORTED, "GEMM dimension too large");
+  GemmShape g{};
+  g.T = (int)T;
+  g.K = (int)K;
+  g.n_seg = n_seg;
+  g.layout = layout;
+  int64_t N = 0;
+  for (int i = 0; i < n_seg; ++i) {
+    g.seg_start[i] = (int)N;
+    N += rows[i];
+  }
+  g.seg_start[n_seg] = (int)N;
+  if (layout == SSD_SEG_PAIRS) {
+    if (n_seg != 2 || rows[0] != rows[1]) return fail(SSD_ERR_INVALID, "PAIRS layout needs two equal segments");
+    g.N = (int)(rows[0] * 2);
+    g.tiles_m = (int)((rows[0] + 63) / 64);
+  } else {
+    for (int i = 0; i + 1 < n_seg; ++i)
+      if (rows[i] % 32) return fail(SSD_ERR_UNSUPPORTED, "CONCAT segments must be multiples of 32 rows");
+    g.N = (int)N;
+    g.tiles_m = (int)((N + kTileM - 1) / kTileM);
+  }
+  g.kchunks = (int)((K + kChunkK - 1) / kChunkK);
+  g.status = status;
+  const int sms = device_sms();
+  const bool head = (e.kind == EPI_ARGMAX || e.kind == EPI_TOPK);
+
+  if (dtype == SSD_BF16) {
+    if (K % 8) return fail(SSD_ERR_UNSUPPORTED, "bf16 GEMM needs K % 8 == 0");
+    g.BN = round_bn(T);
+    g.tiles_n = (int)((T + g.BN - 1) / g.BN);
+    g.splits = (g.tiles_n == 1 && !head) ? choose_splits(g.tiles_m, g.kchunks, 2 * sms) : 1;
+    int stages = 101376 / tc_stage_bytes(g.BN);
+    g.stages = stages > 8 ? 8 : (stages < 2 ? 2 : stages);
+  } else if (dtype == SSD_F32) {
+    g.BN = kSimtBN;
+    g.tiles_n = (int)((T + kSimtBN - 1) / kSimtBN);
+    // Same split for every decode-sized T (<= kSimtInvariantRows), so rows are
+    // bit-identical whatever the batch; larger (prefill) batches do not split.
+    g.splits = (T <= kSimtInvariantRows && !head) ? choose_splits(g.tiles_m, g.kchunks, 4 * sms) : 1;
+  } else {
+    return fail(SSD_ERR_UNSUPPORTED, "dtype %d", dtype);
+  }
+
+  const int64_t tiles = (int64_t)g.tiles_m * g.tiles_n;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (g.splits > 1) {
+    if (!workspace) return fail(SSD_ERR_WORKSPACE, "split-K GEMM needs a workspace");
+    if (tiles > kMaxCounters) return fail(SSD_ERR_WORKSPACE, "too many split-K tiles");
+    const int64_t need = kCounterBytes + partial_offset_bytes + tiles * g.splits * g.BN * kTileM * 4;
+    if (need > workspace_bytes)
+      return fail(SSD_ERR_WORKSPACE, "workspace too small: need %lld bytes", (long long)need);
+    g.counters = reinterpret_cast<uint32_t*>(ws);
+    g.partials = reinterpret_cast<float*>(ws + kCounterBytes + partial_offset_bytes);
+  }
+  if (g.tiles_n > 65535) return fail(SSD_ERR_UNSUPPORTED, "too many token tiles");
+  dim3 grid(g.tiles_m * g.splits, g.tiles_n);
+
+  if (dtype == SSD_BF16) {
+    TcMaps maps;
+    for (int i = 0; i < n_seg; ++i) {
+      const int rc = get_map(w[i], (uint64_t)K, (uint64_t)rows[i], (uint64_t)K * 2, 32, &maps.w[i]);
+      if (rc) return rc;
+    }
+    for (int i = n_seg; i < 3; ++i) maps.w[i] = maps.w[0];
+    const int rc = get_map(x, (uint64_t)K, (uint64_t)T, (uint64_t)ldx * 2, (uint32_t)g.BN, &maps.x);
+    if (rc) return rc;
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+      attr_set = true;
+    }
+    tc_gemm_kernel<<<grid, kTcThreads, tc_smem_bytes(g.BN, g.stages), stream>>>(maps, g, e);
+    return check_launch("tc_gemm_kernel");
+  }
+  SimtSegs segs{};
+  for (int i = 0; i < 3; ++i) {
+    segs.p[i] = i < n_seg ? w[i] : w[0];
+    segs.rows[i] = i < n_seg ? (int)rows[i] : 0;
+  }
+  simt_gemm_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(x), ldx, segs, g, e);
+  return check_launch("simt_gemm_kernel");
+}
+
+}  // namespace ssd

@@ -1,0 +1,97 @@
+"""ctypes binding of libssd_b200.so, the sm_100a kernel library.
+
+There is no fallback: if the library is missing or fails to load, every
+operation that needs it raises. The library is built in-tree by
+``csrc/build.py`` (``__graft_entry__.build()`` runs it).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libssd_b200.so"
+
+P = C.c_void_p
+I64 = C.c_int64
+I32 = C.c_int
+F32 = C.c_float
+
+SSD_OK, SSD_ERR_INVALID, SSD_ERR_UNSUPPORTED, SSD_ERR_CUDA, SSD_ERR_OVERFLOW, SSD_ERR_WORKSPACE = range(6)
+SSD_F32, SSD_BF16 = 0, 1
+ACT = {"none": 0, "silu": 1, "gelu": 2, "relu": 3}
+SEG_CONCAT, SEG_PAIRS = 0, 1
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_STORE_F32 = 0, 1, 2, 3
+
+# name -> (restype, argtypes); mirrors include/ssd_b200.h
+SIGNATURES: dict[str, tuple] = {
+    "ssd_version": (I32, []),
+    "ssd_last_error": (C.c_char_p, []),
+    "ssd_device_sm_count": (I32, [I32]),
+    "ssd_workspace_bytes": (I64, [I64, I64]),
+    "ssd_embed": (I32, [P, I64, P, I64, I64, I32, P, P, P]),
+    "ssd_rmsnorm": (I32, [P, I64, I64, I64, P, F32, P, I64, I32, P]),
+    "ssd_linear": (I32, [P, I64, I64, I64, I32, P, P, P, I32, I32, I32, P, I64, P, I64, I32, P, I64, P, P]),
+    "ssd_qkv_rope": (I32, [P, I64, I64, I64, P, P, P, I64, I64, I64, P, P, I64, P, P, P, P, I64, I64, P, I64, I32,
+                           P, I64, P, P]),
+    "ssd_tree_attention": (I32, [P, I64, I64, I64, I64, I64, P, P, I64, I64, P, P, P, I64, I64, P, I64, I32, P, I64,
+                                 P, P]),
+    "ssd_head_argmax": (I32, [P, I64, I64, I64, P, I64, P, P, P, I32, P, I64, P, P]),
+    "ssd_head_topk": (I32, [P, I64, I64, I64, P, I64, P, I64, P, P, I32, P, I64, P, P]),
+    "ssd_level_prune": (I32, [P, P, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, I64, P, I32, I64, P, P, P, P, P,
+                              P, I64, P, P]),
+    "ssd_tree_prune": (I32, [P, I64, P, P, P, P, P, P, I64, P]),
+    "ssd_verify_prep": (I32, [P, I64, P, P, P, P, P, P, P, P, P, P, P, I64, P, P]),
+    "ssd_tree_walk_greedy": (I32, [P, I64, P, P, P, P, P, P, P, P, P, P, P]),
+    "ssd_kv_compact": (I32, [P, I64, I64, I64, I64, I64, I64, P, P, P, I64, I32, P]),
+    "ssd_round_commit": (I32, [P, P, P, P, P, P, P, P, I64, P, P, P]),
+    "ssd_causal_prep": (I32, [P, I64, P, P, P, P, P, P]),
+}
+
+_lib = None
+
+
+class SSDError(RuntimeError):
+    pass
+
+
+def load() -> C.CDLL:
+    """Load the kernel library (once). Raises if it is missing: no fallback."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = Path(os.environ.get("SSD_B200_LIB", LIB_PATH))
+    if not path.exists():
+        raise SSDError(
+            f"{path} not found: build it with `python subnetwork-speculative-decoding_b200/csrc/build.py` "
+            "(the SSD B200 path has no CPU fallback)"
+        )
+    lib = C.CDLL(str(path))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)
+
+
+def check(rc: int, what: str) -> None:
+    """Map a status code to the Python exception the reference raises."""
+    if rc == SSD_OK:
+        return
+    msg = load().ssd_last_error().decode(errors="replace")
+    text = f"{what}: {msg} (status {rc})"
+    if rc == SSD_ERR_INVALID:
+        raise ValueError(text)
+    if rc == SSD_ERR_OVERFLOW:
+        raise RuntimeError(text)
+    raise SSDError(text)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args), name)

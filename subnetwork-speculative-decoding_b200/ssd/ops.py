@@ -1,0 +1,173 @@
+"""Tensor-level wrappers over the C ABI (include/ssd_b200.h).
+
+Each function takes torch CUDA tensors, checks shapes/dtypes, and launches
+on the current torch stream. Nothing here computes on the host: a missing
+library or a non-CUDA tensor is an error.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Sequence
+
+import torch
+
+from ssd import _lib as L
+
+_DT = {torch.float32: L.SSD_F32, torch.bfloat16: L.SSD_BF16}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt not in _DT:
+        raise ValueError(f"unsupported dtype {dt} (float32 or bfloat16)")
+    return _DT[dt]
+
+
+def _p(t: Optional[torch.Tensor]) -> Optional[int]:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("SSD B200 ops take CUDA tensors only (no CPU fallback)")
+    return t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+class Workspace:
+    """Scratch for the GEMM / attention / head kernels plus a device status word.
+
+    The buffer is zeroed once; the kernels' split counters reset themselves.
+    One workspace per stream.
+    """
+
+    def __init__(self, device: torch.device, max_rows: int, vocab: int):
+        L.load()
+        nbytes = int(L.load().ssd_workspace_bytes(max(1, max_rows), max(1, vocab)))
+        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.nbytes = nbytes
+
+    @property
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+    def check_status(self) -> None:
+        """Raise if any kernel recorded a device-side error (bad index, timeout)."""
+        v = int(self.status.item())
+        if v:
+            self.status.zero_()
+            what = []
+            if v & 1:
+                what.append("a pipeline wait timed out")
+            if v & 2:
+                what.append("an index was out of range")
+            raise RuntimeError("SSD device error: " + ", ".join(what))
+
+
+def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor, ws: Workspace) -> None:
+    T = ids.numel()
+    L.call("ssd_embed", _p(ids), T, _p(table), table.shape[0], table.shape[1], dtype_code(table.dtype), _p(out),
+           _p(ws.status), _stream())
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor) -> None:
+    T, d = x.shape
+    L.call("ssd_rmsnorm", _p(x), T, d, x.stride(0), _p(weight), float(eps), _p(out), out.stride(0),
+           dtype_code(out.dtype), _stream())
+
+
+def linear(x: torch.Tensor, weights: Sequence[torch.Tensor], ws: Workspace, *, biases: Sequence = (),
+           epilogue: int = L.EPI_STORE, act: str = "none", layout: int = L.SEG_CONCAT,
+           out: Optional[torch.Tensor] = None, resid: Optional[torch.Tensor] = None, T: Optional[int] = None) -> None:
+    """out/resid <- epilogue(x @ cat(weights)^T + bias). x: [T, K] in the weights' dtype."""
+    T = x.shape[0] if T is None else T
+    K = weights[0].shape[1]
+    n = len(weights)
+    for w in weights:
+        if w.shape[1] != K or not w.is_contiguous():
+            raise ValueError("weight segments must be contiguous [rows, K]")
+    wp = (C.c_void_p * 3)(*[w.data_ptr() for w in weights], *([None] * (3 - n)))
+    rows = (C.c_int64 * 3)(*[w.shape[0] for w in weights], *([0] * (3 - n)))
+    bl = list(biases) + [None] * (3 - len(biases))
+    bp = (C.c_void_p * 3)(*[(b.data_ptr() if b is not None else None) for b in bl[:3]])
+    L.call("ssd_linear", _p(x), x.stride(0), T, K, n, wp, rows, bp, layout, epilogue, L.ACT[act],
+           _p(out), out.stride(0) if out is not None else 0, _p(resid), resid.stride(0) if resid is not None else 0,
+           dtype_code(weights[0].dtype), ws.ptr, ws.nbytes, _p(ws.status), _stream())
+
+
+def qkv_rope(x, wq, wk, wv, n_heads, n_kv, head_dim, cos, sin, positions, slots, k_cache, v_cache, q_out,
+             ws: Workspace, T: Optional[int] = None) -> None:
+    """k_cache/v_cache: [n_kv, max_slots, head_dim] views of one layer."""
+    T = x.shape[0] if T is None else T
+    L.call("ssd_qkv_rope", _p(x), x.stride(0), T, wq.shape[1], _p(wq), _p(wk), _p(wv), n_heads, n_kv, head_dim,
+           _p(cos), _p(sin), cos.shape[0], _p(positions), _p(slots), _p(k_cache), _p(v_cache), k_cache.stride(0),
+           k_cache.shape[1], _p(q_out), q_out.stride(0), dtype_code(wq.dtype), ws.ptr, ws.nbytes, _p(ws.status),
+           _stream())
+
+
+def tree_attention(q, k_cache, v_cache, n_heads, n_kv, head_dim, prefix_len, out, ws: Workspace, *,
+                   spec_base=None, spec_mask=None, kv_bound: int = 0, T: Optional[int] = None) -> None:
+    T = q.shape[0] if T is None else T
+    mw = spec_mask.shape[-1] if spec_mask is not None else 0
+    L.call("ssd_tree_attention", _p(q), q.stride(0), T, n_heads, n_kv, head_dim, _p(k_cache), _p(v_cache),
+           k_cache.stride(0), k_cache.shape[1], _p(prefix_len), _p(spec_base), _p(spec_mask), mw, kv_bound, _p(out),
+           out.stride(0), dtype_code(q.dtype), ws.ptr, ws.nbytes, _p(ws.status), _stream())
+
+
+def head_argmax(x, w, out_idx, ws: Workspace, out_max=None, out_gap=None, T: Optional[int] = None) -> None:
+    T = x.shape[0] if T is None else T
+    L.call("ssd_head_argmax", _p(x), x.stride(0), T, w.shape[1], _p(w), w.shape[0], _p(out_idx), _p(out_max),
+           _p(out_gap), dtype_code(w.dtype), ws.ptr, ws.nbytes, _p(ws.status), _stream())
+
+
+def head_topk(x, w, k: int, out_tok, out_lp, ws: Workspace, vocab_ids=None, T: Optional[int] = None) -> None:
+    T = x.shape[0] if T is None else T
+    L.call("ssd_head_topk", _p(x), x.stride(0), T, w.shape[1], _p(w), w.shape[0], _p(vocab_ids), k, _p(out_tok),
+           _p(out_lp), dtype_code(w.dtype), ws.ptr, ws.nbytes, _p(ws.status), _stream())
+
+
+def level_prune(topk_tok, topk_lp, n_frontier, k, width, level, frontier, next_frontier, tree, root_pos, fed,
+                level_slot_offset, fwd, status) -> None:
+    """tree: DeviceTree; fwd: ForwardInputs (or None when not fed)."""
+    L.call("ssd_level_prune", _p(topk_tok), _p(topk_lp), n_frontier, k, width if width else 0, level, _p(frontier),
+           _p(next_frontier), _p(tree.n_nodes), _p(tree.tokens), _p(tree.parents), _p(tree.depths), _p(tree.ranks),
+           _p(tree.scores), _p(tree.draft_pos), tree.cap, _p(root_pos), 1 if fed else 0, level_slot_offset,
+           _p(fwd.ids) if fed else None, _p(fwd.positions) if fed else None, _p(fwd.slots) if fed else None,
+           _p(fwd.prefix_len) if fed else None, _p(fwd.spec_base) if fed else None, _p(fwd.mask) if fed else None,
+           fwd.mask_words if fed else 0, _p(status), _stream())
+
+
+def tree_prune(tree, max_nodes: Optional[int]) -> None:
+    L.call("ssd_tree_prune", _p(tree.n_nodes), max_nodes or 0, _p(tree.tokens), _p(tree.parents), _p(tree.depths),
+           _p(tree.ranks), _p(tree.scores), _p(tree.draft_pos), tree.cap, _stream())
+
+
+def verify_prep(tree, rows_cap, root_token, root_pos, fwd, status) -> None:
+    L.call("ssd_verify_prep", _p(tree.n_nodes), rows_cap, _p(root_token), _p(root_pos), _p(tree.tokens),
+           _p(tree.parents), _p(tree.depths), _p(fwd.ids), _p(fwd.positions), _p(fwd.slots), _p(fwd.prefix_len),
+           _p(fwd.spec_base), _p(fwd.mask), fwd.mask_words, _p(status), _stream())
+
+
+def tree_walk_greedy(tree, argmax, root_pos, accepted, n_accepted, bonus, keep_slots, n_keep, max_nodes) -> None:
+    L.call("ssd_tree_walk_greedy", _p(tree.n_nodes), max_nodes, _p(argmax), _p(tree.tokens), _p(tree.parents), _p(tree.ranks),
+           _p(root_pos), _p(accepted), _p(n_accepted), _p(bonus), _p(keep_slots), _p(n_keep), _stream())
+
+
+def kv_compact(cache: torch.Tensor, start, keep_slots, n_keep, max_keep: int) -> None:
+    """cache: [L, 2, n_kv, max_slots, head_dim]."""
+    Ln, _, n_kv, _, hd = cache.shape
+    L.call("ssd_kv_compact", _p(cache), Ln, cache.stride(0), cache.stride(1), n_kv, cache.stride(2), hd, _p(start),
+           _p(keep_slots), _p(n_keep), max_keep, dtype_code(cache.dtype), _stream())
+
+
+def round_commit(n_accepted, accepted, tokens, bonus, seq_len, root_token, out_tokens, n_out, round_log,
+                 status) -> None:
+    L.call("ssd_round_commit", _p(n_accepted), _p(accepted), _p(tokens), _p(bonus), _p(seq_len), _p(root_token),
+           _p(out_tokens), _p(n_out), out_tokens.numel(), _p(round_log), _p(status), _stream())
+
+
+def causal_prep(base, T: int, src_ids, fwd) -> None:
+    L.call("ssd_causal_prep", _p(base), T, _p(src_ids), _p(fwd.ids), _p(fwd.positions), _p(fwd.slots),
+           _p(fwd.prefix_len), _stream())

@@ -1,0 +1,282 @@
+"""Kernel-level parity: each sm_100a kernel (through the C ABI) against a plain
+PyTorch fp32 reference of the same op, on seeded inputs.
+
+Tolerances: bf16 tensor-core GEMMs accumulate in fp32 over bf16 operands, so
+they are compared with the fp32 product of the same bf16 values (rtol 1e-2 on
+bf16-rounded outputs, 1e-4 relative on fp32 outputs); the fp32 CUDA-core tier
+is compared at 1e-5 relative.
+"""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from ssd import ops as O
+
+    return O
+
+
+@pytest.fixture(scope="module")
+def ws(ops):
+    return ops.Workspace(torch.device(DEV), max_rows=512, vocab=128256)
+
+
+def _rand(*shape, dtype=torch.bfloat16, scale=1.0, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(*shape, generator=g, device=DEV) * scale).to(dtype)
+
+
+def _close(a, b, rtol, atol_frac):
+    a, b = a.float(), b.float()
+    atol = atol_frac * b.abs().max().item() + 1e-12
+    torch.testing.assert_close(a, b, rtol=rtol, atol=atol)
+
+
+GEMM_SHAPES = [(1, 128, 64), (5, 256, 192), (33, 4096, 4096), (16, 1000, 512), (300, 384, 256), (64, 2048, 8192),
+               (1, 14336, 4096)]
+
+
+@pytest.mark.parametrize("T,N,K", GEMM_SHAPES)
+def test_linear_store_bf16(ops, ws, T, N, K):
+    x = _rand(T, K, seed=1)
+    w = _rand(N, K, scale=0.02, seed=2)
+    out = torch.empty(T, N, dtype=torch.bfloat16, device=DEV)
+    ops.linear(x, [w], ws, out=out)
+    ref = x.float() @ w.float().T
+    torch.cuda.synchronize()
+    ws.check_status()
+    _close(out, ref, rtol=1e-2, atol_frac=1e-2)
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 128, 64), (7, 512, 320), (33, 2048, 2048), (40, 300, 96)])
+def test_linear_store_f32(ops, ws, T, N, K):
+    x = _rand(T, K, dtype=torch.float32, seed=3)
+    w = _rand(N, K, dtype=torch.float32, scale=0.02, seed=4)
+    out = torch.empty(T, N, dtype=torch.float32, device=DEV)
+    ops.linear(x, [w], ws, out=out)
+    ref = (x.double() @ w.double().T).float()
+    torch.cuda.synchronize()
+    _close(out, ref, rtol=1e-5, atol_frac=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("act", ["none", "silu", "gelu", "relu"])
+def test_linear_bias_act(ops, ws, dtype, act):
+    T, N, K = 9, 512, 256
+    x = _rand(T, K, dtype=dtype, seed=5)
+    w = _rand(N, K, dtype=dtype, scale=0.05, seed=6)
+    b = _rand(N, dtype=dtype, scale=0.1, seed=7)
+    out = torch.empty(T, N, dtype=dtype, device=DEV)
+    ops.linear(x, [w], ws, biases=[b], act=act, out=out)
+    ref = x.float() @ w.float().T + b.float()
+    ref = {"none": ref, "silu": torch.nn.functional.silu(ref), "gelu": torch.nn.functional.gelu(ref),
+           "relu": torch.relu(ref)}[act]
+    torch.cuda.synchronize()
+    _close(out, ref, rtol=1e-2 if dtype == torch.bfloat16 else 1e-5, atol_frac=1e-2 if dtype == torch.bfloat16 else 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("T,N,K", [(1, 4096, 4096), (33, 2048, 8192), (6, 64, 128)])
+def test_linear_residual(ops, ws, dtype, T, N, K):
+    x = _rand(T, K, dtype=dtype, seed=8)
+    w = _rand(N, K, dtype=dtype, scale=0.02, seed=9)
+    resid = _rand(T, N, dtype=torch.float32, seed=10)
+    ref = resid + x.float() @ w.float().T
+    ops.linear(x, [w], ws, epilogue=1, resid=resid)
+    torch.cuda.synchronize()
+    _close(resid, ref, rtol=1e-4, atol_frac=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("T,F,K", [(1, 14336, 4096), (17, 128, 64), (33, 8192, 2048)])
+def test_swiglu(ops, ws, dtype, T, F, K):
+    x = _rand(T, K, dtype=dtype, seed=11)
+    wg = _rand(F, K, dtype=dtype, scale=0.02, seed=12)
+    wu = _rand(F, K, dtype=dtype, scale=0.02, seed=13)
+    out = torch.empty(T, F, dtype=dtype, device=DEV)
+    ops.linear(x, [wg, wu], ws, epilogue=2, layout=1, out=out)
+    ref = torch.nn.functional.silu(x.float() @ wg.float().T) * (x.float() @ wu.float().T)
+    torch.cuda.synchronize()
+    _close(out, ref, rtol=1e-2 if dtype == torch.bfloat16 else 1e-5, atol_frac=1e-2 if dtype == torch.bfloat16 else 1e-5)
+
+
+def rope_tables(head_dim, max_pos, theta=500000.0):
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
+    f = torch.arange(max_pos).float()[:, None] * inv[None, :]
+    return f.cos().to(DEV), f.sin().to(DEV)
+
+
+def rope_ref(x, pos, cos, sin):
+    # x [T, H, hd]
+    c = cos[pos.long()][:, None, :].repeat(1, 1, 2)
+    s = sin[pos.long()][:, None, :].repeat(1, 1, 2)
+    h = x.shape[-1] // 2
+    rot = torch.cat([-x[..., h:], x[..., :h]], -1)
+    return x * c + rot * s
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("H,Hkv,hd,d,T", [(32, 8, 128, 4096, 33), (32, 8, 64, 2048, 1), (4, 2, 16, 64, 7)])
+def test_qkv_rope(ops, ws, dtype, H, Hkv, hd, d, T):
+    x = _rand(T, d, dtype=dtype, seed=14)
+    wq = _rand(H * hd, d, dtype=dtype, scale=0.02, seed=15)
+    wk = _rand(Hkv * hd, d, dtype=dtype, scale=0.02, seed=16)
+    wv = _rand(Hkv * hd, d, dtype=dtype, scale=0.02, seed=17)
+    cos, sin = rope_tables(hd, 4096)
+    pos = torch.randint(0, 4000, (T,), device=DEV, dtype=torch.int32)
+    slots = torch.randperm(T + 10, device=DEV)[:T].to(torch.int32)
+    max_slots = T + 16
+    kc = torch.zeros(Hkv, max_slots, hd, dtype=dtype, device=DEV)
+    vc = torch.zeros_like(kc)
+    q = torch.empty(T, H * hd, dtype=dtype, device=DEV)
+    ops.qkv_rope(x, wq, wk, wv, H, Hkv, hd, cos, sin, pos, slots, kc, vc, q, ws)
+    torch.cuda.synchronize()
+    ws.check_status()
+    xf = x.float()
+    qr = rope_ref((xf @ wq.float().T).view(T, H, hd), pos, cos, sin).reshape(T, -1)
+    kr = rope_ref((xf @ wk.float().T).view(T, Hkv, hd), pos, cos, sin)
+    vr = (xf @ wv.float().T).view(T, Hkv, hd)
+    tol = dict(rtol=1e-2, atol_frac=1e-2) if dtype == torch.bfloat16 else dict(rtol=1e-4, atol_frac=1e-5)
+    _close(q, qr, **tol)
+    _close(kc[:, slots.long()].permute(1, 0, 2), kr, **tol)
+    _close(vc[:, slots.long()].permute(1, 0, 2), vr, **tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("T,V,K", [(1, 128256, 4096), (25, 128256, 2048), (3, 1000, 64)])
+def test_head_argmax(ops, ws, dtype, T, V, K):
+    x = _rand(T, K, dtype=dtype, seed=18)
+    w = _rand(V, K, dtype=dtype, scale=0.02, seed=19)
+    idx = torch.empty(T, dtype=torch.int32, device=DEV)
+    mx = torch.empty(T, dtype=torch.float32, device=DEV)
+    gap = torch.empty(T, dtype=torch.float32, device=DEV)
+    ops.head_argmax(x, w, idx, ws, out_max=mx, out_gap=gap)
+    logits = x.double() @ w.double().T
+    top2 = logits.topk(2, dim=-1).values
+    torch.cuda.synchronize()
+    ref = logits.argmax(-1)
+    near_tie = (top2[:, 0] - top2[:, 1]) < 1e-4
+    assert ((idx.long() == ref) | near_tie).all()
+    torch.testing.assert_close(mx.double(), top2[:, 0], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(gap.double(), top2[:, 0] - top2[:, 1], rtol=1e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("T,V,K,k,subset", [(1, 128256, 4096, 4, False), (16, 32768, 2048, 2, True),
+                                             (8, 128, 64, 3, False), (4, 5000, 256, 16, True)])
+def test_head_topk(ops, ws, dtype, T, V, K, k, subset):
+    x = _rand(T, K, dtype=dtype, seed=20)
+    w = _rand(V, K, dtype=dtype, scale=0.05, seed=21)
+    vocab_ids = None
+    if subset:
+        vocab_ids = torch.randperm(V * 3, device=DEV)[:V].sort().values.to(torch.int64)
+    tok = torch.empty(T, k, dtype=torch.int32, device=DEV)
+    lp = torch.empty(T, k, dtype=torch.float32, device=DEV)
+    ops.head_topk(x, w, k, tok, lp, ws, vocab_ids=vocab_ids)
+    logits = x.double() @ w.double().T
+    ref_lp, ref_i = torch.log_softmax(logits, -1).topk(k, dim=-1)
+    torch.cuda.synchronize()
+    ref_tok = vocab_ids[ref_i] if subset else ref_i
+    srt = torch.log_softmax(logits, -1).topk(k + 1, dim=-1).values
+    gaps = (srt[:, :-1] - srt[:, 1:]).abs()
+    ok = (tok.long() == ref_tok) | (gaps < 1e-4)
+    assert ok.all()
+    torch.testing.assert_close(lp.double(), ref_lp, rtol=1e-4, atol=2e-4)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_gemm_batch_invariance(ops, ws, dtype):
+    """A token's output bits do not depend on how many rows share the GEMM."""
+    K, N, T = 4096, 6144, 33
+    x = _rand(T, K, dtype=dtype, seed=22)
+    w = _rand(N, K, dtype=dtype, scale=0.02, seed=23)
+    full = torch.empty(T, N, dtype=torch.float32, device=DEV)
+    ops.linear(x, [w], ws, epilogue=3, out=full)
+    for t in (0, 7, 32):
+        one = torch.empty(1, N, dtype=torch.float32, device=DEV)
+        ops.linear(x[t:t + 1].contiguous(), [w], ws, epilogue=3, out=one)
+        torch.cuda.synchronize()
+        assert torch.equal(one[0], full[t]), f"row {t} differs between T=1 and T={T}"
+
+
+def attention_ref(q, kc, vc, prefix, spec_base, mask, H, Hkv, hd):
+    """Explicit per-row masked softmax attention in fp64."""
+    T = q.shape[0]
+    G = H // Hkv
+    out = torch.zeros(T, H * hd, dtype=torch.float64, device=DEV)
+    S = kc.shape[1]
+    for t in range(T):
+        valid = torch.zeros(S, dtype=torch.bool, device=DEV)
+        valid[: int(prefix[t])] = True
+        if mask is not None:
+            for b in range(mask.shape[1] * 64):
+                if (int(mask[t, b // 64].item()) >> (b % 64)) & 1:
+                    valid[int(spec_base) + b] = True
+        idx = valid.nonzero().flatten()
+        for h in range(H):
+            g = h // G
+            qv = q[t, h * hd:(h + 1) * hd].double()
+            k = kc[g, idx].double()
+            v = vc[g, idx].double()
+            p = torch.softmax(k @ qv / math.sqrt(hd), 0)
+            out[t, h * hd:(h + 1) * hd] = p @ v
+    return out
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("H,Hkv,hd,ctx,T,tree", [(32, 8, 128, 2048, 33, True), (4, 2, 16, 40, 5, True),
+                                                  (32, 8, 64, 300, 1, False), (8, 8, 128, 5000, 9, True)])
+def test_tree_attention(ops, ws, dtype, H, Hkv, hd, ctx, T, tree):
+    torch.manual_seed(0)
+    S = ctx + 80
+    kc = _rand(Hkv, S, hd, dtype=dtype, seed=24)
+    vc = _rand(Hkv, S, hd, dtype=dtype, seed=25)
+    q = _rand(T, H * hd, dtype=dtype, seed=26)
+    if tree:
+        # row 0 = root (prefix only); nodes see random ancestors among spec slots
+        prefix = torch.full((T,), ctx, dtype=torch.int32, device=DEV)
+        m = torch.zeros(T, 1, dtype=torch.int64)
+        for t in range(1, T):
+            bits = (1 << (t - 1))
+            for j in range(t - 1):
+                if torch.rand(()) < 0.3:
+                    bits |= 1 << j
+            m[t, 0] = bits
+        mask = m.to(DEV)  # int64 storage carries the uint64 bit pattern
+        spec_base = torch.tensor([ctx], dtype=torch.int32, device=DEV)
+    else:
+        prefix = torch.tensor([ctx - T + 1 + t for t in range(T)], dtype=torch.int32, device=DEV)
+        mask, spec_base = None, None
+    out = torch.empty(T, H * hd, dtype=dtype, device=DEV)
+    ops.tree_attention(q, kc, vc, H, Hkv, hd, prefix, out, ws, spec_base=spec_base, spec_mask=mask, kv_bound=S)
+    torch.cuda.synchronize()
+    ws.check_status()
+    ref = attention_ref(q, kc, vc, prefix.cpu(), ctx, mask.cpu() if mask is not None else None,
+                        H, Hkv, hd)
+    tol = dict(rtol=2e-2, atol_frac=1e-2) if dtype == torch.bfloat16 else dict(rtol=1e-4, atol_frac=1e-5)
+    _close(out, ref, **tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("keep", [[6, 7, 9], [10, 12, 13, 15], [3, 4, 5], [20]])
+def test_kv_compact(ops, dtype, keep):
+    Lyr, Hkv, S, hd = 3, 2, 32, 64
+    cache = _rand(Lyr, 2, Hkv, S, hd, dtype=dtype, seed=27)
+    ref = cache.clone()
+    start = keep[0]
+    idx = torch.tensor(keep, device=DEV)
+    ref[:, :, :, start:start + len(keep)] = ref.index_select(3, idx)
+    ks = torch.tensor(keep, dtype=torch.int32, device=DEV)
+    st = torch.tensor([start], dtype=torch.int32, device=DEV)
+    nk = torch.tensor([len(keep)], dtype=torch.int32, device=DEV)
+    ops.kv_compact(cache, st, ks, nk, max_keep=8)
+    torch.cuda.synchronize()
+    assert torch.equal(cache, ref)
