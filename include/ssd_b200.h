@@ -53,9 +53,10 @@ int ssd_version(void);
 const char* ssd_last_error(void);
 int ssd_device_sm_count(int device);
 
-/* Workspace bytes the GEMM / attention / head entry points need for up to
- * `max_rows` rows and vocab size `vocab` (rows = tokens of one forward). */
-int64_t ssd_workspace_bytes(int64_t max_rows, int64_t vocab);
+/* Workspace bytes the GEMM / attention / head entry points need for forwards
+ * of up to `max_rows` token rows whose lm_head heads (argmax / top-k) see up
+ * to `max_head_rows` rows, over a vocabulary of `vocab` tokens. */
+int64_t ssd_workspace_bytes(int64_t max_rows, int64_t max_head_rows, int64_t vocab);
 
 /* Embedding gather: resid[t, :] = table[ids[t], :] (fp32 out).
  * Replaces base.embed_tokens(input_ids), ssd/models/subnetwork_draft.py:290-291. */

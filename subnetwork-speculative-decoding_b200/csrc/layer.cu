@@ -200,9 +200,9 @@ using namespace ssd;
 
 extern "C" {
 
-int64_t ssd_workspace_bytes(int64_t max_rows, int64_t vocab) {
+int64_t ssd_workspace_bytes(int64_t max_rows, int64_t max_head_rows, int64_t vocab) {
   const int64_t tiles_v = (vocab + kTileM - 1) / kTileM;
-  const int64_t heads = max_rows * tiles_v * (2 + 2 * kMaxTopK) * 4;
+  const int64_t heads = max_head_rows * tiles_v * (2 + 2 * kMaxTopK) * 4;
   // split-K partials: at most 2 CTAs per SM, each a 128 x BN fp32 tile
   int64_t bn = max_rows > 256 ? 128 : ((max_rows + 15) / 16) * 16;
   if (bn < 16) bn = 16;
@@ -212,8 +212,10 @@ int64_t ssd_workspace_bytes(int64_t max_rows, int64_t vocab) {
   const int64_t splitk_tc = 2LL * device_sms() * bn * kTileM * 4;
   const int64_t splitk_simt = 4LL * device_sms() * simt_tiles_n * 4 * kTileM * 4;
   const int64_t splitk = splitk_tc > splitk_simt ? splitk_tc : splitk_simt;
-  // attention partials: rows * 64 q-heads * 64 splits * (head_dim 128 + 2)
-  const int64_t attn = max_rows * 64 * 64 * 130 * 4;
+  // attention partials: (CTAs <= 2 * SMs + row-tile blocks) x 32 queries x
+  // (head_dim <= 128 + 2) floats; row-tile blocks <= rows * n_heads / 32 with
+  // n_heads <= 128.
+  const int64_t attn = (2LL * device_sms() + max_rows * 4 + 8) * 32 * 130 * 4;
   int64_t body = heads > splitk ? heads : splitk;
   body = body > attn ? body : attn;
   return kCounterBytes + body;

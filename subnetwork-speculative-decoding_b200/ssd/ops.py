@@ -42,9 +42,10 @@ class Workspace:
     One workspace per stream.
     """
 
-    def __init__(self, device: torch.device, max_rows: int, vocab: int):
+    def __init__(self, device: torch.device, max_rows: int, vocab: int, max_head_rows: Optional[int] = None):
         L.load()
-        nbytes = int(L.load().ssd_workspace_bytes(max(1, max_rows), max(1, vocab)))
+        head_rows = max_rows if max_head_rows is None else max_head_rows
+        nbytes = int(L.load().ssd_workspace_bytes(max(1, max_rows), max(1, head_rows), max(1, vocab)))
         self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.nbytes = nbytes

@@ -1,0 +1,214 @@
+"""End-to-end parity of the B200 round (through the C ABI) against the
+reference's recorded outputs and the CPU oracle.
+
+fp32 tier: token ids must equal the reference's exactly (tiny model, and
+BASELINE config 1 at full Llama-3.2-1B size). bf16 tier: speculative output
+equals our own target-only decode, and matches the reference's fp32 decode
+of the same (bf16-rounded) weights up to the first near-tie (top-2 logit gap
+< 1e-2); per-step logits within rtol 2e-2.
+"""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from ssd import synthetic as S
+from ssd.config import BridgeConfig, DraftingConfig
+from ssd.engine.speculative import SpeculativeGenerator, TargetRunner, autoregressive_generate
+from ssd.engine.tree_drafter import TreeDrafter
+from ssd.models import SubnetworkDraftModel
+
+pytestmark = pytest.mark.gpu
+GOLD = Path(__file__).parent / "golden"
+DEV = torch.device("cuda:0")
+
+TREES = {
+    "chain": dict(depth=4, branch=1),
+    "tree": dict(depth=3, branch=[3, 2, 2]),
+    "pruned": dict(depth=5, branch=[4, 3, 2, 2, 1], width=[4, 6, 6, 4, 4], max_nodes=12),
+    "deep_chain": dict(depth=8, branch=1),
+}
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    return json.loads((GOLD / "tiny.json").read_text())
+
+
+def tiny_base(dtype=torch.float32):
+    base = S.build_base_model("tiny", 0, torch.float32, "cpu")
+    return base.to(dtype).to(DEV)
+
+
+@pytest.fixture(scope="module")
+def base32(tiny):
+    b = S.build_base_model("tiny", 0, torch.float32, "cpu")
+    assert S.weights_checksum(b) == tiny["checksum"]
+    return b.to(DEV)
+
+
+def make_draft(base, layers, seed, in_std, out_std, cfg=None):
+    d = SubnetworkDraftModel(base, layers, cfg or BridgeConfig())
+    if d.bridges:
+        S.init_bridges_(d.bridges, seed, in_std=in_std, out_std=out_std)
+        d.bridges.to(base.model.embed_tokens.weight.dtype)
+    return d
+
+
+def test_forward_logits_fp32(tiny, base32):
+    target = TargetRunner(base32)
+    ids = torch.tensor([tiny["forward"]["ids"]], device=DEV)
+    logits = target(ids).logits[0].cpu()
+    np.testing.assert_allclose(logits.numpy(), np.array(tiny["forward"]["logits"]), atol=2e-5, rtol=1e-4)
+
+
+def test_autoregressive_fp32_matches_reference(tiny, base32):
+    target = TargetRunner(base32)
+    for p, ref in zip(tiny["prompts"], tiny["ar"]):
+        res = autoregressive_generate(target, torch.tensor([p]), 40, {-1})
+        assert res.tokens == ref
+
+
+@pytest.mark.parametrize("draft_kind", ["untrained", "perfect"])
+@pytest.mark.parametrize("tree_name", list(TREES))
+def test_speculative_fp32_matches_reference(tiny, base32, draft_kind, tree_name):
+    layers = [0, 3, 5] if draft_kind == "untrained" else list(range(6))
+    draft = make_draft(base32, layers, 0, 0.125, 0.02, BridgeConfig(init_std=0.02))
+    target = TargetRunner(base32)
+    gold = tiny["sd"][f"{draft_kind}/{tree_name}"]
+    gen = SpeculativeGenerator(base32, draft, DraftingConfig(**TREES[tree_name]), target)
+    for p, run in zip(tiny["prompts"], gold["runs"]):
+        res = gen.generate(torch.tensor([p]), 40, {-1})
+        assert res.tokens == run["tokens"]
+        assert res.accepted_per_round == run["accepted_per_round"]
+        assert res.tree_sizes == run["tree_sizes"]
+
+
+@pytest.mark.parametrize("tree_name", list(TREES))
+def test_tree_build_fp32_matches_reference(tiny, base32, tree_name):
+    """Device tree (top-k head, level prune, max_nodes prune) == reference tree."""
+    draft = make_draft(base32, [0, 3, 5], 0, 0.125, 0.02, BridgeConfig(init_std=0.02))
+    target = TargetRunner(base32)
+    ft = tiny["sd"][f"untrained/{tree_name}"]["first_tree"]
+    cache = target.new_cache(64)
+    out = target(torch.tensor([tiny["prompts"][0]], device=DEV), past_key_values=cache, logits_to_keep=1)
+    assert int(out.logits[0, -1].argmax()) == ft["root"]
+    drafter = TreeDrafter(draft, DraftingConfig(**TREES[tree_name]))
+    tree = drafter.build(cache, torch.tensor([[ft["root"]]]), ft["committed"])
+    ref = ft["tree"]
+    for key in ("tokens", "parents", "depths", "ranks", "draft_pos"):
+        assert getattr(tree, key) == ref[key], key
+    np.testing.assert_allclose(tree.scores, ref["scores"], rtol=1e-5, atol=1e-5)
+    assert cache.get_seq_length() == ft["committed"] + 1 + drafter.max_tree_cache()
+
+
+def test_tree_mask_and_keep_positions_fp32(tiny, base32):
+    g = tiny["tree_mask"]
+    draft = make_draft(base32, [0, 2, 5], 1, 0.125, 0.02)
+    cache = draft.new_cache(32)
+    draft(torch.tensor([g["prefix"]], device=DEV), past_key_values=cache)
+    n = len(g["tokens"])
+    mask = torch.zeros(n, n, dtype=torch.bool)
+    for i in range(n):
+        j = i
+        while j != -1:
+            mask[i, j] = True
+            j = g["parents"][j]
+    pos = torch.tensor([[6 + d for d in g["depth"]]])
+    logits = draft(torch.tensor([g["tokens"]], device=DEV), position_ids=pos, past_key_values=cache,
+                   tree_attention_mask=mask).logits[0].cpu()
+    np.testing.assert_allclose(logits.numpy(), np.array(g["logits"]), atol=2e-5, rtol=1e-4)
+    cache.keep_positions(6, torch.tensor(g["keep"]))
+    nxt = draft(torch.tensor([[g["next_token"]]], device=DEV), past_key_values=cache).logits[0, -1].cpu()
+    np.testing.assert_allclose(nxt.numpy(), np.array(g["next_logits"]), atol=2e-5, rtol=1e-4)
+
+
+def test_vocab_subset_and_eos_fp32(tiny, base32):
+    from ssd.data.token_freq import top_vocab
+
+    target = TargetRunner(base32)
+    vs = tiny["vocab_subset"]
+    draft = SubnetworkDraftModel(base32, list(range(6)))
+    sub = top_vocab(torch.arange(128).flip(0), 40, always={127})
+    assert sub.tolist() == vs["ids"]
+    draft.set_vocab_subset(sub)
+    res = SpeculativeGenerator(base32, draft, DraftingConfig(**TREES["tree"]), target).generate(
+        torch.tensor([vs["prompt"]]), 40, {-1})
+    assert res.tokens == vs["tokens"] and res.accepted_per_round == vs["accepted_per_round"]
+    out = draft(torch.tensor([vs["prompt"]], device=DEV))
+    assert out.logits.shape[-1] == 40 and out.vocab_ids is draft.vocab_ids
+    g = tiny["eos"]
+    eos = set(g["eos"])
+    assert autoregressive_generate(target, torch.tensor([g["prompt"]]), 30, eos).tokens == g["ar"]
+    draft = SubnetworkDraftModel(base32, list(range(6)))
+    sd = SpeculativeGenerator(base32, draft, DraftingConfig(**TREES["chain"]), target).generate(
+        torch.tensor([g["prompt"]]), 30, eos)
+    assert sd.tokens == g["sd"] and sd.tokens[-1] in eos
+
+
+def test_identity_bridges_equal_layer_skipping(base32):
+    """Zero-init bridges == the selected layers back to back
+    (reference tests/test_forward_pass.py:119-130)."""
+    import oracle as O
+    from oracle.model import weights_from_hf
+
+    draft = SubnetworkDraftModel(base32, [0, 3, 5], BridgeConfig(init_std=0.0))
+    ids = torch.randint(0, 128, (1, 9), generator=torch.Generator().manual_seed(3))
+    ours = draft(ids.to(DEV)).logits[0].cpu().numpy()
+    w, conf = weights_from_hf(base32)
+    skip = O.OracleModel(w, conf, [0, 3, 5], {n: None for n in draft.bridges})
+    skip.pre_layer_bridge, skip.pre_norm_bridge = [None] * 3, None  # plain layer skipping
+    ref = skip.forward(ids[0].tolist())
+    np.testing.assert_allclose(ours, ref, atol=2e-5, rtol=1e-4)
+
+
+def test_batched_forward_shapes(base32):
+    draft = SubnetworkDraftModel(base32, [0, 2, 5])
+    S.init_bridges_(draft.bridges, 4, in_std=0.125, out_std=0.02)
+    draft.bridges.to(DEV)
+    ids = torch.randint(0, 128, (2, 11), generator=torch.Generator().manual_seed(0)).to(DEV)
+    out = draft(ids, output_bridge_states=True)
+    assert out.logits.shape == (2, 11, 128) and out.hidden_states.shape == (2, 11, 64)
+    assert set(out.bridge_states) == {"into_2", "into_5"}
+    assert torch.isfinite(out.logits).all()
+    assert draft(ids, logits_to_keep=3).logits.shape == (2, 3, 128)
+    assert draft(ids, compute_logits=False).logits is None
+
+
+@pytest.mark.parametrize("tree_name", list(TREES))
+def test_bf16_speculative_equals_target_only(tree_name):
+    """bf16 tier on the tiny model: greedy SD output == our target-only decode."""
+    base = tiny_base(torch.bfloat16)
+    target = TargetRunner(base)
+    draft = make_draft(base, [0, 3, 5], 0, 0.125, 0.02, BridgeConfig(init_std=0.02))
+    for s in range(3):
+        p = S.make_prompt(s, 5 + 4 * s, 128)
+        ar = autoregressive_generate(target, p, 40, {-1})
+        sd = SpeculativeGenerator(base, draft, DraftingConfig(**TREES[tree_name]), target).generate(p, 40, {-1})
+        assert sd.tokens == ar.tokens
+        assert sum(sd.accepted_per_round) >= 39
+
+
+@pytest.mark.slow
+def test_c1_full_size_fp32_matches_reference():
+    """BASELINE config 1 at full size: SD output == the reference's own
+    target-only greedy decode (bit-exact ids), fp32."""
+    g = json.loads((GOLD / "c1.json").read_text())
+    spec = S.CONFIGS["c1"]
+    base = S.build_base_model(spec.model, spec.seed, torch.float32, "cpu")
+    assert S.weights_checksum(base) == g["checksum"]
+    base = base.to(DEV)
+    target = TargetRunner(base)
+    draft = SubnetworkDraftModel(base, spec.draft_layers, BridgeConfig(hidden_dim=spec.bridge_hidden))
+    S.init_bridges_(draft.bridges, spec.seed, spec.bridge_in_std, spec.bridge_out_std)
+    draft.bridges.to(DEV)
+    ids = torch.tensor([g["prompt"]])
+    ar = autoregressive_generate(target, ids, spec.max_new_tokens, set())
+    assert ar.tokens == g["ar"]
+    sd = SpeculativeGenerator(base, draft, DraftingConfig(**spec.drafting), target).generate(
+        ids, spec.max_new_tokens, set())
+    assert sd.tokens == g["ar"]
+    assert sd.accepted_per_round == g["accepted_per_round"]

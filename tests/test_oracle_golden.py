@@ -1,0 +1,165 @@
+"""Pin the CPU oracle against golden fixtures produced by the reference itself
+(tests/golden/make_golden.py). CPU only."""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from oracle.model import bridges_from_module, weights_from_hf
+from ssd import synthetic as S
+from ssd.config import BridgeConfig
+
+GOLD = Path(__file__).parent / "golden"
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    return json.loads((GOLD / "tiny.json").read_text())
+
+
+@pytest.fixture(scope="module")
+def base():
+    return S.build_base_model("tiny", 0, torch.float32, "cpu")
+
+
+def make_bridges(d, layers, n_layers, seed, in_std, out_std, cfg=None):
+    from ssd.models.bridges import TransitionBridge
+    from ssd.models.subnetwork_draft import plan_bridges
+
+    cfg = cfg or BridgeConfig()
+    mods = torch.nn.ModuleDict({s.name: TransitionBridge.from_config(d, cfg) for s in plan_bridges(layers, n_layers)})
+    S.init_bridges_(mods, seed, in_std=in_std, out_std=out_std)
+    return bridges_from_module(mods, vars(cfg))
+
+
+def oracle_models(base, layers, bridges=None):
+    w, conf = weights_from_hf(base)
+    target = O.OracleModel(w, conf, list(range(conf["layers"])))
+    draft = O.OracleModel(w, conf, layers, bridges)
+    return target, draft
+
+
+def test_weights_checksum(tiny, base):
+    assert S.weights_checksum(base) == tiny["checksum"], "CPU RNG on this host differs from the fixture host"
+
+
+def test_forward_logits(tiny, base):
+    target, _ = oracle_models(base, list(range(6)))
+    logits = target.forward(tiny["forward"]["ids"])
+    np.testing.assert_allclose(logits, np.array(tiny["forward"]["logits"]), atol=1e-5, rtol=1e-4)
+
+
+def test_autoregressive_tokens(tiny, base):
+    target, _ = oracle_models(base, list(range(6)))
+    for p, ref in zip(tiny["prompts"], tiny["ar"]):
+        assert O.autoregressive_generate(target, p, 40, {-1})["tokens"] == ref
+
+
+TREES = {
+    "chain": dict(depth=4, branch=1),
+    "tree": dict(depth=3, branch=[3, 2, 2]),
+    "pruned": dict(depth=5, branch=[4, 3, 2, 2, 1], width=[4, 6, 6, 4, 4], max_nodes=12),
+    "deep_chain": dict(depth=8, branch=1),
+}
+
+
+@pytest.mark.parametrize("draft_kind", ["untrained", "perfect"])
+@pytest.mark.parametrize("tree_name", list(TREES))
+def test_speculative_rounds(tiny, base, draft_kind, tree_name):
+    layers = [0, 3, 5] if draft_kind == "untrained" else list(range(6))
+    br = make_bridges(64, layers, 6, 0, 0.125, 0.02, BridgeConfig(init_std=0.02)) if draft_kind == "untrained" else {}
+    target, draft = oracle_models(base, layers, br)
+    gold = tiny["sd"][f"{draft_kind}/{tree_name}"]
+    for p, run in zip(tiny["prompts"], gold["runs"]):
+        res = O.speculative_generate(target, draft, TREES[tree_name], p, 40, {-1})
+        assert res["tokens"] == run["tokens"]
+        assert res["accepted_per_round"] == run["accepted_per_round"]
+        assert res["tree_sizes"] == run["tree_sizes"]
+    # the first round's tree, structure and scores
+    ft = gold["first_tree"]
+    cache = target.new_cache(64)
+    logits = target.forward(tiny["prompts"][0], None, cache, logits_to_keep=1)[-1]
+    assert int(np.argmax(logits)) == ft["root"]
+    drafter = O.OracleTreeDrafter(draft, **{k: TREES[tree_name].get(k) for k in ("depth", "branch", "width",
+                                                                                  "max_nodes")})
+    tree = drafter.build(cache, [ft["root"]], ft["committed"])
+    ref = ft["tree"]
+    for key in ("tokens", "parents", "depths", "ranks", "draft_pos"):
+        assert getattr(tree, key) == ref[key], key
+    np.testing.assert_allclose(tree.scores, ref["scores"], rtol=1e-5, atol=1e-6)
+
+
+def test_vocab_subset(tiny, base):
+    target, draft = oracle_models(base, list(range(6)))
+    vs = tiny["vocab_subset"]
+    sub = O.top_vocab(np.arange(128)[::-1].copy(), 40, {127})
+    assert sub.tolist() == vs["ids"]
+    draft.set_vocab_subset(sub)
+    res = O.speculative_generate(target, draft, TREES["tree"], vs["prompt"], 40, {-1})
+    assert res["tokens"] == vs["tokens"]
+    assert res["accepted_per_round"] == vs["accepted_per_round"]
+
+
+def test_eos_stop(tiny, base):
+    target, draft = oracle_models(base, list(range(6)))
+    g = tiny["eos"]
+    eos = set(g["eos"])
+    assert O.autoregressive_generate(target, g["prompt"], 30, eos)["tokens"] == g["ar"]
+    assert O.speculative_generate(target, draft, TREES["chain"], g["prompt"], 30, eos)["tokens"] == g["sd"]
+
+
+def test_tree_mask_and_keep_positions(tiny, base):
+    g = tiny["tree_mask"]
+    br = make_bridges(64, [0, 2, 5], 6, 1, 0.125, 0.02)
+    _, draft = oracle_models(base, [0, 2, 5], br)
+    cache = draft.new_cache(32)
+    draft.forward(g["prefix"], None, cache)
+    n = len(g["tokens"])
+    mask = np.zeros((n, n), dtype=bool)
+    for i in range(n):
+        j = i
+        while j != -1:
+            mask[i, j] = True
+            j = g["parents"][j]
+    pos = [6 + d for d in g["depth"]]
+    logits = draft.forward(g["tokens"], pos, cache, tree_mask=mask)
+    np.testing.assert_allclose(logits, np.array(g["logits"]), atol=1e-5, rtol=1e-4)
+    cache.keep_positions(6, g["keep"])
+    nxt = draft.forward([g["next_token"]], None, cache)[-1]
+    np.testing.assert_allclose(nxt, np.array(g["next_logits"]), atol=1e-5, rtol=1e-4)
+
+
+def test_sampling_stream_matches_reference(tiny):
+    """Same seeds -> same torch random stream -> the oracle reproduces the
+    reference's sampled tokens (allowing a rare flip from float rounding)."""
+    g = tiny["sampling"]
+    base8 = S.build_base_model("tiny_v8", 1, torch.float32, "cpu")
+    with torch.no_grad():
+        base8.lm_head.weight.mul_(8.0)
+    assert S.weights_checksum(base8) == g["checksum"]
+    br = make_bridges(64, [0, 5], 6, 2, 0.125, 0.05, BridgeConfig(init_std=0.05))
+    target, draft = oracle_models(base8, [0, 5], br)
+    for run in g["runs"]:
+        same = 0
+        for s, ref in enumerate(run["tokens"]):
+            same += O.speculative_generate(target, draft, run["cfg"], [1, 5, 2], 3, set(), seed=s)["tokens"] == ref
+        assert same >= 0.95 * len(run["tokens"])
+
+
+def test_plan_bridges():
+    assert O.plan_bridges([0, 2, 5], 6) == [("into_2", 1, 2), ("into_5", 3, 5)]
+    assert [s[0] for s in O.plan_bridges([1, 2, 4], 6)] == ["into_1", "into_4", "into_norm"]
+
+
+def test_c1_fixture_prompt_and_checksum_format():
+    p = GOLD / "c1.json"
+    if not p.exists():
+        pytest.skip("c1 fixture not generated")
+    g = json.loads(p.read_text())
+    assert len(g["prompt"]) == 128 and len(g["ar"]) == 64
+    assert g["prompt"] == S.make_prompt(0, 128, 128256)[0].tolist()
+    assert g["sd"] == g["ar"], "the reference's own SD must equal its AR (greedy identity)"
