@@ -1,0 +1,594 @@
+#!/usr/bin/env python
+"""Benchmark of the SSD speculative-decoding round on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3|c2|c1]
+    python bench.py --impl reference ...      # CPU port of the reference path
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Workload (default c3 = BASELINE config 3): Llama-3-8B architecture, bf16,
+random N(0, 0.02) weights (seed 2) with planted acceptance (o/down of
+non-draft layers x 0.05), draft layers [0, 15, 31] + 2 bridges, greedy tree
+depth 6 / branch [4,2,2,1,1,1] / max_nodes 32, 2048-token prompts, 256 new
+tokens. Eight independent sequences (prompt seeds 2..9) are split
+round-robin over the ranks (data parallel, fixed total work: strong scaling).
+
+A step = every sequence of this rank decoded once: each sequence's prefill is
+untimed, its 256-token speculative decode is timed with CUDA events between a
+barrier + synchronize on both sides (max over ranks). `value` = decode tok/s
+of all ranks; `e2e` = the same through the public API
+(SpeculativeGenerator.generate on a pinned host prompt, returning host
+tokens; prefill and copies included). The target-only baseline is timed on
+the same sequences; the CPU baseline runs the oracle (numpy port of the
+reference path) on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "subnetwork-speculative-decoding_b200")
+for _p in (PKG, ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "decode tok/s at bs=1 + mean accepted tokens/round; speedup vs target-only AR"
+N_SEQUENCES = 8
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3"])
+    ap.add_argument("--sequences", type=int, default=N_SEQUENCES)
+    ap.add_argument("--max-new", type=int, default=None, help="override new tokens per sequence")
+    ap.add_argument("--prompt-len", type=int, default=None, help="override the prompt length")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ar", action="store_true", help="skip the target-only baseline")
+    ap.add_argument("--ncu-case", choices=["gemm", "attention"], default=None,
+                    help="run one small launch set of a kernel for an ncu capture, then exit")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int, pci_bus_id: str | None):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        sel = pci_bus_id or str(device_index)
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200", "-i", sel]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        sm, smax, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active") and not v.lower().startswith("not"):
+                    reasons.add(n)
+        os.unlink(self.file.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ------------------------------------------------------------------ helpers
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def model_bytes(w, layers=None, bridges=(), head_rows=None) -> float:
+    """Algorithmic weight bytes one forward reads (each weight once)."""
+    es = 2 if str(w.dtype) == "torch.bfloat16" else 4
+    layers = range(w.L) if layers is None else layers
+    per_layer = (w.H * w.hd + 2 * w.Hkv * w.hd) * w.d + w.H * w.hd * w.d + 3 * w.d * w.F + 2 * w.d
+    total = per_layer * len(list(layers)) * es + w.d * es
+    for b in bridges:
+        total += sum(p.numel() * p.element_size() for p in b.parameters())
+    total += (head_rows if head_rows is not None else w.V) * w.d * es
+    return float(total)
+
+
+def build(spec, dev):
+    import torch
+
+    from ssd import synthetic as S
+    from ssd.config import BridgeConfig, DraftingConfig
+    from ssd.data.token_freq import top_vocab
+    from ssd.engine.speculative import TargetRunner
+    from ssd.models import SubnetworkDraftModel
+
+    gen = "cpu" if spec.dtype == torch.float32 else "cuda"
+    base = S.build_base_model(spec.model, spec.seed, spec.dtype, dev, plant_layers=spec.draft_layers,
+                              plant_scale=spec.plant_scale, gen_device=gen)
+    target = TargetRunner(base)
+    draft = SubnetworkDraftModel(base, spec.draft_layers, BridgeConfig(hidden_dim=spec.bridge_hidden))
+    S.init_bridges_(draft.bridges, spec.seed, spec.bridge_in_std, spec.bridge_out_std)
+    draft.bridges.to(spec.dtype)
+    if spec.draft_vocab:
+        draft.set_vocab_subset(top_vocab(S.zipf_counts(base.config.vocab_size, spec.seed), spec.draft_vocab))
+    cfg = DraftingConfig(**spec.drafting)
+    return base, target, draft, cfg
+
+
+def sync_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sync_sum(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ------------------------------------------------------------ kernel roofline
+def gemm_roofline(w, rows: int, dev) -> dict:
+    """Average duration of the tcgen05 GEMM launches of one verify forward
+    (rows = root + tree): each GEMM type is captured once per layer (32
+    distinct weight matrices, > L2) in a CUDA graph and replayed with CUDA
+    events around it. achieved = algorithmic bytes / device time."""
+    import torch
+
+    from ssd import _lib as L
+    from ssd import ops
+
+    ws = ops.Workspace(dev, max_rows=max(rows, 64), vocab=w.V, max_head_rows=rows)
+    g = torch.Generator(device=dev).manual_seed(0)
+    x_d = (torch.randn(rows, w.d, generator=g, device=dev) * 0.5).to(w.dtype)
+    x_a = (torch.randn(rows, w.H * w.hd, generator=g, device=dev) * 0.5).to(w.dtype)
+    x_f = (torch.randn(rows, w.F, generator=g, device=dev) * 0.5).to(w.dtype)
+    q_out = torch.empty(rows, (w.H + 2 * w.Hkv) * w.hd, dtype=w.dtype, device=dev)
+    h_out = torch.empty(rows, w.F, dtype=w.dtype, device=dev)
+    resid = torch.zeros(rows, w.d, dtype=torch.float32, device=dev)
+    idx = torch.empty(rows, dtype=torch.int32, device=dev)
+    es = 2 if w.dtype == torch.bfloat16 else 4
+    kinds = {
+        "qkv": (lambda lw: ops.linear(x_d, [lw.q, lw.k, lw.v], ws, out=q_out),
+                (w.H + 2 * w.Hkv) * w.hd * w.d * es + rows * w.d * es + rows * (w.H + 2 * w.Hkv) * w.hd * es),
+        "o_proj": (lambda lw: ops.linear(x_a, [lw.o], ws, epilogue=L.EPI_RESIDUAL, resid=resid),
+                   w.d * w.H * w.hd * es + rows * w.H * w.hd * es + 2 * rows * w.d * 4),
+        "gate_up": (lambda lw: ops.linear(x_d, [lw.gate, lw.up], ws, epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS,
+                                          out=h_out),
+                    2 * w.F * w.d * es + rows * w.d * es + rows * w.F * es),
+        "down": (lambda lw: ops.linear(x_f, [lw.down], ws, epilogue=L.EPI_RESIDUAL, resid=resid),
+                 w.d * w.F * es + rows * w.F * es + 2 * rows * w.d * 4),
+    }
+    out = {}
+    total_b, total_t = 0.0, 0.0
+    s = torch.cuda.Stream(device=dev)
+    for name, (fn, nbytes) in kinds.items():
+        for lw in w.layers[:2]:  # eager warm-up (map cache, attributes)
+            fn(lw)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.graph(graph, stream=s):
+            for lw in w.layers:
+                fn(lw)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        for _ in range(2):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        t = e0.elapsed_time(e1) / 1e3 / (reps * len(w.layers))
+        out[name] = {"us": t * 1e6, "gbs": nbytes / t / 1e9, "bytes": nbytes}
+        total_b += nbytes * w.L
+        total_t += t * w.L
+    # lm_head + argmax over the full vocabulary (1 GB, > L2)
+    graph = torch.cuda.CUDAGraph()
+    ops.head_argmax(x_d, w.lm_head, idx, ws)
+    torch.cuda.synchronize(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.graph(graph, stream=s):
+        ops.head_argmax(x_d, w.lm_head, idx, ws)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = e0.elapsed_time(e1) / 1e3 / 5
+    nb = w.V * w.d * es + rows * w.d * es
+    out["lm_head_argmax"] = {"us": t * 1e6, "gbs": nb / t / 1e9, "bytes": nb}
+    total_b += nb
+    total_t += t
+    return {"per_type": out, "bytes": total_b, "seconds": total_t, "launches": 4 * w.L + 1,
+            "gbs": total_b / total_t / 1e9}
+
+
+# ------------------------------------------------------------- CPU baseline
+def build_oracle(spec):
+    """The oracle (numpy restatement of the reference path) in fp32 on the
+    host, with the workload's weights, bridges and draft vocabulary."""
+    import numpy as np
+    import torch
+
+    import oracle as O
+    from oracle.model import bridges_from_module, weights_from_hf
+    from ssd import synthetic as S
+    from ssd.config import BridgeConfig
+    from ssd.models.bridges import TransitionBridge
+    from ssd.models.subnetwork_draft import plan_bridges
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    base = S.build_base_model(spec.model, spec.seed, torch.float32, "cpu", plant_layers=spec.draft_layers,
+                              plant_scale=spec.plant_scale)
+    w, conf = weights_from_hf(base, np.float32)
+    bcfg = BridgeConfig(hidden_dim=spec.bridge_hidden)
+    mods = torch.nn.ModuleDict({s.name: TransitionBridge.from_config(conf["hidden"], bcfg)
+                                for s in plan_bridges(spec.draft_layers, conf["layers"])})
+    S.init_bridges_(mods, spec.seed, spec.bridge_in_std, spec.bridge_out_std)
+    br = bridges_from_module(mods, vars(bcfg), np.float32)
+    target = O.OracleModel(w, conf, list(range(conf["layers"])), dtype=np.float32)
+    draft = O.OracleModel(w, conf, spec.draft_layers, br, dtype=np.float32)
+    if spec.draft_vocab:
+        draft.set_vocab_subset(O.top_vocab(S.zipf_counts(conf["vocab"], spec.seed).numpy(), spec.draft_vocab))
+    return base, target, draft
+
+
+CPU_SAMPLE = dict(prompt_len=64, n_tokens=6)
+
+
+def oracle_step(spec, target, draft, seq: int) -> tuple[int, float, list]:
+    """One bounded sample: speculative decode of CPU_SAMPLE tokens after a
+    short prompt of sequence `seq`, prefill included."""
+    import oracle as O
+    from ssd import synthetic as S
+
+    ids = S.make_prompt(spec.seed + seq, CPU_SAMPLE["prompt_len"], target.conf["vocab"])[0].tolist()
+    t0 = time.time()
+    res = O.speculative_generate(target, draft, dict(spec.drafting), ids, CPU_SAMPLE["n_tokens"], set())
+    return len(res["tokens"]), time.time() - t0, res["accepted_per_round"]
+
+
+def cpu_sample_text(spec, steps: int) -> str:
+    return (f"oracle (numpy fp32 port of the reference path) speculative decode of {CPU_SAMPLE['n_tokens']} tokens "
+            f"after a {CPU_SAMPLE['prompt_len']}-token prompt (prefill included), {steps} sequence(s), same "
+            f"{spec.model} weights/tree as the GPU arm")
+
+
+def cpu_baseline(spec, steps: int = 1) -> dict:
+    t0 = time.time()
+    _, target, draft = build_oracle(spec)
+    build_s = time.time() - t0
+    n, t, acc = 0, 0.0, []
+    for s in range(steps):
+        dn, dt, da = oracle_step(spec, target, draft, s)
+        n, t, acc = n + dn, t + dt, acc + da
+    return {"value": n / t, "unit": "tok/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": cpu_sample_text(spec, steps) + f"; build {build_s:.0f}s",
+            "mean_accepted": sum(acc) / max(1, len(acc))}
+
+
+def reference_arm(args) -> None:
+    """--impl reference: the CPU port of the reference path on the host cores,
+    rank 0 only; each step is one bounded sample (one sequence)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from ssd import synthetic as S
+
+    spec = S.CONFIGS[args.workload]
+    t0 = time.time()
+    _, target, draft = build_oracle(spec)
+    build_s = time.time() - t0
+    for i in range(args.warmup):
+        oracle_step(spec, target, draft, i)
+    n, t, acc = 0, 0.0, []
+    for i in range(args.steps):
+        dn, dt, da = oracle_step(spec, target, draft, args.warmup + i)
+        n, t, acc = n + dn, t + dt, acc + da
+    value = n / t
+    cores = os.cpu_count() or 1
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "model": spec.model, "tree": spec.drafting},
+        "mean_accepted": sum(acc) / max(1, len(acc)),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": cpu_sample_text(spec, args.steps) + f"; build {build_s:.0f}s"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ main arm
+def ncu_case(args, dev) -> None:
+    """Small fixed launch set of one kernel for `ncu -k ...` captures."""
+    import torch
+
+    from ssd import _lib as L
+    from ssd import ops
+
+    torch.manual_seed(0)
+    if args.ncu_case == "gemm":
+        # the 8B down_proj shape at verify size: K=14336 -> 4096, 33 rows
+        K, N, T = 14336, 4096, 33
+        ws = ops.Workspace(dev, 64, 1, 1)
+        x = (torch.randn(T, K, device=dev) * 0.5).bfloat16()
+        wts = [(torch.randn(N, K, device=dev) * 0.02).bfloat16() for _ in range(3)]
+        resid = torch.zeros(T, N, device=dev)
+        for wt in wts:
+            ops.linear(x, [wt], ws, epilogue=L.EPI_RESIDUAL, resid=resid)
+    else:
+        from ssd.models.runner import ForwardInputs
+
+        H, Hkv, hd, ctx, T = 32, 8, 128, 16384, 33
+        ws = ops.Workspace(dev, 64, 1, 64)
+        kc = torch.randn(Hkv, ctx + 64, hd, device=dev).bfloat16()
+        vc = torch.randn(Hkv, ctx + 64, hd, device=dev).bfloat16()
+        q = torch.randn(T, H * hd, device=dev).bfloat16()
+        out = torch.empty_like(q)
+        f = ForwardInputs(T, dev, 1)
+        f.prefix_len.fill_(ctx)
+        f.spec_base.fill_(ctx)
+        f.mask[:, 0] = torch.tensor([(1 << (t % 60)) - 1 if t else 0 for t in range(T)], device=dev)
+        for _ in range(3):
+            ops.tree_attention(q, kc, vc, H, Hkv, hd, f.prefix_len, out, ws, spec_base=f.spec_base, spec_mask=f.mask,
+                               kv_bound=ctx + 64)
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"ncu_case": args.ncu_case, "ok": True}))
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if args.ncu_case:
+        ncu_case(args, dev)
+        return
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    from ssd import _lib
+    from ssd import synthetic as S
+    from ssd.engine.round import GreedyRound, TargetStep, TreePlan, cache_capacity
+    from ssd.engine.speculative import SpeculativeGenerator, _finish
+
+    spec = S.CONFIGS[args.workload]
+    P = args.prompt_len or spec.prompt_len
+    max_new = args.max_new or spec.max_new_tokens
+    t_build = time.time()
+    base, target, draft, cfg = build(spec, dev)
+    w = target.weights
+    seqs = [S.make_prompt(spec.seed + i, P, w.V) for i in range(args.sequences)]
+    mine = seqs[rank::world]
+    cap = cache_capacity(P, max_new, TreePlan(cfg))
+    eng = GreedyRound(target, draft, cfg, target.new_cache(cap), max_new)
+    plan_rows = eng.plan.rows
+    build_s = time.time() - t_build
+
+    def decode(ids, phase_acc=None):
+        eng.prefill(ids.to(dev))
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        evs = []
+        e0.record()
+        out = eng.tokens()
+        while not _finish(out, set(), max_new)[1]:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if phase_acc is not None else None
+            eng.run_round(True, ev)
+            if ev is not None:
+                evs.append(ev)
+            out = eng.tokens()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        if phase_acc is not None:
+            for ev in evs:
+                for i, name in enumerate(eng.PHASES):
+                    phase_acc[name] = phase_acc.get(name, 0.0) + ev[i].elapsed_time(ev[i + 1]) / 1e3
+        t = sync_max(e0.elapsed_time(e1) / 1e3, world)
+        barrier(world)
+        return _finish(out, set(), max_new)[0], eng.committed_per_round(), t
+
+    # warm-up (captures the graphs)
+    for _ in range(args.warmup):
+        for ids in mine:
+            decode(ids)
+    # timed
+    try:
+        pr = torch.cuda.get_device_properties(dev)
+        pci = f"{int(pr.pci_domain_id):08X}:{int(pr.pci_bus_id):02X}:{int(pr.pci_device_id):02X}.0"
+    except (AttributeError, TypeError, ValueError):
+        pci = None
+    clocks = ClockSampler(local, pci)
+    launches0 = _lib.launch_count()
+    phases: dict = {}
+    t_total, n_tok, accs, rounds = 0.0, 0, [], 0
+    for _ in range(args.steps):
+        for ids in mine:
+            toks, acc, t = decode(ids, phases)
+            t_total += t
+            n_tok += len(toks)
+            accs += acc
+            rounds += len(acc)
+    clk = clocks.stop()
+    n_tok_all = sync_sum(n_tok, world)
+    per_step = t_total / args.steps
+    value = n_tok_all / t_total
+    gpu_launches = int(getattr(eng, "launches_per_round", 0) * rounds)
+
+    # target-only baseline on the same sequences (one pass)
+    ar_value = None
+    if not args.no_ar:
+        ar = TargetStep(target, target.new_cache(cap), max_new)
+        t_ar, n_ar = 0.0, 0
+        for j, ids in enumerate(mine):
+            ar.prefill(ids.to(dev))
+            torch.cuda.synchronize(dev)
+            if j == 0:
+                ar.run(2)
+                ar.prefill(ids.to(dev))
+                torch.cuda.synchronize(dev)
+            barrier(world)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            out = ar.tokens()
+            while not _finish(out, set(), max_new)[1]:
+                ar.run(max(1, min(4, max_new - len(out))))
+                out = ar.tokens()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            t_ar += sync_max(e0.elapsed_time(e1) / 1e3, world)
+            n_ar += len(_finish(out, set(), max_new)[0])
+        ar_value = sync_sum(n_ar, world) / t_ar
+        del ar
+
+    # end to end through the public API (pinned host prompt -> host tokens)
+    gen = SpeculativeGenerator(base, draft, cfg, target)
+    gen.generate(mine[0].pin_memory(), max_new, set())  # capture
+    t_e2e, n_e2e = 0.0, 0
+    e2e_engine = gen.engine()
+    d2h0 = getattr(e2e_engine, "d2h_bytes", 0)
+    for ids in mine:
+        pinned = ids.pin_memory()
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        t0 = time.perf_counter()
+        res = gen.generate(pinned, max_new, set())
+        t_e2e += sync_max(time.perf_counter() - t0, world)
+        n_e2e += len(res.tokens)
+    d2h = getattr(e2e_engine, "d2h_bytes", 0) - d2h0
+    e2e_value = sync_sum(n_e2e, world) / t_e2e
+
+    # kernel roofline of the dominant kernel (tcgen05 GEMM, verify forward)
+    peaks = measured_peaks()
+    roof = gemm_roofline(w, plan_rows, dev) if rank == 0 else None
+
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cb = cpu_baseline(spec)
+        except MemoryError as exc:
+            cb = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                  "sample": f"not run: {exc}"}
+
+    if rank == 0:
+        tgt_bytes = model_bytes(w)
+        d_bytes = model_bytes(w, spec.draft_layers, list(draft.bridges.values()),
+                              head_rows=draft.head_weight().shape[0])
+        kv_tok = 2 * w.L * w.Hkv * w.hd * (2 if w.dtype == torch.bfloat16 else 4)
+        mean_acc = sum(accs) / max(1, len(accs))
+        ctx = P + max_new / 2
+        round_bytes = cfg.depth * d_bytes + tgt_bytes + ctx * kv_tok * (1 + cfg.depth * len(spec.draft_layers) / w.L)
+        ar_bytes = tgt_bytes + ctx * kv_tok
+        bw = peaks["hbm_gbs"] * 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16" if spec.dtype == torch.bfloat16 else "f32",
+            "data": "synthetic (seeded random weights and prompts)",
+            "config": {"workload": f"{args.workload}: {spec.model} planted x{spec.plant_scale}, draft "
+                                   f"{spec.draft_layers}, tree {spec.drafting}, prompt {P}, {max_new} new tokens, "
+                                   f"{args.sequences} sequences split over ranks",
+                       "global_batch": 1, "seq_len": P + max_new, "parallelism": f"dp{world} (independent sequences)",
+                       "l2": "weights (>15 GB) exceed L2 between rounds"},
+            "mean_accepted": mean_acc,
+            "ar_value": ar_value,
+            "speedup_vs_ar": (value / ar_value) if ar_value else None,
+            "phase_ms_per_round": {k: v / max(1, rounds) * 1e3 for k, v in phases.items()},
+            "weight_kv_roofline": {
+                "sd_tok_s_bound": bw * mean_acc / round_bytes, "ar_tok_s_bound": bw / ar_bytes,
+                "sd_frac": value / (bw * mean_acc / round_bytes),
+                "ar_frac": (ar_value / (bw / ar_bytes)) if ar_value else None,
+                "round_bytes": round_bytes, "ar_token_bytes": ar_bytes, "peak_gbs": peaks["hbm_gbs"],
+                "peak_source": peaks["source"]},
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(sum(x.numel() * 8 for x in mine)),
+                    "d2h_bytes_per_step": int(d2h),
+                    "note": "SpeculativeGenerator.generate per sequence: H2D prompt, prefill, decode, D2H tokens"},
+            "gpu_launches": gpu_launches,
+            "roofline": {"kernel": "tc_gemm_kernel (verify-forward GEMM mix + lm_head argmax)", "bound": "hbm",
+                         "achieved": roof["gbs"] if roof else None, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": (roof["gbs"] / peaks["hbm_gbs"]) if roof else None, "traffic": None,
+                         "peak_source": peaks["source"],
+                         "per_type": roof["per_type"] if roof else None},
+            "cpu_baseline": cb,
+            "clocks": clk,
+            "build_s": build_s,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

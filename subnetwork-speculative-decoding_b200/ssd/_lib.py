@@ -93,5 +93,19 @@ def check(rc: int, what: str) -> None:
     raise SSDError(text)
 
 
+# Kernels each entry point launches (host-only queries launch none).
+KERNELS_PER_CALL = {"ssd_head_argmax": 2, "ssd_head_topk": 2}
+_HOST_ONLY = {"ssd_version", "ssd_last_error", "ssd_device_sm_count", "ssd_workspace_bytes"}
+_launches = 0
+
+
+def launch_count() -> int:
+    """Kernels launched (or captured into a graph) through this binding so far."""
+    return _launches
+
+
 def call(name: str, *args) -> None:
+    global _launches
     check(getattr(load(), name)(*args), name)
+    if name not in _HOST_ONLY:
+        _launches += KERNELS_PER_CALL.get(name, 1)

@@ -119,6 +119,7 @@ class _Decoder:
         (speculative.py:222-224 with temperature 0)."""
         w = self.w
         P = int(prompt.numel())
+        self.cache.reset()
         self.cache.check_room(P)
         fwd = R.ForwardInputs(P, self.device, mask_words=1)
         fwd.fill(prompt.reshape(-1), torch.arange(P), 0, None)
@@ -150,7 +151,9 @@ class _Decoder:
         return int(self.state[N_OUT].item())
 
     def tokens(self) -> list[int]:
+        """Committed tokens so far (one small device->host read)."""
         n = min(self.n_out(), self.out_cap)
+        self.d2h_bytes = getattr(self, "d2h_bytes", 0) + 4 + 4 * n
         return self.out_tokens[:n].tolist()
 
 
@@ -176,7 +179,9 @@ class TargetStep(_Decoder):
     def run(self, n_steps: int, use_graph: bool = True) -> None:
         if use_graph:
             if self.graph is None:
+                before = ops.launch_count()
                 self.graph = self._capture(self.step)
+                self.launches_per_round = ops.launch_count() - before
             for _ in range(n_steps):
                 self.graph.replay()
         else:
@@ -271,13 +276,28 @@ class GreedyRound(_Decoder):
         self.verify_phase()
         self.commit_phase()
 
-    def run_round(self, use_graph: bool = True) -> None:
-        if use_graph:
-            if self.graph is None:
-                self.graph = self._capture(self.round)
-            self.graph.replay()
-        else:
-            self.round()
+    PHASES = ("draft", "verify", "bookkeeping")
+
+    def run_round(self, use_graph: bool = True, events: Optional[list] = None) -> None:
+        """One round. With use_graph the three phases replay as captured CUDA
+        graphs; `events` (4 CUDA events) are recorded between them so the
+        caller can read per-phase device time without host syncs."""
+        fns = (self.draft_phase, self.verify_phase, self.commit_phase)
+        if use_graph and self.graph is None:
+            self.graph = []
+            for fn in fns:
+                before = ops.launch_count()
+                self.graph.append(self._capture(fn))
+                self.launches_per_round = getattr(self, "launches_per_round", 0) + ops.launch_count() - before
+        for i, fn in enumerate(fns):
+            if events is not None:
+                events[i].record()
+            if use_graph:
+                self.graph[i].replay()
+            else:
+                fn()
+        if events is not None:
+            events[3].record()
 
     def committed_per_round(self) -> list[int]:
         n = int(self.round_log[0].item())

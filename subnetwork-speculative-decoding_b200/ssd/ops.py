@@ -35,6 +35,10 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
+def launch_count() -> int:
+    return L.launch_count()
+
+
 class Workspace:
     """Scratch for the GEMM / attention / head kernels plus a device status word.
 
