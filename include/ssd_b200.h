@@ -86,6 +86,21 @@ int ssd_linear(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, cons
                int64_t ldo, float* resid, int64_t ldr, int dtype, void* workspace, int64_t workspace_bytes,
                uint32_t* status, void* stream);
 
+/* ssd_linear without a workspace, for callers that cannot allocate device
+ * memory (a server that reserves all memory at start-up, a plain C caller
+ * with no allocator, code that must avoid the allocator's synchronisation).
+ * No counterpart in the reference: it is an addition of this library.
+ * Same arguments and results as ssd_linear; its split-K scratch is a fixed
+ * 12 MiB array inside the library that every GPU loading the library keeps
+ * until exit. Limit: T <= 64 rows for bf16, T <= 16 for fp32; larger calls
+ * fail with SSD_ERR_UNSUPPORTED. Every call shares that array: calls that
+ * overlap on the GPU race, so keep them ordered on one stream. The first call
+ * on a device looks up the array's address and should come before any stream
+ * capture. Allocates nothing. */
+int ssd_linear_noalloc(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, const void* const* w,
+                       const int64_t* rows, const void* const* bias, int seg_layout, int epilogue, int act, void* out,
+                       int64_t ldo, float* resid, int64_t ldr, int dtype, uint32_t* status, void* stream);
+
 /* Fused QKV projection + rotate-half RoPE + KV-cache write:
  * q_out[t] = rope(x[t] @ Wq^T, pos[t]); k/v rows of token t are written to
  * cache slot slots[t] of this layer (k rotated). rope_cos/rope_sin are fp32

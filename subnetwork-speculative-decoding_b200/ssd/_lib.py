@@ -33,6 +33,7 @@ SIGNATURES: dict[str, tuple] = {
     "ssd_embed": (I32, [P, I64, P, I64, I64, I32, P, P, P]),
     "ssd_rmsnorm": (I32, [P, I64, I64, I64, P, F32, P, I64, I32, P]),
     "ssd_linear": (I32, [P, I64, I64, I64, I32, P, P, P, I32, I32, I32, P, I64, P, I64, I32, P, I64, P, P]),
+    "ssd_linear_noalloc": (I32, [P, I64, I64, I64, I32, P, P, P, I32, I32, I32, P, I64, P, I64, I32, P, P]),
     "ssd_qkv_rope": (I32, [P, I64, I64, I64, P, P, P, I64, I64, I64, P, P, I64, P, P, P, P, I64, I64, P, I64, I32,
                            P, I64, P, P]),
     "ssd_tree_attention": (I32, [P, I64, I64, I64, I64, I64, P, P, I64, I64, P, P, P, I64, I64, P, I64, I32, P, I64,

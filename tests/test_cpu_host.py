@@ -1,0 +1,142 @@
+"""CPU tests: the C-ABI library loads and exports every symbol the header
+declares; host-side logic (config schema and validation, bridge planning,
+static tree plans, mask conversion) matches the reference's behaviour."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from ssd import _lib as L
+from ssd.config import DraftingConfig, SSDConfig, profile_name, validate_layer_indices
+from ssd.engine.round import TreePlan, cache_capacity
+from ssd.models.subnetwork_draft import plan_bridges
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "ssd_b200.h"
+
+
+def header_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(ssd_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = L.load()
+    names = header_symbols()
+    assert len(names) >= 18
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in ssd_b200.h but not exported"
+        assert n in L.SIGNATURES, f"{n} has no ctypes signature"
+    assert set(L.SIGNATURES) <= set(names)
+    assert lib.ssd_version() == 1
+
+
+def test_library_rejects_bad_arguments_without_gpu():
+    """Argument validation happens on the host, before any launch."""
+    with pytest.raises(ValueError):
+        L.call("ssd_tree_attention", None, 0, 1, 3, 2, 16, None, None, 0, 0, None, None, None, 0, 0, None, 0, 0,
+               None, 0, None, None)
+    with pytest.raises(L.SSDError):
+        L.call("ssd_kv_compact", None, 1, 1, 1, 1, 1, 64, None, None, None, 99, 1, None)
+
+
+YAML = """
+model:
+  base_model: meta-llama/Llama-3.2-1B-Instruct
+  torch_dtype: bfloat16
+draft_layers: [0, 7, 15]
+bridge:
+  hidden_dim: 4096
+drafting:
+  depth: 4
+  branch: [3, 2, 2, 1]
+  width: 8
+  max_nodes: 24
+  draft_vocab: 32768
+training:
+  output_dir: outputs/l1b
+  stage1: {steps: 10}
+"""
+
+
+def test_config_roundtrip(tmp_path):
+    p = tmp_path / "c.yaml"
+    p.write_text(YAML)
+    cfg = SSDConfig.from_yaml(p)
+    assert cfg.draft_layers == [0, 7, 15] and cfg.bridge.hidden_dim == 4096
+    assert cfg.drafting.per_depth(cfg.drafting.branch, "branch") == [3, 2, 2, 1]
+    assert cfg.training.stage1.steps == 10
+    assert profile_name(cfg.draft_layers) == "L0-7-15"
+
+
+@pytest.mark.parametrize("bad", ["drafting: {depth: 0}\ndraft_layers: [0]", "draft_layers: 3",
+                                 "draft_layers: [0]\nbogus: 1", "draft_layers: [0]\ndrafting: {nope: 1}",
+                                 "draft_layers: [0]\ndrafting: {depth: 2, branch: [1, 2, 3]}",
+                                 "draft_layers: [0]\ndrafting: {top_p: 0}"])
+def test_config_rejects(tmp_path, bad):
+    p = tmp_path / "bad.yaml"
+    p.write_text(bad)
+    with pytest.raises(ValueError):
+        SSDConfig.from_yaml(p)
+
+
+@pytest.mark.parametrize("bad", [[0, 6], [3, 3], [4, 2], []])
+def test_invalid_layer_indices(bad):
+    with pytest.raises(ValueError):
+        validate_layer_indices(bad, 6)
+
+
+def test_plan_bridges_matches_reference_naming():
+    assert [(s.name, s.src_boundary, s.tgt_boundary) for s in plan_bridges([0, 2, 5], 6)] == [
+        ("into_2", 1, 2), ("into_5", 3, 5)]
+    assert [s.name for s in plan_bridges([1, 2, 4], 6)] == ["into_1", "into_4", "into_norm"]
+    assert [s.name for s in plan_bridges([0, 15, 31], 32)] == ["into_15", "into_31"]
+
+
+@pytest.mark.parametrize("cfg,levels,verify,cache", [
+    (dict(depth=4, branch=[3, 2, 2, 1], width=8, max_nodes=24), [3, 6, 8, 8], 24, 17),
+    (dict(depth=6, branch=[4, 2, 2, 1, 1, 1], max_nodes=32), [4, 8, 16, 16, 16, 16], 32, 60),
+    (dict(depth=4, branch=1), [1, 1, 1, 1], 4, 3),
+    (dict(depth=5, branch=[4, 3, 2, 2, 1], width=[4, 6, 6, 4, 4], max_nodes=12), [4, 6, 6, 4, 4], 12, 20),
+])
+def test_tree_plan_static_sizes(cfg, levels, verify, cache):
+    """Same level sizes / verify nodes / tree cache as the reference's
+    TreeDrafter.max_nodes_per_level, max_verify_nodes, max_tree_cache."""
+    p = TreePlan(DraftingConfig(**cfg))
+    assert p.level_sizes == levels and p.n_verify == verify and p.max_tree_cache == cache
+    assert p.rows == verify + 1
+    assert cache_capacity(2048, 256, p) >= 2048 + 256 + cfg["depth"] + max(verify, cache) + 2
+
+
+def test_forward_inputs_mask_conversion():
+    """A dense [q, past+q] tree mask becomes prefix length + bitmask."""
+    from ssd.models.runner import ForwardInputs
+
+    class _Dev:
+        pass
+
+    fi = ForwardInputs.__new__(ForwardInputs)
+    fi.cap, fi.mask_words = 8, 2
+    fi.ids = torch.zeros(8, dtype=torch.int32)
+    fi.positions = torch.zeros(8, dtype=torch.int32)
+    fi.slots = torch.zeros(8, dtype=torch.int32)
+    fi.prefix_len = torch.zeros(8, dtype=torch.int32)
+    fi.spec_base = torch.zeros(1, dtype=torch.int32)
+    fi.mask = torch.zeros(8, 2, dtype=torch.int64)
+    past, T = 6, 4
+    parents = [-1, 0, 0, 1]
+    m = torch.zeros(T, past + T, dtype=torch.bool)
+    m[:, :past] = True
+    for i in range(T):
+        j = i
+        while j != -1:
+            m[i, past + j] = True
+            j = parents[j]
+    fi.fill(torch.tensor([1, 2, 3, 4]), torch.tensor([6, 7, 7, 8]), past, m)
+    # node 0 is an ancestor of every row -> it joins the prefix
+    assert fi.prefix_len[:T].tolist() == [past + 1] * T and int(fi.spec_base) == past + 1
+    assert fi.mask[:T, 0].tolist() == [0, 0b001, 0b010, 0b101]
+    fi.fill(torch.tensor([5, 6]), torch.tensor([6, 7]), past, None)
+    assert fi.prefix_len[:2].tolist() == [past + 1, past + 2] and not fi.use_mask
