@@ -18,6 +18,7 @@ struct TcMaps {
 };
 
 constexpr int kTcThreads = 192;
+constexpr int kMaxClusterSplits = 8;  // portable cluster size
 constexpr int kABytes = kTileM * kChunkK * 2;  // 16 KB of weights per stage
 
 __host__ __device__ inline int tc_stage_bytes(int BN) { return kABytes + BN * kChunkK * 2; }
@@ -143,17 +144,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       umma_commit(accum);
       if (!mbar_wait(accum, 0)) report_error(g.status, kErrWaitTimeout);
     }
-  } else {
-    // Epilogue warps 2..5. A warp may only touch TMEM lanes 32*(warp%4)..+31.
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
-    float* stage = reinterpret_cast<float*>(smem);
-    bool ok = mbar_wait(accum, 0);
-    if (!ok) report_error(g.status, kErrWaitTimeout);
+  }
+  // Epilogue warps 2..5 drain TMEM into this CTA's partial tile (the idle
+  // ring). A warp may only touch TMEM lanes 32*(warp%4)..+31.
+  const bool epi = warp >= 2;
+  const int q = warp & 3;
+  const int r = q * 32 + lane;
+  float* stage = reinterpret_cast<float*>(smem);
+  const int ncols = min(g.BN, g.T - tile_n * g.BN);
+  bool ok = true;
+  if (epi) {
+    if (!mbar_wait(accum, 0)) {
+      report_error(g.status, kErrWaitTimeout);
+      *abort_flag = 1;
+    }
     tc_fence_after();
-    const int ncols = min(g.BN, g.T - tile_n * g.BN);
     named_bar_sync(1, 128);  // all four warps past the wait before the ring is reused
-    ok = ok && (*abort_flag == 0);
+    ok = (*abort_flag == 0);  // uniform across the epilogue warps
     if (ok) {
       for (int c0 = 0; c0 < g.BN; c0 += 16) {
         float v[16];
@@ -163,8 +170,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (c0 + i < ncols) stage[(c0 + i) * kTileM + r] = (nk > 0) ? v[i] : 0.f;
       }
     }
-    named_bar_sync(1, 128);
-    if (ok) finish_tile<bf16>(stage, flag, tile_m, tile_n, split, g, e, r, 1);
+  }
+  if (g.splits == 1) {
+    if (epi) {
+      named_bar_sync(1, 128);
+      if (ok) run_epilogue<bf16>(stage, tile_m, tile_n * g.BN, ncols, g, e, r, 1);
+    }
+  } else {
+    // The `splits` CTAs of this tile form one cluster (rank = split). After
+    // the barrier every partial tile is complete; CTA `split` then owns token
+    // columns split, split + splits, ...: it sums them over all ranks in rank
+    // order (deterministic, independent of T) straight from the peers' shared
+    // memory and runs the epilogue on them. The second barrier keeps every
+    // CTA's shared memory alive until all peers have read it.
+    cluster_sync_all();
+    if (epi && ok) {
+      uint32_t peer[kMaxClusterSplits];
+#pragma unroll
+      for (int s = 0; s < kMaxClusterSplits; ++s)
+        peer[s] = s < g.splits ? dsmem_map(smem_u32(stage), static_cast<uint32_t>(s)) : 0u;
+      for (int c = split; c < ncols; c += g.splits) {
+        const uint32_t off = static_cast<uint32_t>((c * kTileM + r) * 4);
+        float v[kMaxClusterSplits];
+#pragma unroll
+        for (int s = 0; s < kMaxClusterSplits; ++s) v[s] = s < g.splits ? dsmem_ld(peer[s] + off) : 0.f;
+        float acc = 0.f;
+#pragma unroll
+        for (int s = 0; s < kMaxClusterSplits; ++s)
+          if (s < g.splits) acc += v[s];
+        stage[c * kTileM + r] = acc;
+      }
+      named_bar_sync(1, 128);
+      run_epilogue<bf16>(stage, tile_m, tile_n * g.BN, ncols, g, e, r, 1, split, g.splits);
+    }
+    cluster_sync_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -326,6 +365,35 @@ int choose_splits(int tiles_m, int kchunks, int cta_slots) {
   return s < 1 ? 1 : s;
 }
 
+void set_tc_attributes() {
+  static bool done = false;
+  if (!done) {
+    cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    done = true;
+  }
+}
+
+int tc_stages(int BN) {
+  const int stages = 101376 / tc_stage_bytes(BN);
+  return stages > 8 ? 8 : (stages < 2 ? 2 : stages);
+}
+
+// Split count for a tile grid of `tiles_m` weight tiles: fill ~2 CTAs per SM,
+// at most one portable cluster per tile. Depends on the weight shape only, so
+// every decode-sized T uses the same split (rows are batch-invariant).
+// (Requiring all clusters to be co-resident per cudaOccupancyMaxActiveClusters
+// measured slower: the query is conservative and the smaller splits it
+// leaves underfill HBM.)
+int choose_cluster_splits(int tiles_m, int kchunks, int cta_slots) {
+  int s = choose_splits(tiles_m, kchunks, cta_slots);
+  if (s > kMaxClusterSplits) s = kMaxClusterSplits;
+  // Power-of-two clusters pack the GPCs without leftover slots (6-CTA
+  // clusters measured 2.6x slower per byte than 8-CTA ones).
+  int p = 1;
+  while (p * 2 <= s) p *= 2;
+  return p;
+}
+
 }  // namespace
 
 int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, const void* const* w,
@@ -365,9 +433,8 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
     if (K % 8) return fail(SSD_ERR_UNSUPPORTED, "bf16 GEMM needs K % 8 == 0");
     g.BN = round_bn(T);
     g.tiles_n = (int)((T + g.BN - 1) / g.BN);
-    g.splits = (g.tiles_n == 1 && !head) ? choose_splits(g.tiles_m, g.kchunks, 2 * sms) : 1;
-    int stages = 101376 / tc_stage_bytes(g.BN);
-    g.stages = stages > 8 ? 8 : (stages < 2 ? 2 : stages);
+    g.splits = (g.tiles_n == 1 && !head) ? choose_cluster_splits(g.tiles_m, g.kchunks, 2 * sms) : 1;
+    g.stages = tc_stages(g.BN);
   } else if (dtype == SSD_F32) {
     g.BN = kSimtBN;
     g.tiles_n = (int)((T + kSimtBN - 1) / kSimtBN);
@@ -401,12 +468,22 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
     for (int i = n_seg; i < 3; ++i) maps.w[i] = maps.w[0];
     const int rc = get_map(x, (uint64_t)K, (uint64_t)T, (uint64_t)ldx * 2, (uint32_t)g.BN, &maps.x);
     if (rc) return rc;
-    static bool attr_set = false;
-    if (!attr_set) {
-      cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
-      attr_set = true;
-    }
-    tc_gemm_kernel<<<grid, kTcThreads, tc_smem_bytes(g.BN, g.stages), stream>>>(maps, g, e);
+    set_tc_attributes();
+    // K-split CTAs of one tile run as one thread-block cluster (DSMEM reduction).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = tc_smem_bytes(g.BN, g.stages);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = g.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, tc_gemm_kernel, maps, g, e);
+    if (err != cudaSuccess) return fail(SSD_ERR_CUDA, "tc_gemm_kernel launch: %s", cudaGetErrorString(err));
     return check_launch("tc_gemm_kernel");
   }
   SimtSegs segs{};

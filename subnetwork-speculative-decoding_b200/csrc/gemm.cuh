@@ -92,9 +92,11 @@ __host__ __device__ inline int head_rec_size(int kind, int k) { return kind == E
 // Apply the epilogue to a finished fp32 tile stage[c * 128 + r] (c = token
 // within the tile, r = row within the 128-feature tile). Runs on 128
 // threads; `tid` in [0, 128). `bar_id` names a barrier over those threads.
+// Columns c0, c0 + cstep, ... < ncols are processed (a cluster splits the
+// columns of one tile among its CTAs).
 template <typename T>
 __device__ void run_epilogue(float* stage, int tile_m, int t0, int ncols, const GemmShape& g, const EpiArgs& e,
-                             int tid, int bar_id) {
+                             int tid, int bar_id, int c0 = 0, int cstep = 1) {
   const int r = tid;
   switch (e.kind) {
     case EPI_STORE:
@@ -104,7 +106,7 @@ __device__ void run_epilogue(float* stage, int tile_m, int t0, int ncols, const 
       if (n >= g.N) return;
       const int s = seg_of(g, n);
       const float b = load_bias<T>(e.bias[s], n - g.seg_start[s]);
-      for (int c = 0; c < ncols; ++c) {
+      for (int c = c0; c < ncols; c += cstep) {
         const int t = t0 + c;
         float v = stage[c * kTileM + r] + b;
         if (e.kind == EPI_RESIDUAL) {
@@ -124,7 +126,7 @@ __device__ void run_epilogue(float* stage, int tile_m, int t0, int ncols, const 
       const int F = g.seg_start[1];
       if (f >= F) return;
       const float bg = load_bias<T>(e.bias[0], f), bu = load_bias<T>(e.bias[1], f);
-      for (int c = 0; c < ncols; ++c) {
+      for (int c = c0; c < ncols; c += cstep) {
         const float gv = stage[c * kTileM + r] + bg;
         const float uv = stage[c * kTileM + r + 64] + bu;
         static_cast<T*>(e.out)[(int64_t)(t0 + c) * e.ldo + f] = from_f32<T>(silu_f(gv) * uv);
@@ -139,7 +141,7 @@ __device__ void run_epilogue(float* stage, int tile_m, int t0, int ncols, const 
       const int local = is_q ? n : (is_k ? n - e.n_q : n - e.n_q - e.n_kv);
       const int head = local / hd, j = local - head * hd;
       const int partner = (j < half) ? r + half : r - half;  // same head, same tile (hd divides 128)
-      for (int c = 0; c < ncols; ++c) {
+      for (int c = c0; c < ncols; c += cstep) {
         const int t = t0 + c;
         float v = stage[c * kTileM + r];
         if (is_q || is_k) {
