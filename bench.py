@@ -240,6 +240,48 @@ def gemm_roofline(w, rows: int, dev) -> dict:
         out[name] = {"us": t * 1e6, "gbs": nbytes / t / 1e9, "bytes": nbytes}
         total_b += nbytes * w.L
         total_t += t * w.L
+    # non-GEMM kernels of the same forward: RMSNorm and tree attention over a
+    # cache of the bench context (their bytes are the activations / the KV)
+    from ssd.models.runner import ForwardInputs
+
+    ctx = 2304
+    kc = (torch.randn(w.L, 2, w.Hkv, ctx + 64, w.hd, generator=g, device=dev) * 0.5).to(w.dtype)
+    f = ForwardInputs(rows, dev, 1)
+    f.prefix_len.fill_(ctx - rows + 1)
+    f.spec_base.fill_(ctx - rows + 1)
+    f.mask[:, 0] = torch.tensor([(1 << min(t, 62)) | ((1 << max(t - 1, 0)) - 1) if t else 0 for t in range(rows)],
+                                device=dev)
+    f.use_mask = True
+    q_in = (torch.randn(rows, w.H * w.hd, generator=g, device=dev) * 0.5).to(w.dtype)
+    a_out = torch.empty_like(q_in)
+    xn = torch.empty(rows, w.d, dtype=w.dtype, device=dev)
+    kv_bytes = ctx * w.Hkv * w.hd * 2 * es
+    extra = {
+        "attention": (lambda li: ops.tree_attention(q_in, kc[li, 0], kc[li, 1], w.H, w.Hkv, w.hd, f.prefix_len, a_out,
+                                                    ws, spec_base=f.spec_base, spec_mask=f.mask, kv_bound=ctx + 64),
+                      kv_bytes + 2 * rows * w.H * w.hd * es),
+        "rmsnorm": (lambda li: ops.rmsnorm(resid, w.layers[li].ln1, 1e-5, xn), rows * w.d * (4 + es) + w.d * es),
+    }
+    for name, (fn, nbytes) in extra.items():
+        for li in range(2):
+            fn(li)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.graph(graph, stream=s):
+            for li in range(w.L):
+                fn(li)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        t = e0.elapsed_time(e1) / 1e3 / (5 * w.L)
+        out[name] = {"us": t * 1e6, "gbs": nbytes / t / 1e9, "bytes": nbytes}
+    del kc
     # lm_head + argmax over the full vocabulary (1 GB, > L2)
     graph = torch.cuda.CUDAGraph()
     ops.head_argmax(x_d, w.lm_head, idx, ws)

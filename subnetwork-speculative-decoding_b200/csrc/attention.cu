@@ -58,6 +58,8 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const AttnArgs a) {
   const int row0 = rt * a.rows_per_tile;
   const int nrows = min(a.rows_per_tile, a.T - row0);
   const int nq = nrows * a.G;
+  pdl_wait();
+  pdl_trigger();
   const int sb = a.spec_base ? a.spec_base[0] : 0;
 
   if (threadIdx.x == 0) s_misc[0] = 0;
@@ -306,6 +308,8 @@ __global__ void __launch_bounds__(256) attn_mma_kernel(const AttnArgs a) {
   const int Mg = min(a.rows_per_group, M - q0);
   const int t_first = q0 / a.G;
   const int ntok = (q0 + Mg - 1) / a.G - t_first + 1;
+  pdl_wait();
+  pdl_trigger();
   const int sb = a.spec_base ? a.spec_base[0] : 0;
   const int mw = a.mask ? a.mask_words : 0;
 
@@ -709,21 +713,8 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
       set = true;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)blocks, (unsigned)a.n_splits);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = a.cluster_merge ? (unsigned)a.n_splits : 1u;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, a);
-    if (err != cudaSuccess) return fail(SSD_ERR_CUDA, "attn_mma_kernel launch: %s", cudaGetErrorString(err));
-    return check_launch("attn_mma_kernel");
+    return launch_kernel("attn_mma_kernel", kern, dim3((unsigned)blocks, (unsigned)a.n_splits), dim3(256), smem, s,
+                         1u, a.cluster_merge ? (unsigned)a.n_splits : 1u, a);
   }
   if (a.G > kAttnQ) return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: GQA group > 32");
   a.rows_per_tile = kAttnQ / a.G;
@@ -752,16 +743,14 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
       cudaFuncSetAttribute(attn_simt_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
       set = true;
     }
-    attn_simt_kernel<float><<<grid, 256, smem, s>>>(a);
+    return launch_kernel("attn_simt_kernel", attn_simt_kernel<float>, grid, dim3(256), smem, s, 1u, 1u, a);
   } else if (dtype == SSD_BF16) {
     static bool set = false;
     if (!set) {
       cudaFuncSetAttribute(attn_simt_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
       set = true;
     }
-    attn_simt_kernel<bf16><<<grid, 256, smem, s>>>(a);
-  } else {
-    return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: dtype %d", dtype);
+    return launch_kernel("attn_simt_kernel", attn_simt_kernel<bf16>, grid, dim3(256), smem, s, 1u, 1u, a);
   }
-  return check_launch("attn_simt_kernel");
+  return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: dtype %d", dtype);
 }

@@ -176,6 +176,18 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// ------------------------------------- programmatic dependent launch (PDL)
+// Every kernel of the library is launched with programmatic stream
+// serialization, so it may start while its predecessor in the stream is
+// still running. Protocol (each kernel): only prologue work and reads of
+// data no kernel writes (weights) before pdl_wait(); pdl_wait() returns once
+// the predecessor grid has completed and its writes are visible; pdl_trigger()
+// (always after pdl_wait) lets the successor start its own prologue. Since a
+// kernel triggers only after its own wait, everything two launches back is
+// complete whenever a kernel starts.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------ thread-block clusters
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

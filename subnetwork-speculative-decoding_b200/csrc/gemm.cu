@@ -80,18 +80,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
       const uint32_t tx = kABytes + g.BN * kChunkK * 2;
-      int issued = 0;
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % g.stages;
-        if (i >= g.stages && !mbar_wait(&empty[s], ((i / g.stages) - 1) & 1)) {
-          report_error(g.status, kErrWaitTimeout);
-          *abort_flag = 1;
-          break;
-        }
-        if (*abort_flag) break;
-        uint8_t* a = smem + s * stage_bytes;
-        uint8_t* b = a + kABytes;
-        mbar_arrive_expect_tx(&full[s], tx);
+      auto load_a = [&](int i) {
+        uint8_t* a = smem + (i % g.stages) * stage_bytes;
         const int kx = (kc0 + i) * kChunkK;
 #pragma unroll
         for (int grp = 0; grp < 4; ++grp) {
@@ -106,11 +96,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               if (n >= g.seg_start[q]) seg = q;
             row = n - g.seg_start[seg];  // rows past the segment end are zero-filled by TMA
           }
-          tma_load_2d(a + grp * 32 * 128, &maps.w[seg], &full[s], kx, row, pol_w);
+          tma_load_2d(a + grp * 32 * 128, &maps.w[seg], &full[i % g.stages], kx, row, pol_w);
         }
-        tma_load_2d(b, &maps.x, &full[s], kx, tile_n * g.BN, pol_x);
+      };
+      auto load_b = [&](int i) {
+        uint8_t* b = smem + (i % g.stages) * stage_bytes + kABytes;
+        tma_load_2d(b, &maps.x, &full[i % g.stages], (kc0 + i) * kChunkK, tile_n * g.BN, pol_x);
+      };
+      // Weights are never written by any kernel: stream the first stages
+      // while the predecessor kernel is still finishing (PDL).
+      const int pre = nk < g.stages ? nk : g.stages;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], tx);
+        load_a(i);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) load_b(i);
+      int issued = pre;
+      for (int i = pre; i < nk; ++i) {
+        const int s = i % g.stages;
+        if (!mbar_wait(&empty[s], ((i / g.stages) - 1) & 1)) {
+          report_error(g.status, kErrWaitTimeout);
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        mbar_arrive_expect_tx(&full[s], tx);
+        load_a(i);
+        load_b(i);
         ++issued;
       }
+      pdl_trigger();
       // On abort, wait (bounded) for the copies already in flight to land so
       // no TMA write targets shared memory after the CTA exits.
       if (*abort_flag) {
@@ -154,6 +170,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int ncols = min(g.BN, g.T - tile_n * g.BN);
   bool ok = true;
   if (epi) {
+    pdl_wait();  // the epilogue writes buffers earlier kernels may still read
     if (!mbar_wait(accum, 0)) {
       report_error(g.status, kErrWaitTimeout);
       *abort_flag = 1;
@@ -230,6 +247,8 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const T* __restrict__ x,
   __shared__ float xs[kSimtBN][kSimtKC];
   __shared__ float stage[kSimtBN * kTileM];
   __shared__ int flag;
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_m = blockIdx.x / g.splits, split = blockIdx.x % g.splits;
   const int tile_n = blockIdx.y;
@@ -470,29 +489,16 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
     if (rc) return rc;
     set_tc_attributes();
     // K-split CTAs of one tile run as one thread-block cluster (DSMEM reduction).
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(kTcThreads);
-    cfg.dynamicSmemBytes = tc_smem_bytes(g.BN, g.stages);
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = g.splits;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t err = cudaLaunchKernelEx(&cfg, tc_gemm_kernel, maps, g, e);
-    if (err != cudaSuccess) return fail(SSD_ERR_CUDA, "tc_gemm_kernel launch: %s", cudaGetErrorString(err));
-    return check_launch("tc_gemm_kernel");
+    return launch_kernel("tc_gemm_kernel", tc_gemm_kernel, grid, dim3(kTcThreads), tc_smem_bytes(g.BN, g.stages),
+                         stream, (unsigned)g.splits, 1u, maps, g, e);
   }
   SimtSegs segs{};
   for (int i = 0; i < 3; ++i) {
     segs.p[i] = i < n_seg ? w[i] : w[0];
     segs.rows[i] = i < n_seg ? (int)rows[i] : 0;
   }
-  simt_gemm_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(x), ldx, segs, g, e);
-  return check_launch("simt_gemm_kernel");
+  return launch_kernel("simt_gemm_kernel", simt_gemm_kernel<float>, grid, dim3(256), 0, stream, 1u, 1u,
+                       static_cast<const float*>(x), ldx, segs, g, e);
 }
 
 }  // namespace ssd

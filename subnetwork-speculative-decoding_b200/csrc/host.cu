@@ -35,6 +35,14 @@ int device_sms() {
   return cache[dev];
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("SSD_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 TensorMapEncodeFn tensor_map_encoder() {
   static TensorMapEncodeFn fn = nullptr;
   static std::once_flag once;

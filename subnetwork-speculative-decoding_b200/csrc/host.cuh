@@ -7,6 +7,9 @@
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
+
+#include <utility>
 
 #include "../../include/ssd_b200.h"
 
@@ -36,5 +39,38 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
 
 constexpr int64_t kMaxCounters = 1 << 16;
 constexpr int64_t kCounterBytes = kMaxCounters * 4;
+
+// Whether launches carry the programmatic-dependent-launch attribute
+// (default on; SSD_PDL=0 turns it off for A/B timing).
+bool pdl_enabled();
+
+// Launch `kern` with programmatic stream serialization (see pdl_wait in
+// common.cuh) and, if cluster_x * cluster_y > 1, a thread-block cluster.
+template <typename... KArgs, typename... Args>
+int launch_kernel(const char* name, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                  unsigned cluster_x, unsigned cluster_y, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  ++n;
+  if (cluster_x * cluster_y > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = cluster_y;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (err != cudaSuccess) return fail(SSD_ERR_CUDA, "%s launch: %s", name, cudaGetErrorString(err));
+  return check_launch(name);
+}
 
 }  // namespace ssd

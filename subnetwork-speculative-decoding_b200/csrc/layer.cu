@@ -10,6 +10,8 @@ namespace ssd {
 template <typename T>
 __global__ void embed_kernel(const int32_t* ids, const T* table, int64_t vocab, int64_t d, float* out,
                              uint32_t* status) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   int id = ids[t];
   if (id < 0 || id >= vocab) {
@@ -26,6 +28,8 @@ __global__ void embed_kernel(const int32_t* ids, const T* table, int64_t vocab, 
 // weight multiply.
 template <typename T>
 __global__ void rmsnorm_kernel(const float* x, int64_t d, int64_t ldx, const T* w, float eps, T* out, int64_t ldo) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const float* row = x + (int64_t)t * ldx;
   float ss = 0.f;
@@ -50,6 +54,8 @@ __global__ void rmsnorm_kernel(const float* x, int64_t d, int64_t ldx, const T* 
 // ------------------------------------------------------------ head reducers
 // Merge the per-tile {max1, idx1, max2} records of each row.
 __global__ void argmax_reduce_kernel(const float* part, int tiles, int32_t* out_idx, float* out_max, float* out_gap) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const float* rec = part + (int64_t)t * tiles * 3;
   float m1 = -INFINITY, m2 = -INFINITY;
@@ -107,6 +113,8 @@ __global__ void argmax_reduce_kernel(const float* part, int tiles, int32_t* out_
 // the k best (value desc, index asc); emits tokens through vocab_ids.
 __global__ void topk_reduce_kernel(const float* part, int tiles, int k, const int64_t* vocab_ids, int32_t* out_tok,
                                    float* out_lp) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int rec = 2 + 2 * k;
   const float* base = part + (int64_t)t * tiles * rec;
@@ -226,9 +234,11 @@ int ssd_embed(const int32_t* ids, int64_t T, const void* table, int64_t vocab, i
   if (T <= 0 || d <= 0 || !ids || !table || !resid) return fail(SSD_ERR_INVALID, "ssd_embed: bad arguments");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SSD_F32)
-    embed_kernel<float><<<(unsigned)T, 256, 0, s>>>(ids, static_cast<const float*>(table), vocab, d, resid, status);
+    return launch_kernel("embed_kernel", embed_kernel<float>, dim3((unsigned)T), dim3(256), 0, s, 1, 1, ids,
+                         static_cast<const float*>(table), vocab, d, resid, status);
   else if (dtype == SSD_BF16)
-    embed_kernel<bf16><<<(unsigned)T, 256, 0, s>>>(ids, static_cast<const bf16*>(table), vocab, d, resid, status);
+    return launch_kernel("embed_kernel", embed_kernel<bf16>, dim3((unsigned)T), dim3(256), 0, s, 1, 1, ids,
+                         static_cast<const bf16*>(table), vocab, d, resid, status);
   else
     return fail(SSD_ERR_UNSUPPORTED, "ssd_embed: dtype %d", dtype);
   return check_launch("embed_kernel");
@@ -239,11 +249,11 @@ int ssd_rmsnorm(const float* x, int64_t T, int64_t d, int64_t ldx, const void* w
   if (T <= 0 || d <= 0 || !x || !weight || !out) return fail(SSD_ERR_INVALID, "ssd_rmsnorm: bad arguments");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SSD_F32)
-    rmsnorm_kernel<float><<<(unsigned)T, 256, 0, s>>>(x, d, ldx, static_cast<const float*>(weight), eps,
-                                                       static_cast<float*>(out), ldo);
+    return launch_kernel("rmsnorm_kernel", rmsnorm_kernel<float>, dim3((unsigned)T), dim3(256), 0, s, 1, 1, x, d, ldx,
+                         static_cast<const float*>(weight), eps, static_cast<float*>(out), ldo);
   else if (dtype == SSD_BF16)
-    rmsnorm_kernel<bf16><<<(unsigned)T, 256, 0, s>>>(x, d, ldx, static_cast<const bf16*>(weight), eps,
-                                                      static_cast<bf16*>(out), ldo);
+    return launch_kernel("rmsnorm_kernel", rmsnorm_kernel<bf16>, dim3((unsigned)T), dim3(256), 0, s, 1, 1, x, d, ldx,
+                         static_cast<const bf16*>(weight), eps, static_cast<bf16*>(out), ldo);
   else
     return fail(SSD_ERR_UNSUPPORTED, "ssd_rmsnorm: dtype %d", dtype);
   return check_launch("rmsnorm_kernel");
@@ -328,8 +338,8 @@ int ssd_head_argmax(const void* x, int64_t ldx, int64_t T, int64_t K, const void
   int rc = launch_gemm(x, ldx, T, K, 1, ws, rows, SSD_SEG_CONCAT, e, dtype, workspace, workspace_bytes, status, s,
                        T * tiles * 3 * 4);
   if (rc) return rc;
-  argmax_reduce_kernel<<<(unsigned)T, 256, 0, s>>>(e.part, (int)tiles, out_idx, out_max, out_gap);
-  return check_launch("argmax_reduce_kernel");
+  return launch_kernel("argmax_reduce_kernel", argmax_reduce_kernel, dim3((unsigned)T), dim3(256), 0, s, 1, 1, e.part,
+                       (int)tiles, out_idx, out_max, out_gap);
 }
 
 int ssd_head_topk(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w, int64_t vocab,
@@ -352,8 +362,8 @@ int ssd_head_topk(const void* x, int64_t ldx, int64_t T, int64_t K, const void* 
   int rc = launch_gemm(x, ldx, T, K, 1, ws, rows, SSD_SEG_CONCAT, e, dtype, workspace, workspace_bytes, status, s,
                        T * tiles * rec * 4);
   if (rc) return rc;
-  topk_reduce_kernel<<<(unsigned)T, 256, 0, s>>>(e.part, (int)tiles, (int)k, vocab_ids, out_tok, out_logprob);
-  return check_launch("topk_reduce_kernel");
+  return launch_kernel("topk_reduce_kernel", topk_reduce_kernel, dim3((unsigned)T), dim3(256), 0, s, 1, 1, e.part,
+                       (int)tiles, (int)k, vocab_ids, out_tok, out_logprob);
 }
 
 }  // extern "C"

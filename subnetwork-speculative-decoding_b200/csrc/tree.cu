@@ -33,6 +33,8 @@ __global__ void level_prune_kernel(const int32_t* topk_tok, const float* topk_lp
   int* s_par = reinterpret_cast<int*>(s_score + n);
   int* s_rank = s_par + n;  // position in the sorted order
   __shared__ int s_base;
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x == 0) s_base = *n_nodes;
   __syncthreads();
   const int base = s_base;
@@ -114,6 +116,8 @@ __global__ void tree_prune_kernel(int32_t* n_nodes, int max_nodes, int32_t* toke
   int* s_dpos = s_rank + cap;
   int* s_keep = s_dpos + cap;
   int* s_new = s_keep + cap;
+  pdl_wait();
+  pdl_trigger();
   const int n = min(*n_nodes, cap);
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     s_score[i] = scores[i];
@@ -174,6 +178,8 @@ __global__ void verify_prep_kernel(const int32_t* n_nodes, int rows_cap, const i
                                    const int32_t* depths, int32_t* ids, int32_t* positions, int32_t* slots,
                                    int32_t* prefix_len, int32_t* spec_base, uint64_t* mask, int mask_words,
                                    uint32_t* status) {
+  pdl_wait();
+  pdl_trigger();
   int n = *n_nodes;
   const int c = root_pos[0];
   if (n + 1 > rows_cap) {
@@ -204,6 +210,8 @@ __global__ void tree_walk_greedy_kernel(const int32_t* n_nodes, int max_n, const
                                         const int32_t* tokens, const int32_t* parents, const int32_t* ranks,
                                         const int32_t* root_pos, int32_t* accepted, int32_t* n_accepted,
                                         int32_t* bonus, int32_t* keep_slots, int32_t* n_keep) {
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x != 0) return;
   const int n = min(*n_nodes, max_n);
   const int c = root_pos[0];
@@ -238,6 +246,8 @@ __global__ void kv_compact_kernel(uint8_t* cache, int64_t n_layers, int64_t laye
                                   int64_t n_kv, int64_t head_stride_b, int64_t row_bytes, const int32_t* start,
                                   const int32_t* keep_slots, const int32_t* n_keep, int max_keep) {
   constexpr int kMaxKeep = 32;
+  pdl_wait();
+  pdl_trigger();
   const int64_t groups = row_bytes / (int64_t)sizeof(VEC);
   const int64_t total = n_layers * 2 * n_kv * groups;
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -265,6 +275,8 @@ __global__ void kv_compact_kernel(uint8_t* cache, int64_t n_layers, int64_t laye
 __global__ void round_commit_kernel(const int32_t* n_accepted, const int32_t* accepted, const int32_t* tokens,
                                     const int32_t* bonus, int32_t* seq_len, int32_t* root_token, int32_t* out_tokens,
                                     int32_t* n_out, int out_cap, int32_t* round_log, uint32_t* status) {
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x != 0) return;
   const int na = *n_accepted;
   int o = *n_out;
@@ -291,6 +303,8 @@ __global__ void round_commit_kernel(const int32_t* n_accepted, const int32_t* ac
 // `src_ids` (device) when given.
 __global__ void causal_prep_kernel(const int32_t* base, int T, const int32_t* src_ids, int32_t* ids,
                                    int32_t* positions, int32_t* slots, int32_t* prefix_len) {
+  pdl_wait();
+  pdl_trigger();
   const int b = base[0];
   for (int r = threadIdx.x + blockIdx.x * blockDim.x; r < T; r += blockDim.x * gridDim.x) {
     if (src_ids) ids[r] = src_ids[r];
@@ -321,20 +335,19 @@ int ssd_level_prune(const int32_t* topk_tok, const float* topk_lp, int64_t n_fro
   if (fed && level_slot_offset + keep > mask_words * 64)
     return fail(SSD_ERR_UNSUPPORTED, "ssd_level_prune: tree slots exceed the ancestor mask");
   const size_t smem = (size_t)n * (8 + 4 + 4);
-  level_prune_kernel<<<1, 256, smem, static_cast<cudaStream_t>(stream)>>>(
-      topk_tok, topk_lp, (int)n_frontier, (int)k, (int)keep, (int)level, frontier, next_frontier, n_nodes, tokens,
+  return launch_kernel("level_prune_kernel", level_prune_kernel, dim3(1), dim3(256), smem,
+      static_cast<cudaStream_t>(stream), 1, 1, topk_tok, topk_lp, (int)n_frontier, (int)k, (int)keep, (int)level, frontier, next_frontier, n_nodes, tokens,
       parents, depths, ranks, scores, draft_pos, (int)cap, root_pos, fed, (int)level_slot_offset, fwd_ids, fwd_pos,
       fwd_slots, fwd_plen, fwd_spec_base, fwd_mask, (int)mask_words, status);
-  return check_launch("level_prune_kernel");
 }
 
 int ssd_tree_prune(int32_t* n_nodes, int64_t max_nodes, int32_t* tokens, int32_t* parents, int32_t* depths,
                    int32_t* ranks, double* scores, int32_t* draft_pos, int64_t cap, void* stream) {
   if (cap <= 0 || cap > 4096) return fail(SSD_ERR_INVALID, "ssd_tree_prune: bad capacity");
   const size_t smem = (size_t)cap * (8 + 7 * 4);
-  tree_prune_kernel<<<1, 256, smem, static_cast<cudaStream_t>(stream)>>>(n_nodes, (int)max_nodes, tokens, parents,
-                                                                          depths, ranks, scores, draft_pos, (int)cap);
-  return check_launch("tree_prune_kernel");
+  return launch_kernel("tree_prune_kernel", tree_prune_kernel, dim3(1), dim3(256), smem,
+                       static_cast<cudaStream_t>(stream), 1, 1, n_nodes, (int)max_nodes, tokens, parents, depths,
+                       ranks, scores, draft_pos, (int)cap);
 }
 
 int ssd_verify_prep(const int32_t* n_nodes, int64_t rows_cap, const int32_t* root_token, const int32_t* root_pos,
@@ -343,20 +356,18 @@ int ssd_verify_prep(const int32_t* n_nodes, int64_t rows_cap, const int32_t* roo
                     int64_t mask_words, uint32_t* status, void* stream) {
   if (rows_cap <= 0 || mask_words <= 0 || rows_cap - 1 > mask_words * 64)
     return fail(SSD_ERR_INVALID, "ssd_verify_prep: rows exceed the ancestor mask");
-  verify_prep_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      n_nodes, (int)rows_cap, root_token, root_pos, tokens, parents, depths, ids, positions, slots, prefix_len,
+  return launch_kernel("verify_prep_kernel", verify_prep_kernel, dim3(1), dim3(256), 0,
+      static_cast<cudaStream_t>(stream), 1, 1, n_nodes, (int)rows_cap, root_token, root_pos, tokens, parents, depths, ids, positions, slots, prefix_len,
       spec_base, mask, (int)mask_words, status);
-  return check_launch("verify_prep_kernel");
 }
 
 int ssd_tree_walk_greedy(const int32_t* n_nodes, int64_t max_nodes, const int32_t* argmax, const int32_t* tokens,
                          const int32_t* parents, const int32_t* ranks, const int32_t* root_pos, int32_t* accepted,
                          int32_t* n_accepted, int32_t* bonus, int32_t* keep_slots, int32_t* n_keep, void* stream) {
   if (max_nodes < 0 || max_nodes > 4096) return fail(SSD_ERR_INVALID, "ssd_tree_walk_greedy: bad max_nodes");
-  tree_walk_greedy_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      n_nodes, (int)max_nodes, argmax, tokens, parents, ranks, root_pos, accepted, n_accepted, bonus, keep_slots,
+  return launch_kernel("tree_walk_greedy_kernel", tree_walk_greedy_kernel, dim3(1), dim3(32), 0,
+      static_cast<cudaStream_t>(stream), 1, 1, n_nodes, (int)max_nodes, argmax, tokens, parents, ranks, root_pos, accepted, n_accepted, bonus, keep_slots,
       n_keep);
-  return check_launch("tree_walk_greedy_kernel");
 }
 
 int ssd_kv_compact(void* cache, int64_t n_layers, int64_t layer_stride, int64_t kv_stride, int64_t n_kv_heads,
@@ -369,27 +380,25 @@ int ssd_kv_compact(void* cache, int64_t n_layers, int64_t layer_stride, int64_t 
   const int64_t groups = row_bytes / 16;
   const int64_t total = n_layers * 2 * n_kv_heads * groups;
   const unsigned blocks = (unsigned)((total + 255) / 256);
-  kv_compact_kernel<uint4><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<uint8_t*>(cache), n_layers, layer_stride * es, kv_stride * es, n_kv_heads, head_stride * es,
+  return launch_kernel("kv_compact_kernel", kv_compact_kernel<uint4>, dim3(blocks), dim3(256), 0,
+      static_cast<cudaStream_t>(stream), 1, 1, static_cast<uint8_t*>(cache), n_layers, layer_stride * es, kv_stride * es, n_kv_heads, head_stride * es,
       row_bytes, start, keep_slots, n_keep, (int)max_keep);
-  return check_launch("kv_compact_kernel");
 }
 
 int ssd_round_commit(const int32_t* n_accepted, const int32_t* accepted, const int32_t* tokens,
                      const int32_t* bonus, int32_t* seq_len, int32_t* root_token, int32_t* out_tokens,
                      int32_t* n_out, int64_t out_cap, int32_t* round_log, uint32_t* status, void* stream) {
-  round_commit_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      n_accepted, accepted, tokens, bonus, seq_len, root_token, out_tokens, n_out, (int)out_cap, round_log, status);
-  return check_launch("round_commit_kernel");
+  return launch_kernel("round_commit_kernel", round_commit_kernel, dim3(1), dim3(32), 0,
+      static_cast<cudaStream_t>(stream), 1, 1, n_accepted, accepted, tokens, bonus, seq_len, root_token, out_tokens, n_out, (int)out_cap, round_log, status);
 }
 
 int ssd_causal_prep(const int32_t* base, int64_t T, const int32_t* src_ids, int32_t* ids, int32_t* positions,
                     int32_t* slots, int32_t* prefix_len, void* stream) {
   if (T <= 0) return fail(SSD_ERR_INVALID, "ssd_causal_prep: T must be positive");
   const unsigned blocks = (unsigned)((T + 255) / 256 > 64 ? 64 : (T + 255) / 256);
-  causal_prep_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(base, (int)T, src_ids, ids, positions,
-                                                                             slots, prefix_len);
-  return check_launch("causal_prep_kernel");
+  return launch_kernel("causal_prep_kernel", causal_prep_kernel, dim3(blocks), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), 1, 1, base, (int)T, src_ids, ids, positions, slots,
+                       prefix_len);
 }
 
 }  // extern "C"
