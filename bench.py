@@ -423,7 +423,8 @@ def ncu_case(args, dev) -> None:
     else:
         from ssd.models.runner import ForwardInputs
 
-        H, Hkv, hd, ctx, T = 32, 8, 128, 16384, 33
+        H, Hkv, hd, T = 32, 8, 128, 33
+        ctx = args.prompt_len or 16384
         ws = ops.Workspace(dev, 64, 1, 64)
         kc = torch.randn(Hkv, ctx + 64, hd, device=dev).bfloat16()
         vc = torch.randn(Hkv, ctx + 64, hd, device=dev).bfloat16()

@@ -7,6 +7,10 @@
 // so each K/V byte of the slice is read once for all those queries. Slices
 // produce (max, sum, acc) partials; the last CTA of a (head, row-group) to
 // finish merges them in slice order (deterministic).
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "common.cuh"
 #include "host.cuh"
 
@@ -282,20 +286,25 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 __host__ __device__ constexpr int mma_rec(int hd) { return hd + 4; }
 // Shared memory before the per-token metadata: the double-buffered K/V
 // stages, reused after the key loop for the partial rows (cluster merge).
+constexpr int kStages = 4;  // K/V blocks in flight per CTA (memory-level parallelism)
 __host__ __device__ constexpr int mma_region(int hd) {
-  return (4 * 64 * hd * 2) > (kMmaMaxRows * mma_rec(hd) * 4) ? (4 * 64 * hd * 2) : (kMmaMaxRows * mma_rec(hd) * 4);
+  return (kStages * 2 * 64 * hd * 2) > (kMmaMaxRows * mma_rec(hd) * 4) ? (kStages * 2 * 64 * hd * 2)
+                                                                        : (kMmaMaxRows * mma_rec(hd) * 4);
 }
+// Q rows of the group, bf16, 16-byte chunks XOR-swizzled by row.
+__host__ __device__ constexpr int mma_qbytes(int hd) { return kMmaMaxRows * hd * 2; }
 constexpr int kMmaMeta = (kMmaMaxTok + 1) * 4 + kMmaMaxTok * 4 * 8 + 16;
 
 template <int HD>
-__global__ void __launch_bounds__(256) attn_mma_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
   constexpr int CH = HD / 8;   // 16-byte chunks per K/V row
   constexpr int KS = HD / 16;  // k-steps over head_dim (QK^T)
   constexpr int NTD = HD / 8;  // n-tiles over head_dim (PV)
   constexpr int KB = 64;       // keys per block
   extern __shared__ __align__(128) uint8_t attn_smem[];
-  uint8_t* kv = attn_smem;                            // [2 stages][K|V][64][HD] bf16, swizzled
-  int* s_plen = reinterpret_cast<int*>(attn_smem + mma_region(HD));
+  uint8_t* kv = attn_smem;  // [kStages][K|V][64][HD] bf16, swizzled
+  uint8_t* qs = attn_smem + mma_region(HD);  // [kMmaMaxRows][HD] bf16, swizzled
+  int* s_plen = reinterpret_cast<int*>(qs + mma_qbytes(HD));
   uint64_t* s_mask = reinterpret_cast<uint64_t*>(s_plen + kMmaMaxTok + 1);  // [tok][mask_words]
   int* s_misc = reinterpret_cast<int*>(s_mask + kMmaMaxTok * 4);           // need_end, min_plen, last
 
@@ -345,20 +354,19 @@ __global__ void __launch_bounds__(256) attn_mma_kernel(const AttnArgs a) {
   const bool ok0 = rl0 < Mg, ok1 = rl1 < Mg;
   const int qr0 = q0 + rl0, qr1 = q0 + rl1;
   const int tok0 = ok0 ? qr0 / a.G - t_first : 0, tok1 = ok1 ? qr1 / a.G - t_first : 0;
+  // Stage the group's Q rows (A operand) in shared memory; rows past Mg are 0.
   const bf16* qb = static_cast<const bf16*>(a.q);
-  uint32_t qf[KS][4];
-  {
-    const bf16* p0 = qb + (int64_t)(qr0 / a.G) * a.ldq + (int64_t)(h * a.G + qr0 % a.G) * HD;
-    const bf16* p1 = qb + (int64_t)(qr1 / a.G) * a.ldq + (int64_t)(h * a.G + qr1 % a.G) * HD;
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-      const int c = ks * 16 + 2 * tq;
-      qf[ks][0] = (active && ok0) ? *reinterpret_cast<const uint32_t*>(p0 + c) : 0u;
-      qf[ks][1] = (active && ok1) ? *reinterpret_cast<const uint32_t*>(p1 + c) : 0u;
-      qf[ks][2] = (active && ok0) ? *reinterpret_cast<const uint32_t*>(p0 + c + 8) : 0u;
-      qf[ks][3] = (active && ok1) ? *reinterpret_cast<const uint32_t*>(p1 + c + 8) : 0u;
+  for (int idx = threadIdx.x; idx < a.rows_per_group * CH; idx += blockDim.x) {
+    const int r = idx / CH, c = idx % CH;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (r < Mg) {
+      const int qr = q0 + r;
+      v = *reinterpret_cast<const uint4*>(qb + (int64_t)(qr / a.G) * a.ldq + (int64_t)(h * a.G + qr % a.G) * HD +
+                                          c * 8);
     }
+    *reinterpret_cast<uint4*>(qs + r * HD * 2 + ((c ^ (r & 7)) << 4)) = v;
   }
+  const uint32_t qs_s = smem_u32(qs);
   const int pl0 = ok0 ? s_plen[tok0] : 0, pl1 = ok1 ? s_plen[tok1] : 0;
 
   float o[NTD][4];
@@ -372,31 +380,34 @@ __global__ void __launch_bounds__(256) attn_mma_kernel(const AttnArgs a) {
   const uint32_t kv_s = smem_u32(kv);
   auto stage_k = [&](int st) { return kv_s + st * 2 * KB * HD * 2; };
   auto stage_v = [&](int st) { return kv_s + st * 2 * KB * HD * 2 + KB * HD * 2; };
-  auto load_block = [&](int b, int st) {
-    const int kb = k_lo + b * KB;
-    for (int idx = threadIdx.x; idx < KB * CH; idx += blockDim.x) {
-      const int key = idx / CH, c = idx % CH;
-      const int slot = kb + key;
-      const bool valid = slot < k_hi;
-      const int64_t off = (int64_t)(valid ? slot : 0) * HD + c * 8;
-      const uint32_t dst = key * HD * 2 + ((c ^ (key & 7)) << 4);
-      cp_async16(stage_k(st) + dst, kbase + off, valid);
-      cp_async16(stage_v(st) + dst, vbase + off, valid);
+  // kStages-deep ring: every iteration commits exactly one (possibly empty)
+  // cp.async group, so waiting for all but the newest kStages-1 groups means
+  // block b has landed.
+  auto load_block = [&](int b) {
+    if (b < nblocks) {
+      const int st = b % kStages;
+      const int kb = k_lo + b * KB;
+      for (int idx = threadIdx.x; idx < KB * CH; idx += blockDim.x) {
+        const int key = idx / CH, c = idx % CH;
+        const int slot = kb + key;
+        const bool valid = slot < k_hi;
+        const int64_t off = (int64_t)(valid ? slot : 0) * HD + c * 8;
+        const uint32_t dst = key * HD * 2 + ((c ^ (key & 7)) << 4);
+        cp_async16(stage_k(st) + dst, kbase + off, valid);
+        cp_async16(stage_v(st) + dst, vbase + off, valid);
+      }
     }
     cp_async_commit();
   };
 
-  if (nblocks > 0) load_block(0, 0);
+#pragma unroll
+  for (int b = 0; b < kStages - 1; ++b) load_block(b);
   for (int b = 0; b < nblocks; ++b) {
-    if (b + 1 < nblocks) {
-      load_block(b + 1, (b + 1) & 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    load_block(b + kStages - 1);
+    cp_async_wait<kStages - 1>();
     __syncthreads();
     if (active) {
-      const int st = b & 1;
+      const int st = b % kStages;
       const int kb = k_lo + b * KB;
       float s[8][4];
 #pragma unroll
@@ -404,14 +415,20 @@ __global__ void __launch_bounds__(256) attn_mma_kernel(const AttnArgs a) {
       const int mi = lane >> 3, ri = lane & 7;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
+        uint32_t qf[4];  // A fragment: rows warp*16 + (lane & 15), k-chunk 2*ks + (lane >> 4)
+        {
+          const int qrow = warp * 16 + (lane & 15);
+          const int qc = 2 * ks + (lane >> 4);
+          ldsm_x4(qs_s + qrow * HD * 2 + ((qc ^ (qrow & 7)) << 4), qf[0], qf[1], qf[2], qf[3]);
+        }
 #pragma unroll
         for (int ntp = 0; ntp < 4; ++ntp) {
           const int key = (2 * ntp + (mi >> 1)) * 8 + ri;
           const int c = 2 * ks + (mi & 1);
           uint32_t b0, b1, b2, b3;
           ldsm_x4(stage_k(st) + key * HD * 2 + ((c ^ (key & 7)) << 4), b0, b1, b2, b3);
-          mma_16816(s[2 * ntp], qf[ks], b0, b1);
-          mma_16816(s[2 * ntp + 1], qf[ks], b2, b3);
+          mma_16816(s[2 * ntp], qf, b0, b1);
+          mma_16816(s[2 * ntp + 1], qf, b2, b3);
         }
       }
       // scale + mask: rows rl0 (s[.][0..1]) and rl1 (s[.][2..3])
@@ -494,8 +511,9 @@ __global__ void __launch_bounds__(256) attn_mma_kernel(const AttnArgs a) {
         }
       }
     }
-    __syncthreads();  // the stage is refilled two blocks later
+    __syncthreads();  // stage b % kStages is refilled by the next iteration
   }
+  cp_async_wait<0>();  // (only empty groups remain) the stages may now be reused
 
   // row sums across the quad
 #pragma unroll
@@ -560,14 +578,22 @@ __global__ void __launch_bounds__(256) attn_mma_kernel(const AttnArgs a) {
       float acc[DPL];
 #pragma unroll
       for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-      for (int s = 0; s < a.n_splits; ++s) {
-        const float ws = __shfl_sync(0xffffffffu, wgt, s);
-        const uint32_t ps = __shfl_sync(0xffffffffu, peer, s);
-        float v[DPL];
+      // all peer loads in flight first, then accumulate in slice order
+      float v[kMaxAttnClusterSplits][DPL];
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) v[i] = dsmem_ld(ps + (uint32_t)(r * rec + 4 + lane * DPL + i) * 4);
+      for (int s = 0; s < kMaxAttnClusterSplits; ++s) {
+        const uint32_t ps = __shfl_sync(0xffffffffu, peer, s < a.n_splits ? s : 0);
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[i] = fmaf(ws, v[i], acc[i]);
+        for (int i = 0; i < DPL; ++i)
+          v[s][i] = s < a.n_splits ? dsmem_ld(ps + (uint32_t)(r * rec + 4 + lane * DPL + i) * 4) : 0.f;
+      }
+#pragma unroll
+      for (int s = 0; s < kMaxAttnClusterSplits; ++s) {
+        const float ws = __shfl_sync(0xffffffffu, wgt, s < a.n_splits ? s : 0);
+        if (s < a.n_splits) {
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc[i] = fmaf(ws, v[s][i], acc[i]);
+        }
       }
       const float inv = L > 0.f ? 1.f / L : 0.f;
       bf16* op = outp + (int64_t)(qr / a.G) * a.ldo + (int64_t)(h * a.G + qr % a.G) * HD + lane * DPL;
@@ -640,6 +666,40 @@ __global__ void __launch_bounds__(256) attn_mma_kernel(const AttnArgs a) {
   if (threadIdx.x == 0) a.counters[kAttnCounterBase + blk] = 0u;
 }
 
+// Clusters of `s` CTAs (one row group's key slices) that can be resident at
+// once, from the occupancy API; cached per kernel, size and device.
+int attn_resident_clusters(void (*kern)(const AttnArgs), int s, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<void*, int, size_t, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(reinterpret_cast<void*>(kern), s, smem, dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, s);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = s;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = n;
+  return n;
+}
+
 }  // namespace ssd
 
 using namespace ssd;
@@ -686,12 +746,24 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
     a.rows_per_group = (int)(((M + a.groups - 1) / a.groups + 15) / 16 * 16);
     const int64_t blocks = (int64_t)a.n_kv * a.groups;
     if (blocks > 16384) return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: too many row groups");
+    const size_t smem = (size_t)mma_region((int)head_dim) + mma_qbytes((int)head_dim) + kMmaMeta;
+    void (*kern)(const AttnArgs) = head_dim == 128 ? attn_mma_kernel<128> : attn_mma_kernel<64>;
+    static bool set128 = false, set64 = false;
+    bool& set = head_dim == 128 ? set128 : set64;
+    if (!set) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+      set = true;
+    }
     int64_t splits = (2 * sms) / blocks;
     const int64_t by_len = (kv_bound + 255) / 256;
     if (splits > by_len) splits = by_len;
-    // Up to 8 slices of <= 1024 keys merge inside one cluster through DSMEM;
-    // longer contexts use more slices and a merge through global memory.
-    if (kv_bound <= 8 * 1024 && splits > kMaxAttnClusterSplits) splits = kMaxAttnClusterSplits;
+    // Up to 8 slices of <= 1024 keys merge inside one cluster through DSMEM,
+    // with every cluster resident at once; longer contexts use more slices
+    // and a merge through global memory.
+    if (kv_bound <= 8 * 1024) {
+      if (splits > kMaxAttnClusterSplits) splits = kMaxAttnClusterSplits;
+      while (splits > 1 && attn_resident_clusters(kern, (int)splits, smem) < blocks) --splits;
+    }
     if (splits > kMmaMaxSplits) splits = kMmaMaxSplits;
     if (splits < 1) splits = 1;
     int64_t split_len = ((kv_bound + splits - 1) / splits + 63) / 64 * 64;
@@ -704,14 +776,6 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
         return fail(SSD_ERR_WORKSPACE, "ssd_tree_attention: workspace too small (need %lld)", (long long)need);
       a.counters = static_cast<uint32_t*>(workspace);
       a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
-    }
-    const size_t smem = (size_t)mma_region((int)head_dim) + kMmaMeta;
-    void (*kern)(const AttnArgs) = head_dim == 128 ? attn_mma_kernel<128> : attn_mma_kernel<64>;
-    static bool set128 = false, set64 = false;
-    bool& set = head_dim == 128 ? set128 : set64;
-    if (!set) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
-      set = true;
     }
     return launch_kernel("attn_mma_kernel", kern, dim3((unsigned)blocks, (unsigned)a.n_splits), dim3(256), smem, s,
                          1u, a.cluster_merge ? (unsigned)a.n_splits : 1u, a);

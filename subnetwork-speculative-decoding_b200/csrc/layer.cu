@@ -33,7 +33,21 @@ __global__ void rmsnorm_kernel(const float* x, int64_t d, int64_t ldx, const T* 
   const int t = blockIdx.x;
   const float* row = x + (int64_t)t * ldx;
   float ss = 0.f;
-  for (int64_t i = threadIdx.x; i < d; i += blockDim.x) ss = fmaf(row[i], row[i], ss);
+  if ((d & 3) == 0 && (ldx & 3) == 0 && d <= 4LL * 4 * blockDim.x) {
+    // up to 4 float4 per thread, all loads issued before use (latency-bound op)
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    const int n4 = (int)(d >> 2);
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = threadIdx.x + j * blockDim.x;
+      v[j] = i < n4 ? r4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+  } else {
+    for (int64_t i = threadIdx.x; i < d; i += blockDim.x) ss = fmaf(row[i], row[i], ss);
+  }
   __shared__ float red[32];
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
