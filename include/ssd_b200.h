@@ -219,6 +219,56 @@ int ssd_round_commit(const int32_t* n_accepted, const int32_t* accepted, const i
 int ssd_causal_prep(const int32_t* base, int64_t T, const int32_t* src_ids, int32_t* ids, int32_t* positions,
                     int32_t* slots, int32_t* prefix_len, void* stream);
 
+/* ------------------------------------------------------------- sampling
+ * warp(logits) = softmax(logits / temperature) restricted to the top-p
+ * nucleus (smallest prefix of the descending order with mass >= top_p),
+ * renormalised, as warp_probs (ssd/engine/tree_drafter.py:34-45). A row's
+ * warp is summarised by 16-byte parameters {max, 1/T, lambda, log Z}; the
+ * nucleus threshold lambda is found by a deterministic radix select. Random
+ * numbers are Philox4x32-10 keyed by *seed with counter (round, row, i, stream). */
+
+/* Warp parameters of `rows` logit rows [rows, ld] (fp32) into params_out. */
+int ssd_warp_params(const float* logits, int64_t ld, int64_t rows, int64_t V, float temperature, float top_p,
+                    void* params_out, void* stream);
+
+/* Warped probabilities of rows [rows, ld] into out [rows, ldo] (fp32) from
+ * their warp parameters; zero outside the nucleus. */
+int ssd_warp_probs(const float* logits, int64_t ld, int64_t rows, int64_t V, const void* params, float* out,
+                   int64_t ldo, void* stream);
+
+/* Per row: k tokens drawn without replacement from the warped distribution
+ * (Gumbel top-k, in draw order) and their warped log-probs; fewer than k
+ * kept tokens leave token -1 / log-prob -inf. Row r uses RNG row id
+ * row_base + r. Replaces the sampling branch of TreeDrafter._propose
+ * (tree_drafter.py:134-145). */
+int ssd_gumbel_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, const void* params, int64_t k,
+                    const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round, int64_t row_base,
+                    int32_t* out_tok, float* out_logprob, void* stream);
+
+/* One token drawn from warp(logits[0..V)) into out[0] (scratch: V floats).
+ * Replaces _first_token's sampling branch (ssd/engine/speculative.py:81-84). */
+int ssd_sample_token(const float* logits, int64_t V, float temperature, float top_p, const uint64_t* seed,
+                     const int32_t* round, int64_t row_id, int64_t stream_id, float* scratch, int32_t* out,
+                     void* stream);
+
+/* Multi-candidate speculative sampling without replacement over the device
+ * tree: at each node p = warp(target row), children in rank order accepted
+ * with prob min(1, p(x)/q(x)); on rejection p <- norm(max(p - q, 0)) (if it
+ * has mass), q(x) <- 0 renormalised; when every child is rejected the bonus
+ * is drawn from p. q of a node's children = warp(draft logits row 0 for the
+ * root, row draft_pos - root_pos for a fed node) over the draft vocabulary
+ * (vocab_ids, NULL = the first Vd ids). target_params / draft_params are
+ * ssd_warp_params of the target rows [rows, ldt] and the draft_rows draft
+ * rows [draft_rows, ldd]. p_scratch / q_scratch: V floats each. Outputs as
+ * ssd_tree_walk_greedy. Replaces sample_verify (ssd/engine/verify.py:60-95). */
+int ssd_tree_walk_sample(const int32_t* n_nodes, int64_t max_nodes, const int32_t* tokens, const int32_t* parents,
+                         const int32_t* ranks, const int32_t* draft_pos, const int32_t* root_pos,
+                         const float* target_logits, int64_t ldt, const void* target_params, int64_t V,
+                         const float* draft_logits, int64_t ldd, const void* draft_params, int64_t draft_rows,
+                         int64_t Vd, const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round,
+                         float* p_scratch, float* q_scratch, int32_t* accepted, int32_t* n_accepted, int32_t* bonus,
+                         int32_t* keep_slots, int32_t* n_keep, uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

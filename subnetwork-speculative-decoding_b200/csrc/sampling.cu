@@ -1,0 +1,545 @@
+// Sampling (temperature > 0): warped distributions, Gumbel top-k drafting and
+// multi-candidate speculative sampling without replacement.
+//
+// warp(logits) = softmax(logits / T) restricted to the nucleus: sort the
+// probabilities in descending order and keep the smallest prefix whose mass
+// reaches top_p (an element is dropped when the mass strictly before it
+// exceeds top_p), renormalised. Each row's warp is summarised by parameters
+// {m, 1/T, lambda, log Z}: token i has log-prob (l_i - m)/T - log Z if
+// l_i >= lambda, else probability 0. lambda is found without sorting by a
+// 4-level radix select over the order-preserving bits of the logits, summing
+// probability mass in 2^-48 fixed point with integer atomics, so the result
+// does not depend on thread scheduling. All other reductions use a fixed
+// per-thread partition and a fixed combine order (deterministic).
+//
+// Random numbers: Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random
+// numbers: as easy as 1, 2, 3", SC 2011), keyed by the caller's seed, with
+// counter (round, row, index, stream); no state is kept between launches.
+#include "common.cuh"
+#include "host.cuh"
+
+namespace ssd {
+
+constexpr int kSampThreads = 1024;
+constexpr int kSampWarps = kSampThreads / 32;
+constexpr int kMaxK = 16;
+
+struct WarpParams {
+  float m;       // row max logit
+  float inv_t;   // 1 / temperature
+  float lambda;  // smallest kept logit
+  float log_z;   // log of the kept mass normaliser (relative to exp((l - m) / T))
+};
+
+// ------------------------------------------------------------------- Philox
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+    k.x += 0x9E3779B9u;
+    k.y += 0xBB67AE85u;
+  }
+  return c;
+}
+// Uniform in the open interval (0, 1) from 24 random bits.
+__device__ __forceinline__ float u01(uint32_t x) { return (static_cast<float>(x >> 8) + 0.5f) * (1.0f / 16777216.0f); }
+__device__ __forceinline__ float uniform(uint64_t seed, uint32_t round, uint32_t row, uint32_t idx, uint32_t stream) {
+  const uint4 r = philox4x32_10(make_uint4(round, row, idx, stream),
+                                make_uint2(static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32)));
+  return u01(r.x);
+}
+
+// ------------------------------------------------------ block reductions
+// Deterministic: every thread combines its own elements in index order, then
+// a fixed shuffle tree per warp, then warp results in warp order.
+__device__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < kSampWarps; ++i) t += red[i];
+  return t;
+}
+__device__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = -INFINITY;
+  for (int i = 0; i < kSampWarps; ++i) t = fmaxf(t, red[i]);
+  return t;
+}
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// Warp parameters of one row (all threads of the block). `red` >= 32 floats,
+// `hist` 256 x u64, `sel` 4 u64 of shared memory.
+__device__ WarpParams row_warp(const float* row, int V, float temperature, float top_p, float* red,
+                               unsigned long long* hist, unsigned long long* sel) {
+  WarpParams P;
+  P.inv_t = 1.0f / temperature;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += kSampThreads) mx = fmaxf(mx, row[i]);
+  P.m = block_max(mx, red);
+  float z = 0.f;
+  for (int i = threadIdx.x; i < V; i += kSampThreads) z += expf((row[i] - P.m) * P.inv_t);
+  const float Z = block_sum(z, red);
+  if (!(top_p < 1.0f)) {
+    P.lambda = -INFINITY;
+    P.log_z = logf(Z);
+    return P;
+  }
+  const double scale = 281474976710656.0 / (double)Z;  // 2^48 / Z
+  const unsigned long long target = static_cast<unsigned long long>((double)top_p * 281474976710656.0);
+  uint32_t prefix = 0;
+  unsigned long long mass_gt = 0;
+  for (int level = 0; level < 4; ++level) {
+    const int shift = 24 - 8 * level;
+    for (int b = threadIdx.x; b < 256; b += kSampThreads) hist[b] = 0ull;
+    __syncthreads();
+    for (int i = threadIdx.x; i < V; i += kSampThreads) {
+      const float l = row[i];
+      const uint32_t k = order_key(l);
+      if (level == 0 || (k >> (shift + 8)) == prefix) {
+        const unsigned long long fp =
+            static_cast<unsigned long long>((double)expf((l - P.m) * P.inv_t) * scale);
+        atomicAdd(&hist[(k >> shift) & 255u], fp);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      // lowest non-empty bin whose mass strictly above it is <= top_p
+      unsigned long long S = mass_gt, sel_S = mass_gt;
+      int s = -1;
+      for (int b = 255; b >= 0; --b) {
+        if (hist[b] == 0ull) continue;
+        if (S > target) break;
+        s = b;
+        sel_S = S;
+        S += hist[b];
+      }
+      if (s < 0) s = 255;  // unreachable for a finite row
+      sel[0] = (static_cast<unsigned long long>(prefix) << 8) | static_cast<unsigned>(s);
+      sel[1] = sel_S;
+    }
+    __syncthreads();
+    prefix = static_cast<uint32_t>(sel[0]);
+    mass_gt = sel[1];
+  }
+  P.lambda = key_float(prefix);
+  float zk = 0.f;
+  for (int i = threadIdx.x; i < V; i += kSampThreads) {
+    const float l = row[i];
+    if (l >= P.lambda) zk += expf((l - P.m) * P.inv_t);
+  }
+  P.log_z = logf(block_sum(zk, red));
+  return P;
+}
+
+__device__ __forceinline__ float warped_lp(const WarpParams& P, float l) {
+  return l >= P.lambda ? (l - P.m) * P.inv_t - P.log_z : -INFINITY;
+}
+
+// One warp-parameter record per row.
+__global__ void __launch_bounds__(kSampThreads) warp_params_kernel(const float* logits, int64_t ld, int V,
+                                                                   float temperature, float top_p,
+                                                                   WarpParams* out) {
+  __shared__ float red[32];
+  __shared__ unsigned long long hist[256];
+  __shared__ unsigned long long sel[4];
+  pdl_wait();
+  pdl_trigger();
+  const WarpParams P = row_warp(logits + (int64_t)blockIdx.x * ld, V, temperature, top_p, red, hist, sel);
+  if (threadIdx.x == 0) out[blockIdx.x] = P;
+}
+
+// Warped probabilities of every row (grid: column blocks x rows).
+__global__ void warp_probs_kernel(const float* logits, int64_t ld, int V, const WarpParams* params, float* out,
+                                  int64_t ldo) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.y;
+  const WarpParams P = params[r];
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
+    const float lp = warped_lp(P, logits[(int64_t)r * ld + i]);
+    out[(int64_t)r * ldo + i] = lp == -INFINITY ? 0.f : expf(lp);
+  }
+}
+
+// Gumbel top-k (sampling without replacement, in draw order) per row over
+// the warped distribution; tokens through vocab_ids. Missing draws (support
+// < k) get token -1 and log-prob -inf. RNG counter: (round, row_id[row], i, 0).
+__global__ void __launch_bounds__(kSampThreads) gumbel_topk_kernel(const float* logits, int64_t ld, int V,
+                                                                   const WarpParams* params, int k,
+                                                                   const int64_t* vocab_ids, const uint64_t* seed,
+                                                                   const int32_t* round, int row_base,
+                                                                   int32_t* out_tok, float* out_lp) {
+  __shared__ float s_key[kSampWarps];
+  __shared__ int s_idx[kSampWarps];
+  __shared__ int s_own[kSampWarps];
+  pdl_wait();
+  pdl_trigger();
+  const float* row = logits + (int64_t)blockIdx.x * ld;
+  const WarpParams P = params[blockIdx.x];
+  const uint64_t sd = seed[0];
+  const uint32_t rnd = static_cast<uint32_t>(round ? round[0] : 0);
+  const uint32_t row_id = static_cast<uint32_t>(row_base + blockIdx.x);
+  // local top-k (descending key, ascending index on ties)
+  float kk[kMaxK];
+  int ki[kMaxK];
+#pragma unroll
+  for (int j = 0; j < kMaxK; ++j) {
+    kk[j] = -INFINITY;
+    ki[j] = INT32_MAX;
+  }
+  for (int i = threadIdx.x; i < V; i += kSampThreads) {
+    const float lp = warped_lp(P, row[i]);
+    if (lp == -INFINITY) continue;
+    const float g = -logf(-logf(uniform(sd, rnd, row_id, static_cast<uint32_t>(i), 0u)));
+    const float key = lp + g;
+    if (key > kk[k - 1] || (key == kk[k - 1] && i < ki[k - 1])) {
+      int j = k - 1;
+      while (j > 0 && (key > kk[j - 1] || (key == kk[j - 1] && i < ki[j - 1]))) {
+        kk[j] = kk[j - 1];
+        ki[j] = ki[j - 1];
+        --j;
+      }
+      kk[j] = key;
+      ki[j] = i;
+    }
+  }
+  int head = 0;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int q = 0; q < k; ++q) {
+    float bk = head < k ? kk[head] : -INFINITY;
+    int bi = head < k ? ki[head] : INT32_MAX;
+    int own = threadIdx.x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const int oo = __shfl_xor_sync(0xffffffffu, own, o);
+      if (ok > bk || (ok == bk && oi < bi)) {
+        bk = ok;
+        bi = oi;
+        own = oo;
+      }
+    }
+    if (lane == 0) {
+      s_key[w] = bk;
+      s_idx[w] = bi;
+      s_own[w] = own;
+    }
+    __syncthreads();
+    float gk = -INFINITY;
+    int gi = INT32_MAX, go = -1;
+    for (int j = 0; j < kSampWarps; ++j)
+      if (s_key[j] > gk || (s_key[j] == gk && s_idx[j] < gi)) {
+        gk = s_key[j];
+        gi = s_idx[j];
+        go = s_own[j];
+      }
+    if (threadIdx.x == go) ++head;
+    if (threadIdx.x == 0) {
+      const bool ok = gk != -INFINITY;
+      out_tok[(int64_t)blockIdx.x * k + q] = ok ? (vocab_ids ? (int)vocab_ids[gi] : gi) : -1;
+      out_lp[(int64_t)blockIdx.x * k + q] = ok ? warped_lp(P, row[gi]) : -INFINITY;
+    }
+    __syncthreads();
+  }
+}
+
+// Inverse-CDF draw from unnormalised non-negative weights w[0..n) with
+// uniform u: contiguous per-thread chunks, exclusive scan in thread order.
+__device__ int draw_from(const float* w, int n, float u, float* red, float* scan) {
+  const int chunk = (n + kSampThreads - 1) / kSampThreads;
+  const int b = threadIdx.x * chunk, e = min(n, b + chunk);
+  float s = 0.f;
+  for (int i = b; i < e; ++i) s += w[i];
+  scan[threadIdx.x] = s;
+  __syncthreads();
+  __shared__ int s_pick;
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int i = 0; i < kSampThreads; ++i) {
+      const float v = scan[i];
+      scan[i] = tot;
+      tot += v;
+    }
+    red[0] = tot;
+    s_pick = -1;
+  }
+  __syncthreads();
+  const float target = u * red[0];
+  const float lo = scan[threadIdx.x];
+  if (target >= lo && target < lo + s && s > 0.f) {
+    // the chunk's running sum can round below lo + s: fall back to its last
+    // positive weight, never to a zero-weight index
+    float c = lo;
+    int pick = -1, last_pos = -1;
+    for (int i = b; i < e; ++i) {
+      if (!(w[i] > 0.f)) continue;
+      last_pos = i;
+      c += w[i];
+      if (target < c) {
+        pick = i;
+        break;
+      }
+    }
+    atomicMax(&s_pick, pick >= 0 ? pick : last_pos);
+  }
+  __syncthreads();
+  int pick = s_pick;
+  if (pick < 0) {  // rounding at the top end: last positive weight
+    __shared__ int s_last;
+    if (threadIdx.x == 0) s_last = -1;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += kSampThreads)
+      if (w[i] > 0.f) atomicMax(&s_last, i);
+    __syncthreads();
+    pick = s_last < 0 ? 0 : s_last;
+  }
+  __syncthreads();
+  return pick;
+}
+
+// Token ~ warp(logits row): one launch, one row. Writes the token to out[0];
+// the RNG counter is (round[0], row_id, 0, stream).
+__global__ void __launch_bounds__(kSampThreads) sample_token_kernel(const float* logits, int V, float temperature,
+                                                                    float top_p, const uint64_t* seed,
+                                                                    const int32_t* round, int row_id, int stream,
+                                                                    float* scratch, int32_t* out) {
+  __shared__ float red[32];
+  __shared__ unsigned long long hist[256];
+  __shared__ unsigned long long sel[4];
+  __shared__ float scan[kSampThreads];
+  pdl_wait();
+  pdl_trigger();
+  const WarpParams P = row_warp(logits, V, temperature, top_p, red, hist, sel);
+  for (int i = threadIdx.x; i < V; i += kSampThreads) {
+    const float lp = warped_lp(P, logits[i]);
+    scratch[i] = lp == -INFINITY ? 0.f : expf(lp);
+  }
+  __syncthreads();
+  const float u = uniform(seed[0], static_cast<uint32_t>(round ? round[0] : 0), static_cast<uint32_t>(row_id), 0u,
+                          static_cast<uint32_t>(stream));
+  const int pick = draw_from(scratch, V, u, red, scan);
+  if (threadIdx.x == 0) out[0] = pick;
+}
+
+// Multi-candidate speculative sampling without replacement over the device
+// tree (one CTA). Target row r of `tlogits` belongs to row r of the verify
+// forward (0 = root); the draft distribution a node's children were drawn
+// from is draft row 0 for the root, else draft_pos - root_pos. Warp
+// parameters of every target and draft row come precomputed (tparams,
+// dparams), so the walk only materialises p and q along the accepted path.
+// p, q: scratch of V floats each (q is 0 outside the draft vocabulary).
+// RNG counters: acceptance (round, cur + 1, child, 1), bonus (round, cur + 1, 0, 2).
+__global__ void __launch_bounds__(kSampThreads) sample_verify_kernel(
+    const int32_t* n_nodes, int max_nodes, const int32_t* tokens, const int32_t* parents, const int32_t* ranks,
+    const int32_t* draft_pos, const int32_t* root_pos, const float* tlogits, int64_t ldt, const WarpParams* tparams,
+    int V, const float* dlogits, int64_t ldd, const WarpParams* dparams, int draft_rows, int Vd,
+    const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round, float* p, float* q, int32_t* accepted,
+    int32_t* n_accepted, int32_t* bonus, int32_t* keep_slots, int32_t* n_keep, uint32_t* status) {
+  __shared__ float red[32];
+  __shared__ float scan[kSampThreads];
+  __shared__ int kids[64];
+  __shared__ int s_nk;
+  __shared__ int s_chosen;
+  pdl_wait();
+  pdl_trigger();
+  const int n = min(*n_nodes, max_nodes);
+  const int c0 = root_pos[0];
+  const uint64_t sd = seed[0];
+  const uint32_t rnd = static_cast<uint32_t>(round ? round[0] : 0);
+  int cur = -1, na = 0;
+  if (threadIdx.x == 0) keep_slots[0] = c0;
+  for (int step = 0; step <= n; ++step) {
+    // p = warp(target row of cur)
+    const float* trow = tlogits + (int64_t)(cur + 1) * ldt;
+    const WarpParams PT = tparams[cur + 1];
+    for (int i = threadIdx.x; i < V; i += kSampThreads) {
+      const float lp = warped_lp(PT, trow[i]);
+      p[i] = lp == -INFINITY ? 0.f : expf(lp);
+    }
+    // children of cur in rank order (ties by index)
+    if (threadIdx.x == 0) {
+      int m = 0;
+      for (int i = 0; i < n && m < 64; ++i)
+        if (parents[i] == cur) kids[m++] = i;
+      for (int a = 1; a < m; ++a) {
+        const int x = kids[a];
+        int b = a - 1;
+        while (b >= 0 && ranks[kids[b]] > ranks[x]) {
+          kids[b + 1] = kids[b];
+          --b;
+        }
+        kids[b + 1] = x;
+      }
+      s_nk = m;
+      s_chosen = -1;
+    }
+    __syncthreads();
+    const int nk = s_nk;
+    if (nk > 0) {
+      const int drow = cur < 0 ? 0 : draft_pos[cur] - c0;
+      if (drow < 0 || drow >= draft_rows) {
+        if (threadIdx.x == 0) report_error(status, kErrBadIndex);
+        break;
+      }
+      // q over the full vocabulary (0 outside the draft vocabulary)
+      const float* dr = dlogits + (int64_t)drow * ldd;
+      const WarpParams PD = dparams[drow];
+      if (vocab_ids) {
+        for (int i = threadIdx.x; i < V; i += kSampThreads) q[i] = 0.f;
+        __syncthreads();
+        for (int j = threadIdx.x; j < Vd; j += kSampThreads) {
+          const int64_t v = vocab_ids[j];
+          const float lp = warped_lp(PD, dr[j]);
+          if (v >= 0 && v < V) q[v] = lp == -INFINITY ? 0.f : expf(lp);
+        }
+      } else {
+        for (int i = threadIdx.x; i < V; i += kSampThreads) {
+          const float lp = i < Vd ? warped_lp(PD, dr[i]) : -INFINITY;
+          q[i] = lp == -INFINITY ? 0.f : expf(lp);
+        }
+      }
+      __syncthreads();
+      float zp = 1.f, zq = 1.f;  // p / zp and q / zq are the current distributions
+      for (int ci = 0; ci < nk; ++ci) {
+        const int c = kids[ci];
+        const int x = tokens[c];
+        const bool in = x >= 0 && x < V;
+        const float qx = in ? q[x] / zq : 0.f;
+        if (!(qx > 0.f)) continue;
+        const float px = p[x] / zp;
+        const float u = uniform(sd, rnd, static_cast<uint32_t>(cur + 1), static_cast<uint32_t>(ci), 1u);
+        if (u < fminf(1.f, px / qx)) {
+          if (threadIdx.x == 0) s_chosen = c;
+          break;
+        }
+        // reject: p <- max(p - q, 0) renormalised, only if that has mass
+        float rs = 0.f;
+        for (int i = threadIdx.x; i < V; i += kSampThreads) rs += fmaxf(p[i] / zp - q[i] / zq, 0.f);
+        const float R = block_sum(rs, red);
+        if (R > 0.f) {
+          for (int i = threadIdx.x; i < V; i += kSampThreads) p[i] = fmaxf(p[i] / zp - q[i] / zq, 0.f);
+          zp = R;
+        }
+        // q <- q without x, renormalised; stop when nothing is left
+        __syncthreads();
+        if (threadIdx.x == 0) q[x] = 0.f;
+        __syncthreads();
+        float qs = 0.f;
+        for (int i = threadIdx.x; i < V; i += kSampThreads) qs += q[i];
+        const float Q = block_sum(qs, red);
+        if (!(Q > 0.f)) break;
+        zq = Q;
+      }
+      __syncthreads();
+      if (s_chosen >= 0) {
+        const int c = s_chosen;
+        if (threadIdx.x == 0) {
+          accepted[na] = c;
+          keep_slots[1 + na] = c0 + 1 + c;
+        }
+        ++na;
+        cur = c;
+        __syncthreads();
+        continue;
+      }
+    }
+    __syncthreads();
+    const float u = uniform(sd, rnd, static_cast<uint32_t>(cur + 1), 0u, 2u);
+    const int pick = draw_from(p, V, u, red, scan);
+    if (threadIdx.x == 0) {
+      *bonus = pick;
+      *n_accepted = na;
+      *n_keep = na + 1;
+    }
+    return;
+  }
+  if (threadIdx.x == 0) {
+    *bonus = 0;
+    *n_accepted = na;
+    *n_keep = na + 1;
+  }
+}
+
+}  // namespace ssd
+
+using namespace ssd;
+
+extern "C" {
+
+int ssd_warp_params(const float* logits, int64_t ld, int64_t rows, int64_t V, float temperature, float top_p,
+                    void* params_out, void* stream) {
+  if (rows <= 0 || V <= 0 || !(temperature > 0.f) || !(top_p > 0.f) || top_p > 1.f)
+    return fail(SSD_ERR_INVALID, "ssd_warp_params: need rows, V > 0, temperature > 0, 0 < top_p <= 1");
+  return launch_kernel("warp_params_kernel", warp_params_kernel, dim3((unsigned)rows), dim3(kSampThreads), 0,
+                       static_cast<cudaStream_t>(stream), 1, 1, logits, ld, (int)V, temperature, top_p,
+                       static_cast<WarpParams*>(params_out));
+}
+
+int ssd_warp_probs(const float* logits, int64_t ld, int64_t rows, int64_t V, const void* params, float* out,
+                   int64_t ldo, void* stream) {
+  if (rows <= 0 || V <= 0 || !logits || !params || !out || rows > 65535)
+    return fail(SSD_ERR_INVALID, "ssd_warp_probs: bad arguments");
+  const unsigned bx = (unsigned)((V + 1023) / 1024 < 64 ? (V + 1023) / 1024 : 64);
+  return launch_kernel("warp_probs_kernel", warp_probs_kernel, dim3(bx, (unsigned)rows), dim3(1024), 0,
+                       static_cast<cudaStream_t>(stream), 1, 1, logits, ld, (int)V,
+                       static_cast<const WarpParams*>(params), out, ldo);
+}
+
+int ssd_gumbel_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, const void* params, int64_t k,
+                    const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round, int64_t row_base,
+                    int32_t* out_tok, float* out_logprob, void* stream) {
+  if (k < 1 || k > kMaxK) return fail(SSD_ERR_UNSUPPORTED, "ssd_gumbel_topk: k must be 1..16");
+  if (!seed) return fail(SSD_ERR_INVALID, "ssd_gumbel_topk: seed is NULL");
+  return launch_kernel("gumbel_topk_kernel", gumbel_topk_kernel, dim3((unsigned)rows), dim3(kSampThreads), 0,
+                       static_cast<cudaStream_t>(stream), 1, 1, logits, ld, (int)V,
+                       static_cast<const WarpParams*>(params), (int)k, vocab_ids, seed, round, (int)row_base, out_tok,
+                       out_logprob);
+}
+
+int ssd_sample_token(const float* logits, int64_t V, float temperature, float top_p, const uint64_t* seed,
+                     const int32_t* round, int64_t row_id, int64_t stream_id, float* scratch, int32_t* out,
+                     void* stream) {
+  if (V <= 0 || !(temperature > 0.f) || !(top_p > 0.f) || top_p > 1.f || !seed || !scratch || !out)
+    return fail(SSD_ERR_INVALID, "ssd_sample_token: bad arguments");
+  return launch_kernel("sample_token_kernel", sample_token_kernel, dim3(1), dim3(kSampThreads), 0,
+                       static_cast<cudaStream_t>(stream), 1, 1, logits, (int)V, temperature, top_p, seed, round,
+                       (int)row_id, (int)stream_id, scratch, out);
+}
+
+int ssd_tree_walk_sample(const int32_t* n_nodes, int64_t max_nodes, const int32_t* tokens, const int32_t* parents,
+                         const int32_t* ranks, const int32_t* draft_pos, const int32_t* root_pos,
+                         const float* target_logits, int64_t ldt, const void* target_params, int64_t V,
+                         const float* draft_logits, int64_t ldd, const void* draft_params, int64_t draft_rows,
+                         int64_t Vd, const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round,
+                         float* p_scratch, float* q_scratch, int32_t* accepted, int32_t* n_accepted, int32_t* bonus,
+                         int32_t* keep_slots, int32_t* n_keep, uint32_t* status, void* stream) {
+  if (max_nodes < 0 || max_nodes > 4096 || V <= 0 || Vd <= 0 || draft_rows <= 0 || !seed || !p_scratch ||
+      !q_scratch || !target_params || !draft_params)
+    return fail(SSD_ERR_INVALID, "ssd_tree_walk_sample: bad arguments");
+  if (!vocab_ids && Vd > V) return fail(SSD_ERR_INVALID, "ssd_tree_walk_sample: draft vocabulary exceeds V");
+  return launch_kernel("sample_verify_kernel", sample_verify_kernel, dim3(1), dim3(kSampThreads), 0,
+                       static_cast<cudaStream_t>(stream), 1, 1, n_nodes, (int)max_nodes, tokens, parents, ranks,
+                       draft_pos, root_pos, target_logits, ldt, static_cast<const WarpParams*>(target_params), (int)V,
+                       draft_logits, ldd, static_cast<const WarpParams*>(draft_params), (int)draft_rows, (int)Vd,
+                       vocab_ids, seed, round, p_scratch, q_scratch, accepted, n_accepted, bonus, keep_slots, n_keep,
+                       status);
+}
+
+}  // extern "C"

@@ -1,4 +1,4 @@
-"""Device-resident speculative-decoding round (greedy) and target-only step.
+"""Device-resident speculative-decoding round and target-only step.
 
 The reference drives a round from Python with a host sync per tree level
 (ssd/engine/tree_drafter.py:133,143-144; ssd/engine/verify.py:47). Here the
@@ -10,8 +10,12 @@ quantity (committed length, root token, tree) from device memory:
   forward over root + tree -> argmax -> tree walk -> KV compaction -> commit
 
 so it is captured once in a CUDA graph and replayed; the host reads back the
-committed tokens once per round. With temperature 0 every level has a static
-size (min(parents x branch, width)), which is what makes the shapes static.
+committed tokens once per round. Every level has a static maximum size
+(min(parents x branch, width)); a level with fewer candidates (sampling,
+where a parent's nucleus can hold fewer than `branch` tokens) leaves empty
+slots that the prune kernels skip, so the shapes stay static. The sampling
+round (ssd/engine/sampling.py) overrides the two head hooks, `_propose` and
+`_walk`, of the greedy round defined here.
 """
 
 from __future__ import annotations
@@ -128,7 +132,7 @@ class _Decoder:
         R.run_stack(w, self.target.layer_indices, [None] * len(self.target.layer_indices), None, fwd, P, self.cache,
                     scratch, ws, self.cache.max_length)
         xn = R.final_norm(w, scratch, P - 1, P)
-        ops.head_argmax(xn, w.lm_head, self.argmax[:1], ws, out_max=self.amax[:1], out_gap=self.gap[:1])
+        self._first_token(xn, ws)
         self.state.zero_()
         self.state[SEQ] = P
         self.state[ROOT_TOK:ROOT_TOK + 1].copy_(self.argmax[:1])
@@ -137,6 +141,11 @@ class _Decoder:
         self.round_log.zero_()
         ws.check_status()
         self.cache.seq_len = P
+
+    def _first_token(self, xn: torch.Tensor, ws: ops.Workspace) -> None:
+        """First generated token from the last prompt row into argmax[0]
+        (_first_token, speculative.py:81-84; greedy here)."""
+        ops.head_argmax(xn, self.w.lm_head, self.argmax[:1], ws, out_max=self.amax[:1], out_gap=self.gap[:1])
 
     def _capture(self, fn) -> torch.cuda.CUDAGraph:
         g = torch.cuda.CUDAGraph()
@@ -172,9 +181,13 @@ class TargetStep(_Decoder):
         R.run_stack(w, self.target.layer_indices, [None] * len(self.target.layer_indices), None, self.fwd_root, 1,
                     self.cache, self.scratch, self.ws, self.cache.max_length)
         xn = R.final_norm(w, self.scratch, 0, 1)
-        ops.head_argmax(xn, w.lm_head, self.argmax[:1], self.ws, out_max=self.amax[:1], out_gap=self.gap[:1])
+        self._next_token(xn)
         ops.round_commit(st[ZERO:ZERO + 1], self.argmax, self.out_tokens, self.argmax[:1], st[SEQ:SEQ + 1],
                          st[ROOT_TOK:ROOT_TOK + 1], self.out_tokens, st[N_OUT:N_OUT + 1], None, self.ws.status)
+
+    def _next_token(self, xn: torch.Tensor) -> None:
+        """Next token into argmax[0]: lm_head fused with the argmax."""
+        ops.head_argmax(xn, self.w.lm_head, self.argmax[:1], self.ws, out_max=self.amax[:1], out_gap=self.gap[:1])
 
     def run(self, n_steps: int, use_graph: bool = True) -> None:
         if use_graph:
@@ -234,8 +247,7 @@ class GreedyRound(_Decoder):
         p, st = self.plan, self.state
         ops.causal_prep(st[SEQ:SEQ + 1], 1, st[ROOT_TOK:ROOT_TOK + 1], self.fwd_root)
         xn = self._draft_forward(self.fwd_root, 1)
-        ops.head_topk(xn, self.head_w, p.branch[0], self.topk_tok[0], self.topk_lp[0], self.ws,
-                      vocab_ids=self.vocab_ids)
+        self._propose(xn, 0, 1, p.branch[0], self.topk_tok[0], self.topk_lp[0])
         self.tree.n_nodes.zero_()
         for d in range(p.depth):
             frontier = self.root_frontier if d == 0 else self.level_nodes[d - 1]
@@ -245,9 +257,16 @@ class GreedyRound(_Decoder):
                             self.fwd_level[d], self.ws.status)
             if p.fed[d]:
                 xn = self._draft_forward(self.fwd_level[d], p.level_sizes[d])
-                ops.head_topk(xn, self.head_w, p.branch[d + 1], self.topk_tok[d + 1], self.topk_lp[d + 1],
-                              self.ws, vocab_ids=self.vocab_ids)
+                self._propose(xn, 1 + p.slot_offsets[d], p.level_sizes[d], p.branch[d + 1], self.topk_tok[d + 1],
+                              self.topk_lp[d + 1])
         ops.tree_prune(self.tree, p.cfg.max_nodes)
+
+    def _propose(self, xn: torch.Tensor, row0: int, T: int, k: int, out_tok: torch.Tensor,
+                 out_lp: torch.Tensor) -> None:
+        """k children per draft row (TreeDrafter._propose, tree_drafter.py:124-132
+        for greedy): the draft head fused with a log-softmax top-k. `row0` is
+        the row's index among the round's draft rows (0 = root)."""
+        ops.head_topk(xn, self.head_w, k, out_tok, out_lp, self.ws, vocab_ids=self.vocab_ids)
 
     def verify_phase(self) -> None:
         """verify_inputs + target forward + greedy_verify (verify.py:32-57)."""
@@ -257,6 +276,12 @@ class GreedyRound(_Decoder):
         R.run_stack(w, self.target.layer_indices, [None] * len(self.target.layer_indices), None, self.fwd_verify,
                     p.rows, self.cache, self.scratch, self.ws, self.cache.max_length)
         xn = R.final_norm(w, self.scratch, 0, p.rows)
+        self._walk(xn)
+
+    def _walk(self, xn: torch.Tensor) -> None:
+        """Target head over root + tree rows, then the acceptance walk
+        (greedy_verify, verify.py:45-57): lm_head fused with the argmax."""
+        p, st, w = self.plan, self.state, self.w
         ops.head_argmax(xn, w.lm_head, self.argmax[: p.rows], self.ws, out_max=self.amax[: p.rows],
                         out_gap=self.gap[: p.rows])
         ops.tree_walk_greedy(self.tree, self.argmax, st[SEQ:SEQ + 1], self.accepted, st[N_ACC:N_ACC + 1],

@@ -7,8 +7,9 @@ the target's KV for every layer of all committed tokens except the last one
 root + tree with the target in one forward, keeps the root and the accepted
 path in the cache and commits accepted + bonus tokens.
 
-Greedy rounds run as one CUDA graph over device-resident state
-(ssd/engine/round.py); the host reads the committed tokens once per round.
+Rounds run as CUDA graphs over device-resident state (ssd/engine/round.py,
+greedy; ssd/engine/sampling.py, temperature > 0); the host reads the
+committed tokens once per round.
 The target-only baseline runs the same layer kernels one token per step.
 """
 
@@ -62,11 +63,6 @@ def _sync(dev) -> None:
     torch.cuda.synchronize(dev)
 
 
-def _check_greedy(temperature: float) -> None:
-    if temperature != 0:
-        raise NotImplementedError("sampling (temperature > 0) uses the device sampling path (ssd.engine.sampling)")
-
-
 @torch.no_grad()
 def autoregressive_generate(target: TargetRunner, input_ids: torch.Tensor, max_new_tokens: int, eos_ids: set[int],
                             temperature: float = 0.0, top_p: float = 1.0, seed: Optional[int] = None,
@@ -76,7 +72,8 @@ def autoregressive_generate(target: TargetRunner, input_ids: torch.Tensor, max_n
     if temperature != 0:
         from ssd.engine.sampling import sampled_autoregressive
 
-        return sampled_autoregressive(target, input_ids, max_new_tokens, eos_ids, temperature, top_p, seed)
+        return sampled_autoregressive(target, input_ids, max_new_tokens, eos_ids, temperature, top_p, seed,
+                                      use_graph=use_graph, steps_per_sync=steps_per_sync, max_cache=max_cache)
     dev = target.weights.device
     n_prompt = int(input_ids.shape[-1])
     cap = max_cache or cache_capacity(n_prompt, max_new_tokens)
@@ -123,7 +120,7 @@ class SpeculativeGenerator:
         self.target = target or TargetRunner(base)
         self.draft = draft
         self.cfg = cfg
-        self.plan = TreePlan(cfg) if cfg.temperature == 0 else None
+        self.plan = TreePlan(cfg)
 
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int, eos_ids: set[int], seed: Optional[int] = None,
@@ -133,7 +130,8 @@ class SpeculativeGenerator:
         if cfg.temperature != 0:
             from ssd.engine.sampling import sampled_speculative
 
-            return sampled_speculative(self, input_ids, max_new_tokens, eos_ids, seed)
+            return sampled_speculative(self, input_ids, max_new_tokens, eos_ids, seed, use_graph=use_graph,
+                                       max_cache=max_cache)
         dev = self.target.weights.device
         n_prompt = int(input_ids.shape[-1])
         cap = max_cache or cache_capacity(n_prompt, max_new_tokens, self.plan)

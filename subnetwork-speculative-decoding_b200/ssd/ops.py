@@ -176,3 +176,55 @@ def round_commit(n_accepted, accepted, tokens, bonus, seq_len, root_token, out_t
 def causal_prep(base, T: int, src_ids, fwd) -> None:
     L.call("ssd_causal_prep", _p(base), T, _p(src_ids), _p(fwd.ids), _p(fwd.positions), _p(fwd.slots),
            _p(fwd.prefix_len), _stream())
+
+
+# ------------------------------------------------------------------ sampling
+def warp_params_buffer(rows: int, device) -> torch.Tensor:
+    """Storage for `rows` warp-parameter records {max, 1/T, lambda, log Z}."""
+    return torch.zeros(max(1, rows), 4, dtype=torch.float32, device=device)
+
+
+def warp_params(logits: torch.Tensor, temperature: float, top_p: float, out: torch.Tensor,
+                rows: Optional[int] = None, V: Optional[int] = None) -> None:
+    """Warp parameters of fp32 logit rows [rows, V] (warp_probs, tree_drafter.py:34-45)."""
+    rows = logits.shape[0] if rows is None else rows
+    V = logits.shape[1] if V is None else V
+    if logits.dtype != torch.float32 or out.shape[0] < rows:
+        raise ValueError("warp_params: fp32 logits and a params buffer of >= rows records")
+    L.call("ssd_warp_params", _p(logits), logits.stride(0), rows, V, float(temperature), float(top_p), _p(out),
+           _stream())
+
+
+def warp_probs(logits: torch.Tensor, params: torch.Tensor, out: torch.Tensor, rows: Optional[int] = None) -> None:
+    """Warped probabilities (warp_probs, tree_drafter.py:34-45) from warp parameters."""
+    rows = logits.shape[0] if rows is None else rows
+    L.call("ssd_warp_probs", _p(logits), logits.stride(0), rows, logits.shape[1], _p(params), _p(out), out.stride(0),
+           _stream())
+
+
+def gumbel_topk(logits: torch.Tensor, params: torch.Tensor, k: int, seed: torch.Tensor, round_: Optional[torch.Tensor],
+                row_base: int, out_tok: torch.Tensor, out_lp: torch.Tensor, vocab_ids=None,
+                rows: Optional[int] = None) -> None:
+    """k draws without replacement per row, in draw order (tree_drafter.py:134-145)."""
+    rows = logits.shape[0] if rows is None else rows
+    L.call("ssd_gumbel_topk", _p(logits), logits.stride(0), rows, logits.shape[1], _p(params), k, _p(vocab_ids),
+           _p(seed), _p(round_), row_base, _p(out_tok), _p(out_lp), _stream())
+
+
+def sample_token(logits: torch.Tensor, temperature: float, top_p: float, seed: torch.Tensor,
+                 round_: Optional[torch.Tensor], row_id: int, stream_id: int, scratch: torch.Tensor,
+                 out: torch.Tensor) -> None:
+    """out[0] ~ warp(logits) (_first_token, speculative.py:81-84)."""
+    L.call("ssd_sample_token", _p(logits), logits.shape[-1], float(temperature), float(top_p), _p(seed), _p(round_),
+           row_id, stream_id, _p(scratch), _p(out), _stream())
+
+
+def tree_walk_sample(tree, tlogits, tparams, dlogits, dparams, draft_rows: int, seed, round_, p_scratch, q_scratch,
+                     root_pos, accepted, n_accepted, bonus, keep_slots, n_keep, max_nodes: int, status,
+                     vocab_ids=None) -> None:
+    """sample_verify (verify.py:60-95) over the device tree."""
+    L.call("ssd_tree_walk_sample", _p(tree.n_nodes), max_nodes, _p(tree.tokens), _p(tree.parents), _p(tree.ranks),
+           _p(tree.draft_pos), _p(root_pos), _p(tlogits), tlogits.stride(0), _p(tparams), tlogits.shape[1],
+           _p(dlogits), dlogits.stride(0), _p(dparams), draft_rows, dlogits.shape[1], _p(vocab_ids), _p(seed),
+           _p(round_), _p(p_scratch), _p(q_scratch), _p(accepted), _p(n_accepted), _p(bonus), _p(keep_slots),
+           _p(n_keep), _p(status), _stream())

@@ -1,0 +1,376 @@
+"""Sampling path (temperature > 0) on the device, against the oracle.
+
+Random draws cannot match the reference's torch.Generator streams, so the
+checks are: warped probabilities equal the oracle's warp_probs
+(tree_drafter.py:34-45) to fp32 rounding, with the same nucleus; every
+sampler's draws pass a chi-square test (p > 0.01) against the exact
+distribution; and the speculative output of an unpruned tree is distributed
+exactly as target sampling (verify.py:10-18), checked on the joint of the
+first generated tokens against the oracle target's warped conditionals.
+All seeds are fixed, so every test is deterministic.
+"""
+
+import itertools
+
+import numpy as np
+import pytest
+import torch
+from scipy import stats
+
+import oracle as O
+from oracle.model import weights_from_hf
+from oracle.tree import warp_probs as oracle_warp
+from ssd import ops
+from ssd import synthetic as S
+from ssd.config import BridgeConfig, DraftingConfig
+from ssd.engine import sampling as SP
+from ssd.engine.speculative import SpeculativeGenerator, TargetRunner, autoregressive_generate
+from ssd.engine.tree_drafter import DraftTree, TreeDrafter
+from ssd.models import SubnetworkDraftModel
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+P_MIN = 0.01
+
+
+def chi2_pvalue(counts: np.ndarray, probs: np.ndarray, min_expected: float = 5.0) -> float:
+    """Pearson chi-square p-value; cells with expected count < min_expected
+    are pooled. A draw in a cell of probability 0 fails outright."""
+    counts = np.asarray(counts, dtype=np.float64).reshape(-1)
+    probs = np.asarray(probs, dtype=np.float64).reshape(-1)
+    assert counts[probs <= 0].sum() == 0, "a draw landed on a zero-probability outcome"
+    n = counts.sum()
+    exp = probs * n
+    big = exp >= min_expected
+    obs_l, exp_l = list(counts[big]), list(exp[big])
+    rest = (~big) & (probs > 0)
+    if rest.any():
+        obs_l.append(counts[rest].sum())
+        exp_l.append(exp[rest].sum())
+    if len(obs_l) < 2:
+        return 1.0
+    exp_a = np.array(exp_l)
+    exp_a *= np.sum(obs_l) / exp_a.sum()
+    return float(stats.chisquare(obs_l, exp_a).pvalue)
+
+
+def _logit_rows(rows, V, scale, seed):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(rows, V, generator=g) * scale).to(DEV)
+
+
+# ---------------------------------------------------------------- warp
+@pytest.mark.parametrize("V", [8, 1000, 128256])
+@pytest.mark.parametrize("temperature,top_p", [(1.0, 1.0), (0.7, 0.9), (1.3, 0.5), (0.5, 0.95)])
+def test_warp_probs_match_oracle(V, temperature, top_p):
+    logits = _logit_rows(6, V, 3.0, V + int(100 * top_p))
+    ours = SP.warp_probs_device(logits, temperature, top_p).cpu().double().numpy()
+    ref = oracle_warp(logits.cpu().double().numpy(), temperature, top_p)
+    for r in range(logits.shape[0]):
+        p = np.exp(logits[r].cpu().double().numpy() / temperature - logits[r].max().item() / temperature)
+        p /= p.sum()
+        sp = np.sort(p)[::-1]
+        before = np.cumsum(sp) - sp
+        near = top_p < 1 and np.abs(before - top_p).min() < 1e-5  # fp32 mass vs fp64 at the boundary
+        if not near:
+            assert np.array_equal(ours[r] > 0, ref[r] > 0), f"nucleus differs in row {r}"
+            np.testing.assert_allclose(ours[r], ref[r], rtol=2e-4, atol=1e-7)
+        np.testing.assert_allclose(ours[r].sum(), 1.0, rtol=1e-4)
+
+
+def test_warp_params_all_ties_and_peaked_rows():
+    V = 4096
+    rows = torch.zeros(3, V, device=DEV)
+    rows[1, 17] = 50.0  # one token holds essentially all mass
+    rows[2, :5] = 12.0  # five tied tokens hold almost all mass
+    for top_p in (1.0, 0.3):
+        probs = SP.warp_probs_device(rows, 1.0, top_p).cpu().numpy()
+        np.testing.assert_allclose(probs[0], np.full(V, 1.0 / V), rtol=1e-4)
+        assert probs[1, 17] > 0.999
+        # ties at the nucleus boundary are kept together
+        if top_p < 1:
+            np.testing.assert_allclose(probs[2, :5], 0.2, rtol=1e-4)
+            assert probs[2, 5:].sum() == 0
+
+
+# ------------------------------------------------------------ samplers
+def _params(logits, temperature, top_p):
+    prm = ops.warp_params_buffer(logits.shape[0], DEV)
+    ops.warp_params(logits, temperature, top_p, prm)
+    return prm
+
+
+@pytest.mark.parametrize("top_p", [1.0, 0.7])
+def test_gumbel_topk_draws_without_replacement(top_p):
+    V, rows, k = 8, 40000, 3
+    base = torch.tensor([1.0, 0.5, 0.2, -0.3, 0.8, -1.0, 0.0, 0.3], device=DEV)
+    logits = base.repeat(rows, 1).contiguous()
+    T = 0.8
+    prm = _params(logits, T, top_p)
+    seed = torch.tensor([1234], dtype=torch.int64, device=DEV)
+    tok = torch.empty(rows, k, dtype=torch.int32, device=DEV)
+    lp = torch.empty(rows, k, dtype=torch.float32, device=DEV)
+    ops.gumbel_topk(logits, prm, k, seed, None, 0, tok, lp)
+    tok, lp = tok.cpu().numpy(), lp.cpu().numpy()
+    p = oracle_warp(base.cpu().double().numpy(), T, top_p)
+    support = int((p > 0).sum())
+    valid = tok >= 0
+    assert (valid.sum(1) == min(k, support)).all()
+    assert np.isneginf(lp[~valid]).all()
+    for r in range(0, rows, 997):  # distinct tokens per row, log-probs of the warp
+        t = tok[r][valid[r]]
+        assert len(set(t.tolist())) == len(t)
+        np.testing.assert_allclose(lp[r][valid[r]], np.log(p[t]), rtol=1e-4, atol=1e-5)
+    first = np.bincount(tok[:, 0], minlength=V)
+    assert chi2_pvalue(first, p) > P_MIN
+    # joint of the first two draws: p(a) p(b) / (1 - p(a))
+    joint = np.zeros((V, V))
+    for a, b in zip(tok[:, 0], tok[:, 1]):
+        if b >= 0:
+            joint[a, b] += 1
+    exact = np.zeros((V, V))
+    for a, b in itertools.permutations(range(V), 2):
+        if p[a] < 1:
+            exact[a, b] = p[a] * p[b] / (1 - p[a])
+    assert chi2_pvalue(joint, exact) > P_MIN
+
+
+def test_gumbel_topk_vocab_ids_and_row_ids():
+    Vd, rows, k = 6, 4, 4
+    logits = _logit_rows(rows, Vd, 1.0, 5)
+    prm = _params(logits, 1.0, 1.0)
+    ids = torch.tensor([3, 9, 11, 20, 21, 40], dtype=torch.int64, device=DEV)
+    seed = torch.tensor([7], dtype=torch.int64, device=DEV)
+    tok = torch.empty(rows, k, dtype=torch.int32, device=DEV)
+    lp = torch.empty(rows, k, dtype=torch.float32, device=DEV)
+    ops.gumbel_topk(logits, prm, k, seed, None, 0, tok, lp, vocab_ids=ids)
+    assert set(tok.cpu().numpy().reshape(-1).tolist()) <= set(ids.tolist())
+    # the same row with another row id draws independently; the same id repeats
+    tok2 = torch.empty_like(tok)
+    ops.gumbel_topk(logits, prm, k, seed, None, 0, tok2, lp, vocab_ids=ids)
+    assert torch.equal(tok, tok2)
+    ops.gumbel_topk(logits, prm, k, seed, None, 100, tok2, lp, vocab_ids=ids)
+    assert not torch.equal(tok, tok2)
+
+
+@pytest.mark.parametrize("top_p", [1.0, 0.6])
+def test_sample_token_distribution(top_p):
+    V, n = 8, 3000
+    logits = torch.tensor([0.2, 1.1, -0.4, 0.9, 0.0, -2.0, 0.7, 0.3], device=DEV)
+    seed = torch.tensor([99], dtype=torch.int64, device=DEV)
+    scratch = torch.empty(V, dtype=torch.float32, device=DEV)
+    out = torch.empty(n, dtype=torch.int32, device=DEV)
+    for i in range(n):
+        ops.sample_token(logits, 0.9, top_p, seed, None, i, 3, scratch, out[i:i + 1])
+    counts = np.bincount(out.cpu().numpy(), minlength=V)
+    assert chi2_pvalue(counts, oracle_warp(logits.cpu().double().numpy(), 0.9, top_p)) > P_MIN
+
+
+def test_sample_token_large_vocab_support():
+    V = 128256
+    logits = _logit_rows(1, V, 2.0, 11)[0]
+    seed = torch.tensor([5], dtype=torch.int64, device=DEV)
+    scratch = torch.empty(V, dtype=torch.float32, device=DEV)
+    out = torch.empty(200, dtype=torch.int32, device=DEV)
+    for i in range(200):
+        ops.sample_token(logits, 1.0, 0.5, seed, None, i, 3, scratch, out[i:i + 1])
+    p = oracle_warp(logits.cpu().double().numpy(), 1.0, 0.5)
+    assert (p[out.cpu().numpy()] > 0).all()
+
+
+# ------------------------------------------------------------- tree walk
+def _rand_tree_from_q(q_root, q_child, branch, rng):
+    """A depth-2 tree whose children are drawn from q without replacement."""
+    tree = DraftTree()
+    V = len(q_root)
+
+    def draw(q, k):
+        keys = np.log(np.maximum(q, 1e-300)) + rng.gumbel(size=V)
+        keys[q <= 0] = -np.inf
+        order = np.argsort(-keys)[: min(k, int((q > 0).sum()))]
+        return order.tolist()
+
+    tree.child_q[-1] = torch.tensor(q_root, dtype=torch.float32)
+    for r, t in enumerate(draw(q_root, branch[0])):
+        tree.tokens.append(t), tree.parents.append(-1), tree.depths.append(1), tree.ranks.append(r)
+        tree.scores.append(0.0), tree.draft_pos.append(-1)
+    for par in range(len(tree.tokens)):
+        qc = q_child[tree.tokens[par]]
+        tree.child_q[par] = torch.tensor(qc, dtype=torch.float32)
+        for r, t in enumerate(draw(qc, branch[1])):
+            tree.tokens.append(t), tree.parents.append(par), tree.depths.append(2), tree.ranks.append(r)
+            tree.scores.append(0.0), tree.draft_pos.append(-1)
+    return tree
+
+
+def test_tree_walk_sample_first_token_is_target_distributed():
+    """Unpruned tree drawn from q: the first committed token (accepted root
+    child or bonus) ~ p_root, and the second given the first ~ p_child."""
+    V = 6
+    rng = np.random.default_rng(0)
+    tl = rng.normal(size=(V + 1, V)) * 1.2  # target rows: root, then one per first token
+    dl = rng.normal(size=(V + 1, V)) * 1.2  # draft rows
+    T, top_p = 0.9, 1.0
+    p_root = oracle_warp(tl[0], T, top_p)
+    q_root = oracle_warp(dl[0], T, top_p)
+    q_child = [oracle_warp(dl[1 + t], T, top_p) for t in range(V)]
+    gen = torch.Generator().manual_seed(0)
+    n = 2500
+    firsts = np.zeros(V)
+    pairs = np.zeros((V, V))
+    for _ in range(n):
+        tree = _rand_tree_from_q(q_root, q_child, [3, 2], rng)
+        rows = [tl[0]] + [tl[1 + tree.tokens[i]] if tree.depths[i] == 1 else tl[0] for i in range(len(tree))]
+        logits = torch.tensor(np.stack(rows), dtype=torch.float32)
+        acc, bonus = SP.sample_verify_device(tree, logits, T, top_p, gen)
+        toks = [tree.tokens[i] for i in acc] + [bonus]
+        firsts[toks[0]] += 1
+        if len(toks) > 1 and tree.depths[acc[0]] == 1:
+            pairs[toks[0], toks[1]] += 1
+    assert chi2_pvalue(firsts, p_root) > P_MIN
+    exact = np.array([p_root[a] * oracle_warp(tl[1 + a], T, top_p) for a in range(V)])
+    exact *= pairs.sum(1, keepdims=True) / np.maximum(exact.sum(1, keepdims=True), 1e-300)
+    assert chi2_pvalue(pairs, exact / pairs.sum()) > P_MIN
+
+
+def test_tree_walk_sample_deterministic_cases():
+    V = 5
+    rng = np.random.default_rng(1)
+    logits = torch.tensor(rng.normal(size=(1, V)), dtype=torch.float32)
+    q = oracle_warp(logits[0].double().numpy(), 1.0, 1.0)
+    # p == q: the first child is always accepted
+    tree = DraftTree(tokens=[2, 4], parents=[-1, -1], depths=[1, 1], ranks=[0, 1], scores=[0, 0], draft_pos=[-1, -1])
+    tree.child_q[-1] = torch.tensor(q, dtype=torch.float32)
+    rows = logits.repeat(3, 1)
+    for s in range(20):
+        acc, bonus = SP.sample_verify_device(tree, rows, 1.0, 1.0, torch.Generator().manual_seed(s))
+        assert acc == [0]
+    # a child outside the target's nucleus is never accepted
+    t2 = torch.tensor([[8.0, 0.0, -9.0, 0.0, 0.0]] * 3)
+    tree.child_q[-1] = torch.tensor([0.0, 0.0, 0.5, 0.0, 0.5])
+    for s in range(20):
+        acc, bonus = SP.sample_verify_device(tree, t2, 1.0, 0.5, torch.Generator().manual_seed(s))
+        assert acc == [] and bonus == 0
+    # empty tree: the bonus ~ p
+    empty = DraftTree()
+    acc, bonus = SP.sample_verify_device(empty, t2[:1], 1.0, 0.5, torch.Generator().manual_seed(0))
+    assert acc == [] and bonus == 0
+
+
+# ------------------------------------------------------------- engines
+@pytest.fixture(scope="module")
+def v8():
+    base = S.build_base_model("tiny_v8", 0, torch.float32, "cpu").to(DEV)
+    w, conf = weights_from_hf(base)
+    return base, O.OracleModel(w, conf, list(range(conf["layers"])))
+
+
+def _exact_joint(oracle_target, prompt, T, top_p, n_tok):
+    """Exact joint of the first n_tok generated tokens under warped target sampling."""
+    V = oracle_target.conf["vocab"]
+    out = np.zeros((V,) * n_tok)
+    for seq in itertools.product(range(V), repeat=n_tok - 1):
+        logits = oracle_target.forward(list(prompt) + list(seq))
+        pr = 1.0
+        for j in range(n_tok - 1):
+            pr *= oracle_warp(logits[len(prompt) - 1 + j], T, top_p)[seq[j]]
+        out[seq] = pr * oracle_warp(logits[-1], T, top_p)
+    return out
+
+
+def _joint_counts(gen_fn, n, V, n_tok):
+    counts = np.zeros((V,) * n_tok)
+    for s in range(n):
+        toks = gen_fn(s)
+        counts[tuple(toks[:n_tok])] += 1
+    return counts
+
+
+DRAFTS = {
+    "unpruned": dict(depth=2, branch=[3, 2]),
+    "chain": dict(depth=3, branch=1),
+}
+
+
+@pytest.mark.parametrize("tree_name", list(DRAFTS))
+@pytest.mark.parametrize("temperature,top_p", [(0.6, 1.0), (1.0, 0.8)])
+def test_sampled_speculative_matches_target_distribution(v8, tree_name, temperature, top_p):
+    base, oracle_target = v8
+    draft = SubnetworkDraftModel(base, [0, 3, 5], BridgeConfig(init_std=0.02))
+    S.init_bridges_(draft.bridges, 0, in_std=0.125, out_std=0.02)
+    draft.bridges.to(DEV)
+    target = TargetRunner(base)
+    cfg = DraftingConfig(temperature=temperature, top_p=top_p, **DRAFTS[tree_name])
+    gen = SpeculativeGenerator(base, draft, cfg, target)
+    prompt = [1, 5, 2, 7]
+    n_tok, n = 3, 4000
+    counts = _joint_counts(lambda s: gen.generate(torch.tensor([prompt]), n_tok, {-1}, seed=s).tokens, n, 8, n_tok)
+    exact = _exact_joint(oracle_target, prompt, temperature, top_p, n_tok)
+    assert chi2_pvalue(counts, exact) > P_MIN
+    assert chi2_pvalue(counts.sum(2), exact.sum(2)) > P_MIN
+
+
+def test_sampled_speculative_vocab_subset(v8):
+    base, oracle_target = v8
+    draft = SubnetworkDraftModel(base, list(range(6)))
+    draft.set_vocab_subset(torch.tensor([0, 2, 3, 6, 7]))
+    cfg = DraftingConfig(depth=2, branch=[2, 2], temperature=0.7)
+    gen = SpeculativeGenerator(base, draft, cfg, TargetRunner(base))
+    prompt = [4, 4, 1]
+    counts = _joint_counts(lambda s: gen.generate(torch.tensor([prompt]), 2, {-1}, seed=s).tokens, 4000, 8, 2)
+    assert chi2_pvalue(counts, _exact_joint(oracle_target, prompt, 0.7, 1.0, 2)) > P_MIN
+
+
+def test_sampled_autoregressive_matches_target_distribution(v8):
+    base, oracle_target = v8
+    target = TargetRunner(base)
+    prompt = [3, 0, 6]
+    fn = lambda s: autoregressive_generate(target, torch.tensor([prompt]), 2, {-1}, temperature=0.8, top_p=0.9,
+                                           seed=s).tokens
+    counts = _joint_counts(fn, 3000, 8, 2)
+    assert chi2_pvalue(counts, _exact_joint(oracle_target, prompt, 0.8, 0.9, 2)) > P_MIN
+
+
+def test_sampled_generation_is_seeded_and_eos_stops(v8):
+    base, _ = v8
+    draft = SubnetworkDraftModel(base, [0, 2, 5])
+    S.init_bridges_(draft.bridges, 1, in_std=0.125, out_std=0.02)
+    draft.bridges.to(DEV)
+    gen = SpeculativeGenerator(base, draft, DraftingConfig(depth=3, branch=[2, 2, 1], temperature=1.0),
+                               TargetRunner(base))
+    a = gen.generate(torch.tensor([[1, 2, 3]]), 30, {-1}, seed=11).tokens
+    b = gen.generate(torch.tensor([[1, 2, 3]]), 30, {-1}, seed=11).tokens
+    c = gen.generate(torch.tensor([[1, 2, 3]]), 30, {-1}, seed=12).tokens
+    assert a == b and a != c and len(a) == 30
+    r = gen.generate(torch.tensor([[1, 2, 3]]), 30, {a[5]}, seed=11)
+    assert r.tokens == a[: a.index(a[5]) + 1]
+    assert sum(r.accepted_per_round) >= len(r.tokens) - 1
+
+
+def test_sampled_tree_build_api(v8):
+    base, _ = v8
+    draft = SubnetworkDraftModel(base, [0, 3, 5])
+    S.init_bridges_(draft.bridges, 0, in_std=0.125, out_std=0.02)
+    draft.bridges.to(DEV)
+    cfg = DraftingConfig(depth=3, branch=[3, 2, 2], width=[3, 4, 4], temperature=0.8, top_p=0.9)
+    target = TargetRunner(base)
+    cache = target.new_cache(64)
+    prompt = torch.tensor([[1, 5, 2, 7]], device=DEV)
+    target(prompt, past_key_values=cache, logits_to_keep=1)
+    root = 3
+    ref_cache = target.new_cache(64)
+    target(prompt, past_key_values=ref_cache, logits_to_keep=1)
+    root_logits = draft(torch.tensor([[root]], device=DEV), past_key_values=ref_cache).logits[0, -1].cpu()
+    tree = TreeDrafter(draft, cfg).build(cache, torch.tensor([[root]]), 4, torch.Generator().manual_seed(0))
+    q0 = oracle_warp(root_logits.double().numpy(), 0.8, 0.9)
+    np.testing.assert_allclose(tree.child_q[-1].numpy(), q0, rtol=1e-4, atol=1e-6)
+    kids = tree.children()
+    for par, ks in kids.items():
+        toks = [tree.tokens[k] for k in ks]
+        assert len(set(toks)) == len(toks)
+        assert all(tree.child_q[par][t] > 0 for t in toks)
+        for k in ks:
+            base_s = 0.0 if par == -1 else tree.scores[par]
+            np.testing.assert_allclose(tree.scores[k] - base_s, np.log(float(tree.child_q[par][tree.tokens[k]])),
+                                       rtol=1e-4, atol=1e-4)
+    assert len(tree) <= sum(TreeDrafter(draft, cfg).max_nodes_per_level())
