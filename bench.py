@@ -57,7 +57,7 @@ def parse():
     ap.add_argument("--prompt-len", type=int, default=None, help="override the prompt length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ar", action="store_true", help="skip the target-only baseline")
-    ap.add_argument("--ncu-case", choices=["gemm", "attention"], default=None,
+    ap.add_argument("--ncu-case", choices=["gemm", "gemm_mix", "attention"], default=None,
                     help="run one small launch set of a kernel for an ncu capture, then exit")
     return ap.parse_args()
 
@@ -183,6 +183,23 @@ def barrier(world: int) -> None:
 
 
 # ------------------------------------------------------------ kernel roofline
+# DRAM bytes (read + write) of one launch of each verify-forward GEMM of the 8B
+# target at 33 rows, from `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum`
+# (cold L2) of `python bench.py --ncu-case gemm_mix` on a B200; the summary and
+# command are in profiles/tc_gemm_verify_mix_8b.md.
+NCU_DRAM_BYTES_8B_33 = {"qkv": 50707200 + 35584, "o_proj": 34445312 + 7680, "gate_up": 235248640 + 2761216,
+                        "down": 119024128 + 2936832, "lm_head_argmax": 1051216896 + 12325376}
+
+
+def gemm_traffic_per_launch(w, rows: int):
+    """Measured DRAM bytes per average launch of the verify GEMM mix (4 per
+    layer + lm_head), for the 8B shape at 33 rows only (else None)."""
+    if (w.d, w.F, w.V, w.L, rows) != (4096, 14336, 128256, 32, 33):
+        return None
+    t = NCU_DRAM_BYTES_8B_33
+    return (sum(t[k] for k in ("qkv", "o_proj", "gate_up", "down")) * w.L + t["lm_head_argmax"]) / (4 * w.L + 1)
+
+
 def gemm_roofline(w, rows: int, dev) -> dict:
     """Average duration of the tcgen05 GEMM launches of one verify forward
     (rows = root + tree): each GEMM type is captured once per layer (32
@@ -307,33 +324,30 @@ def gemm_roofline(w, rows: int, dev) -> dict:
 
 
 # ------------------------------------------------------------- CPU baseline
-def build_oracle(spec):
+def build_oracle(spec, base=None, draft=None):
     """The oracle (numpy restatement of the reference path) in fp32 on the
-    host, with the workload's weights, bridges and draft vocabulary."""
+    host with the GPU arm's exact weights: the workload's bf16 weights are
+    drawn by the same seeded recipe (on the GPU, where drawing 8e9 normals
+    takes seconds instead of the better part of an hour on one host thread),
+    then copied to host memory and widened to fp32. Bridges and the draft
+    vocabulary likewise. Nothing of this package runs on the measured path."""
     import numpy as np
     import torch
 
     import oracle as O
     from oracle.model import bridges_from_module, weights_from_hf
-    from ssd import synthetic as S
-    from ssd.config import BridgeConfig
-    from ssd.models.bridges import TransitionBridge
-    from ssd.models.subnetwork_draft import plan_bridges
 
     torch.set_num_threads(os.cpu_count() or 1)
-    base = S.build_base_model(spec.model, spec.seed, torch.float32, "cpu", plant_layers=spec.draft_layers,
-                              plant_scale=spec.plant_scale)
+    if base is None:
+        dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+        base, _, draft, _ = build(spec, dev)
     w, conf = weights_from_hf(base, np.float32)
-    bcfg = BridgeConfig(hidden_dim=spec.bridge_hidden)
-    mods = torch.nn.ModuleDict({s.name: TransitionBridge.from_config(conf["hidden"], bcfg)
-                                for s in plan_bridges(spec.draft_layers, conf["layers"])})
-    S.init_bridges_(mods, spec.seed, spec.bridge_in_std, spec.bridge_out_std)
-    br = bridges_from_module(mods, vars(bcfg), np.float32)
+    br = bridges_from_module(draft.bridges, vars(draft.bridge_config), np.float32)
     target = O.OracleModel(w, conf, list(range(conf["layers"])), dtype=np.float32)
-    draft = O.OracleModel(w, conf, spec.draft_layers, br, dtype=np.float32)
-    if spec.draft_vocab:
-        draft.set_vocab_subset(O.top_vocab(S.zipf_counts(conf["vocab"], spec.seed).numpy(), spec.draft_vocab))
-    return base, target, draft
+    odraft = O.OracleModel(w, conf, spec.draft_layers, br, dtype=np.float32)
+    if draft.vocab_ids is not None:
+        odraft.set_vocab_subset(draft.vocab_ids.cpu().numpy())
+    return base, target, odraft
 
 
 CPU_SAMPLE = dict(prompt_len=64, n_tokens=6)
@@ -341,33 +355,44 @@ CPU_SAMPLE = dict(prompt_len=64, n_tokens=6)
 
 def oracle_step(spec, target, draft, seq: int) -> tuple[int, float, list]:
     """One bounded sample: speculative decode of CPU_SAMPLE tokens after a
-    short prompt of sequence `seq`, prefill included."""
+    short prompt of sequence `seq`. Returns (decoded tokens, decode seconds,
+    committed per round); the prefill is excluded like the GPU arm's."""
     import oracle as O
     from ssd import synthetic as S
 
     ids = S.make_prompt(spec.seed + seq, CPU_SAMPLE["prompt_len"], target.conf["vocab"])[0].tolist()
-    t0 = time.time()
     res = O.speculative_generate(target, draft, dict(spec.drafting), ids, CPU_SAMPLE["n_tokens"], set())
-    return len(res["tokens"]), time.time() - t0, res["accepted_per_round"]
+    return len(res["tokens"]) - 1, res["decode_s"], res["accepted_per_round"]
 
 
 def cpu_sample_text(spec, steps: int) -> str:
-    return (f"oracle (numpy fp32 port of the reference path) speculative decode of {CPU_SAMPLE['n_tokens']} tokens "
-            f"after a {CPU_SAMPLE['prompt_len']}-token prompt (prefill included), {steps} sequence(s), same "
-            f"{spec.model} weights/tree as the GPU arm")
+    return (f"oracle (numpy fp32 port of the reference path, the GPU arm's weights widened to fp32) speculative "
+            f"decode of {CPU_SAMPLE['n_tokens']} tokens after a {CPU_SAMPLE['prompt_len']}-token prompt, prefill "
+            f"excluded, {steps} sequence(s), same {spec.model} tree")
 
 
-def cpu_baseline(spec, steps: int = 1) -> dict:
+def cpu_baseline(spec, steps: int = 1, base=None, draft=None) -> dict:
     t0 = time.time()
-    _, target, draft = build_oracle(spec)
+    _, target, odraft = build_oracle(spec, base, draft)
     build_s = time.time() - t0
     n, t, acc = 0, 0.0, []
     for s in range(steps):
-        dn, dt, da = oracle_step(spec, target, draft, s)
+        dn, dt, da = oracle_step(spec, target, odraft, s)
         n, t, acc = n + dn, t + dt, acc + da
     return {"value": n / t, "unit": "tok/s", "cores": os.cpu_count() or 1, "kind": "port",
-            "sample": cpu_sample_text(spec, steps) + f"; build {build_s:.0f}s",
+            "sample": cpu_sample_text(spec, steps) + f"; setup {build_s:.0f}s",
             "mean_accepted": sum(acc) / max(1, len(acc))}
+
+
+def workload_config(args, spec, world: int) -> dict:
+    """The `config` object of both arms' JSON lines."""
+    P = args.prompt_len or spec.prompt_len
+    max_new = args.max_new or spec.max_new_tokens
+    planted = f" planted x{spec.plant_scale}" if spec.plant_scale else ""
+    return {"workload": f"{args.workload}: {spec.model}{planted}, draft {spec.draft_layers}, tree {spec.drafting}, "
+                        f"prompt {P}, {max_new} new tokens, {args.sequences} sequences split over ranks",
+            "global_batch": 1, "seq_len": P + max_new, "parallelism": f"dp{world} (independent sequences)",
+            "l2": "weights exceed L2 between rounds (no flush needed)"}
 
 
 def reference_arm(args) -> None:
@@ -393,10 +418,10 @@ def reference_arm(args) -> None:
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "model": spec.model, "tree": spec.drafting},
+        "config": workload_config(args, spec, args.gpus),
         "mean_accepted": sum(acc) / max(1, len(acc)),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
-                         "sample": cpu_sample_text(spec, args.steps) + f"; build {build_s:.0f}s"},
+                         "sample": cpu_sample_text(spec, args.steps) + f"; setup {build_s:.0f}s"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -411,7 +436,31 @@ def ncu_case(args, dev) -> None:
     from ssd import ops
 
     torch.manual_seed(0)
-    if args.ncu_case == "gemm":
+    if args.ncu_case == "gemm_mix":
+        # one launch of each verify-forward GEMM of the 8B target at 33 rows, in layer order:
+        # qkv(+RoPE+KV write), o_proj(+residual), gate/up(+SwiGLU), down(+residual), lm_head(+argmax)
+        d, H, Hkv, hd, F, V, T = 4096, 32, 8, 128, 14336, 128256, 33
+        ws = ops.Workspace(dev, 64, V, 64)
+        mk = lambda n, k: (torch.randn(n, k, device=dev) * 0.02).bfloat16()
+        wq, wk, wv, wo = mk(H * hd, d), mk(Hkv * hd, d), mk(Hkv * hd, d), mk(d, H * hd)
+        wg, wu, wd, lm = mk(F, d), mk(F, d), mk(d, F), mk(V, d)
+        x = (torch.randn(T, d, device=dev) * 0.5).bfloat16()
+        pos = torch.arange(2048, 2048 + T, dtype=torch.int32, device=dev)
+        inv = 1.0 / (500000.0 ** (torch.arange(0, hd, 2, device=dev).float() / hd))
+        f = torch.arange(4096, device=dev).float()[:, None] * inv[None, :]
+        cos, sin = f.cos().contiguous(), f.sin().contiguous()
+        kc = torch.zeros(Hkv, 4096, hd, device=dev).bfloat16()
+        vc = torch.zeros_like(kc)
+        q = torch.empty(T, H * hd, device=dev).bfloat16()
+        resid = torch.zeros(T, d, device=dev)
+        hid = torch.empty(T, F, device=dev).bfloat16()
+        idx = torch.empty(T, dtype=torch.int32, device=dev)
+        ops.qkv_rope(x, wq, wk, wv, H, Hkv, hd, cos, sin, pos, pos, kc, vc, q, ws)
+        ops.linear(q, [wo], ws, epilogue=L.EPI_RESIDUAL, resid=resid)
+        ops.linear(x, [wg, wu], ws, epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid)
+        ops.linear(hid, [wd], ws, epilogue=L.EPI_RESIDUAL, resid=resid)
+        ops.head_argmax(x, lm, idx, ws)
+    elif args.ncu_case == "gemm":
         # the 8B down_proj shape at verify size: K=14336 -> 4096, 33 rows
         K, N, T = 14336, 4096, 33
         ws = ops.Workspace(dev, 64, 1, 1)
@@ -482,6 +531,8 @@ def main() -> None:
         eng.prefill(ids.to(dev))
         torch.cuda.synchronize(dev)
         barrier(world)
+        if phase_acc is not None:  # timed: the launch-list capture (ncu --profile-from-start off) sees decode only
+            torch.cuda.profiler.start()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         evs = []
         e0.record()
@@ -495,6 +546,7 @@ def main() -> None:
         e1.record()
         torch.cuda.synchronize(dev)
         if phase_acc is not None:
+            torch.cuda.profiler.stop()
             for ev in evs:
                 for i, name in enumerate(eng.PHASES):
                     phase_acc[name] = phase_acc.get(name, 0.0) + ev[i].elapsed_time(ev[i + 1]) / 1e3
@@ -579,7 +631,7 @@ def main() -> None:
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cb = cpu_baseline(spec)
+            cb = cpu_baseline(spec, base=base, draft=draft)
         except MemoryError as exc:
             cb = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
                   "sample": f"not run: {exc}"}
@@ -599,11 +651,7 @@ def main() -> None:
             "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16" if spec.dtype == torch.bfloat16 else "f32",
             "data": "synthetic (seeded random weights and prompts)",
-            "config": {"workload": f"{args.workload}: {spec.model} planted x{spec.plant_scale}, draft "
-                                   f"{spec.draft_layers}, tree {spec.drafting}, prompt {P}, {max_new} new tokens, "
-                                   f"{args.sequences} sequences split over ranks",
-                       "global_batch": 1, "seq_len": P + max_new, "parallelism": f"dp{world} (independent sequences)",
-                       "l2": "weights (>15 GB) exceed L2 between rounds"},
+            "config": workload_config(args, spec, world),
             "mean_accepted": mean_acc,
             "ar_value": ar_value,
             "speedup_vs_ar": (value / ar_value) if ar_value else None,
@@ -620,7 +668,9 @@ def main() -> None:
             "gpu_launches": gpu_launches,
             "roofline": {"kernel": "tc_gemm_kernel (verify-forward GEMM mix + lm_head argmax)", "bound": "hbm",
                          "achieved": roof["gbs"] if roof else None, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": (roof["gbs"] / peaks["hbm_gbs"]) if roof else None, "traffic": None,
+                         "frac": (roof["gbs"] / peaks["hbm_gbs"]) if roof else None,
+                         "traffic": gemm_traffic_per_launch(w, plan_rows),
+                         "algorithmic_bytes_per_launch": (roof["bytes"] / roof["launches"]) if roof else None,
                          "peak_source": peaks["source"],
                          "per_type": roof["per_type"] if roof else None},
             "cpu_baseline": cb,

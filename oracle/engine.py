@@ -53,8 +53,11 @@ def speculative_generate(target, draft, drafting: dict, ids, max_new_tokens: int
     """SpeculativeGenerator.generate (speculative.py:132-174).
 
     drafting: dict with depth, branch, width, max_nodes, temperature, top_p.
-    Returns tokens, accepted_per_round, tree_sizes (and trees if keep_trees).
+    Returns tokens, accepted_per_round, tree_sizes (and trees if keep_trees),
+    and wall-clock seconds of the prefill and of the decode loop.
     """
+    import time
+
     gen = _gen(seed)
     T = float(drafting.get("temperature", 0.0))
     P = float(drafting.get("top_p", 1.0))
@@ -64,9 +67,11 @@ def speculative_generate(target, draft, drafting: dict, ids, max_new_tokens: int
     n_prompt = len(ids)
     extra = max(drafter.max_verify_nodes(), drafter.max_tree_cache()) + 1
     cache = target.new_cache(n_prompt + max_new_tokens + drafting["depth"] + extra + 1)
+    t0 = time.perf_counter()
     logits = target.forward(ids, None, cache, logits_to_keep=1)[-1]
     out = [first_token(logits, T, P, gen)]
-    res = {"tokens": [], "accepted_per_round": [], "tree_sizes": [], "trees": []}
+    t1 = time.perf_counter()
+    res = {"tokens": [], "accepted_per_round": [], "tree_sizes": [], "trees": [], "prefill_s": t1 - t0}
     while not finish(out, eos_ids, max_new_tokens)[1]:
         committed = cache.get_seq_length()
         tree = drafter.build(cache, [out[-1]], committed, gen)
@@ -87,4 +92,5 @@ def speculative_generate(target, draft, drafting: dict, ids, max_new_tokens: int
                                      ranks=list(tree.ranks), scores=list(tree.scores), accepted=list(accepted),
                                      bonus=bonus))
     res["tokens"] = finish(out, eos_ids, max_new_tokens)[0]
+    res["decode_s"] = time.perf_counter() - t1
     return res
