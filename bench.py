@@ -154,32 +154,21 @@ def build(spec, dev):
 
 
 def sync_max(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
+    from ssd.engine import dp
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return dp.all_max(x, world)
 
 
 def sync_sum(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
+    from ssd.engine import dp
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    return dp.all_sum(x, world)
 
 
 def barrier(world: int) -> None:
-    if world > 1:
-        import torch.distributed as dist
+    from ssd.engine import dp
 
-        dist.barrier()
+    dp.barrier(world)
 
 
 # ------------------------------------------------------------ kernel roofline
@@ -521,7 +510,9 @@ def main() -> None:
     base, target, draft, cfg = build(spec, dev)
     w = target.weights
     seqs = [S.make_prompt(spec.seed + i, P, w.V) for i in range(args.sequences)]
-    mine = seqs[rank::world]
+    from ssd.engine import dp
+
+    mine = dp.shard(seqs, rank, world)
     cap = cache_capacity(P, max_new, TreePlan(cfg))
     eng = GreedyRound(target, draft, cfg, target.new_cache(cap), max_new)
     plan_rows = eng.plan.rows
