@@ -36,6 +36,7 @@ struct AttnArgs {
   int mask_words;
   int kv_bound, split_len, n_splits, rows_per_tile, row_tiles;
   int groups, rows_per_group;  // tensor-core kernel: query rows (token x GQA head) per CTA
+  int rt, kw;                  // tensor-core kernel: 16-row tiles and key lanes per CTA
   int cluster_merge;           // key slices of a row group form a cluster and merge through DSMEM
   void* out;
   int64_t ldo;
@@ -239,27 +240,36 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const AttnArgs a) {
 }
 
 // ------------------------------------------------------ tensor-core kernel
-// bf16, head_dim 64 or 128. A CTA = one KV head x one group of up to 128
-// query rows (row q = token * G + GQA head, 16 rows per warp) x one key
-// slice. K/V blocks of 64 keys are staged by cp.async (double buffered, 16-B
-// chunks XOR-swizzled by row so ldmatrix is conflict-free); S = Q K^T and
-// O += P V run on mma.sync m16n8k16 with fp32 accumulators; the online
-// softmax runs on the accumulator registers in the log2 domain.
-constexpr int kMmaWarps = 8;
-constexpr int kMmaMaxRows = kMmaWarps * 16;
+// bf16, head_dim 64 or 128, warp-specialised. A CTA = one KV head x one group
+// of query rows (row q = token * G + GQA head) x one key slice. The last warp
+// produces: it streams the slice's 64-key K/V blocks into a kWsStages-deep
+// shared-memory ring with cp.async (16-byte chunks XOR-swizzled by key so
+// ldmatrix is conflict-free), completing each stage on an mbarrier. Consumer
+// warp (ri, kw) owns 16 query rows (row tile ri, Q fragments kept in
+// registers) and takes blocks kw, kw + KW, ... of the slice: S = Q K^T and
+// O += P V on mma.sync m16n8k16 with fp32 accumulators, online softmax in
+// base 2 on the accumulator registers, and releases the stage on its own, so
+// no CTA-wide barrier sits in the key loop. With few query rows (decode,
+// small tree levels) KW > 1 key lanes split the slice inside the CTA. The
+// (slice, key lane) partials of a row merge in a fixed order: inside one
+// cluster through DSMEM, or through a global workspace for long contexts.
+constexpr int kWsMaxConsumers = 8;                   // consumer warps per CTA
+constexpr int kWsStages = 4;                         // K/V blocks in flight per CTA
+constexpr int kMmaMaxRows = kWsMaxConsumers * 16;    // query rows per CTA
 constexpr int kMmaMaxTok = kMmaMaxRows + 1;
 constexpr int kMmaMaxSplits = 32;
 constexpr int kMaxAttnClusterSplits = 8;
+constexpr int kMaxPartials = 32;                     // key slices x key lanes merged per row
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   const int sz = valid ? 16 : 0;
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(sz) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+// Arrive on an mbarrier once this thread's earlier cp.async copies have landed.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -282,33 +292,33 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Partial record of one query row of one key slice: {m, l, pad, pad, o[hd]}.
+// Partial record of one query row of one (key slice, key lane): {m, l, pad, pad, o[hd]}.
 __host__ __device__ constexpr int mma_rec(int hd) { return hd + 4; }
-// Shared memory before the per-token metadata: the double-buffered K/V
-// stages, reused after the key loop for the partial rows (cluster merge).
-constexpr int kStages = 4;  // K/V blocks in flight per CTA (memory-level parallelism)
-__host__ __device__ constexpr int mma_region(int hd) {
-  return (kStages * 2 * 64 * hd * 2) > (kMmaMaxRows * mma_rec(hd) * 4) ? (kStages * 2 * 64 * hd * 2)
-                                                                        : (kMmaMaxRows * mma_rec(hd) * 4);
+__host__ __device__ constexpr int ws_ring_bytes(int hd) { return kWsStages * 2 * 64 * hd * 2; }
+// The ring is reused for the partial records [kw][rows][rec] after the key loop.
+__host__ __device__ inline int ws_region_bytes(int hd, int kw, int rows) {
+  const int part = kw * rows * mma_rec(hd) * 4;
+  return ws_ring_bytes(hd) > part ? ws_ring_bytes(hd) : part;
 }
-// Q rows of the group, bf16, 16-byte chunks XOR-swizzled by row.
-__host__ __device__ constexpr int mma_qbytes(int hd) { return kMmaMaxRows * hd * 2; }
-constexpr int kMmaMeta = (kMmaMaxTok + 1) * 4 + kMmaMaxTok * 4 * 8 + 16;
+constexpr int kWsMeta = (kMmaMaxTok + 1) * 4 + kMmaMaxTok * 4 * 8 + 16 + 2 * kWsStages * 8 + 16;
 
 template <int HD>
-__global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(const AttnArgs a) {
   constexpr int CH = HD / 8;   // 16-byte chunks per K/V row
   constexpr int KS = HD / 16;  // k-steps over head_dim (QK^T)
   constexpr int NTD = HD / 8;  // n-tiles over head_dim (PV)
   constexpr int KB = 64;       // keys per block
-  extern __shared__ __align__(128) uint8_t attn_smem[];
-  uint8_t* kv = attn_smem;  // [kStages][K|V][64][HD] bf16, swizzled
-  uint8_t* qs = attn_smem + mma_region(HD);  // [kMmaMaxRows][HD] bf16, swizzled
-  int* s_plen = reinterpret_cast<int*>(qs + mma_qbytes(HD));
-  uint64_t* s_mask = reinterpret_cast<uint64_t*>(s_plen + kMmaMaxTok + 1);  // [tok][mask_words]
-  int* s_misc = reinterpret_cast<int*>(s_mask + kMmaMaxTok * 4);           // need_end, min_plen, last
+  extern __shared__ __align__(1024) uint8_t attn_smem[];
+  const int region = ws_region_bytes(HD, a.kw, a.rows_per_group);
+  int* s_plen = reinterpret_cast<int*>(attn_smem + region);
+  uint64_t* s_mask = reinterpret_cast<uint64_t*>(s_plen + kMmaMaxTok + 1);  // [tok][4]
+  int* s_misc = reinterpret_cast<int*>(s_mask + kMmaMaxTok * 4);           // need_end, min_plen, last, pad
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_misc + 4);
+  uint64_t* empty = full + kWsStages;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwc = a.rt * a.kw;  // consumer warps; warp nwc produces
+  const int nwarps = nwc + 1;
   const int blk = blockIdx.x;
   const int h = blk / a.groups, gr = blk % a.groups;
   const int split = blockIdx.y;
@@ -317,6 +327,7 @@ __global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
   const int Mg = min(a.rows_per_group, M - q0);
   const int t_first = q0 / a.G;
   const int ntok = (q0 + Mg - 1) / a.G - t_first + 1;
+  const int P = a.n_splits * a.kw;  // partials per row
   pdl_wait();
   pdl_trigger();
   const int sb = a.spec_base ? a.spec_base[0] : 0;
@@ -325,6 +336,11 @@ __global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
   if (threadIdx.x == 0) {
     s_misc[0] = 0;
     s_misc[1] = INT32_MAX;
+    for (int st = 0; st < kWsStages; ++st) {
+      mbar_init(&full[st], 32);      // one cp.async arrival per producer lane
+      mbar_init(&empty[st], a.rt);   // one arrival per consumer warp of the block's key lane
+    }
+    fence_mbar_init();
   }
   __syncthreads();
   for (int i = threadIdx.x; i < ntok; i += blockDim.x) {
@@ -346,48 +362,34 @@ __global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
   const int k_lo = split * a.split_len;
   const int k_hi = min(k_lo + a.split_len, need_end);
   const int nblocks = k_hi > k_lo ? (k_hi - k_lo + KB - 1) / KB : 0;
+  const uint32_t ring_s = smem_u32(attn_smem);
+  auto stage_k = [&](int st) { return ring_s + st * 2 * KB * HD * 2; };
+  auto stage_v = [&](int st) { return ring_s + st * 2 * KB * HD * 2 + KB * HD * 2; };
 
-  // Q fragments of this warp's 16 rows (A operand, row-major 16 x 16 per k-step).
-  const bool active = warp * 16 < Mg;
   const int g = lane >> 2, tq = lane & 3;
-  const int rl0 = warp * 16 + g, rl1 = rl0 + 8;  // rows within the group
-  const bool ok0 = rl0 < Mg, ok1 = rl1 < Mg;
+  const int ri = warp % a.rt, kw = warp / a.rt;
+  const int rl0 = ri * 16 + g, rl1 = rl0 + 8;  // rows within the group
+  const bool ok0 = warp < nwc && rl0 < Mg, ok1 = warp < nwc && rl1 < Mg;
   const int qr0 = q0 + rl0, qr1 = q0 + rl1;
-  const int tok0 = ok0 ? qr0 / a.G - t_first : 0, tok1 = ok1 ? qr1 / a.G - t_first : 0;
-  // Stage the group's Q rows (A operand) in shared memory; rows past Mg are 0.
-  const bf16* qb = static_cast<const bf16*>(a.q);
-  for (int idx = threadIdx.x; idx < a.rows_per_group * CH; idx += blockDim.x) {
-    const int r = idx / CH, c = idx % CH;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (r < Mg) {
-      const int qr = q0 + r;
-      v = *reinterpret_cast<const uint4*>(qb + (int64_t)(qr / a.G) * a.ldq + (int64_t)(h * a.G + qr % a.G) * HD +
-                                          c * 8);
-    }
-    *reinterpret_cast<uint4*>(qs + r * HD * 2 + ((c ^ (r & 7)) << 4)) = v;
-  }
-  const uint32_t qs_s = smem_u32(qs);
-  const int pl0 = ok0 ? s_plen[tok0] : 0, pl1 = ok1 ? s_plen[tok1] : 0;
-
   float o[NTD][4];
 #pragma unroll
   for (int i = 0; i < NTD; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  const float sc = a.scale * 1.4426950408889634f;  // softmax in base 2
+  bool failed = false;
 
-  const bf16* kbase = static_cast<const bf16*>(a.kc) + (int64_t)h * a.head_stride;
-  const bf16* vbase = static_cast<const bf16*>(a.vc) + (int64_t)h * a.head_stride;
-  const uint32_t kv_s = smem_u32(kv);
-  auto stage_k = [&](int st) { return kv_s + st * 2 * KB * HD * 2; };
-  auto stage_v = [&](int st) { return kv_s + st * 2 * KB * HD * 2 + KB * HD * 2; };
-  // kStages-deep ring: every iteration commits exactly one (possibly empty)
-  // cp.async group, so waiting for all but the newest kStages-1 groups means
-  // block b has landed.
-  auto load_block = [&](int b) {
-    if (b < nblocks) {
-      const int st = b % kStages;
+  if (warp == nwc) {
+    // ---- producer: block b -> stage b % kWsStages, in block order
+    const bf16* kbase = static_cast<const bf16*>(a.kc) + (int64_t)h * a.head_stride;
+    const bf16* vbase = static_cast<const bf16*>(a.vc) + (int64_t)h * a.head_stride;
+    for (int b = 0; b < nblocks; ++b) {
+      const int st = b % kWsStages;
+      if (b >= kWsStages && !mbar_wait(&empty[st], ((b / kWsStages) - 1) & 1)) {
+        if (lane == 0) report_error(a.status, kErrWaitTimeout);
+        failed = true;
+        break;
+      }
       const int kb = k_lo + b * KB;
-      for (int idx = threadIdx.x; idx < KB * CH; idx += blockDim.x) {
+      for (int idx = lane; idx < KB * CH; idx += 32) {
         const int key = idx / CH, c = idx % CH;
         const int slot = kb + key;
         const bool valid = slot < k_hi;
@@ -396,49 +398,59 @@ __global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
         cp_async16(stage_k(st) + dst, kbase + off, valid);
         cp_async16(stage_v(st) + dst, vbase + off, valid);
       }
+      cp_async_mbar_arrive(&full[st]);
     }
-    cp_async_commit();
-  };
-
+    cp_async_wait_all();  // no copy may land after the ring is reused or the CTA exits
+  } else if (warp < nwc) {
+    // ---- consumer (ri, kw)
+    // Q fragments (A operand, rows g / g + 8 of the tile) straight from global.
+    const bf16* qb = static_cast<const bf16*>(a.q);
+    const bf16* qrow0 = qb + (int64_t)(qr0 / a.G) * a.ldq + (int64_t)(h * a.G + qr0 % a.G) * HD;
+    const bf16* qrow1 = qb + (int64_t)(qr1 / a.G) * a.ldq + (int64_t)(h * a.G + qr1 % a.G) * HD;
+    uint32_t qf[KS][4];
 #pragma unroll
-  for (int b = 0; b < kStages - 1; ++b) load_block(b);
-  for (int b = 0; b < nblocks; ++b) {
-    load_block(b + kStages - 1);
-    cp_async_wait<kStages - 1>();
-    __syncthreads();
-    if (active) {
-      const int st = b % kStages;
+    for (int ks = 0; ks < KS; ++ks) {
+      const int c0 = ks * 16 + 2 * tq;
+      qf[ks][0] = ok0 ? *reinterpret_cast<const uint32_t*>(qrow0 + c0) : 0u;
+      qf[ks][1] = ok1 ? *reinterpret_cast<const uint32_t*>(qrow1 + c0) : 0u;
+      qf[ks][2] = ok0 ? *reinterpret_cast<const uint32_t*>(qrow0 + c0 + 8) : 0u;
+      qf[ks][3] = ok1 ? *reinterpret_cast<const uint32_t*>(qrow1 + c0 + 8) : 0u;
+    }
+    const int tok0 = ok0 ? qr0 / a.G - t_first : 0, tok1 = ok1 ? qr1 / a.G - t_first : 0;
+    const int pl0 = ok0 ? s_plen[tok0] : 0, pl1 = ok1 ? s_plen[tok1] : 0;
+    const float sc = a.scale * 1.4426950408889634f;  // softmax in base 2
+    const int mi = lane >> 3, rj = lane & 7;
+    for (int b = kw; b < nblocks; b += a.kw) {
+      const int st = b % kWsStages;
+      if (!mbar_wait(&full[st], (b / kWsStages) & 1)) {
+        if (lane == 0) report_error(a.status, kErrWaitTimeout);
+        failed = true;
+        break;
+      }
       const int kb = k_lo + b * KB;
-      float s[8][4];
+      float sacc[8][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-      const int mi = lane >> 3, ri = lane & 7;
+      for (int i = 0; i < 8; ++i) sacc[i][0] = sacc[i][1] = sacc[i][2] = sacc[i][3] = 0.f;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
-        uint32_t qf[4];  // A fragment: rows warp*16 + (lane & 15), k-chunk 2*ks + (lane >> 4)
-        {
-          const int qrow = warp * 16 + (lane & 15);
-          const int qc = 2 * ks + (lane >> 4);
-          ldsm_x4(qs_s + qrow * HD * 2 + ((qc ^ (qrow & 7)) << 4), qf[0], qf[1], qf[2], qf[3]);
-        }
 #pragma unroll
         for (int ntp = 0; ntp < 4; ++ntp) {
-          const int key = (2 * ntp + (mi >> 1)) * 8 + ri;
+          const int key = (2 * ntp + (mi >> 1)) * 8 + rj;
           const int c = 2 * ks + (mi & 1);
           uint32_t b0, b1, b2, b3;
           ldsm_x4(stage_k(st) + key * HD * 2 + ((c ^ (key & 7)) << 4), b0, b1, b2, b3);
-          mma_16816(s[2 * ntp], qf, b0, b1);
-          mma_16816(s[2 * ntp + 1], qf, b2, b3);
+          mma_16816(sacc[2 * ntp], qf[ks], b0, b1);
+          mma_16816(sacc[2 * ntp + 1], qf[ks], b2, b3);
         }
       }
-      // scale + mask: rows rl0 (s[.][0..1]) and rl1 (s[.][2..3])
-      const bool full = (kb + KB <= min_plen) && (kb + KB <= k_hi);
+      // scale + mask: rows rl0 (sacc[.][0..1]) and rl1 (sacc[.][2..3])
+      const bool all_in = (kb + KB <= min_plen) && (kb + KB <= k_hi);
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float v = s[nt][e] * sc;
-          if (!full) {
+          float v = sacc[nt][e] * sc;
+          if (!all_in) {
             const int slot = kb + nt * 8 + 2 * tq + (e & 1);
             const bool r1 = e >= 2;
             bool ok = slot < k_hi && (r1 ? ok1 : ok0);
@@ -453,15 +465,15 @@ __global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
             }
             if (!ok) v = -INFINITY;
           }
-          s[nt][e] = v;
+          sacc[nt][e] = v;
         }
       }
       // online softmax (each row is shared by the 4 lanes of a quad)
       float bm0 = -INFINITY, bm1 = -INFINITY;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
-        bm0 = fmaxf(bm0, fmaxf(s[nt][0], s[nt][1]));
-        bm1 = fmaxf(bm1, fmaxf(s[nt][2], s[nt][3]));
+        bm0 = fmaxf(bm0, fmaxf(sacc[nt][0], sacc[nt][1]));
+        bm1 = fmaxf(bm1, fmaxf(sacc[nt][2], sacc[nt][3]));
       }
 #pragma unroll
       for (int off = 1; off <= 2; off <<= 1) {
@@ -474,12 +486,12 @@ __global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
       float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
-        s[nt][0] = (s[nt][0] == -INFINITY) ? 0.f : exp2f(s[nt][0] - mn0);
-        s[nt][1] = (s[nt][1] == -INFINITY) ? 0.f : exp2f(s[nt][1] - mn0);
-        s[nt][2] = (s[nt][2] == -INFINITY) ? 0.f : exp2f(s[nt][2] - mn1);
-        s[nt][3] = (s[nt][3] == -INFINITY) ? 0.f : exp2f(s[nt][3] - mn1);
-        ps0 += s[nt][0] + s[nt][1];
-        ps1 += s[nt][2] + s[nt][3];
+        sacc[nt][0] = (sacc[nt][0] == -INFINITY) ? 0.f : exp2f(sacc[nt][0] - mn0);
+        sacc[nt][1] = (sacc[nt][1] == -INFINITY) ? 0.f : exp2f(sacc[nt][1] - mn0);
+        sacc[nt][2] = (sacc[nt][2] == -INFINITY) ? 0.f : exp2f(sacc[nt][2] - mn1);
+        sacc[nt][3] = (sacc[nt][3] == -INFINITY) ? 0.f : exp2f(sacc[nt][3] - mn1);
+        ps0 += sacc[nt][0] + sacc[nt][1];
+        ps1 += sacc[nt][2] + sacc[nt][3];
       }
       l0 = l0 * al0 + ps0;
       l1 = l1 * al1 + ps1;
@@ -496,13 +508,13 @@ __global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         uint32_t pf[4];
-        pf[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-        pf[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-        pf[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-        pf[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+        pf[0] = pack_bf16(sacc[2 * kk][0], sacc[2 * kk][1]);
+        pf[1] = pack_bf16(sacc[2 * kk][2], sacc[2 * kk][3]);
+        pf[2] = pack_bf16(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
+        pf[3] = pack_bf16(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
 #pragma unroll
         for (int dtp = 0; dtp < NTD / 2; ++dtp) {
-          const int key = 16 * kk + (mi & 1) * 8 + ri;
+          const int key = 16 * kk + (mi & 1) * 8 + rj;
           const int c = 2 * dtp + (mi >> 1);
           uint32_t b0, b1, b2, b3;
           ldsm_x4_t(stage_v(st) + key * HD * 2 + ((c ^ (key & 7)) << 4), b0, b1, b2, b3);
@@ -510,20 +522,23 @@ __global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
           mma_16816(o[2 * dtp + 1], pf, b2, b3);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
     }
-    __syncthreads();  // stage b % kStages is refilled by the next iteration
-  }
-  cp_async_wait<0>();  // (only empty groups remain) the stages may now be reused
-
-  // row sums across the quad
+    // row sums across the quad
 #pragma unroll
-  for (int off = 1; off <= 2; off <<= 1) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    for (int off = 1; off <= 2; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
   }
+  // Every consumer is done with the ring (and the producer's copies have
+  // landed): the ring becomes the partial records. A CTA that hit a wait
+  // limit still takes part in the barriers below, so its cluster peers finish.
+  __syncthreads();
   bf16* outp = static_cast<bf16*>(a.out);
-  if (a.n_splits == 1) {
-    if (active) {
+  if (P == 1) {
+    if (warp < nwc) {
       const float i0 = l0 > 0.f ? 1.f / l0 : 0.f, i1 = l1 > 0.f ? 1.f / l1 : 0.f;
       bf16* o0 = outp + (int64_t)(qr0 / a.G) * a.ldo + (int64_t)(h * a.G + qr0 % a.G) * HD;
       bf16* o1 = outp + (int64_t)(qr1 / a.G) * a.ldo + (int64_t)(h * a.G + qr1 % a.G) * HD;
@@ -537,76 +552,14 @@ __global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
     return;
   }
   const int rec = mma_rec(HD);
-  if (a.cluster_merge) {
-    // The key slices of this (head, row group) form one cluster: each keeps
-    // its partial rows in its own shared memory (the K/V stages are idle),
-    // then CTA `split` merges rows split, split + n_splits, ... from every
-    // peer in slice order and writes them out.
-    float* sp = reinterpret_cast<float*>(attn_smem);
-    if (active) {
-      if (tq == 0) {
-        if (ok0) {
-          sp[rl0 * rec] = m0;
-          sp[rl0 * rec + 1] = l0;
-        }
-        if (ok1) {
-          sp[rl1 * rec] = m1;
-          sp[rl1 * rec + 1] = l1;
-        }
-      }
-#pragma unroll
-      for (int dt = 0; dt < NTD; ++dt) {
-        const int d = 4 + dt * 8 + 2 * tq;
-        if (ok0) *reinterpret_cast<float2*>(sp + rl0 * rec + d) = make_float2(o[dt][0], o[dt][1]);
-        if (ok1) *reinterpret_cast<float2*>(sp + rl1 * rec + d) = make_float2(o[dt][2], o[dt][3]);
-      }
-    }
-    cluster_sync_all();
-    constexpr int DPL = HD / 32;
-    const uint32_t mine = smem_u32(sp);
-    const uint32_t peer = lane < a.n_splits ? dsmem_map(mine, static_cast<uint32_t>(lane)) : 0u;
-    for (int r = split + warp * a.n_splits; r < Mg; r += kMmaWarps * a.n_splits) {
-      const int qr = q0 + r;
-      float ms = -INFINITY, ls = 0.f;
-      if (lane < a.n_splits) {
-        ms = dsmem_ld(peer + (uint32_t)(r * rec) * 4);
-        ls = dsmem_ld(peer + (uint32_t)(r * rec + 1) * 4);
-      }
-      const float M = warp_max(ms);
-      const float wgt = (ms == -INFINITY || M == -INFINITY) ? 0.f : exp2f(ms - M);
-      const float L = warp_sum(ls * wgt);
-      float acc[DPL];
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-      // all peer loads in flight first, then accumulate in slice order
-      float v[kMaxAttnClusterSplits][DPL];
-#pragma unroll
-      for (int s = 0; s < kMaxAttnClusterSplits; ++s) {
-        const uint32_t ps = __shfl_sync(0xffffffffu, peer, s < a.n_splits ? s : 0);
-#pragma unroll
-        for (int i = 0; i < DPL; ++i)
-          v[s][i] = s < a.n_splits ? dsmem_ld(ps + (uint32_t)(r * rec + 4 + lane * DPL + i) * 4) : 0.f;
-      }
-#pragma unroll
-      for (int s = 0; s < kMaxAttnClusterSplits; ++s) {
-        const float ws = __shfl_sync(0xffffffffu, wgt, s < a.n_splits ? s : 0);
-        if (s < a.n_splits) {
-#pragma unroll
-          for (int i = 0; i < DPL; ++i) acc[i] = fmaf(ws, v[s][i], acc[i]);
-        }
-      }
-      const float inv = L > 0.f ? 1.f / L : 0.f;
-      bf16* op = outp + (int64_t)(qr / a.G) * a.ldo + (int64_t)(h * a.G + qr % a.G) * HD + lane * DPL;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) op[i] = f2bf(acc[i] * inv);
-    }
-    cluster_sync_all();
-    return;
-  }
-  float* part = a.part + ((int64_t)blk * a.n_splits + split) * a.rows_per_group * rec;
-  if (active) {
-    float* p0 = part + (int64_t)rl0 * rec;
-    float* p1 = part + (int64_t)rl1 * rec;
+  // This CTA's records: [kw][row][rec], in shared memory (cluster merge) or
+  // in the global workspace slot of (row group, slice).
+  const bool in_smem = a.cluster_merge || a.n_splits == 1;
+  float* recs = in_smem ? reinterpret_cast<float*>(attn_smem)
+                        : a.part + ((int64_t)blk * a.n_splits + split) * a.kw * a.rows_per_group * rec;
+  if (warp < nwc) {
+    float* p0 = recs + ((int64_t)kw * a.rows_per_group + rl0) * rec;
+    float* p1 = recs + ((int64_t)kw * a.rows_per_group + rl1) * rec;
     if (tq == 0) {
       if (ok0) {
         p0[0] = m0;
@@ -624,6 +577,68 @@ __global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
       if (ok1) *reinterpret_cast<float2*>(p1 + d) = make_float2(o[dt][2], o[dt][3]);
     }
   }
+  constexpr int DPL = HD / 32;  // dims per lane (2 or 4)
+  // Merge one row over its P partials (p = slice * kw + lane of the key
+  // split), weights from the (m, l) pairs, accumulation in p order.
+  auto merge_row = [&](int r, auto&& rec_at) {
+    const int qr = q0 + r;
+    float ms = -INFINITY, ls = 0.f;
+    if (lane < P) {
+      ms = rec_at(lane, 0);
+      ls = rec_at(lane, 1);
+    }
+    const float Mx = warp_max(ms);
+    const float wgt = (ms == -INFINITY || Mx == -INFINITY) ? 0.f : exp2f(ms - Mx);
+    const float L = warp_sum(ls * wgt);
+    float acc[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+    for (int p0 = 0; p0 < P; p0 += 8) {
+      float v[8][DPL];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) v[u][i] = (p0 + u < P) ? rec_at(p0 + u, 4 + lane * DPL + i) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float ws = __shfl_sync(0xffffffffu, wgt, (p0 + u) & 31);
+        if (p0 + u < P) {
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc[i] = fmaf(ws, v[u][i], acc[i]);
+        }
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    bf16* op = outp + (int64_t)(qr / a.G) * a.ldo + (int64_t)(h * a.G + qr % a.G) * HD + lane * DPL;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) op[i] = f2bf(acc[i] * inv);
+  };
+  if (a.cluster_merge) {
+    // The key slices of this (head, row group) form one cluster: CTA `split`
+    // merges rows split, split + n_splits, ... from every peer's records.
+    cluster_sync_all();
+    const uint32_t mine = smem_u32(attn_smem);
+    for (int r = split + warp * a.n_splits; r < Mg; r += nwarps * a.n_splits) {
+      auto at = [&](int p, int f) {
+        const int sl = p / a.kw, kl = p % a.kw;
+        const uint32_t base = dsmem_map(mine, static_cast<uint32_t>(sl));
+        return dsmem_ld(base + (uint32_t)((kl * a.rows_per_group + r) * rec + f) * 4);
+      };
+      merge_row(r, at);
+    }
+    cluster_sync_all();
+    return;
+  }
+  if (a.n_splits == 1) {
+    // one slice, several key lanes: merge inside the CTA
+    __syncthreads();
+    const float* sp = recs;
+    for (int r = warp; r < Mg; r += nwarps) {
+      auto at = [&](int p, int f) { return sp[((int64_t)p * a.rows_per_group + r) * rec + f]; };
+      merge_row(r, at);
+    }
+    return;
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -633,47 +648,22 @@ __global__ void __launch_bounds__(256, 1) attn_mma_kernel(const AttnArgs a) {
   __syncthreads();
   if (!s_misc[2]) return;
   __threadfence();
-  // Merge the slices in order: one warp per row, lanes over head_dim.
-  constexpr int DPL = HD / 32;  // dims per lane (2 or 4)
-  const float* base = a.part + (int64_t)blk * a.n_splits * a.rows_per_group * rec;
-  for (int r = warp; r < Mg; r += kMmaWarps) {
-    const int qr = q0 + r;
-    float ms = -INFINITY, ls = 0.f;
-    if (lane < a.n_splits) {
-      const float* p = base + ((int64_t)lane * a.rows_per_group + r) * rec;
-      ms = __ldcg(p);
-      ls = __ldcg(p + 1);
-    }
-    const float M = warp_max(ms);
-    const float wgt = (ms == -INFINITY || M == -INFINITY) ? 0.f : exp2f(ms - M);
-    const float L = warp_sum(ls * wgt);
-    float acc[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-    for (int s = 0; s < a.n_splits; ++s) {
-      const float ws = __shfl_sync(0xffffffffu, wgt, s);
-      const float* p = base + ((int64_t)s * a.rows_per_group + r) * rec + 4 + lane * DPL;
-      if (ws != 0.f) {
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[i] = fmaf(ws, __ldcg(p + i), acc[i]);
-      }
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    bf16* op = outp + (int64_t)(qr / a.G) * a.ldo + (int64_t)(h * a.G + qr % a.G) * HD + lane * DPL;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) op[i] = f2bf(acc[i] * inv);
+  const float* gbase = a.part + (int64_t)blk * a.n_splits * a.kw * a.rows_per_group * rec;
+  for (int r = warp; r < Mg; r += nwarps) {
+    auto at = [&](int p, int f) { return __ldcg(gbase + ((int64_t)p * a.rows_per_group + r) * rec + f); };
+    merge_row(r, at);
   }
   if (threadIdx.x == 0) a.counters[kAttnCounterBase + blk] = 0u;
 }
 
 // Clusters of `s` CTAs (one row group's key slices) that can be resident at
 // once, from the occupancy API; cached per kernel, size and device.
-int attn_resident_clusters(void (*kern)(const AttnArgs), int s, size_t smem) {
+int attn_resident_clusters(void (*kern)(const AttnArgs), int s, size_t smem, int threads) {
   static std::mutex mu;
   static std::map<std::tuple<void*, int, size_t, int>, int> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const auto key = std::make_tuple(reinterpret_cast<void*>(kern), s, smem, dev);
+  const auto key = std::make_tuple(reinterpret_cast<void*>(kern), s, smem, dev * 4096 + threads);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -681,7 +671,7 @@ int attn_resident_clusters(void (*kern)(const AttnArgs), int s, size_t smem) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1, s);
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -740,21 +730,33 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int sms = device_sms();
   if (dtype == SSD_BF16 && (head_dim == 64 || head_dim == 128)) {
-    // Tensor-core path: all query rows of a KV head in as few CTAs as possible.
+    // Tensor-core path: all query rows of a KV head in as few CTAs as
+    // possible (<= 8 row tiles of 16 per CTA); with fewer row tiles, up to 4
+    // key lanes per CTA split the key slice.
     const int64_t M = T * a.G;
-    a.groups = (int)((M + kMmaMaxRows - 1) / kMmaMaxRows);
-    a.rows_per_group = (int)(((M + a.groups - 1) / a.groups + 15) / 16 * 16);
+    const int64_t tiles = (M + 15) / 16;
+    if (tiles <= kWsMaxConsumers) {
+      a.groups = 1;
+      a.rt = (int)tiles;
+      a.kw = kWsMaxConsumers / a.rt < 4 ? kWsMaxConsumers / a.rt : 4;
+    } else {
+      a.groups = (int)((tiles + kWsMaxConsumers - 1) / kWsMaxConsumers);
+      a.rt = (int)((tiles + a.groups - 1) / a.groups);
+      a.kw = 1;
+    }
+    a.rows_per_group = a.rt * 16;
+    const int threads = 32 * (a.rt * a.kw + 1);
     const int64_t blocks = (int64_t)a.n_kv * a.groups;
     if (blocks > 16384) return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: too many row groups");
-    const size_t smem = (size_t)mma_region((int)head_dim) + mma_qbytes((int)head_dim) + kMmaMeta;
-    void (*kern)(const AttnArgs) = head_dim == 128 ? attn_mma_kernel<128> : attn_mma_kernel<64>;
+    const size_t smem = (size_t)ws_region_bytes((int)head_dim, a.kw, a.rows_per_group) + kWsMeta;
+    void (*kern)(const AttnArgs) = head_dim == 128 ? attn_ws_kernel<128> : attn_ws_kernel<64>;
     static bool set128 = false, set64 = false;
     bool& set = head_dim == 128 ? set128 : set64;
     if (!set) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
       set = true;
     }
-    int64_t splits = (2 * sms) / blocks;
+    int64_t splits = sms / blocks;
     const int64_t by_len = (kv_bound + 255) / 256;
     if (splits > by_len) splits = by_len;
     // Up to 8 slices of <= 1024 keys merge inside one cluster through DSMEM,
@@ -762,22 +764,28 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
     // and a merge through global memory.
     if (kv_bound <= 8 * 1024) {
       if (splits > kMaxAttnClusterSplits) splits = kMaxAttnClusterSplits;
-      while (splits > 1 && attn_resident_clusters(kern, (int)splits, smem) < blocks) --splits;
+      while (splits > 1 && attn_resident_clusters(kern, (int)splits, smem, threads) < blocks) --splits;
+    } else {
+      int64_t want = (2 * sms) / blocks;
+      if (want > by_len) want = by_len;
+      if (want > splits) splits = want;
     }
+    if (splits * a.kw > kMaxPartials) splits = kMaxPartials / a.kw;
     if (splits > kMmaMaxSplits) splits = kMmaMaxSplits;
     if (splits < 1) splits = 1;
     int64_t split_len = ((kv_bound + splits - 1) / splits + 63) / 64 * 64;
     a.split_len = (int)split_len;
     a.n_splits = (int)((kv_bound + split_len - 1) / split_len);
-    a.cluster_merge = (a.n_splits > 1 && a.n_splits <= kMaxAttnClusterSplits) ? 1 : 0;
+    a.cluster_merge = (a.n_splits > 1 && a.n_splits <= kMaxAttnClusterSplits && kv_bound <= 8 * 1024) ? 1 : 0;
     if (a.n_splits > 1 && !a.cluster_merge) {
-      const int64_t need = kCounterBytes + blocks * a.n_splits * a.rows_per_group * mma_rec((int)head_dim) * 4;
+      const int64_t need =
+          kCounterBytes + blocks * a.n_splits * a.kw * a.rows_per_group * mma_rec((int)head_dim) * 4;
       if (!workspace || need > workspace_bytes)
         return fail(SSD_ERR_WORKSPACE, "ssd_tree_attention: workspace too small (need %lld)", (long long)need);
       a.counters = static_cast<uint32_t*>(workspace);
       a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
     }
-    return launch_kernel("attn_mma_kernel", kern, dim3((unsigned)blocks, (unsigned)a.n_splits), dim3(256), smem, s,
+    return launch_kernel("attn_ws_kernel", kern, dim3((unsigned)blocks, (unsigned)a.n_splits), dim3(threads), smem, s,
                          1u, a.cluster_merge ? (unsigned)a.n_splits : 1u, a);
   }
   if (a.G > kAttnQ) return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: GQA group > 32");

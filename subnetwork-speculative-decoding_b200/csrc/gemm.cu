@@ -230,6 +230,333 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ------------------------------------------------------- tcgen05, stream-K
+// Decode-sized GEMMs (T <= 128 token rows, one token tile) as a persistent
+// stream-K kernel: the tiles_m x kchunks (weight tile, 64-wide K chunk)
+// iterations are cut into gridDim.x equal contiguous ranges, one per CTA
+// (two CTAs per SM), so every SM streams the same number of weight bytes
+// whatever the tile count: no wave quantisation and no clusters. A range
+// crosses tile boundaries; each piece of a tile it covers is a segment. The
+// MMA warp accumulates a segment in one of two TMEM buffers while the
+// epilogue warps drain the other. A segment covering a whole tile runs the
+// epilogue directly. A tile split across P CTAs is finished by all P of
+// them: each writes its partial tile (CTA c: slot 2c for its first segment,
+// 2c+1 for its last), and after its own segments each sums the P partials
+// of its share of the token columns in K order. The sums are deterministic
+// and the cut depends only on the weight shape and the grid, so a row's
+// result does not depend on how many rows are batched.
+__device__ __forceinline__ int sk_cta_of(int64_t it, int64_t W, int G) {
+  return (int)(((it + 1) * G - 1) / W);
+}
+__device__ __forceinline__ int64_t sk_begin(int c, int64_t W, int G) { return (int64_t)c * W / G; }
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_sk_kernel(const __grid_constant__ TcMaps maps, const GemmShape g, const EpiArgs e) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stage_bytes = tc_stage_bytes(g.BN);
+  float* stage = reinterpret_cast<float*>(smem + g.stages * stage_bytes);
+  uint8_t* bar_base = smem + g.stages * stage_bytes + g.BN * kTileM * 4;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_base);
+  uint64_t* empty = full + g.stages;
+  uint64_t* accf = empty + g.stages;  // [2] accumulator buffer b holds a finished segment
+  uint64_t* acce = accf + 2;          // [2] accumulator buffer b drained by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+  int* flag = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abort_flag = flag + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x, cta = blockIdx.x;
+  const int64_t W = (int64_t)g.tiles_m * g.kchunks;
+  const int64_t it0 = sk_begin(cta, W, G), it1 = sk_begin(cta + 1, W, G);
+  const int n = (int)(it1 - it0);
+  const uint32_t cols = tc_tmem_cols(g.BN);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < g.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // The whole warp produces: lane 0 owns the barriers, lanes 0..nA-1 each
+    // issue one A box of a stage and lane nA the B box, so the TMA
+    // instructions of one stage issue in parallel.
+    const int nA = kTileM / g.a_box;
+    if (n > 0) {
+      if (lane == 0) {
+        for (int i = 0; i < g.n_seg; ++i) tma_prefetch_desc(&maps.w[i]);
+        tma_prefetch_desc(&maps.x);
+      }
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      const uint32_t tx = kABytes + g.BN * kChunkK * 2;
+      auto load_a = [&](int i, int j) {
+        const int64_t it = it0 + i;
+        const int tile = (int)(it / g.kchunks);
+        const int kx = (int)(it - (int64_t)tile * g.kchunks) * kChunkK;
+        uint8_t* a = smem + (i % g.stages) * stage_bytes + j * g.a_box * 128;
+        int seg, row;
+        if (g.layout == SSD_SEG_PAIRS) {
+          if (g.a_box == 64) {
+            seg = j;
+            row = tile * 64;
+          } else {
+            seg = j >> 1;
+            row = tile * 64 + (j & 1) * 32;
+          }
+        } else {
+          const int nn = tile * kTileM + j * g.a_box;
+          seg = 0;
+          for (int q = 1; q < g.n_seg; ++q)
+            if (nn >= g.seg_start[q]) seg = q;
+          row = nn - g.seg_start[seg];  // rows past the segment end are zero-filled by TMA
+        }
+        tma_load_2d(a, &maps.w[seg], &full[i % g.stages], kx, row, pol_w);
+      };
+      auto load_b = [&](int i) {
+        const int64_t it = it0 + i;
+        const int kc = (int)(it % g.kchunks);
+        uint8_t* bb = smem + (i % g.stages) * stage_bytes + kABytes;
+        tma_load_2d(bb, &maps.x, &full[i % g.stages], kc * kChunkK, 0, pol_x);
+      };
+      // Weights are never written by any kernel: stream the first stages
+      // while the predecessor kernel is still finishing (PDL).
+      const int pre = n < g.stages ? n : g.stages;
+      for (int i = 0; i < pre; ++i) {
+        if (lane == 0) mbar_arrive_expect_tx(&full[i], tx);
+        __syncwarp();
+        if (lane < nA) load_a(i, lane);
+      }
+      pdl_wait();
+      if (lane == nA)
+        for (int i = 0; i < pre; ++i) load_b(i);
+      int issued = pre;
+      for (int i = pre; i < n; ++i) {
+        const int s = i % g.stages;
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(&empty[s], ((i / g.stages) - 1) & 1) && !*abort_flag;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          if (lane == 0) {
+            report_error(g.status, kErrWaitTimeout);
+            *abort_flag = 1;
+          }
+          break;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&full[s], tx);
+        __syncwarp();
+        if (lane < nA) load_a(i, lane);
+        if (lane == nA) load_b(i);
+        ++issued;
+      }
+      if (lane == 0) {
+        pdl_trigger();
+        if (*abort_flag) {
+          for (int i = (issued > g.stages ? issued - g.stages : 0); i < issued; ++i)
+            (void)mbar_wait(&full[i % g.stages], (i / g.stages) & 1);
+        }
+      }
+    } else if (lane == 0) {
+      pdl_trigger();
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kTileM, g.BN);
+      bool ok = true;
+      int seg = 0;
+      for (int64_t it = it0; it < it1 && ok; ++seg) {
+        const int tile = (int)(it / g.kchunks);
+        const int64_t seg_end = min(it1, (int64_t)(tile + 1) * g.kchunks);
+        const int b = seg & 1;
+        if (seg >= 2 && !mbar_wait(&acce[b], ((seg >> 1) - 1) & 1)) {
+          report_error(g.status, kErrWaitTimeout);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + b * cols;
+        const int64_t seg_begin = it;
+        for (; it < seg_end; ++it) {
+          const int i = (int)(it - it0);
+          const int s = i % g.stages;
+          if (*abort_flag || !mbar_wait(&full[s], (i / g.stages) & 1)) {
+            report_error(g.status, kErrWaitTimeout);
+            *abort_flag = 1;  // before the commit below, so the epilogue sees it
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * stage_bytes);
+          const uint32_t bb = a + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kChunkK / 16; ++kk)
+            umma_bf16(d, sdesc_k_sw128(a + kk * 32), sdesc_k_sw128(bb + kk * 32), idesc,
+                      (it != seg_begin || kk != 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        // Arrives when every MMA issued so far has retired (also on abort, so
+        // the epilogue never reads TMEM that is still being written).
+        umma_commit(&accf[b]);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // Epilogue warps 2..5; warp w may only touch TMEM lanes 32*(w%4)..+31.
+    // A whole tile is finished here at once. A split segment is drained
+    // straight into this CTA's partial slot and counted; only after all its
+    // segments does the CTA finish its (at most two) split tiles, so no CTA
+    // waits while holding back a partial another CTA needs.
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int ncols = min(g.BN, g.T);
+    uint32_t* arrived = g.counters;
+    uint32_t* finished = g.counters + kMaxCounters / 2;
+    pdl_wait();  // the epilogue writes buffers earlier kernels may still read
+    int split_tile[2] = {-1, -1};
+    int n_split = 0;
+    bool failed = false;
+    int seg = 0;
+    for (int64_t it = it0; it < it1; ++seg) {
+      const int tile = (int)(it / g.kchunks);
+      const int64_t tile_begin = (int64_t)tile * g.kchunks;
+      const int64_t seg_end = min(it1, tile_begin + g.kchunks);
+      const bool whole = (it == tile_begin) && (seg_end == tile_begin + g.kchunks);
+      const int b = seg & 1;
+      bool bad = !mbar_wait(&accf[b], (seg >> 1) & 1);
+      if (bad) report_error(g.status, kErrWaitTimeout);
+      tc_fence_after();
+      bad = named_bar_or(1, 128, bad || *abort_flag != 0);  // one decision for all 128 threads
+      if (bad) {
+        if (r == 0) *abort_flag = 1;
+        failed = true;
+        break;
+      }
+      const uint32_t src = tmem + b * cols + (static_cast<uint32_t>(q * 32) << 16);
+      if (whole) {
+        for (int c0 = 0; c0 < g.BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(src + c0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (c0 + i < ncols) stage[(c0 + i) * kTileM + r] = v[i];
+        }
+        tc_fence_before();
+        named_bar_sync(1, 128);
+        if (r == 0) mbar_arrive(&acce[b]);  // TMEM buffer b may take segment seg + 2
+        run_epilogue<bf16>(stage, tile, 0, ncols, g, e, r, 1);
+        named_bar_sync(1, 128);  // the stage is reused by the next segment
+      } else {
+        float* mine = g.partials + (int64_t)(2 * cta + (seg == 0 ? 0 : 1)) * kTileM * g.BN + r;
+        for (int c0 = 0; c0 < g.BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(src + c0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (c0 + i < ncols) __stcg(mine + (c0 + i) * kTileM, v[i]);
+        }
+        tc_fence_before();
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (r == 0) {
+          mbar_arrive(&acce[b]);
+          atomicAdd(&arrived[tile], 1u);
+        }
+        split_tile[n_split++] = tile;
+      }
+      it = seg_end;
+    }
+    // Finish the split tiles: participant j of P owns token columns j, j + P,
+    // ...; it sums the P partials of those columns in K order and runs the
+    // epilogue on them.
+    for (int k = 0; k < n_split && !failed; ++k) {
+      const int tile = split_tile[k];
+      const int64_t tile_begin = (int64_t)tile * g.kchunks;
+      const int first = sk_cta_of(tile_begin, W, G);
+      const int last = sk_cta_of(tile_begin + g.kchunks - 1, W, G);
+      const int P = last - first + 1;
+      const int j = cta - first;
+      bool ok = true;
+      if (r == 0) {
+        uint32_t n_in = 0;
+        for (uint32_t i = 0; i < kWaitLimit; ++i) {
+          n_in = ld_acquire_u32(&arrived[tile]);
+          if ((int)n_in >= P) break;
+        }
+        ok = (int)n_in >= P;
+        if (!ok) report_error(g.status, kErrWaitTimeout);
+      }
+      if (named_bar_or(1, 128, !ok)) {
+        failed = true;
+        break;
+      }
+      __threadfence();
+      // (column, partial) pairs of this participant, partial index fastest;
+      // loads go out 32 at a time and are summed into the stage in K order.
+      // Slots: every participant after `first` starts its range inside the
+      // tile (its first segment); `first` covers the tile start.
+      const int first_slot = 2 * first + (sk_begin(first, W, G) == tile_begin ? 0 : 1);
+      const int n_own = (ncols - j + P - 1) / P;
+      const int total = n_own * P;
+      for (int m0 = 0; m0 < total; m0 += 32) {
+        float v[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+          const int m = m0 + u;
+          v[u] = 0.f;
+          if (m < total) {
+            const int pi = m % P;
+            const int col = j + (m / P) * P;
+            const int slot = pi == 0 ? first_slot : 2 * (first + pi);
+            v[u] = __ldcg(g.partials + (int64_t)slot * kTileM * g.BN + col * kTileM + r);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+          const int m = m0 + u;
+          if (m < total) {
+            const int pi = m % P;
+            float* dst = stage + (j + (m / P) * P) * kTileM + r;
+            *dst = (pi == 0 ? 0.f : *dst) + v[u];
+          }
+        }
+      }
+      named_bar_sync(1, 128);
+      run_epilogue<bf16>(stage, tile, 0, ncols, g, e, r, 1, j, P);
+      named_bar_sync(1, 128);
+      if (r == 0) {
+        const unsigned t = atomicAdd(&finished[tile], 1u);
+        if ((int)t == P - 1) {  // every participant has read the partials: reset for the next launch
+          arrived[tile] = 0u;
+          finished[tile] = 0u;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * cols);
+  }
+}
+
 // ------------------------------------------------------------------ SIMT path
 // CUDA-core mainloop for the fp32 parity tier: 256 threads = 8 warps x 16
 // feature rows; lanes stride K (coalesced weight rows), 4 tokens per tile.
@@ -392,8 +719,47 @@ void set_tc_attributes() {
   }
 }
 
-int tc_stages(int BN) {
-  const int stages = 101376 / tc_stage_bytes(BN);
+// Stream-K variant, opt-in with SSD_GEMM_SK=1 (CTAs per SM: SSD_SK_CTAS=1|2,
+// default 2). Its main loop streams at the HBM peak, but finishing the split
+// tiles through L2 (write, fence, count, re-read) costs ~10 us per launch on
+// B200, more than the cluster kernel's DSMEM reduction, so it is not the
+// default.
+int sk_ctas_per_sm() {
+  static const int v = [] {
+    const char* s = getenv("SSD_SK_CTAS");
+    return (s && atoi(s) == 1) ? 1 : 2;
+  }();
+  return v;
+}
+bool sk_enabled() {
+  static const bool v = [] {
+    const char* s = getenv("SSD_GEMM_SK");
+    return s && s[0] == '1';
+  }();
+  return v;
+}
+constexpr int kSkBarBytes = 512;
+int sk_stages(int BN) {
+  const int budget = sk_ctas_per_sm() == 2 ? 113 * 1024 : 232448;
+  const int avail = budget - 1024 - kSkBarBytes - BN * kTileM * 4;
+  const int st = avail / tc_stage_bytes(BN);
+  return st > 16 ? 16 : (st < 2 ? 2 : st);
+}
+size_t sk_smem_bytes(int BN, int stages) {
+  return 1024 + (size_t)stages * tc_stage_bytes(BN) + (size_t)BN * kTileM * 4 + kSkBarBytes;
+}
+
+// Cluster split-K kernel: CTAs resident per SM, chosen from the weight shape
+// only (so the split, and with it every row's rounding, never depends on T).
+// One CTA's tiled-TMA stream tops out near 34 GB/s, so an SM's bandwidth grows
+// with the CTAs it holds, while each CTA's ring shrinks to fit; measured on
+// the 8B shapes: two per SM suit split GEMMs that already reach 8-way splits
+// and single-wave unsplit ones, more per SM pays when it buys a deeper split
+// (q/k/v: 4 -> 8) or fewer waves (lm_head: 1002 tiles).
+int tc_ctas_per_sm(int tiles_m, int kchunks, bool head, int sms);
+int tc_stages(int BN, int per_sm) {
+  const int budget = (233472 - per_sm * 1024) / per_sm - 1024 - 256;
+  const int stages = budget / tc_stage_bytes(BN);
   return stages > 8 ? 8 : (stages < 2 ? 2 : stages);
 }
 
@@ -411,6 +777,19 @@ int choose_cluster_splits(int tiles_m, int kchunks, int cta_slots) {
   int p = 1;
   while (p * 2 <= s) p *= 2;
   return p;
+}
+
+int tc_ctas_per_sm(int tiles_m, int kchunks, bool head, int sms) {
+  if (head || tiles_m * 2 >= 2 * sms) return tiles_m > 2 * sms ? 4 : 2;
+  int best = 2, best_s = choose_cluster_splits(tiles_m, kchunks, 2 * sms);
+  for (int per = 3; per <= 4; ++per) {
+    const int s = choose_cluster_splits(tiles_m, kchunks, per * sms);
+    if (s > best_s) {
+      best = per;
+      best_s = s;
+    }
+  }
+  return best;
 }
 
 }  // namespace
@@ -452,8 +831,9 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
     if (K % 8) return fail(SSD_ERR_UNSUPPORTED, "bf16 GEMM needs K % 8 == 0");
     g.BN = round_bn(T);
     g.tiles_n = (int)((T + g.BN - 1) / g.BN);
-    g.splits = (g.tiles_n == 1 && !head) ? choose_cluster_splits(g.tiles_m, g.kchunks, 2 * sms) : 1;
-    g.stages = tc_stages(g.BN);
+    const int per_sm = tc_ctas_per_sm(g.tiles_m, g.kchunks, head, sms);
+    g.splits = (g.tiles_n == 1 && !head) ? choose_cluster_splits(g.tiles_m, g.kchunks, per_sm * sms) : 1;
+    g.stages = tc_stages(g.BN, per_sm);
   } else if (dtype == SSD_F32) {
     g.BN = kSimtBN;
     g.tiles_n = (int)((T + kSimtBN - 1) / kSimtBN);
@@ -479,15 +859,49 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
   dim3 grid(g.tiles_m * g.splits, g.tiles_n);
 
   if (dtype == SSD_BF16) {
+    const bool sk = g.tiles_n == 1 && g.BN <= 128 && sk_enabled();
+    // Stream-K: one TMA box per weight segment a tile touches (128 rows when
+    // every segment starts on a tile boundary, 64 + 64 for gate/up pairs),
+    // else four 32-row boxes.
+    g.a_box = 32;
+    if (sk) {
+      if (layout == SSD_SEG_PAIRS) {
+        g.a_box = 64;
+      } else {
+        bool aligned = true;
+        for (int i = 1; i < n_seg; ++i) aligned = aligned && (g.seg_start[i] % kTileM == 0);
+        if (aligned) g.a_box = 128;
+      }
+    }
     TcMaps maps;
     for (int i = 0; i < n_seg; ++i) {
-      const int rc = get_map(w[i], (uint64_t)K, (uint64_t)rows[i], (uint64_t)K * 2, 32, &maps.w[i]);
+      const int rc = get_map(w[i], (uint64_t)K, (uint64_t)rows[i], (uint64_t)K * 2, (uint32_t)g.a_box, &maps.w[i]);
       if (rc) return rc;
     }
     for (int i = n_seg; i < 3; ++i) maps.w[i] = maps.w[0];
     const int rc = get_map(x, (uint64_t)K, (uint64_t)T, (uint64_t)ldx * 2, (uint32_t)g.BN, &maps.x);
     if (rc) return rc;
     set_tc_attributes();
+    if (sk) {
+      const int64_t W = (int64_t)g.tiles_m * g.kchunks;
+      int64_t G = (int64_t)sms * sk_ctas_per_sm();
+      if (G > W) G = W;
+      if (g.tiles_m > kMaxCounters / 2) return fail(SSD_ERR_WORKSPACE, "too many weight tiles");
+      const int64_t need = kCounterBytes + partial_offset_bytes + 2 * G * kTileM * g.BN * 4;
+      if (!workspace || need > workspace_bytes)
+        return fail(SSD_ERR_WORKSPACE, "workspace too small: need %lld bytes", (long long)need);
+      g.counters = reinterpret_cast<uint32_t*>(ws);
+      g.partials = reinterpret_cast<float*>(ws + kCounterBytes + partial_offset_bytes);
+      g.stages = sk_stages(g.BN);
+      g.splits = 1;
+      static bool sk_attr = false;
+      if (!sk_attr) {
+        cudaFuncSetAttribute(tc_gemm_sk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+        sk_attr = true;
+      }
+      return launch_kernel("tc_gemm_sk_kernel", tc_gemm_sk_kernel, dim3((unsigned)G), dim3(kTcThreads),
+                           sk_smem_bytes(g.BN, g.stages), stream, 1u, 1u, maps, g, e);
+    }
     // K-split CTAs of one tile run as one thread-block cluster (DSMEM reduction).
     return launch_kernel("tc_gemm_kernel", tc_gemm_kernel, grid, dim3(kTcThreads), tc_smem_bytes(g.BN, g.stages),
                          stream, (unsigned)g.splits, 1u, maps, g, e);

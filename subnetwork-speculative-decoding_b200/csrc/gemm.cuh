@@ -67,6 +67,7 @@ struct GemmShape {
   int kchunks;        // ceil(K / 64)
   int stages;
   int tiles_m, tiles_n;
+  int a_box;          // weight rows per TMA box (stream-K kernel: 128, 64 or 32)
   uint32_t* counters;
   float* partials;
   uint32_t* status;
@@ -175,7 +176,7 @@ __device__ void run_epilogue(float* stage, int tile_m, int t0, int ncols, const 
       // One warp per token column; lanes scan the 128 rows of the tile.
       const int warp = tid >> 5, lane = tid & 31;
       const int rec = head_rec_size(e.kind, e.topk);
-      for (int c = warp; c < ncols; c += 4) {
+      for (int c = c0 + warp * cstep; c < ncols; c += 4 * cstep) {
         const int t = t0 + c;
         float v[4];
         int idx[4];

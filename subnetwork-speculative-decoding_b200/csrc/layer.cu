@@ -231,14 +231,18 @@ int64_t ssd_workspace_bytes(int64_t max_rows, int64_t max_head_rows, int64_t voc
   // tcgen05: <= 2 CTAs/SM, one 128 x BN tile each; SIMT (fp32): <= 4 CTAs/SM
   // per 4-token tile, up to kSimtInvariantRows / 4 token tiles.
   const int64_t simt_tiles_n = (kSimtInvariantRows + 3) / 4;
-  const int64_t splitk_tc = 2LL * device_sms() * bn * kTileM * 4;
+  // tcgen05: cluster split-K partials (<= 2 CTAs/SM, one tile each) or the
+  // stream-K kernel's two partial slots per CTA (<= 2 CTAs/SM)
+  const int64_t splitk_tc = 4LL * device_sms() * bn * kTileM * 4;
   const int64_t splitk_simt = 4LL * device_sms() * simt_tiles_n * 4 * kTileM * 4;
   const int64_t splitk = splitk_tc > splitk_simt ? splitk_tc : splitk_simt;
   // attention partials: (CTAs <= 2 * SMs + row-tile blocks) x 32 queries x
   // (head_dim <= 128 + 2) floats; row-tile blocks <= rows * n_heads / 32 with
   // n_heads <= 128.
-  const int64_t attn = (2LL * device_sms() + max_rows * 4 + 8) * 32 * 130 * 4;
-  int64_t body = heads > splitk ? heads : splitk;
+  // (tensor-core kernel: <= 128 query rows x 132 floats per CTA-slice record set)
+  const int64_t attn = (2LL * device_sms() + max_rows * 4 + 8) * 128 * 132 * 4;
+  // a head GEMM keeps its partial records and the stream-K partials at once
+  int64_t body = heads + splitk;
   body = body > attn ? body : attn;
   return kCounterBytes + body;
 }
