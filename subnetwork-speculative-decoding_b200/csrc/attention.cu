@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const AttnArgs a) {
 // small tree levels) KW > 1 key lanes split the slice inside the CTA. The
 // (slice, key lane) partials of a row merge in a fixed order: inside one
 // cluster through DSMEM, or through a global workspace for long contexts.
-constexpr int kWsMaxConsumers = 8;                   // consumer warps per CTA
+constexpr int kWsMaxConsumers = 7;                   // consumer warps per CTA (+ producer: 256 threads)
 constexpr int kWsStages = 4;                         // K/V blocks in flight per CTA
 constexpr int kMmaMaxRows = kWsMaxConsumers * 16;    // query rows per CTA
 constexpr int kMmaMaxTok = kMmaMaxRows + 1;
@@ -295,10 +295,14 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 // Partial record of one query row of one (key slice, key lane): {m, l, pad, pad, o[hd]}.
 __host__ __device__ constexpr int mma_rec(int hd) { return hd + 4; }
 __host__ __device__ constexpr int ws_ring_bytes(int hd) { return kWsStages * 2 * 64 * hd * 2; }
-// The ring is reused for the partial records [kw][rows][rec] after the key loop.
+// Partial records pushed to the CTA that merges them: [p][owned row][rec]
+// with p = slice * kw + key lane and owned rows r = rank, rank + slices, ...
+// (at most ceil(rows / slices) per CTA); sized for up to 8 slices.
+__host__ __device__ inline int ws_recv_bytes(int hd, int kw, int rows) {
+  return (rows + kMaxAttnClusterSplits) * kw * mma_rec(hd) * 4;
+}
 __host__ __device__ inline int ws_region_bytes(int hd, int kw, int rows) {
-  const int part = kw * rows * mma_rec(hd) * 4;
-  return ws_ring_bytes(hd) > part ? ws_ring_bytes(hd) : part;
+  return ws_ring_bytes(hd) + ws_recv_bytes(hd, kw, rows);
 }
 constexpr int kWsMeta = (kMmaMaxTok + 1) * 4 + kMmaMaxTok * 4 * 8 + 16 + 2 * kWsStages * 8 + 16;
 
@@ -359,8 +363,11 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
   __syncthreads();
   const int need_end = min(min(s_misc[0], a.kv_bound), a.max_slots);
   const int min_plen = s_misc[1];
-  const int k_lo = split * a.split_len;
-  const int k_hi = min(k_lo + a.split_len, need_end);
+  // Slices cut the live key range (known only on the device), not the
+  // static bound the grid was sized for, so every slice gets the same work.
+  const int slice = ((need_end + a.n_splits - 1) / a.n_splits + KB - 1) / KB * KB;
+  const int k_lo = split * slice;
+  const int k_hi = min(k_lo + slice, need_end);
   const int nblocks = k_hi > k_lo ? (k_hi - k_lo + KB - 1) / KB : 0;
   const uint32_t ring_s = smem_u32(attn_smem);
   auto stage_k = [&](int st) { return ring_s + st * 2 * KB * HD * 2; };
@@ -552,34 +559,9 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
     return;
   }
   const int rec = mma_rec(HD);
-  // This CTA's records: [kw][row][rec], in shared memory (cluster merge) or
-  // in the global workspace slot of (row group, slice).
-  const bool in_smem = a.cluster_merge || a.n_splits == 1;
-  float* recs = in_smem ? reinterpret_cast<float*>(attn_smem)
-                        : a.part + ((int64_t)blk * a.n_splits + split) * a.kw * a.rows_per_group * rec;
-  if (warp < nwc) {
-    float* p0 = recs + ((int64_t)kw * a.rows_per_group + rl0) * rec;
-    float* p1 = recs + ((int64_t)kw * a.rows_per_group + rl1) * rec;
-    if (tq == 0) {
-      if (ok0) {
-        p0[0] = m0;
-        p0[1] = l0;
-      }
-      if (ok1) {
-        p1[0] = m1;
-        p1[1] = l1;
-      }
-    }
-#pragma unroll
-    for (int dt = 0; dt < NTD; ++dt) {
-      const int d = 4 + dt * 8 + 2 * tq;
-      if (ok0) *reinterpret_cast<float2*>(p0 + d) = make_float2(o[dt][0], o[dt][1]);
-      if (ok1) *reinterpret_cast<float2*>(p1 + d) = make_float2(o[dt][2], o[dt][3]);
-    }
-  }
   constexpr int DPL = HD / 32;  // dims per lane (2 or 4)
-  // Merge one row over its P partials (p = slice * kw + lane of the key
-  // split), weights from the (m, l) pairs, accumulation in p order.
+  // Merge one row over its P partials (p = slice * kw + key lane), weights
+  // from the (m, l) pairs, accumulation in p order.
   auto merge_row = [&](int r, auto&& rec_at) {
     const int qr = q0 + r;
     float ms = -INFINITY, ls = 0.f;
@@ -613,31 +595,79 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
 #pragma unroll
     for (int i = 0; i < DPL; ++i) op[i] = f2bf(acc[i] * inv);
   };
-  if (a.cluster_merge) {
-    // The key slices of this (head, row group) form one cluster: CTA `split`
-    // merges rows split, split + n_splits, ... from every peer's records.
-    cluster_sync_all();
-    const uint32_t mine = smem_u32(attn_smem);
-    for (int r = split + warp * a.n_splits; r < Mg; r += nwarps * a.n_splits) {
-      auto at = [&](int p, int f) {
-        const int sl = p / a.kw, kl = p % a.kw;
-        const uint32_t base = dsmem_map(mine, static_cast<uint32_t>(sl));
-        return dsmem_ld(base + (uint32_t)((kl * a.rows_per_group + r) * rec + f) * 4);
-      };
-      merge_row(r, at);
+  if (a.cluster_merge || a.n_splits == 1) {
+    // Push: every consumer stores its rows' partials straight into the
+    // receive area of the CTA that merges the row (rank r % slices; DSMEM
+    // stores, no remote loads), then one barrier, then a local merge.
+    const int ns = a.n_splits;
+    const int owned = (a.rows_per_group + ns - 1) / ns;
+    float* recv = reinterpret_cast<float*>(attn_smem + ws_ring_bytes(HD));
+    const uint32_t recv_s = smem_u32(recv);
+    if (warp < nwc) {
+      const int p = split * a.kw + kw;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int rl = half ? rl1 : rl0;
+        if (!(half ? ok1 : ok0)) continue;
+        const int owner = rl % ns, j = rl / ns;
+        const uint32_t dst0 = (uint32_t)(((p * owned + j) * rec) * 4);
+        const float mm = half ? m1 : m0, ll = half ? l1 : l0;
+        if (a.cluster_merge) {
+          const uint32_t base = dsmem_map(recv_s, static_cast<uint32_t>(owner));
+          if (tq == 0) dsmem_st2(base + dst0, mm, ll);
+#pragma unroll
+          for (int dt = 0; dt < NTD; ++dt) {
+            const int d = 4 + dt * 8 + 2 * tq;
+            dsmem_st2(base + dst0 + d * 4, half ? o[dt][2] : o[dt][0], half ? o[dt][3] : o[dt][1]);
+          }
+        } else {
+          float* dst = recv + (p * owned + j) * rec;
+          if (tq == 0) {
+            dst[0] = mm;
+            dst[1] = ll;
+          }
+#pragma unroll
+          for (int dt = 0; dt < NTD; ++dt) {
+            const int d = 4 + dt * 8 + 2 * tq;
+            *reinterpret_cast<float2*>(dst + d) =
+                make_float2(half ? o[dt][2] : o[dt][0], half ? o[dt][3] : o[dt][1]);
+          }
+        }
+      }
     }
-    cluster_sync_all();
+    if (a.cluster_merge)
+      cluster_sync_all();
+    else
+      __syncthreads();
+    const int n_own = Mg > split ? (Mg - split + ns - 1) / ns : 0;
+    for (int j = warp; j < n_own; j += nwarps) {
+      auto at = [&](int pp, int f) { return recv[(pp * owned + j) * rec + f]; };
+      merge_row(split + j * ns, at);
+    }
     return;
   }
-  if (a.n_splits == 1) {
-    // one slice, several key lanes: merge inside the CTA
-    __syncthreads();
-    const float* sp = recs;
-    for (int r = warp; r < Mg; r += nwarps) {
-      auto at = [&](int p, int f) { return sp[((int64_t)p * a.rows_per_group + r) * rec + f]; };
-      merge_row(r, at);
+  // Long contexts: records in the global workspace slot of (row group,
+  // slice); the last slice to finish merges.
+  float* recs = a.part + ((int64_t)blk * a.n_splits + split) * a.kw * a.rows_per_group * rec;
+  if (warp < nwc) {
+    float* p0 = recs + ((int64_t)kw * a.rows_per_group + rl0) * rec;
+    float* p1 = recs + ((int64_t)kw * a.rows_per_group + rl1) * rec;
+    if (tq == 0) {
+      if (ok0) {
+        p0[0] = m0;
+        p0[1] = l0;
+      }
+      if (ok1) {
+        p1[0] = m1;
+        p1[1] = l1;
+      }
     }
-    return;
+#pragma unroll
+    for (int dt = 0; dt < NTD; ++dt) {
+      const int d = 4 + dt * 8 + 2 * tq;
+      if (ok0) *reinterpret_cast<float2*>(p0 + d) = make_float2(o[dt][0], o[dt][1]);
+      if (ok1) *reinterpret_cast<float2*>(p1 + d) = make_float2(o[dt][2], o[dt][3]);
+    }
   }
   __threadfence();
   __syncthreads();
