@@ -239,6 +239,28 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const AttnArgs a) {
   if (a.n_splits > 1 && threadIdx.x == 0) a.counters[kAttnCounterBase + blk] = 0u;
 }
 
+// Validity of keys kb .. kb + 63 for one query row as a 64-bit word: the
+// contiguous prefix [0, plen), plus the speculative slots whose bit is set in
+// the row's ancestor mask (bit i = slot sb + i, mw words), clipped to the
+// slice end k_hi. Built with a few integer ops instead of a per-key branch.
+__device__ __forceinline__ uint64_t key_block_bits(int kb, int k_hi, int plen, const uint64_t* row_mask, int mw,
+                                                   int sb) {
+  const int n_hi = min(max(k_hi - kb, 0), 64);
+  const uint64_t hi = n_hi >= 64 ? ~0ull : ((1ull << n_hi) - 1ull);
+  const int n_pre = min(max(plen - kb, 0), 64);
+  const uint64_t pre = n_pre >= 64 ? ~0ull : ((1ull << n_pre) - 1ull);
+  uint64_t spec = 0ull;
+  const int off = kb - sb;  // mask bit of slot kb
+  if (mw > 0 && off < mw * 64 && off > -64) {
+    const int w0 = (off >= 0) ? (off >> 6) : -1;
+    const int sh = off - w0 * 64;  // 0..63
+    const uint64_t lo = (w0 >= 0 && w0 < mw) ? row_mask[w0] : 0ull;
+    const uint64_t up = (w0 + 1 >= 0 && w0 + 1 < mw) ? row_mask[w0 + 1] : 0ull;
+    spec = sh == 0 ? lo : ((lo >> sh) | (up << (64 - sh)));
+  }
+  return (pre | spec) & hi;
+}
+
 // ------------------------------------------------------ tensor-core kernel
 // bf16, head_dim 64 or 128, warp-specialised. A CTA = one KV head x one group
 // of query rows (row q = token * G + GQA head) x one key slice. The last warp
@@ -362,7 +384,6 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
   }
   __syncthreads();
   const int need_end = min(min(s_misc[0], a.kv_bound), a.max_slots);
-  const int min_plen = s_misc[1];
   // Slices cut the live key range (known only on the device), not the
   // static bound the grid was sized for, so every slice gets the same work.
   const int slice = ((need_end + a.n_splits - 1) / a.n_splits + KB - 1) / KB * KB;
@@ -450,29 +471,17 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
           mma_16816(sacc[2 * ntp + 1], qf[ks], b2, b3);
         }
       }
-      // scale + mask: rows rl0 (sacc[.][0..1]) and rl1 (sacc[.][2..3])
-      const bool all_in = (kb + KB <= min_plen) && (kb + KB <= k_hi);
+      // scale + mask: rows rl0 (sacc[.][0..1]) and rl1 (sacc[.][2..3]); this
+      // lane holds keys nt * 8 + 2 * tq + {0, 1} of each n-tile
+      const uint64_t vb0 = ok0 ? key_block_bits(kb, k_hi, pl0, s_mask + tok0 * 4, mw, sb) >> (2 * tq) : 0ull;
+      const uint64_t vb1 = ok1 ? key_block_bits(kb, k_hi, pl1, s_mask + tok1 * 4, mw, sb) >> (2 * tq) : 0ull;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float v = sacc[nt][e] * sc;
-          if (!all_in) {
-            const int slot = kb + nt * 8 + 2 * tq + (e & 1);
-            const bool r1 = e >= 2;
-            bool ok = slot < k_hi && (r1 ? ok1 : ok0);
-            if (ok) {
-              const int pl = r1 ? pl1 : pl0;
-              if (slot >= pl) {
-                const int bit = slot - sb;
-                ok = false;
-                if (mw && bit >= 0 && bit < mw * 64)
-                  ok = (s_mask[(r1 ? tok1 : tok0) * 4 + (bit >> 6)] >> (bit & 63)) & 1ull;
-              }
-            }
-            if (!ok) v = -INFINITY;
-          }
-          sacc[nt][e] = v;
+          const uint64_t vb = e >= 2 ? vb1 : vb0;
+          const bool ok = ((vb >> (nt * 8 + (e & 1))) & 1ull) != 0ull;
+          sacc[nt][e] = ok ? sacc[nt][e] * sc : -INFINITY;
         }
       }
       // online softmax (each row is shared by the 4 lanes of a quad)
@@ -686,6 +695,440 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
   if (threadIdx.x == 0) a.counters[kAttnCounterBase + blk] = 0u;
 }
 
+// ------------------------------------------------------------ tcgen05 kernel
+// bf16, head_dim 64 or 128. A CTA = one KV head x up to 128 query rows (one
+// M = 128 tcgen05 tile; rows past the group are zero) x one key slice.
+// Warp 0 streams the slice's 64-key K and V blocks by TMA (128-byte swizzle,
+// straight from the cache rows) into a kTcAttnStages ring. Warp 1 (one
+// lane) issues S = Q K^T into one of two TMEM S buffers and O += P V into a
+// TMEM O accumulator (V read MN-major as stored). Warps 2..5 own one query
+// row per thread (= TMEM lane): they load S, apply the tree mask, run the
+// online softmax in base 2 with a lazy reference max (P = 2^(s - m_ref)
+// stays below 2^8, so O is rescaled only when a row's max grows by more than
+// 8), write P as bf16 into shared memory for the P V product and, at the
+// end, read O back. Partials of the key slices merge as in the mma.sync
+// kernel: pushed into the merging CTA of the cluster, or through global
+// memory for long contexts.
+// 2^x on the special-function unit (PTX ex2.approx.ftz.f32; 2^-inf = +0).
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr int kTcAttnStages = 4;
+constexpr int kTcAttnMaxTok = 129;  // token rows spanned by 128 query rows (keeps the metadata 8-byte aligned)
+constexpr int kTcAttnThreads = 192;
+constexpr float kLazyRescale = 8.f;  // log2 headroom of P before O is rescaled
+
+struct AttnMaps {
+  CUtensorMap k;  // [n_kv * max_slots, hd] bf16, box {64, 64}
+  CUtensorMap v;
+};
+
+template <int HD>
+struct TcAttnLayout {
+  static constexpr int NR = HD / 64;                 // 128-byte regions per K/V/Q row
+  static constexpr int Q_BYTES = NR * 128 * 128;     // NR regions of [128 rows x 128 B]
+  static constexpr int KV_REGION = 64 * 128;         // [64 keys x 128 B]
+  static constexpr int STAGE = 2 * NR * KV_REGION;   // K regions, then V regions
+  static constexpr int P_BYTES = 128 * 128;          // [128 rows x 64 keys] bf16
+  static constexpr int OFF_RING = Q_BYTES;
+  static constexpr int OFF_P = Q_BYTES + kTcAttnStages * STAGE;
+  static constexpr int OFF_META = OFF_P + 2 * P_BYTES;
+  static constexpr int META = (kTcAttnMaxTok + 1) * 4 + kTcAttnMaxTok * 4 * 8 + 16 + (2 * kTcAttnStages + 10) * 8 + 16;
+  static constexpr int SMEM = 1024 + OFF_META + META;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kTcAttnThreads, 1)
+    attn_tc_kernel(const __grid_constant__ AttnMaps maps, const AttnArgs a) {
+  using Lay = TcAttnLayout<HD>;
+  constexpr int NR = Lay::NR;
+  constexpr int KB = 64;
+  extern __shared__ uint8_t attn_smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(attn_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* qs = sm;
+  uint8_t* ring = sm + Lay::OFF_RING;
+  uint8_t* ps = sm + Lay::OFF_P;
+  int* s_plen = reinterpret_cast<int*>(sm + Lay::OFF_META);
+  uint64_t* s_mask = reinterpret_cast<uint64_t*>(s_plen + kTcAttnMaxTok + 1);  // [tok][4]
+  int* s_misc = reinterpret_cast<int*>(s_mask + kTcAttnMaxTok * 4);           // need_end, min_plen, last, abort
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(s_misc + 4);
+  uint64_t* kv_empty = kv_full + kTcAttnStages;
+  uint64_t* s_full = kv_empty + kTcAttnStages;  // [2]
+  uint64_t* s_free = s_full + 2;                // [2]
+  uint64_t* p_full = s_free + 2;                // [2]
+  uint64_t* p_free = p_full + 2;                // [2]
+  uint64_t* o_full = p_free + 2;
+  uint64_t* q_ready = o_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
+  volatile int* abort_flag = s_misc + 3;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int blk = blockIdx.x;
+  const int h = blk / a.groups, gr = blk % a.groups;
+  const int split = blockIdx.y;
+  const int M = a.T * a.G;
+  const int q0 = gr * a.rows_per_group;
+  const int Mg = min(a.rows_per_group, M - q0);
+  const int t_first = q0 / a.G;
+  const int ntok = (q0 + Mg - 1) / a.G - t_first + 1;
+  const int P = a.n_splits;
+  pdl_wait();
+  pdl_trigger();
+  const int sb = a.spec_base ? a.spec_base[0] : 0;
+  const int mw = a.mask ? a.mask_words : 0;
+
+  if (threadIdx.x == 0) {
+    s_misc[0] = 0;
+    s_misc[1] = INT32_MAX;
+    s_misc[3] = 0;
+    for (int st = 0; st < kTcAttnStages; ++st) {
+      mbar_init(&kv_full[st], 1);
+      mbar_init(&kv_empty[st], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_free[i], 1);
+    }
+    mbar_init(o_full, 1);
+    mbar_init(q_ready, 5);  // warps 1..5 have staged their Q rows
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();  // barriers, TMEM and the meta accumulators are initialised
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  for (int i = threadIdx.x; i < ntok; i += blockDim.x) {
+    const int t = t_first + i;
+    const int pl = a.prefix_len[t];
+    s_plen[i] = pl;
+    int end = pl;
+    for (int w = 0; w < mw; ++w) {
+      const uint64_t m = a.mask[(int64_t)t * mw + w];
+      s_mask[i * 4 + w] = m;
+      if (m) end = max(end, sb + w * 64 + 64 - __clzll(m));
+    }
+    atomicMax(&s_misc[0], end);
+    atomicMin(&s_misc[1], pl);
+  }
+  __syncthreads();  // per-token metadata complete
+  const int need_end = min(min(s_misc[0], a.kv_bound), a.max_slots);
+  const int slice = ((need_end + a.n_splits - 1) / a.n_splits + KB - 1) / KB * KB;
+  const int k_lo = split * slice;
+  const int k_hi = min(k_lo + slice, need_end);
+  const int nblocks = k_hi > k_lo ? (k_hi - k_lo + KB - 1) / KB : 0;
+  const uint32_t qs_s = smem_u32(qs), ring_s = smem_u32(ring), ps_s = smem_u32(ps);
+  if (warp >= 1) {
+    // Q rows (A operand, K-major, 128-byte swizzle; rows past Mg are zero),
+    // staged by warps 1..5 while warp 0 already streams K/V.
+    const bf16* qb = static_cast<const bf16*>(a.q);
+    for (int idx = threadIdx.x - 32; idx < 128 * (HD / 8); idx += kTcAttnThreads - 32) {
+      const int r = idx / (HD / 8), c = idx % (HD / 8);
+      const int qr = q0 + (r < Mg ? r : 0);
+      const bf16* src = qb + (int64_t)(qr / a.G) * a.ldq + (int64_t)(h * a.G + qr % a.G) * HD + c * 8;
+      cp_async16(qs_s + (c >> 3) * (128 * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4), src, r < Mg);
+    }
+    cp_async_wait_all();
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(q_ready);
+  }
+  const uint32_t tm_o = tmem + 128;  // O accumulator columns [128, 128 + HD)
+
+  // softmax-side state (warps 2..5)
+  const int q = warp & 3;
+  const int r = q * 32 + lane;  // query row of this thread = TMEM lane
+  const bool row_ok = warp >= 2 && r < Mg;
+  float m_ref = -INFINITY, l = 0.f;
+
+  if (warp == 0) {
+    if (lane == 0 && nblocks > 0) {
+      tma_prefetch_desc(&maps.k);
+      tma_prefetch_desc(&maps.v);
+      const uint64_t pol = l2_policy_evict_first();
+      int issued = 0;
+      for (int b = 0; b < nblocks; ++b) {
+        const int st = b % kTcAttnStages;
+        if (b >= kTcAttnStages && !mbar_wait(&kv_empty[st], ((b / kTcAttnStages) - 1) & 1)) {
+          report_error(a.status, kErrWaitTimeout);
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        mbar_arrive_expect_tx(&kv_full[st], Lay::STAGE);
+        const int row = h * a.max_slots + k_lo + b * KB;
+        uint8_t* dst = ring + st * Lay::STAGE;
+#pragma unroll
+        for (int g = 0; g < NR; ++g) tma_load_2d(dst + g * Lay::KV_REGION, &maps.k, &kv_full[st], g * 64, row, pol);
+#pragma unroll
+        for (int g = 0; g < NR; ++g)
+          tma_load_2d(dst + (NR + g) * Lay::KV_REGION, &maps.v, &kv_full[st], g * 64, row, pol);
+        ++issued;
+      }
+      if (*abort_flag) {  // let every copy already issued land before the CTA moves on
+        for (int b = (issued > kTcAttnStages ? issued - kTcAttnStages : 0); b < issued; ++b)
+          (void)mbar_wait(&kv_full[b % kTcAttnStages], (b / kTcAttnStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_s = idesc_bf16_f32(128, KB);
+      const uint32_t id_pv = idesc_bf16_f32_bmn(128, HD);
+      bool ok = mbar_wait(q_ready, 0);
+      if (!ok) {
+        report_error(a.status, kErrWaitTimeout);
+        *abort_flag = 1;
+      }
+      auto pv = [&](int j) {
+        if (!ok) return;
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1) || *abort_flag) {
+          report_error(a.status, kErrWaitTimeout);
+          *abort_flag = 1;
+          ok = false;
+          return;
+        }
+        tc_fence_after();
+        const uint32_t vb = ring_s + (j % kTcAttnStages) * Lay::STAGE + NR * Lay::KV_REGION;
+        const uint32_t pb = ps_s + (j & 1) * Lay::P_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < KB / 16; ++kk)
+          umma_bf16(tm_o, sdesc_k_sw128(pb + kk * 32), sdesc_mn_sw128(vb + kk * 2048, Lay::KV_REGION, 1024), id_pv,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&p_free[j & 1]);
+        umma_commit(&kv_empty[j % kTcAttnStages]);
+      };
+      for (int b = 0; b < nblocks && ok; ++b) {
+        const int st = b % kTcAttnStages;
+        if (!mbar_wait(&kv_full[st], (b / kTcAttnStages) & 1) ||
+            (b >= 2 && !mbar_wait(&s_free[b & 1], ((b >> 1) - 1) & 1)) || *abort_flag) {
+          report_error(a.status, kErrWaitTimeout);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kb = ring_s + st * Lay::STAGE;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t off = (ks & 3) * 32;
+          umma_bf16(tmem + (b & 1) * KB, sdesc_k_sw128(qs_s + (ks >> 2) * (128 * 128) + off),
+                    sdesc_k_sw128(kb + (ks >> 2) * Lay::KV_REGION + off), id_s, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[b & 1]);
+        if (b >= 1) pv(b - 1);
+      }
+      if (nblocks > 0) pv(nblocks - 1);
+      // Arrives once every MMA above has retired (also after an abort).
+      umma_commit(o_full);
+    }
+  } else {
+    // ---- softmax warps: thread = query row r
+    const int tok = row_ok ? (q0 + r) / a.G - t_first : 0;
+    const int plen = row_ok ? s_plen[tok] : 0;
+    const float sc = a.scale * 1.4426950408889634f;  // base 2
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    bool bad = false;
+    for (int b = 0; b < nblocks; ++b) {
+      const int sbuf = b & 1;
+      bad = !mbar_wait(&s_full[sbuf], (b >> 1) & 1) || *abort_flag;
+      if (__any_sync(0xffffffffu, bad)) {
+        if (lane == 0) {
+          report_error(a.status, kErrWaitTimeout);
+          *abort_flag = 1;
+        }
+        bad = true;
+        break;
+      }
+      tc_fence_after();
+      float sv[KB];
+      tmem_ld64(tmem + lane_base + sbuf * KB, sv);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sbuf]);
+      const int kb = k_lo + b * KB;
+      const uint64_t vbits = row_ok ? key_block_bits(kb, k_hi, plen, s_mask + tok * 4, mw, sb) : 0ull;
+      const uint32_t vlo = static_cast<uint32_t>(vbits), vhi = static_cast<uint32_t>(vbits >> 32);
+      float bmx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int j = 0; j < KB; ++j) {
+        const bool ok = ((j < 32 ? vlo >> j : vhi >> (j - 32)) & 1u) != 0u;
+        const float v = ok ? sv[j] * sc : -INFINITY;
+        sv[j] = v;
+        bmx[j & 3] = fmaxf(bmx[j & 3], v);
+      }
+      const float bm = fmaxf(fmaxf(bmx[0], bmx[1]), fmaxf(bmx[2], bmx[3]));
+      const bool grow = bm > m_ref + kLazyRescale || (m_ref == -INFINITY && bm > -INFINITY);
+      if (__any_sync(0xffffffffu, grow)) {
+        const float m_new = grow ? bm : m_ref;
+        const float alpha = (!grow || m_ref == -INFINITY) ? (grow ? 0.f : 1.f) : exp2f(m_ref - m_new);
+        if (b > 0) {
+          // O holds earlier blocks: rescale it once P V of block b - 1 is done
+          const bool w_ok = mbar_wait(&p_free[(b - 1) & 1], ((b - 1) >> 1) & 1);
+          if (!w_ok) report_error(a.status, kErrWaitTimeout);
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < HD / 64; ++c) {
+            float ov[64];
+            tmem_ld64(tm_o + lane_base + c * 64, ov);
+#pragma unroll
+            for (int i = 0; i < 64; ++i) ov[i] *= alpha;
+#pragma unroll
+            for (int i = 0; i < 64; i += 16) tmem_st16(tm_o + lane_base + c * 64 + i, ov + i);
+          }
+          tmem_wait_st();
+        }
+        l *= alpha;
+        m_ref = m_new;
+      }
+      uint32_t pk[KB / 2];
+      float lsx[4] = {0.f, 0.f, 0.f, 0.f};
+      const float mr = m_ref == -INFINITY ? 0.f : m_ref;  // a row with no key yet has only -inf scores
+#pragma unroll
+      for (int j = 0; j < KB; j += 2) {
+        const float p0 = ex2_fast(sv[j] - mr);
+        const float p1 = ex2_fast(sv[j + 1] - mr);
+        lsx[(j >> 1) & 3] += p0 + p1;
+        pk[j >> 1] = pack_bf16(p0, p1);
+      }
+      l += (lsx[0] + lsx[1]) + (lsx[2] + lsx[3]);
+      if (b >= 2) {
+        const bool w_ok = mbar_wait(&p_free[sbuf], ((b - 2) >> 1) & 1);  // P V of block b - 2 read this buffer
+        if (!w_ok) report_error(a.status, kErrWaitTimeout);
+      }
+      uint8_t* prow = ps + sbuf * Lay::P_BYTES + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[sbuf]);
+    }
+    (void)bad;
+  }
+  // ---- results: warps 2..5 read their O rows
+  float o[HD];
+#pragma unroll
+  for (int i = 0; i < HD; ++i) o[i] = 0.f;
+  if (warp >= 2) {
+    const bool w_ok = mbar_wait(o_full, 0);
+    if (!w_ok) report_error(a.status, kErrWaitTimeout);
+    tc_fence_after();
+    if (nblocks > 0 && w_ok && !*abort_flag) {
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) tmem_ld64(tm_o + (static_cast<uint32_t>(q * 32) << 16) + c * 64, o + c * 64);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+  bf16* outp = static_cast<bf16*>(a.out);
+  if (P == 1) {
+    if (row_ok) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int qr = q0 + r;
+      bf16* op = outp + (int64_t)(qr / a.G) * a.ldo + (int64_t)(h * a.G + qr % a.G) * HD;
+#pragma unroll
+      for (int d = 0; d < HD; d += 2) *reinterpret_cast<uint32_t*>(op + d) = pack_bf16(o[d] * inv, o[d + 1] * inv);
+    }
+    return;
+  }
+  const int rec = mma_rec(HD);
+  constexpr int DPL = HD / 32;
+  const int nwarps = kTcAttnThreads / 32;
+  auto merge_row = [&](int rr, auto&& rec_at) {
+    const int qr = q0 + rr;
+    float ms = -INFINITY, ls = 0.f;
+    if (lane < P) {
+      ms = rec_at(lane, 0);
+      ls = rec_at(lane, 1);
+    }
+    const float Mx = warp_max(ms);
+    const float wgt = (ms == -INFINITY || Mx == -INFINITY) ? 0.f : exp2f(ms - Mx);
+    const float L = warp_sum(ls * wgt);
+    float acc[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+    for (int p0 = 0; p0 < P; p0 += 8) {
+      float v[8][DPL];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) v[u][i] = (p0 + u < P) ? rec_at(p0 + u, 4 + lane * DPL + i) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float ws = __shfl_sync(0xffffffffu, wgt, (p0 + u) & 31);
+        if (p0 + u < P) {
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc[i] = fmaf(ws, v[u][i], acc[i]);
+        }
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    bf16* op = outp + (int64_t)(qr / a.G) * a.ldo + (int64_t)(h * a.G + qr % a.G) * HD + lane * DPL;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) op[i] = f2bf(acc[i] * inv);
+  };
+  if (a.cluster_merge) {
+    // Every slice of the cluster is past its key loop: the rings are free and
+    // become the receive areas. Push, barrier, merge locally.
+    cluster_sync_all();
+    const int ns = a.n_splits;
+    const int owned = (a.rows_per_group + ns - 1) / ns;
+    float* recv = reinterpret_cast<float*>(ring);
+    if (row_ok) {
+      const int owner = r % ns, j = r / ns;
+      const uint32_t base = dsmem_map(smem_u32(recv), static_cast<uint32_t>(owner)) +
+                            (uint32_t)(((split * owned + j) * rec) * 4);
+      dsmem_st4(base, m_ref, l, 0.f, 0.f);
+#pragma unroll
+      for (int d = 0; d < HD; d += 4) dsmem_st4(base + (uint32_t)(4 + d) * 4, o[d], o[d + 1], o[d + 2], o[d + 3]);
+    }
+    cluster_sync_all();
+    const int n_own = Mg > split ? (Mg - split + ns - 1) / ns : 0;
+    for (int j = warp; j < n_own; j += nwarps) {
+      auto at = [&](int pp, int f) { return recv[(pp * owned + j) * rec + f]; };
+      merge_row(split + j * ns, at);
+    }
+    return;
+  }
+  // Long contexts: records in the global workspace slot of (row group, slice).
+  float* recs = a.part + ((int64_t)blk * a.n_splits + split) * a.rows_per_group * rec;
+  if (row_ok) {
+    float* pr = recs + (int64_t)r * rec;
+    pr[0] = m_ref;
+    pr[1] = l;
+#pragma unroll
+    for (int d = 0; d < HD; d += 2) *reinterpret_cast<float2*>(pr + 4 + d) = make_float2(o[d], o[d + 1]);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(&a.counters[kAttnCounterBase + blk], 1u);
+    s_misc[2] = (prev == (uint32_t)(a.n_splits - 1)) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!s_misc[2]) return;
+  __threadfence();
+  const float* gbase = a.part + (int64_t)blk * a.n_splits * a.rows_per_group * rec;
+  for (int rr = warp; rr < Mg; rr += nwarps) {
+    auto at = [&](int pp, int f) { return __ldcg(gbase + ((int64_t)pp * a.rows_per_group + rr) * rec + f); };
+    merge_row(rr, at);
+  }
+  if (threadIdx.x == 0) a.counters[kAttnCounterBase + blk] = 0u;
+}
+
 // Clusters of `s` CTAs (one row group's key slices) that can be resident at
 // once, from the occupancy API; cached per kernel, size and device.
 int attn_resident_clusters(void (*kern)(const AttnArgs), int s, size_t smem, int threads) {
@@ -718,6 +1161,48 @@ int attn_resident_clusters(void (*kern)(const AttnArgs), int s, size_t smem, int
   std::lock_guard<std::mutex> lk(mu);
   cache[key] = n;
   return n;
+}
+
+int attn_resident_clusters_tc(void (*kern)(const AttnMaps, const AttnArgs), int s, size_t smem, int threads) {
+  static std::mutex mu;
+  static std::map<std::tuple<void*, int, size_t, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(reinterpret_cast<void*>(kern), s, smem, dev * 4096 + threads);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, s);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = s;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = n;
+  return n;
+}
+
+// bf16 tree attention with more than 16 query rows per KV head runs on the
+// tcgen05 kernel; SSD_ATTN=mma keeps every size on the mma.sync kernel.
+bool attn_use_tcgen05() {
+  static const bool v = [] {
+    const char* e = getenv("SSD_ATTN");
+    return !(e && e[0] == 'm');
+  }();
+  return v;
 }
 
 }  // namespace ssd
@@ -759,6 +1244,66 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
   a.scale = 1.0f / sqrtf((float)head_dim);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int sms = device_sms();
+  // More than one 16-row tile of queries per KV head: the tcgen05 kernel
+  // (measured faster from 32 rows up); decode-sized row counts stay on the
+  // warp-specialised mma.sync kernel, whose key lanes split the slice.
+  if (dtype == SSD_BF16 && (head_dim == 64 || head_dim == 128) && T * (n_heads / n_kv_heads) > 16 &&
+      attn_use_tcgen05()) {
+    // tcgen05 path: up to 128 query rows of a KV head per CTA (one M = 128
+    // tile), key slices merged in a cluster or through global memory.
+    const int64_t M = T * a.G;
+    a.groups = (int)((M + 127) / 128);
+    a.rows_per_group = (int)((M + a.groups - 1) / a.groups);
+    a.rt = 8;
+    a.kw = 1;
+    const int64_t blocks = (int64_t)a.n_kv * a.groups;
+    if (blocks > 16384) return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: too many row groups");
+    if ((int64_t)a.n_kv * max_slots > (int64_t)1 << 31)
+      return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: cache too large for a tensor map");
+    AttnMaps maps;
+    int rc = tma_map_bf16_2d(k_cache, (uint64_t)head_dim, (uint64_t)(a.n_kv * max_slots), (uint64_t)head_dim * 2, 64,
+                             &maps.k);
+    if (rc) return rc;
+    rc = tma_map_bf16_2d(v_cache, (uint64_t)head_dim, (uint64_t)(a.n_kv * max_slots), (uint64_t)head_dim * 2, 64,
+                         &maps.v);
+    if (rc) return rc;
+    if (cache_head_stride != max_slots * head_dim)
+      return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: K/V heads must be contiguous [n_kv, max_slots, hd]");
+    const size_t smem = head_dim == 128 ? TcAttnLayout<128>::SMEM : TcAttnLayout<64>::SMEM;
+    void (*kern)(const AttnMaps, const AttnArgs) = head_dim == 128 ? attn_tc_kernel<128> : attn_tc_kernel<64>;
+    static bool tset128 = false, tset64 = false;
+    bool& set = head_dim == 128 ? tset128 : tset64;
+    if (!set) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+      set = true;
+    }
+    int64_t splits = sms / blocks;
+    const int64_t by_len = (kv_bound + 255) / 256;
+    if (splits > by_len) splits = by_len;
+    if (kv_bound <= 8 * 1024) {
+      if (splits > kMaxAttnClusterSplits) splits = kMaxAttnClusterSplits;
+      while (splits > 1 && attn_resident_clusters_tc(kern, (int)splits, smem, kTcAttnThreads) < blocks) --splits;
+    } else {
+      int64_t want = (2 * sms) / blocks;
+      if (want > by_len) want = by_len;
+      if (want > splits) splits = want;
+    }
+    if (splits > kMaxPartials) splits = kMaxPartials;
+    if (splits < 1) splits = 1;
+    const int64_t split_len = ((kv_bound + splits - 1) / splits + 63) / 64 * 64;
+    a.split_len = (int)split_len;
+    a.n_splits = (int)((kv_bound + split_len - 1) / split_len);
+    a.cluster_merge = (a.n_splits > 1 && a.n_splits <= kMaxAttnClusterSplits && kv_bound <= 8 * 1024) ? 1 : 0;
+    if (a.n_splits > 1 && !a.cluster_merge) {
+      const int64_t need = kCounterBytes + blocks * a.n_splits * a.rows_per_group * mma_rec((int)head_dim) * 4;
+      if (!workspace || need > workspace_bytes)
+        return fail(SSD_ERR_WORKSPACE, "ssd_tree_attention: workspace too small (need %lld)", (long long)need);
+      a.counters = static_cast<uint32_t*>(workspace);
+      a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
+    }
+    return launch_kernel("attn_tc_kernel", kern, dim3((unsigned)blocks, (unsigned)a.n_splits), dim3(kTcAttnThreads),
+                         smem, s, 1u, a.cluster_merge ? (unsigned)a.n_splits : 1u, maps, a);
+  }
   if (dtype == SSD_BF16 && (head_dim == 64 || head_dim == 128)) {
     // Tensor-core path: all query rows of a KV head in as few CTAs as
     // possible (<= 8 row tiles of 16 per CTA); with fewer row tiles, up to 4

@@ -794,6 +794,11 @@ int tc_ctas_per_sm(int tiles_m, int kchunks, bool head, int sms) {
 
 }  // namespace
 
+int tma_map_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_outer,
+                    CUtensorMap* out) {
+  return get_map(base, inner, outer, row_stride_bytes, box_outer, out);
+}
+
 int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, const void* const* w,
                 const int64_t* rows, int layout, const EpiArgs& e, int dtype, void* workspace,
                 int64_t workspace_bytes, uint32_t* status, cudaStream_t stream, int64_t partial_offset_bytes) {

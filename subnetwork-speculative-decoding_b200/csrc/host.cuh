@@ -28,6 +28,10 @@ typedef CUresult (*TensorMapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint3
                                       const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 TensorMapEncodeFn tensor_map_encoder();
+// Cached 2-D bf16 tensor map: rows of `inner` elements, box {64, box_outer},
+// 128-byte swizzle (the K-major tcgen05 operand layout).
+int tma_map_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_outer,
+                    CUtensorMap* out);
 
 struct EpiArgs;
 // Shared GEMM launcher (gemm.cu). `partial_offset_bytes` reserves the start
