@@ -58,10 +58,34 @@ int ssd_device_sm_count(int device);
  * to `max_head_rows` rows, over a vocabulary of `vocab` tokens. */
 int64_t ssd_workspace_bytes(int64_t max_rows, int64_t max_head_rows, int64_t vocab);
 
+/* RMSNorm folded into the GEMMs around it (bf16 path).
+ * SsdNormOut: an epilogue that updates the fp32 residual also writes the
+ * input of the next RMSNorm's consumer, out[t, n] = resid[t, n] * weight[n]
+ * (bf16), and the sum of squares of resid[t, n] over each 128-feature tile i
+ * of row t into ssq[t * ld_ssq + i].
+ * SsdRowNorm: a GEMM whose input rows are such products scales output
+ * column t (token t) by rsqrt(sum_i ssq[t * ld + i] / d + eps) before its
+ * epilogue, which completes the RMSNorm (W (x_t w) s_t = W RMSNorm(x_t)).
+ * Either pointer argument may be NULL (no folding). */
+typedef struct SsdNormOut {
+  const void* weight;
+  void* out;
+  int64_t ldo;
+  float* ssq;
+  int64_t ld_ssq;
+} SsdNormOut;
+typedef struct SsdRowNorm {
+  const float* ssq;
+  int64_t ld;
+  int64_t parts;
+  int64_t d;
+  float eps;
+} SsdRowNorm;
+
 /* Embedding gather: resid[t, :] = table[ids[t], :] (fp32 out).
  * Replaces base.embed_tokens(input_ids), ssd/models/subnetwork_draft.py:290-291. */
 int ssd_embed(const int32_t* ids, int64_t T, const void* table, int64_t vocab, int64_t d, int dtype,
-              float* resid, uint32_t* status, void* stream);
+              float* resid, const SsdNormOut* norm_out, uint32_t* status, void* stream);
 
 /* RMSNorm of the fp32 residual stream into the GEMM activation dtype:
  * out = weight * (x * rsqrt(mean(x^2) + eps)).
@@ -84,7 +108,7 @@ enum { SSD_EPI_STORE = 0, SSD_EPI_RESIDUAL = 1, SSD_EPI_SWIGLU = 2, SSD_EPI_STOR
 int ssd_linear(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, const void* const* w,
                const int64_t* rows, const void* const* bias, int seg_layout, int epilogue, int act, void* out,
                int64_t ldo, float* resid, int64_t ldr, int dtype, void* workspace, int64_t workspace_bytes,
-               uint32_t* status, void* stream);
+               const SsdRowNorm* in_norm, const SsdNormOut* norm_out, uint32_t* status, void* stream);
 
 /* ssd_linear without a workspace, for callers that cannot allocate device
  * memory (a server that reserves all memory at start-up, a plain C caller
@@ -112,7 +136,7 @@ int ssd_qkv_rope(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w
                  int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, const float* rope_cos, const float* rope_sin,
                  int64_t max_pos, const int32_t* positions, const int32_t* slots, void* k_cache, void* v_cache,
                  int64_t cache_head_stride, int64_t max_slots, void* q_out, int64_t ldq, int dtype, void* workspace,
-                 int64_t workspace_bytes, uint32_t* status, void* stream);
+                 int64_t workspace_bytes, const SsdRowNorm* in_norm, uint32_t* status, void* stream);
 
 /* Tree attention over the shared cache (split-KV, GQA). Row t attends cache
  * slots [0, prefix_len[t]) and, if spec_mask is given, slot spec_base[0] + j
@@ -132,7 +156,7 @@ int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t n_heads, i
  * ssd/engine/speculative.py:81-84). */
 int ssd_head_argmax(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w, int64_t vocab,
                     int32_t* out_idx, float* out_max, float* out_gap, int dtype, void* workspace,
-                    int64_t workspace_bytes, uint32_t* status, void* stream);
+                    int64_t workspace_bytes, const SsdRowNorm* in_norm, uint32_t* status, void* stream);
 
 /* Draft head: (sub-vocab) lm_head fused with log_softmax + per-row top-k
  * (k <= 16). Column j of W is token vocab_ids[j] (identity if NULL).
@@ -141,7 +165,8 @@ int ssd_head_argmax(const void* x, int64_t ldx, int64_t T, int64_t K, const void
  * 347-349, tree_drafter.py:128-133). */
 int ssd_head_topk(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w, int64_t vocab,
                   const int64_t* vocab_ids, int64_t k, int32_t* out_tok, float* out_logprob, int dtype,
-                  void* workspace, int64_t workspace_bytes, uint32_t* status, void* stream);
+                  void* workspace, int64_t workspace_bytes, const SsdRowNorm* in_norm, uint32_t* status,
+                  void* stream);
 
 /* ---------------------------------------------------------------- tree ops
  * The tree lives in device arrays: tokens[i], parents[i] (-1 = root),

@@ -1274,7 +1274,7 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
     static bool tset128 = false, tset64 = false;
     bool& set = head_dim == 128 ? tset128 : tset64;
     if (!set) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+      allow_max_dynamic_smem(kern);
       set = true;
     }
     int64_t splits = sms / blocks;
@@ -1328,7 +1328,7 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
     static bool set128 = false, set64 = false;
     bool& set = head_dim == 128 ? set128 : set64;
     if (!set) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+      allow_max_dynamic_smem(kern);
       set = true;
     }
     int64_t splits = sms / blocks;
@@ -1387,14 +1387,14 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
   if (dtype == SSD_F32) {
     static bool set = false;
     if (!set) {
-      cudaFuncSetAttribute(attn_simt_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+      allow_max_dynamic_smem(attn_simt_kernel<float>);
       set = true;
     }
     return launch_kernel("attn_simt_kernel", attn_simt_kernel<float>, grid, dim3(256), smem, s, 1u, 1u, a);
   } else if (dtype == SSD_BF16) {
     static bool set = false;
     if (!set) {
-      cudaFuncSetAttribute(attn_simt_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+      allow_max_dynamic_smem(attn_simt_kernel<bf16>);
       set = true;
     }
     return launch_kernel("attn_simt_kernel", attn_simt_kernel<bf16>, grid, dim3(256), smem, s, 1u, 1u, a);

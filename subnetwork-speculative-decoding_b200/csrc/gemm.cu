@@ -714,7 +714,7 @@ int choose_splits(int tiles_m, int kchunks, int cta_slots) {
 void set_tc_attributes() {
   static bool done = false;
   if (!done) {
-    cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    allow_max_dynamic_smem(tc_gemm_kernel);
     done = true;
   }
 }
@@ -740,7 +740,7 @@ bool sk_enabled() {
 }
 constexpr int kSkBarBytes = 512;
 int sk_stages(int BN) {
-  const int budget = sk_ctas_per_sm() == 2 ? 113 * 1024 : 232448;
+  const int budget = (sk_ctas_per_sm() == 2 ? 113 * 1024 : 232448) - 1024;  // static epilogue scales
   const int avail = budget - 1024 - kSkBarBytes - BN * kTileM * 4;
   const int st = avail / tc_stage_bytes(BN);
   return st > 16 ? 16 : (st < 2 ? 2 : st);
@@ -758,7 +758,9 @@ size_t sk_smem_bytes(int BN, int stages) {
 // (q/k/v: 4 -> 8) or fewer waves (lm_head: 1002 tiles).
 int tc_ctas_per_sm(int tiles_m, int kchunks, bool head, int sms);
 int tc_stages(int BN, int per_sm) {
-  const int budget = (233472 - per_sm * 1024) / per_sm - 1024 - 256;
+  // per CTA: 1 KB reserved by the system, 1 KB of static shared memory (the
+  // epilogue's row-norm scales), alignment slack and barriers
+  const int budget = (233472 - per_sm * 2048) / per_sm - 1024 - 256;
   const int stages = budget / tc_stage_bytes(BN);
   return stages > 8 ? 8 : (stages < 2 ? 2 : stages);
 }
@@ -901,7 +903,7 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
       g.splits = 1;
       static bool sk_attr = false;
       if (!sk_attr) {
-        cudaFuncSetAttribute(tc_gemm_sk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+        allow_max_dynamic_smem(tc_gemm_sk_kernel);
         sk_attr = true;
       }
       return launch_kernel("tc_gemm_sk_kernel", tc_gemm_sk_kernel, dim3((unsigned)G), dim3(kTcThreads),

@@ -55,6 +55,16 @@ struct EpiArgs {
   // lm_head partial reductions: [T][tiles_m][rec]
   float* part;
   int topk;
+  // RMSNorm folding (SsdRowNorm / SsdNormOut of the C ABI)
+  const float* rn_ssq;  // input rows are resid * w: scale column t by rsqrt(sum ssq[t] / d + eps)
+  int64_t rn_ld;
+  int rn_parts, rn_d;
+  float rn_eps;
+  const void* no_w;  // residual epilogue also writes no_out = resid * no_w and per-tile sums of squares
+  void* no_out;
+  int64_t no_ldo;
+  float* no_ssq;
+  int64_t no_ld;
 };
 
 struct GemmShape {
@@ -99,6 +109,48 @@ template <typename T>
 __device__ void run_epilogue(float* stage, int tile_m, int t0, int ncols, const GemmShape& g, const EpiArgs& e,
                              int tid, int bar_id, int c0 = 0, int cstep = 1) {
   const int r = tid;
+  if (e.rn_ssq) {
+    // Folded RMSNorm of the input rows: scale token column c by
+    // rsqrt(mean of squares + eps), the sums taken in tile order.
+    __shared__ float s_scale[256];
+    const int nsub = ncols > c0 ? (ncols - c0 + cstep - 1) / cstep : 0;
+    for (int j = tid; j < nsub; j += kTileM) {
+      const float* ss = e.rn_ssq + (int64_t)(t0 + c0 + j * cstep) * e.rn_ld;
+      float acc = 0.f;
+      for (int i = 0; i < e.rn_parts; ++i) acc += ss[i];
+      s_scale[j] = rsqrtf(acc / (float)e.rn_d + e.rn_eps);
+    }
+    named_bar_sync(bar_id, kTileM);
+    for (int j = 0; j < nsub; ++j) stage[(c0 + j * cstep) * kTileM + r] *= s_scale[j];
+    named_bar_sync(bar_id, kTileM);
+  }
+  if (e.kind == EPI_RESIDUAL && e.no_w) {
+    // Residual update that also produces the next RMSNorm's input
+    // (resid * w, bf16) and this tile's sums of squares per token.
+    const int n = tile_m * kTileM + r;
+    const bool in = n < g.N;
+    const int s = in ? seg_of(g, n) : 0;
+    const float b = in ? load_bias<T>(e.bias[s], n - g.seg_start[s]) : 0.f;
+    const float wn = in ? to_f32<T>(static_cast<const T*>(e.no_w)[n]) : 0.f;
+    for (int c = c0; c < ncols; c += cstep) {
+      const int t = t0 + c;
+      float rn = 0.f;
+      if (in) {
+        rn = e.resid[(int64_t)t * e.ldr + n] + stage[c * kTileM + r] + b;
+        e.resid[(int64_t)t * e.ldr + n] = rn;
+        static_cast<T*>(e.no_out)[(int64_t)t * e.no_ldo + n] = from_f32<T>(rn * wn);
+      }
+      stage[c * kTileM + r] = rn * rn;
+    }
+    named_bar_sync(bar_id, kTileM);
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int c = c0 + warp * cstep; c < ncols; c += 4 * cstep) {
+      const float* col = stage + c * kTileM;
+      const float v = warp_sum((col[lane] + col[lane + 32]) + (col[lane + 64] + col[lane + 96]));
+      if (lane == 0) e.no_ssq[(int64_t)(t0 + c) * e.no_ld + tile_m] = v;
+    }
+    return;
+  }
   switch (e.kind) {
     case EPI_STORE:
     case EPI_STORE_F32:

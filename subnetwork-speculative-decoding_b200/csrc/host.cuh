@@ -28,6 +28,15 @@ typedef CUresult (*TensorMapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint3
                                       const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 TensorMapEncodeFn tensor_map_encoder();
+// Lets `kern` use all the shared memory a block may have: 227 KB minus the
+// kernel's static shared memory (the attribute call fails outright if the
+// sum would exceed the limit, which would leave the 48 KB default).
+template <typename Kern>
+inline void allow_max_dynamic_smem(Kern kern) {
+  cudaFuncAttributes at{};
+  cudaFuncGetAttributes(&at, kern);
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - (int)at.sharedSizeBytes);
+}
 // Cached 2-D bf16 tensor map: rows of `inner` elements, box {64, box_outer},
 // 128-byte swizzle (the K-major tcgen05 operand layout).
 int tma_map_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_outer,

@@ -9,7 +9,7 @@ namespace ssd {
 // ---------------------------------------------------------------- embedding
 template <typename T>
 __global__ void embed_kernel(const int32_t* ids, const T* table, int64_t vocab, int64_t d, float* out,
-                             uint32_t* status) {
+                             SsdNormOut no, uint32_t* status) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
@@ -19,7 +19,32 @@ __global__ void embed_kernel(const int32_t* ids, const T* table, int64_t vocab, 
     id = 0;
   }
   const T* row = table + (int64_t)id * d;
-  for (int64_t i = threadIdx.x; i < d; i += blockDim.x) out[(int64_t)t * d + i] = to_f32<T>(row[i]);
+  if (!no.weight) {
+    for (int64_t i = threadIdx.x; i < d; i += blockDim.x) out[(int64_t)t * d + i] = to_f32<T>(row[i]);
+    return;
+  }
+  // also the next RMSNorm's input (row * w) and per-128-feature sums of
+  // squares, in the same tile partition as the GEMM epilogues (warp k sums
+  // tiles k, k + 8, ... with a fixed shuffle order)
+  const T* w = static_cast<const T*>(no.weight);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = (int)((d + 127) / 128);
+  for (int tl = warp; tl < tiles; tl += blockDim.x / 32) {
+    float sq[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t i = (int64_t)tl * 128 + lane + 32 * k;
+      float v = 0.f;
+      if (i < d) {
+        v = to_f32<T>(row[i]);
+        out[(int64_t)t * d + i] = v;
+        static_cast<T*>(no.out)[(int64_t)t * no.ldo + i] = from_f32<T>(v * to_f32<T>(w[i]));
+      }
+      sq[k] = v * v;
+    }
+    const float ssq = warp_sum((sq[0] + sq[1]) + (sq[2] + sq[3]));
+    if (lane == 0) no.ssq[(int64_t)t * no.ld_ssq + tl] = ssq;
+  }
 }
 
 // ------------------------------------------------------------------ RMSNorm
@@ -248,15 +273,21 @@ int64_t ssd_workspace_bytes(int64_t max_rows, int64_t max_head_rows, int64_t voc
 }
 
 int ssd_embed(const int32_t* ids, int64_t T, const void* table, int64_t vocab, int64_t d, int dtype, float* resid,
-              uint32_t* status, void* stream) {
+              const SsdNormOut* norm_out, uint32_t* status, void* stream) {
   if (T <= 0 || d <= 0 || !ids || !table || !resid) return fail(SSD_ERR_INVALID, "ssd_embed: bad arguments");
+  SsdNormOut no{};
+  if (norm_out && norm_out->weight) {
+    if (dtype != SSD_BF16 || !norm_out->out || !norm_out->ssq)
+      return fail(SSD_ERR_INVALID, "ssd_embed: norm output needs bf16, out and ssq");
+    no = *norm_out;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SSD_F32)
     return launch_kernel("embed_kernel", embed_kernel<float>, dim3((unsigned)T), dim3(256), 0, s, 1, 1, ids,
-                         static_cast<const float*>(table), vocab, d, resid, status);
+                         static_cast<const float*>(table), vocab, d, resid, no, status);
   else if (dtype == SSD_BF16)
     return launch_kernel("embed_kernel", embed_kernel<bf16>, dim3((unsigned)T), dim3(256), 0, s, 1, 1, ids,
-                         static_cast<const bf16*>(table), vocab, d, resid, status);
+                         static_cast<const bf16*>(table), vocab, d, resid, no, status);
   else
     return fail(SSD_ERR_UNSUPPORTED, "ssd_embed: dtype %d", dtype);
   return check_launch("embed_kernel");
@@ -277,10 +308,33 @@ int ssd_rmsnorm(const float* x, int64_t T, int64_t d, int64_t ldx, const void* w
   return check_launch("rmsnorm_kernel");
 }
 
+// Copies the C ABI's RMSNorm-folding arguments into the epilogue arguments.
+static int set_norms(EpiArgs& e, const SsdRowNorm* in_norm, const SsdNormOut* norm_out, int dtype, const char* who) {
+  if (in_norm && in_norm->ssq) {
+    if (dtype != SSD_BF16 || in_norm->parts <= 0 || in_norm->d <= 0)
+      return fail(SSD_ERR_INVALID, "%s: row norm needs bf16, parts > 0 and d > 0", who);
+    e.rn_ssq = in_norm->ssq;
+    e.rn_ld = in_norm->ld;
+    e.rn_parts = (int)in_norm->parts;
+    e.rn_d = (int)in_norm->d;
+    e.rn_eps = in_norm->eps;
+  }
+  if (norm_out && norm_out->weight) {
+    if (dtype != SSD_BF16 || e.kind != EPI_RESIDUAL || !norm_out->out || !norm_out->ssq)
+      return fail(SSD_ERR_INVALID, "%s: norm output needs bf16, the residual epilogue, out and ssq", who);
+    e.no_w = norm_out->weight;
+    e.no_out = norm_out->out;
+    e.no_ldo = norm_out->ldo;
+    e.no_ssq = norm_out->ssq;
+    e.no_ld = norm_out->ld_ssq;
+  }
+  return SSD_OK;
+}
+
 int ssd_linear(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, const void* const* w,
                const int64_t* rows, const void* const* bias, int seg_layout, int epilogue, int act, void* out,
                int64_t ldo, float* resid, int64_t ldr, int dtype, void* workspace, int64_t workspace_bytes,
-               uint32_t* status, void* stream) {
+               const SsdRowNorm* in_norm, const SsdNormOut* norm_out, uint32_t* status, void* stream) {
   EpiArgs e{};
   e.kind = epilogue;
   e.act = act;
@@ -305,6 +359,7 @@ int ssd_linear(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, cons
   }
   if (seg_layout == SSD_SEG_PAIRS && epilogue != SSD_EPI_SWIGLU)
     return fail(SSD_ERR_INVALID, "ssd_linear: PAIRS layout is only for SwiGLU");
+  if (const int rc = set_norms(e, in_norm, norm_out, dtype, "ssd_linear")) return rc;
   return launch_gemm(x, ldx, T, K, n_seg, w, rows, seg_layout, e, dtype, workspace, workspace_bytes, status,
                      static_cast<cudaStream_t>(stream), 0);
 }
@@ -313,7 +368,7 @@ int ssd_qkv_rope(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w
                  int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, const float* rope_cos, const float* rope_sin,
                  int64_t max_pos, const int32_t* positions, const int32_t* slots, void* k_cache, void* v_cache,
                  int64_t cache_head_stride, int64_t max_slots, void* q_out, int64_t ldq, int dtype, void* workspace,
-                 int64_t workspace_bytes, uint32_t* status, void* stream) {
+                 int64_t workspace_bytes, const SsdRowNorm* in_norm, uint32_t* status, void* stream) {
   if (head_dim <= 0 || head_dim > 128 || (128 % head_dim) || (head_dim & 1))
     return fail(SSD_ERR_UNSUPPORTED, "ssd_qkv_rope: head_dim must divide 128");
   if (!positions || !slots || !k_cache || !v_cache || !q_out || !rope_cos || !rope_sin)
@@ -334,6 +389,7 @@ int ssd_qkv_rope(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w
   e.v_cache = v_cache;
   e.head_stride = cache_head_stride;
   e.max_slots = (int)max_slots;
+  if (const int rc = set_norms(e, in_norm, nullptr, dtype, "ssd_qkv_rope")) return rc;
   const void* w[3] = {wq, wk, wv};
   int64_t rows[3] = {n_heads * head_dim, n_kv_heads * head_dim, n_kv_heads * head_dim};
   return launch_gemm(x, ldx, T, K, 3, w, rows, SSD_SEG_CONCAT, e, dtype, workspace, workspace_bytes, status,
@@ -342,7 +398,7 @@ int ssd_qkv_rope(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w
 
 int ssd_head_argmax(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w, int64_t vocab,
                     int32_t* out_idx, float* out_max, float* out_gap, int dtype, void* workspace,
-                    int64_t workspace_bytes, uint32_t* status, void* stream) {
+                    int64_t workspace_bytes, const SsdRowNorm* in_norm, uint32_t* status, void* stream) {
   const int64_t tiles = (vocab + kTileM - 1) / kTileM;
   const int64_t need = kCounterBytes + T * tiles * 3 * 4;
   if (!workspace || need > workspace_bytes) return fail(SSD_ERR_WORKSPACE, "ssd_head_argmax: workspace too small");
@@ -350,6 +406,7 @@ int ssd_head_argmax(const void* x, int64_t ldx, int64_t T, int64_t K, const void
   EpiArgs e{};
   e.kind = EPI_ARGMAX;
   e.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
+  if (const int rc = set_norms(e, in_norm, nullptr, dtype, "ssd_head_argmax")) return rc;
   const void* ws[1] = {w};
   int64_t rows[1] = {vocab};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -362,7 +419,8 @@ int ssd_head_argmax(const void* x, int64_t ldx, int64_t T, int64_t K, const void
 
 int ssd_head_topk(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w, int64_t vocab,
                   const int64_t* vocab_ids, int64_t k, int32_t* out_tok, float* out_logprob, int dtype,
-                  void* workspace, int64_t workspace_bytes, uint32_t* status, void* stream) {
+                  void* workspace, int64_t workspace_bytes, const SsdRowNorm* in_norm, uint32_t* status,
+                  void* stream) {
   if (k < 1 || k > kMaxTopK || k > vocab) return fail(SSD_ERR_UNSUPPORTED, "ssd_head_topk: k must be 1..16");
   const int64_t tiles = (vocab + kTileM - 1) / kTileM;
   const int64_t rec = 2 + 2 * k;
@@ -374,6 +432,7 @@ int ssd_head_topk(const void* x, int64_t ldx, int64_t T, int64_t K, const void* 
   e.kind = EPI_TOPK;
   e.topk = (int)k;
   e.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
+  if (const int rc = set_norms(e, in_norm, nullptr, dtype, "ssd_head_topk")) return rc;
   const void* ws[1] = {w};
   int64_t rows[1] = {vocab};
   cudaStream_t s = static_cast<cudaStream_t>(stream);

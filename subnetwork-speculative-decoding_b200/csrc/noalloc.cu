@@ -81,5 +81,5 @@ extern "C" int ssd_linear_noalloc(const void* x, int64_t ldx, int64_t T, int64_t
   if (cudaMemsetAsync(scratch, 0, kCounterBytes, s) != cudaSuccess)
     return fail(SSD_ERR_CUDA, "ssd_linear_noalloc: clearing the split counters failed");
   return ssd_linear(x, ldx, T, K, n_seg, w, rows, bias, seg_layout, epilogue, act, out, ldo, resid, ldr, dtype,
-                    scratch, kNoAllocScratchBytes, status, stream);
+                    scratch, kNoAllocScratchBytes, nullptr, nullptr, status, stream);
 }

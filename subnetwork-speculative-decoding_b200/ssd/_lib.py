@@ -24,22 +24,32 @@ ACT = {"none": 0, "silu": 1, "gelu": 2, "relu": 3}
 SEG_CONCAT, SEG_PAIRS = 0, 1
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_STORE_F32 = 0, 1, 2, 3
 
+class SsdNormOut(C.Structure):
+    """include/ssd_b200.h SsdNormOut: next RMSNorm input written by a residual epilogue."""
+    _fields_ = [("weight", P), ("out", P), ("ldo", I64), ("ssq", P), ("ld_ssq", I64)]
+
+
+class SsdRowNorm(C.Structure):
+    """include/ssd_b200.h SsdRowNorm: per-row RMSNorm scale applied in a GEMM epilogue."""
+    _fields_ = [("ssq", P), ("ld", I64), ("parts", I64), ("d", I64), ("eps", F32)]
+
+
 # name -> (restype, argtypes); mirrors include/ssd_b200.h
 SIGNATURES: dict[str, tuple] = {
     "ssd_version": (I32, []),
     "ssd_last_error": (C.c_char_p, []),
     "ssd_device_sm_count": (I32, [I32]),
     "ssd_workspace_bytes": (I64, [I64, I64, I64]),
-    "ssd_embed": (I32, [P, I64, P, I64, I64, I32, P, P, P]),
+    "ssd_embed": (I32, [P, I64, P, I64, I64, I32, P, P, P, P]),
     "ssd_rmsnorm": (I32, [P, I64, I64, I64, P, F32, P, I64, I32, P]),
-    "ssd_linear": (I32, [P, I64, I64, I64, I32, P, P, P, I32, I32, I32, P, I64, P, I64, I32, P, I64, P, P]),
+    "ssd_linear": (I32, [P, I64, I64, I64, I32, P, P, P, I32, I32, I32, P, I64, P, I64, I32, P, I64, P, P, P, P]),
     "ssd_linear_noalloc": (I32, [P, I64, I64, I64, I32, P, P, P, I32, I32, I32, P, I64, P, I64, I32, P, P]),
     "ssd_qkv_rope": (I32, [P, I64, I64, I64, P, P, P, I64, I64, I64, P, P, I64, P, P, P, P, I64, I64, P, I64, I32,
-                           P, I64, P, P]),
+                           P, I64, P, P, P]),
     "ssd_tree_attention": (I32, [P, I64, I64, I64, I64, I64, P, P, I64, I64, P, P, P, I64, I64, P, I64, I32, P, I64,
                                  P, P]),
-    "ssd_head_argmax": (I32, [P, I64, I64, I64, P, I64, P, P, P, I32, P, I64, P, P]),
-    "ssd_head_topk": (I32, [P, I64, I64, I64, P, I64, P, I64, P, P, I32, P, I64, P, P]),
+    "ssd_head_argmax": (I32, [P, I64, I64, I64, P, I64, P, P, P, I32, P, I64, P, P, P]),
+    "ssd_head_topk": (I32, [P, I64, I64, I64, P, I64, P, I64, P, P, I32, P, I64, P, P, P]),
     "ssd_level_prune": (I32, [P, P, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, I64, P, I32, I64, P, P, P, P, P,
                               P, I64, P, P]),
     "ssd_tree_prune": (I32, [P, I64, P, P, P, P, P, P, I64, P]),

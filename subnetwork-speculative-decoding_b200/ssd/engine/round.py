@@ -129,10 +129,10 @@ class _Decoder:
         fwd.fill(prompt.reshape(-1), torch.arange(P), 0, None)
         scratch = R.Scratch(w, P)
         ws = ops.Workspace(self.device, max_rows=P, vocab=w.V, max_head_rows=1)
-        R.run_stack(w, self.target.layer_indices, [None] * len(self.target.layer_indices), None, fwd, P, self.cache,
-                    scratch, ws, self.cache.max_length)
-        xn = R.final_norm(w, scratch, P - 1, P)
-        self._first_token(xn, ws)
+        R.run_stack_auto(w, self.target.layer_indices, [None] * len(self.target.layer_indices), None, fwd, P,
+                         self.cache, scratch, ws, self.cache.max_length)
+        xn, rn = R.head_input(w, scratch, P - 1, P)
+        self._first_token(xn, ws, rn)
         self.state.zero_()
         self.state[SEQ] = P
         self.state[ROOT_TOK:ROOT_TOK + 1].copy_(self.argmax[:1])
@@ -142,10 +142,12 @@ class _Decoder:
         ws.check_status()
         self.cache.seq_len = P
 
-    def _first_token(self, xn: torch.Tensor, ws: ops.Workspace) -> None:
+    def _first_token(self, xn: torch.Tensor, ws: ops.Workspace, rn=None) -> None:
         """First generated token from the last prompt row into argmax[0]
-        (_first_token, speculative.py:81-84; greedy here)."""
-        ops.head_argmax(xn, self.w.lm_head, self.argmax[:1], ws, out_max=self.amax[:1], out_gap=self.gap[:1])
+        (_first_token, speculative.py:81-84; greedy here). rn: the folded
+        final RMSNorm of xn, if any."""
+        ops.head_argmax(xn, self.w.lm_head, self.argmax[:1], ws, out_max=self.amax[:1], out_gap=self.gap[:1],
+                        in_norm=rn)
 
     def _capture(self, fn) -> torch.cuda.CUDAGraph:
         g = torch.cuda.CUDAGraph()
@@ -178,16 +180,17 @@ class TargetStep(_Decoder):
         w = self.w
         st = self.state
         ops.causal_prep(st[SEQ:SEQ + 1], 1, st[ROOT_TOK:ROOT_TOK + 1], self.fwd_root)
-        R.run_stack(w, self.target.layer_indices, [None] * len(self.target.layer_indices), None, self.fwd_root, 1,
-                    self.cache, self.scratch, self.ws, self.cache.max_length)
-        xn = R.final_norm(w, self.scratch, 0, 1)
-        self._next_token(xn)
+        R.run_stack_auto(w, self.target.layer_indices, [None] * len(self.target.layer_indices), None, self.fwd_root,
+                         1, self.cache, self.scratch, self.ws, self.cache.max_length)
+        xn, rn = R.head_input(w, self.scratch, 0, 1)
+        self._next_token(xn, rn)
         ops.round_commit(st[ZERO:ZERO + 1], self.argmax, self.out_tokens, self.argmax[:1], st[SEQ:SEQ + 1],
                          st[ROOT_TOK:ROOT_TOK + 1], self.out_tokens, st[N_OUT:N_OUT + 1], None, self.ws.status)
 
-    def _next_token(self, xn: torch.Tensor) -> None:
+    def _next_token(self, xn: torch.Tensor, rn=None) -> None:
         """Next token into argmax[0]: lm_head fused with the argmax."""
-        ops.head_argmax(xn, self.w.lm_head, self.argmax[:1], self.ws, out_max=self.amax[:1], out_gap=self.gap[:1])
+        ops.head_argmax(xn, self.w.lm_head, self.argmax[:1], self.ws, out_max=self.amax[:1], out_gap=self.gap[:1],
+                        in_norm=rn)
 
     def run(self, n_steps: int, use_graph: bool = True) -> None:
         if use_graph:
@@ -236,18 +239,19 @@ class GreedyRound(_Decoder):
                 raise ValueError("bridges must live on the model's device")
 
     # --------------------------------------------------------------- phases
-    def _draft_forward(self, fwd, T: int) -> torch.Tensor:
+    def _draft_forward(self, fwd, T: int):
+        """Draft sub-network forward; returns the head input (x, folded norm or None)."""
         d = self.draft
-        R.run_stack(self.w, d.layer_indices, d.pre_layer_bridge_modules(), d.pre_norm_bridge_module(), fwd, T,
-                    self.cache, self.scratch, self.ws, self.cache.max_length)
-        return R.final_norm(self.w, self.scratch, 0, T)
+        R.run_stack_auto(self.w, d.layer_indices, d.pre_layer_bridge_modules(), d.pre_norm_bridge_module(), fwd, T,
+                         self.cache, self.scratch, self.ws, self.cache.max_length)
+        return R.head_input(self.w, self.scratch, 0, T)
 
     def draft_phase(self) -> None:
         """TreeDrafter.build (tree_drafter.py:147-208) on the device."""
         p, st = self.plan, self.state
         ops.causal_prep(st[SEQ:SEQ + 1], 1, st[ROOT_TOK:ROOT_TOK + 1], self.fwd_root)
-        xn = self._draft_forward(self.fwd_root, 1)
-        self._propose(xn, 0, 1, p.branch[0], self.topk_tok[0], self.topk_lp[0])
+        xn, rn = self._draft_forward(self.fwd_root, 1)
+        self._propose(xn, 0, 1, p.branch[0], self.topk_tok[0], self.topk_lp[0], rn)
         self.tree.n_nodes.zero_()
         for d in range(p.depth):
             frontier = self.root_frontier if d == 0 else self.level_nodes[d - 1]
@@ -256,34 +260,34 @@ class GreedyRound(_Decoder):
                             self.level_nodes[d], self.tree, st[SEQ:SEQ + 1], p.fed[d], p.slot_offsets[d],
                             self.fwd_level[d], self.ws.status)
             if p.fed[d]:
-                xn = self._draft_forward(self.fwd_level[d], p.level_sizes[d])
+                xn, rn = self._draft_forward(self.fwd_level[d], p.level_sizes[d])
                 self._propose(xn, 1 + p.slot_offsets[d], p.level_sizes[d], p.branch[d + 1], self.topk_tok[d + 1],
-                              self.topk_lp[d + 1])
+                              self.topk_lp[d + 1], rn)
         ops.tree_prune(self.tree, p.cfg.max_nodes)
 
     def _propose(self, xn: torch.Tensor, row0: int, T: int, k: int, out_tok: torch.Tensor,
-                 out_lp: torch.Tensor) -> None:
+                 out_lp: torch.Tensor, rn=None) -> None:
         """k children per draft row (TreeDrafter._propose, tree_drafter.py:124-132
         for greedy): the draft head fused with a log-softmax top-k. `row0` is
         the row's index among the round's draft rows (0 = root)."""
-        ops.head_topk(xn, self.head_w, k, out_tok, out_lp, self.ws, vocab_ids=self.vocab_ids)
+        ops.head_topk(xn, self.head_w, k, out_tok, out_lp, self.ws, vocab_ids=self.vocab_ids, in_norm=rn)
 
     def verify_phase(self) -> None:
         """verify_inputs + target forward + greedy_verify (verify.py:32-57)."""
         p, st, w = self.plan, self.state, self.w
         ops.verify_prep(self.tree, p.rows, st[ROOT_TOK:ROOT_TOK + 1], st[SEQ:SEQ + 1], self.fwd_verify,
                         self.ws.status)
-        R.run_stack(w, self.target.layer_indices, [None] * len(self.target.layer_indices), None, self.fwd_verify,
-                    p.rows, self.cache, self.scratch, self.ws, self.cache.max_length)
-        xn = R.final_norm(w, self.scratch, 0, p.rows)
-        self._walk(xn)
+        R.run_stack_auto(w, self.target.layer_indices, [None] * len(self.target.layer_indices), None,
+                         self.fwd_verify, p.rows, self.cache, self.scratch, self.ws, self.cache.max_length)
+        xn, rn = R.head_input(w, self.scratch, 0, p.rows)
+        self._walk(xn, rn)
 
-    def _walk(self, xn: torch.Tensor) -> None:
+    def _walk(self, xn: torch.Tensor, rn=None) -> None:
         """Target head over root + tree rows, then the acceptance walk
         (greedy_verify, verify.py:45-57): lm_head fused with the argmax."""
         p, st, w = self.plan, self.state, self.w
         ops.head_argmax(xn, w.lm_head, self.argmax[: p.rows], self.ws, out_max=self.amax[: p.rows],
-                        out_gap=self.gap[: p.rows])
+                        out_gap=self.gap[: p.rows], in_norm=rn)
         ops.tree_walk_greedy(self.tree, self.argmax, st[SEQ:SEQ + 1], self.accepted, st[N_ACC:N_ACC + 1],
                              st[BONUS:BONUS + 1], self.keep_slots, st[N_KEEP:N_KEEP + 1], p.n_verify)
 

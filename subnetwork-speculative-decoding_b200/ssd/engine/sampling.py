@@ -70,10 +70,10 @@ class _SamplingState:
     def set_seed(self, seed: int) -> None:
         self.seed_buf.fill_(_as_i64(int(seed) & 0xFFFFFFFFFFFFFFFF))
 
-    def _first_token(self, xn: torch.Tensor, ws: ops.Workspace) -> None:
+    def _first_token(self, xn: torch.Tensor, ws: ops.Workspace, rn=None) -> None:
         """_first_token with temperature > 0 (speculative.py:81-84): lm_head
         logits of the last prompt row, then one warped draw (round 0)."""
-        ops.linear(xn, [self.w.lm_head], ws, epilogue=L.EPI_STORE_F32, out=self.logits1, T=1)
+        ops.linear(xn, [self.w.lm_head], ws, epilogue=L.EPI_STORE_F32, out=self.logits1, T=1, in_norm=rn)
         ops.sample_token(self.logits1[0], self.temperature, self.top_p, self.seed_buf, None, 0, STREAM_TOKEN,
                          self.p_scratch, self.argmax[:1])
 
@@ -87,9 +87,9 @@ class SampledTargetStep(_SamplingState, TargetStep):
         TargetStep.__init__(self, target, cache, max_new)
         self._init_sampling(temperature, top_p, seed)
 
-    def _next_token(self, xn: torch.Tensor) -> None:
+    def _next_token(self, xn: torch.Tensor, rn=None) -> None:
         st = self.state
-        ops.linear(xn, [self.w.lm_head], self.ws, epilogue=L.EPI_STORE_F32, out=self.logits1, T=1)
+        ops.linear(xn, [self.w.lm_head], self.ws, epilogue=L.EPI_STORE_F32, out=self.logits1, T=1, in_norm=rn)
         ops.sample_token(self.logits1[0], self.temperature, self.top_p, self.seed_buf, st[N_OUT:N_OUT + 1], 0,
                          STREAM_TOKEN, self.p_scratch, self.argmax[:1])
 
@@ -113,20 +113,20 @@ class SampledRound(_SamplingState, GreedyRound):
         self.tparams = ops.warp_params_buffer(p.rows, dev)
         self.q_scratch = torch.zeros(self.w.V, **f32)
 
-    def _propose(self, xn, row0, T, k, out_tok, out_lp) -> None:
+    def _propose(self, xn, row0, T, k, out_tok, out_lp, rn=None) -> None:
         """_propose with sampling (tree_drafter.py:134-145): draft logits ->
         warp parameters -> k draws without replacement per row."""
         rows = self.dlogits[row0:row0 + T]
         prm = self.dparams[row0:row0 + T]
-        ops.linear(xn, [self.head_w], self.ws, epilogue=L.EPI_STORE_F32, out=rows, T=T)
+        ops.linear(xn, [self.head_w], self.ws, epilogue=L.EPI_STORE_F32, out=rows, T=T, in_norm=rn)
         ops.warp_params(rows, self.temperature, self.top_p, prm)
         ops.gumbel_topk(rows, prm, k, self.seed_buf, self.round_log[0:1], row0, out_tok, out_lp,
                         vocab_ids=self.vocab_ids)
 
-    def _walk(self, xn) -> None:
+    def _walk(self, xn, rn=None) -> None:
         """sample_verify (verify.py:60-95) on the device."""
         p, st = self.plan, self.state
-        ops.linear(xn, [self.w.lm_head], self.ws, epilogue=L.EPI_STORE_F32, out=self.tlogits, T=p.rows)
+        ops.linear(xn, [self.w.lm_head], self.ws, epilogue=L.EPI_STORE_F32, out=self.tlogits, T=p.rows, in_norm=rn)
         ops.warp_params(self.tlogits, self.temperature, self.top_p, self.tparams)
         ops.tree_walk_sample(self.tree, self.tlogits, self.tparams, self.dlogits, self.dparams, self.draft_rows,
                              self.seed_buf, self.round_log[0:1], self.p_scratch, self.q_scratch, st[SEQ:SEQ + 1],

@@ -170,6 +170,20 @@ class ForwardInputs:
         self.use_mask = width > 0
 
 
+def norm_parts(w) -> int:
+    """Partial sums of squares per row (one per 128-feature tile)."""
+    return (w.d + 127) // 128
+
+
+def folds_norms(w) -> bool:
+    """bf16 forwards fold every RMSNorm into the GEMMs next to it: the
+    residual-updating epilogue writes resid * w_norm and per-tile sums of
+    squares, the consuming GEMM scales each token by rsqrt(mean + eps). The
+    fp32 tier keeps the standalone RMSNorm kernel, whose rounding follows the
+    reference's exactly."""
+    return w.dtype == torch.bfloat16
+
+
 class Scratch:
     """Persistent activation buffers for forwards of up to `rows` rows."""
 
@@ -178,6 +192,9 @@ class Scratch:
         self.rows = rows
         dev = w.device
         self.resid = torch.zeros(rows, w.d, dtype=torch.float32, device=dev)
+        # per-row partial sums of squares (one per 128 features) for the
+        # RMSNorms folded into the GEMMs
+        self.ssq = torch.zeros(rows, norm_parts(w), dtype=torch.float32, device=dev)
         self.q = torch.zeros(rows, w.H * w.hd, dtype=w.dtype, device=dev)
         self.attn = torch.zeros(rows, w.H * w.hd, dtype=w.dtype, device=dev)
         self._xn: dict = {}
@@ -270,6 +287,102 @@ def run_stack(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm_bridge
         run_layer(w, li, fwd, T, cache, scratch, ws, kv_bound)
     if pre_norm_bridge is not None:
         run_bridge(pre_norm_bridge, scratch, T, ws)
+
+
+def _norm_chain(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm_bridge) -> list:
+    """(weight, eps) of every RMSNorm of a forward, in execution order; the
+    last one is the final norm before the head."""
+    out = []
+    for slot, li in enumerate(layer_indices):
+        b = pre_layer_bridges[slot]
+        if b is not None:
+            out.append((b.norm.weight, float(b.norm.eps)))
+        lw = w.layers[li]
+        out.append((lw.ln1, lw.eps1))
+        out.append((lw.ln2, lw.eps2))
+    if pre_norm_bridge is not None:
+        out.append((pre_norm_bridge.norm.weight, float(pre_norm_bridge.norm.eps)))
+    out.append((w.norm, w.norm_eps))
+    return out
+
+
+def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm_bridge, fwd: ForwardInputs, T: int,
+                     cache, scratch: Scratch, ws: ops.Workspace, kv_bound: int) -> None:
+    """run_stack with every RMSNorm folded into the neighbouring kernels (bf16).
+    Leaves resid (pre-norm hidden state), and xn / ssq holding the final
+    norm's folded input for final_norm_folded."""
+    norms = _norm_chain(w, layer_indices, pre_layer_bridges, pre_norm_bridge)
+    parts, d = norm_parts(w), w.d
+    xg = scratch.xn(w.dtype, d)[:T, :d]
+    ssq = scratch.ssq[:T]
+    resid = scratch.resid[:T]
+    out_for = lambda k: ops.NormOut(norms[k][0], xg, ssq)
+    in_for = lambda k: ops.RowNorm(ssq, parts, d, norms[k][1])
+    ops.embed(fwd.ids[:T], w.embed, resid, ws, norm_out=out_for(0))
+    k = 0
+    for slot, li in enumerate(layer_indices):
+        b = pre_layer_bridges[slot]
+        if b is not None:
+            _bridge_folded(b, scratch, T, ws, xg, in_for(k), out_for(k + 1))
+            k += 1
+        lw = w.layers[li]
+        kc, vc = cache.layer(li)
+        ops.qkv_rope(xg, lw.q, lw.k, lw.v, w.H, w.Hkv, w.hd, w.rope_cos, w.rope_sin, fwd.positions, fwd.slots, kc, vc,
+                     scratch.q[:T], ws, T=T, in_norm=in_for(k))
+        ops.tree_attention(scratch.q[:T], kc, vc, w.H, w.Hkv, w.hd, fwd.prefix_len, scratch.attn[:T], ws,
+                           spec_base=fwd.spec_base if fwd.use_mask else None,
+                           spec_mask=fwd.mask if fwd.use_mask else None, kv_bound=kv_bound, T=T)
+        ops.linear(scratch.attn[:T], [lw.o], ws, epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=out_for(k + 1))
+        hid = scratch.hid(w.dtype, w.F, 0)[:T, : w.F]
+        ops.linear(xg, [lw.gate, lw.up], ws, epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid, in_norm=in_for(k + 1))
+        ops.linear(hid, [lw.down], ws, epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=out_for(k + 2))
+        k += 2
+    if pre_norm_bridge is not None:
+        _bridge_folded(pre_norm_bridge, scratch, T, ws, xg, in_for(k), out_for(k + 1))
+        k += 1
+    assert k == len(norms) - 1
+
+
+def _bridge_folded(bridge, scratch: Scratch, T: int, ws: ops.Workspace, xg, rn, nout) -> None:
+    """TransitionBridge x + MLP(RMSNorm(x)) with its RMSNorm folded: xg / rn
+    carry the folded input, the out-projection produces the next norm's."""
+    dt = bridge.norm.weight.dtype
+    mlp = bridge.mlp
+    if bridge.mlp_type == "swiglu":
+        h = scratch.hid(dt, bridge.hidden, 0)[:T, : bridge.hidden]
+        ops.linear(xg, [mlp.gate_proj.weight, mlp.up_proj.weight], ws, biases=[mlp.gate_proj.bias, mlp.up_proj.bias],
+                   epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=h, in_norm=rn)
+    else:
+        h = xg
+        for i, lin in enumerate(mlp.linears()):
+            nxt = scratch.hid(dt, bridge.hidden, i % 2)[:T, : lin.weight.shape[0]]
+            ops.linear(h, [lin.weight], ws, biases=[lin.bias], act=bridge.activation, out=nxt,
+                       in_norm=rn if i == 0 else None)
+            h = nxt
+    ops.linear(h, [mlp.out_proj.weight], ws, biases=[mlp.out_proj.bias], epilogue=L.EPI_RESIDUAL,
+               resid=scratch.resid[:T], norm_out=nout)
+
+
+def final_norm_folded(w: ModelWeights, scratch: Scratch, r0: int, r1: int):
+    """Head input of a folded forward: (resid * w_norm rows, their RowNorm)."""
+    x = scratch.xn(w.dtype, w.d)[r0:r1, : w.d]
+    return x, ops.RowNorm(scratch.ssq[r0:r1], norm_parts(w), w.d, w.norm_eps)
+
+
+def head_input(w: ModelWeights, scratch: Scratch, r0: int, r1: int):
+    """(x, in_norm) for the lm_head of rows r0..r1 after run_stack_auto."""
+    if folds_norms(w):
+        return final_norm_folded(w, scratch, r0, r1)
+    return final_norm(w, scratch, r0, r1), None
+
+
+def run_stack_auto(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm_bridge, fwd: ForwardInputs, T: int,
+                   cache, scratch: Scratch, ws: ops.Workspace, kv_bound: int) -> None:
+    """The engines' forward: folded norms for bf16, standalone ones for fp32."""
+    if folds_norms(w):
+        run_stack_folded(w, layer_indices, pre_layer_bridges, pre_norm_bridge, fwd, T, cache, scratch, ws, kv_bound)
+    else:
+        run_stack(w, layer_indices, pre_layer_bridges, pre_norm_bridge, fwd, T, cache, scratch, ws, kv_bound)
 
 
 def final_norm(w: ModelWeights, scratch: Scratch, r0: int, r1: int) -> torch.Tensor:

@@ -71,10 +71,42 @@ class Workspace:
             raise RuntimeError("SSD device error: " + ", ".join(what))
 
 
-def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor, ws: Workspace) -> None:
+class NormOut:
+    """Next RMSNorm input produced by a residual-updating kernel (SsdNormOut):
+    out[t, n] = resid[t, n] * weight[n] (bf16) and ssq[t, i] = sum of squares
+    of resid[t, :] over the i-th 128-feature tile."""
+
+    def __init__(self, weight: torch.Tensor, out: torch.Tensor, ssq: torch.Tensor):
+        self.weight, self.out, self.ssq = weight, out, ssq
+
+    def c(self):
+        return C.byref(L.SsdNormOut(_p(self.weight), _p(self.out), self.out.stride(0), _p(self.ssq),
+                                    self.ssq.stride(0)))
+
+
+class RowNorm:
+    """RMSNorm completed inside a GEMM (SsdRowNorm): output column t is scaled
+    by rsqrt(sum(ssq[t, :parts]) / d + eps)."""
+
+    def __init__(self, ssq: torch.Tensor, parts: int, d: int, eps: float):
+        self.ssq, self.parts, self.d, self.eps = ssq, parts, d, float(eps)
+
+    def rows(self, r0: int, r1: int) -> "RowNorm":
+        return RowNorm(self.ssq[r0:r1], self.parts, self.d, self.eps)
+
+    def c(self):
+        return C.byref(L.SsdRowNorm(_p(self.ssq), self.ssq.stride(0), self.parts, self.d, self.eps))
+
+
+def _c(x):
+    return None if x is None else x.c()
+
+
+def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor, ws: Workspace,
+          norm_out: Optional[NormOut] = None) -> None:
     T = ids.numel()
     L.call("ssd_embed", _p(ids), T, _p(table), table.shape[0], table.shape[1], dtype_code(table.dtype), _p(out),
-           _p(ws.status), _stream())
+           _c(norm_out), _p(ws.status), _stream())
 
 
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor) -> None:
@@ -85,7 +117,8 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor
 
 def linear(x: torch.Tensor, weights: Sequence[torch.Tensor], ws: Workspace, *, biases: Sequence = (),
            epilogue: int = L.EPI_STORE, act: str = "none", layout: int = L.SEG_CONCAT,
-           out: Optional[torch.Tensor] = None, resid: Optional[torch.Tensor] = None, T: Optional[int] = None) -> None:
+           out: Optional[torch.Tensor] = None, resid: Optional[torch.Tensor] = None, T: Optional[int] = None,
+           in_norm: Optional[RowNorm] = None, norm_out: Optional[NormOut] = None) -> None:
     """out/resid <- epilogue(x @ cat(weights)^T + bias). x: [T, K] in the weights' dtype."""
     T = x.shape[0] if T is None else T
     K = weights[0].shape[1]
@@ -99,17 +132,17 @@ def linear(x: torch.Tensor, weights: Sequence[torch.Tensor], ws: Workspace, *, b
     bp = (C.c_void_p * 3)(*[(b.data_ptr() if b is not None else None) for b in bl[:3]])
     L.call("ssd_linear", _p(x), x.stride(0), T, K, n, wp, rows, bp, layout, epilogue, L.ACT[act],
            _p(out), out.stride(0) if out is not None else 0, _p(resid), resid.stride(0) if resid is not None else 0,
-           dtype_code(weights[0].dtype), ws.ptr, ws.nbytes, _p(ws.status), _stream())
+           dtype_code(weights[0].dtype), ws.ptr, ws.nbytes, _c(in_norm), _c(norm_out), _p(ws.status), _stream())
 
 
 def qkv_rope(x, wq, wk, wv, n_heads, n_kv, head_dim, cos, sin, positions, slots, k_cache, v_cache, q_out,
-             ws: Workspace, T: Optional[int] = None) -> None:
+             ws: Workspace, T: Optional[int] = None, in_norm: Optional[RowNorm] = None) -> None:
     """k_cache/v_cache: [n_kv, max_slots, head_dim] views of one layer."""
     T = x.shape[0] if T is None else T
     L.call("ssd_qkv_rope", _p(x), x.stride(0), T, wq.shape[1], _p(wq), _p(wk), _p(wv), n_heads, n_kv, head_dim,
            _p(cos), _p(sin), cos.shape[0], _p(positions), _p(slots), _p(k_cache), _p(v_cache), k_cache.stride(0),
-           k_cache.shape[1], _p(q_out), q_out.stride(0), dtype_code(wq.dtype), ws.ptr, ws.nbytes, _p(ws.status),
-           _stream())
+           k_cache.shape[1], _p(q_out), q_out.stride(0), dtype_code(wq.dtype), ws.ptr, ws.nbytes, _c(in_norm),
+           _p(ws.status), _stream())
 
 
 def tree_attention(q, k_cache, v_cache, n_heads, n_kv, head_dim, prefix_len, out, ws: Workspace, *,
@@ -121,16 +154,18 @@ def tree_attention(q, k_cache, v_cache, n_heads, n_kv, head_dim, prefix_len, out
            out.stride(0), dtype_code(q.dtype), ws.ptr, ws.nbytes, _p(ws.status), _stream())
 
 
-def head_argmax(x, w, out_idx, ws: Workspace, out_max=None, out_gap=None, T: Optional[int] = None) -> None:
+def head_argmax(x, w, out_idx, ws: Workspace, out_max=None, out_gap=None, T: Optional[int] = None,
+                in_norm: Optional[RowNorm] = None) -> None:
     T = x.shape[0] if T is None else T
     L.call("ssd_head_argmax", _p(x), x.stride(0), T, w.shape[1], _p(w), w.shape[0], _p(out_idx), _p(out_max),
-           _p(out_gap), dtype_code(w.dtype), ws.ptr, ws.nbytes, _p(ws.status), _stream())
+           _p(out_gap), dtype_code(w.dtype), ws.ptr, ws.nbytes, _c(in_norm), _p(ws.status), _stream())
 
 
-def head_topk(x, w, k: int, out_tok, out_lp, ws: Workspace, vocab_ids=None, T: Optional[int] = None) -> None:
+def head_topk(x, w, k: int, out_tok, out_lp, ws: Workspace, vocab_ids=None, T: Optional[int] = None,
+              in_norm: Optional[RowNorm] = None) -> None:
     T = x.shape[0] if T is None else T
     L.call("ssd_head_topk", _p(x), x.stride(0), T, w.shape[1], _p(w), w.shape[0], _p(vocab_ids), k, _p(out_tok),
-           _p(out_lp), dtype_code(w.dtype), ws.ptr, ws.nbytes, _p(ws.status), _stream())
+           _p(out_lp), dtype_code(w.dtype), ws.ptr, ws.nbytes, _c(in_norm), _p(ws.status), _stream())
 
 
 def level_prune(topk_tok, topk_lp, n_frontier, k, width, level, frontier, next_frontier, tree, root_pos, fed,

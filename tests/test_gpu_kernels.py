@@ -282,3 +282,44 @@ def test_kv_compact(ops, dtype, keep):
     ops.kv_compact(cache, st, ks, nk, max_keep=8)
     torch.cuda.synchronize()
     assert torch.equal(cache, ref)
+
+
+@pytest.mark.parametrize("name,over", [("tiny", {}), ("llama32_1b", dict(num_hidden_layers=2, vocab_size=4096))])
+def test_folded_rmsnorm_matches_standalone(name, over):
+    """bf16 forward with the RMSNorms folded into the GEMM epilogues vs the
+    standalone RMSNorm kernel: same logits up to bf16 rounding."""
+    from ssd import synthetic as S
+    from ssd.engine.speculative import TargetRunner
+    from ssd.models import runner as R
+
+    base = S.build_base_model(name, 3, torch.bfloat16, DEV, gen_device="cuda", **over)
+    target = TargetRunner(base)
+    w = target.weights
+    T = 9
+    ids = torch.randint(0, w.V, (T,), generator=torch.Generator().manual_seed(1))
+    outs = []
+    for folded in (False, True):
+        cache = target.new_cache(32)
+        cache.allocate(w.Hkv, w.hd, w.dtype, w.device)
+        fwd = R.ForwardInputs(T, DEV, mask_words=1)
+        fwd.fill(ids, torch.arange(T), 0, None)
+        scratch = R.Scratch(w, T)
+        from ssd import ops as O
+        wsp = O.Workspace(DEV, max_rows=64, vocab=w.V, max_head_rows=T)
+        layers = list(range(w.L))
+        logits = torch.empty(T, w.V, dtype=torch.float32, device=DEV)
+        if folded:
+            R.run_stack_folded(w, layers, [None] * w.L, None, fwd, T, cache, scratch, wsp, cache.max_length)
+            x, rn = R.final_norm_folded(w, scratch, 0, T)
+            O.linear(x, [w.lm_head], wsp, epilogue=3, out=logits, in_norm=rn)
+        else:
+            R.run_stack(w, layers, [None] * w.L, None, fwd, T, cache, scratch, wsp, cache.max_length)
+            x = R.final_norm(w, scratch, 0, T)
+            O.linear(x, [w.lm_head], wsp, epilogue=3, out=logits)
+        torch.cuda.synchronize()
+        wsp.check_status()
+        outs.append(logits)
+    ref, got = outs
+    scale = ref.abs().max()
+    assert (got - ref).abs().max() <= 2e-2 * scale, ((got - ref).abs().max(), scale)
+    assert (got.argmax(-1) == ref.argmax(-1)).float().mean() >= 0.8

@@ -42,7 +42,7 @@ def _noalloc(x, w, status, **kw):
 def _with_workspace(x, w, ws, **kw):
     from ssd import _lib as L
 
-    L.call("ssd_linear", *_args(x, w, **kw), ws.ptr, ws.nbytes, ws.status.data_ptr(),
+    L.call("ssd_linear", *_args(x, w, **kw), ws.ptr, ws.nbytes, None, None, ws.status.data_ptr(),
            torch.cuda.current_stream().cuda_stream)
 
 
