@@ -169,8 +169,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   float* stage = reinterpret_cast<float*>(smem);
   const int ncols = min(g.BN, g.T - tile_n * g.BN);
   bool ok = true;
+  const float* s_scale = epi_scale_smem();
   if (epi) {
     pdl_wait();  // the epilogue writes buffers earlier kernels may still read
+    // The folded-RMSNorm row scales depend only on earlier kernels' output:
+    // compute them while the mainloop runs (published by the barrier below).
+    if (e.rn_ssq) epi_row_scales(e, tile_n * g.BN, ncols, g.splits == 1 ? 0 : split, g.splits, r);
     if (!mbar_wait(accum, 0)) {
       report_error(g.status, kErrWaitTimeout);
       *abort_flag = 1;
@@ -179,19 +183,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     named_bar_sync(1, 128);  // all four warps past the wait before the ring is reused
     ok = (*abort_flag == 0);  // uniform across the epilogue warps
     if (ok) {
+      const bool scale = e.rn_ssq && g.splits == 1;
       for (int c0 = 0; c0 < g.BN; c0 += 16) {
         float v[16];
         tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, v);
 #pragma unroll
         for (int i = 0; i < 16; ++i)
-          if (c0 + i < ncols) stage[(c0 + i) * kTileM + r] = (nk > 0) ? v[i] : 0.f;
+          if (c0 + i < ncols)
+            stage[(c0 + i) * kTileM + r] = (nk > 0) ? (scale ? v[i] * s_scale[c0 + i] : v[i]) : 0.f;
       }
     }
   }
   if (g.splits == 1) {
     if (epi) {
       named_bar_sync(1, 128);
-      if (ok) run_epilogue<bf16>(stage, tile_m, tile_n * g.BN, ncols, g, e, r, 1);
+      if (ok) run_epilogue<bf16>(stage, tile_m, tile_n * g.BN, ncols, g, e, r, 1, 0, 1, true);
     }
   } else {
     // The `splits` CTAs of this tile form one cluster (rank = split). After
@@ -206,19 +212,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
       for (int s = 0; s < kMaxClusterSplits; ++s)
         peer[s] = s < g.splits ? dsmem_map(smem_u32(stage), static_cast<uint32_t>(s)) : 0u;
-      for (int c = split; c < ncols; c += g.splits) {
-        const uint32_t off = static_cast<uint32_t>((c * kTileM + r) * 4);
-        float v[kMaxClusterSplits];
+      // Four owned columns per batch: all their peer loads are in flight
+      // together (one DSMEM round trip per batch, not per column).
+      constexpr int kCols = 4;
+      for (int cb = split, j0 = 0; cb < ncols; cb += kCols * g.splits, j0 += kCols) {
+        float v[kCols][kMaxClusterSplits];
 #pragma unroll
-        for (int s = 0; s < kMaxClusterSplits; ++s) v[s] = s < g.splits ? dsmem_ld(peer[s] + off) : 0.f;
-        float acc = 0.f;
+        for (int u = 0; u < kCols; ++u) {
+          const int c = cb + u * g.splits;
+          const uint32_t off = static_cast<uint32_t>((c * kTileM + r) * 4);
 #pragma unroll
-        for (int s = 0; s < kMaxClusterSplits; ++s)
-          if (s < g.splits) acc += v[s];
-        stage[c * kTileM + r] = acc;
+          for (int s = 0; s < kMaxClusterSplits; ++s)
+            v[u][s] = (s < g.splits && c < ncols) ? dsmem_ld(peer[s] + off) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kCols; ++u) {
+          const int c = cb + u * g.splits;
+          if (c >= ncols) break;
+          float acc = 0.f;
+#pragma unroll
+          for (int s = 0; s < kMaxClusterSplits; ++s)
+            if (s < g.splits) acc += v[u][s];
+          stage[c * kTileM + r] = e.rn_ssq ? acc * s_scale[j0 + u] : acc;
+        }
       }
       named_bar_sync(1, 128);
-      run_epilogue<bf16>(stage, tile_m, tile_n * g.BN, ncols, g, e, r, 1, split, g.splits);
+      run_epilogue<bf16>(stage, tile_m, tile_n * g.BN, ncols, g, e, r, 1, split, g.splits, true);
     }
     cluster_sync_all();
   }

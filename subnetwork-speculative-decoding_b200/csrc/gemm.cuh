@@ -100,26 +100,73 @@ __device__ __forceinline__ float load_bias(const void* b, int i) {
 // top-k -> {max, sumexp, val[k], idx[k]}.
 __host__ __device__ inline int head_rec_size(int kind, int k) { return kind == EPI_ARGMAX ? 3 : 2 + 2 * k; }
 
+// Per-CTA table of folded-RMSNorm row scales, one per owned token column.
+__device__ __forceinline__ float* epi_scale_smem() {
+  __shared__ float s_scale[256];
+  return s_scale;
+}
+
+// Fill epi_scale_smem()[j] = rsqrt(sum(ssq[t, :parts]) / d + eps) for the
+// owned columns c = c0 + j * cstep < ncols (t = t0 + c). 128 threads; one warp
+// per column, lanes over the per-tile partial sums (up to 64 of them loaded
+// at once, more in a second pass), four columns per warp in flight. The sum
+// order is fixed (two lanes' halves, then a butterfly), so every consumer of
+// the same ssq row computes the same scale. No barrier: the caller publishes
+// the table.
+__device__ __forceinline__ void epi_row_scales(const EpiArgs& e, int t0, int ncols, int c0, int cstep, int tid) {
+  float* s_scale = epi_scale_smem();
+  const int nsub = ncols > c0 ? (ncols - c0 + cstep - 1) / cstep : 0;
+  const int warp = tid >> 5, lane = tid & 31;
+  constexpr int kB = 4;
+  for (int j0 = warp; j0 < nsub; j0 += 4 * kB) {
+    float acc[kB];
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const int j = j0 + 4 * u;
+      const float* ss = e.rn_ssq + (int64_t)(t0 + c0 + j * cstep) * e.rn_ld;
+      const float a = (j < nsub && lane < e.rn_parts) ? ss[lane] : 0.f;
+      const float b = (j < nsub && lane + 32 < e.rn_parts) ? ss[lane + 32] : 0.f;
+      acc[u] = a + b;
+    }
+    if (e.rn_parts > 64) {
+#pragma unroll
+      for (int u = 0; u < kB; ++u) {
+        const int j = j0 + 4 * u;
+        if (j >= nsub) continue;
+        const float* ss = e.rn_ssq + (int64_t)(t0 + c0 + j * cstep) * e.rn_ld;
+        for (int i = lane + 64; i < e.rn_parts; i += 32) acc[u] += ss[i];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const float v = warp_sum(acc[u]);
+      const int j = j0 + 4 * u;
+      if (lane == 0 && j < nsub) s_scale[j] = rsqrtf(v / (float)e.rn_d + e.rn_eps);
+    }
+  }
+}
+
+// Columns per batch in the epilogue loops: each batch issues its global
+// loads (residual rows, positions, RoPE tables) together, so a batch costs
+// one memory latency instead of one per column.
+constexpr int kEpiBatch = 8;
+
 // Apply the epilogue to a finished fp32 tile stage[c * 128 + r] (c = token
 // within the tile, r = row within the 128-feature tile). Runs on 128
 // threads; `tid` in [0, 128). `bar_id` names a barrier over those threads.
 // Columns c0, c0 + cstep, ... < ncols are processed (a cluster splits the
-// columns of one tile among its CTAs).
+// columns of one tile among its CTAs). `rn_applied`: the folded-RMSNorm row
+// scales (e.rn_ssq) were already multiplied into the tile by the caller.
 template <typename T>
 __device__ void run_epilogue(float* stage, int tile_m, int t0, int ncols, const GemmShape& g, const EpiArgs& e,
-                             int tid, int bar_id, int c0 = 0, int cstep = 1) {
+                             int tid, int bar_id, int c0 = 0, int cstep = 1, bool rn_applied = false) {
   const int r = tid;
-  if (e.rn_ssq) {
+  if (e.rn_ssq && !rn_applied) {
     // Folded RMSNorm of the input rows: scale token column c by
-    // rsqrt(mean of squares + eps), the sums taken in tile order.
-    __shared__ float s_scale[256];
+    // rsqrt(mean of squares + eps).
+    const float* s_scale = epi_scale_smem();
     const int nsub = ncols > c0 ? (ncols - c0 + cstep - 1) / cstep : 0;
-    for (int j = tid; j < nsub; j += kTileM) {
-      const float* ss = e.rn_ssq + (int64_t)(t0 + c0 + j * cstep) * e.rn_ld;
-      float acc = 0.f;
-      for (int i = 0; i < e.rn_parts; ++i) acc += ss[i];
-      s_scale[j] = rsqrtf(acc / (float)e.rn_d + e.rn_eps);
-    }
+    epi_row_scales(e, t0, ncols, c0, cstep, tid);
     named_bar_sync(bar_id, kTileM);
     for (int j = 0; j < nsub; ++j) stage[(c0 + j * cstep) * kTileM + r] *= s_scale[j];
     named_bar_sync(bar_id, kTileM);
@@ -132,15 +179,26 @@ __device__ void run_epilogue(float* stage, int tile_m, int t0, int ncols, const 
     const int s = in ? seg_of(g, n) : 0;
     const float b = in ? load_bias<T>(e.bias[s], n - g.seg_start[s]) : 0.f;
     const float wn = in ? to_f32<T>(static_cast<const T*>(e.no_w)[n]) : 0.f;
-    for (int c = c0; c < ncols; c += cstep) {
-      const int t = t0 + c;
-      float rn = 0.f;
-      if (in) {
-        rn = e.resid[(int64_t)t * e.ldr + n] + stage[c * kTileM + r] + b;
-        e.resid[(int64_t)t * e.ldr + n] = rn;
-        static_cast<T*>(e.no_out)[(int64_t)t * e.no_ldo + n] = from_f32<T>(rn * wn);
+    for (int cb = c0; cb < ncols; cb += kEpiBatch * cstep) {
+      float rv[kEpiBatch];
+#pragma unroll
+      for (int u = 0; u < kEpiBatch; ++u) {
+        const int c = cb + u * cstep;
+        rv[u] = (in && c < ncols) ? e.resid[(int64_t)(t0 + c) * e.ldr + n] : 0.f;
       }
-      stage[c * kTileM + r] = rn * rn;
+#pragma unroll
+      for (int u = 0; u < kEpiBatch; ++u) {
+        const int c = cb + u * cstep;
+        if (c >= ncols) break;
+        const int t = t0 + c;
+        float rn = 0.f;
+        if (in) {
+          rn = rv[u] + stage[c * kTileM + r] + b;
+          e.resid[(int64_t)t * e.ldr + n] = rn;
+          static_cast<T*>(e.no_out)[(int64_t)t * e.no_ldo + n] = from_f32<T>(rn * wn);
+        }
+        stage[c * kTileM + r] = rn * rn;
+      }
     }
     named_bar_sync(bar_id, kTileM);
     const int warp = tid >> 5, lane = tid & 31;
@@ -159,12 +217,26 @@ __device__ void run_epilogue(float* stage, int tile_m, int t0, int ncols, const 
       if (n >= g.N) return;
       const int s = seg_of(g, n);
       const float b = load_bias<T>(e.bias[s], n - g.seg_start[s]);
+      if (e.kind == EPI_RESIDUAL) {
+        for (int cb = c0; cb < ncols; cb += kEpiBatch * cstep) {
+          float rv[kEpiBatch];
+#pragma unroll
+          for (int u = 0; u < kEpiBatch; ++u) {
+            const int c = cb + u * cstep;
+            rv[u] = c < ncols ? e.resid[(int64_t)(t0 + c) * e.ldr + n] : 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < kEpiBatch; ++u) {
+            const int c = cb + u * cstep;
+            if (c < ncols) e.resid[(int64_t)(t0 + c) * e.ldr + n] = rv[u] + (stage[c * kTileM + r] + b);
+          }
+        }
+        return;
+      }
       for (int c = c0; c < ncols; c += cstep) {
         const int t = t0 + c;
         float v = stage[c * kTileM + r] + b;
-        if (e.kind == EPI_RESIDUAL) {
-          e.resid[(int64_t)t * e.ldr + n] += v;
-        } else if (e.kind == EPI_STORE_F32) {
+        if (e.kind == EPI_STORE_F32) {
           static_cast<float*>(e.out)[(int64_t)t * e.ldo + n] = act_f(e.act, v);
         } else {
           static_cast<T*>(e.out)[(int64_t)t * e.ldo + n] = from_f32<T>(act_f(e.act, v));
@@ -191,34 +263,58 @@ __device__ void run_epilogue(float* stage, int tile_m, int t0, int ncols, const 
       if (n >= g.N) return;
       const int hd = e.head_dim, half = hd >> 1;
       const bool is_q = n < e.n_q, is_k = !is_q && n < e.n_q + e.n_kv;
+      const bool rope = is_q || is_k;
       const int local = is_q ? n : (is_k ? n - e.n_q : n - e.n_q - e.n_kv);
       const int head = local / hd, j = local - head * hd;
       const int partner = (j < half) ? r + half : r - half;  // same head, same tile (hd divides 128)
-      for (int c = c0; c < ncols; c += cstep) {
-        const int t = t0 + c;
-        float v = stage[c * kTileM + r];
-        if (is_q || is_k) {
-          int p = e.positions[t];
-          if (p < 0 || p >= e.max_pos) {
-            report_error(g.status, kErrBadIndex);
-            p = 0;
-          }
-          const int fi = j < half ? j : j - half;
-          const float cs = e.rope_cos[(int64_t)p * half + fi];
-          const float sn = e.rope_sin[(int64_t)p * half + fi];
-          const float o = stage[c * kTileM + partner];
-          v = (j < half) ? (v * cs - o * sn) : (v * cs + o * sn);
+      const int fi = j < half ? j : j - half;
+      for (int cb = c0; cb < ncols; cb += kEpiBatch * cstep) {
+        // Batch the index loads, then the RoPE table loads that depend on them.
+        int idx[kEpiBatch];
+#pragma unroll
+        for (int u = 0; u < kEpiBatch; ++u) {
+          const int c = cb + u * cstep;
+          idx[u] = c < ncols ? (rope ? e.positions[t0 + c] : e.slots[t0 + c]) : 0;
         }
-        if (is_q) {
-          static_cast<T*>(e.out)[(int64_t)t * e.ldo + n] = from_f32<T>(v);
-        } else {
-          const int slot = e.slots[t];
-          if (slot < 0 || slot >= e.max_slots) {
-            report_error(g.status, kErrBadIndex);
-            continue;
+        int slot[kEpiBatch];
+        float cs[kEpiBatch], sn[kEpiBatch];
+#pragma unroll
+        for (int u = 0; u < kEpiBatch; ++u) {
+          const int c = cb + u * cstep;
+          slot[u] = (is_k && c < ncols) ? e.slots[t0 + c] : idx[u];
+          cs[u] = 1.f;
+          sn[u] = 0.f;
+          if (rope && c < ncols) {
+            int p = idx[u];
+            if (p < 0 || p >= e.max_pos) {
+              report_error(g.status, kErrBadIndex);
+              p = 0;
+            }
+            cs[u] = e.rope_cos[(int64_t)p * half + fi];
+            sn[u] = e.rope_sin[(int64_t)p * half + fi];
           }
-          T* cache = static_cast<T*>(is_k ? e.k_cache : e.v_cache);
-          cache[(int64_t)head * e.head_stride + (int64_t)slot * hd + j] = from_f32<T>(v);
+        }
+#pragma unroll
+        for (int u = 0; u < kEpiBatch; ++u) {
+          const int c = cb + u * cstep;
+          if (c >= ncols) break;
+          const int t = t0 + c;
+          float v = stage[c * kTileM + r];
+          if (rope) {
+            const float o = stage[c * kTileM + partner];
+            v = (j < half) ? (v * cs[u] - o * sn[u]) : (v * cs[u] + o * sn[u]);
+          }
+          if (is_q) {
+            static_cast<T*>(e.out)[(int64_t)t * e.ldo + n] = from_f32<T>(v);
+          } else {
+            const int sl = slot[u];
+            if (sl < 0 || sl >= e.max_slots) {
+              report_error(g.status, kErrBadIndex);
+              continue;
+            }
+            T* cache = static_cast<T*>(is_k ? e.k_cache : e.v_cache);
+            cache[(int64_t)head * e.head_stride + (int64_t)sl * hd + j] = from_f32<T>(v);
+          }
         }
       }
       return;
