@@ -294,6 +294,70 @@ int ssd_tree_walk_sample(const int32_t* n_nodes, int64_t max_nodes, const int32_
                          float* p_scratch, float* q_scratch, int32_t* accepted, int32_t* n_accepted, int32_t* bonus,
                          int32_t* keep_slots, int32_t* n_keep, uint32_t* status, void* stream);
 
+
+/* ------------------------------------------------------- tensor parallel
+ * The 70B configuration runs tensor-parallel over `world` GPUs, one process
+ * per GPU: q/k/v and gate/up split by output features (heads, FFN columns),
+ * o_proj and down_proj by input features, the lm_head by vocabulary rows, the
+ * KV cache by KV head; embedding, norms and bridges replicated. Ranks exchange
+ * data through a "region": a device buffer of ssd_tp_region_bytes bytes with
+ * the same layout on every rank, zeroed once, each rank's region mapped into
+ * every rank's address space (peer pointers over NVLink; the host sets the
+ * mapping up, e.g. with torch symmetric memory). Kernels meet their
+ * counterparts on the other ranks through flags in the regions; every wait is
+ * bounded (timeout: status bit 1). Every rank must issue the same sequence of
+ * these calls with the same sizes. No multicast is used. (The reference runs
+ * on one device and has no tensor-parallel code.) */
+#define SSD_TP_MAX_RANKS 8
+typedef struct SsdTpGroup {
+  int32_t rank;
+  int32_t world;
+  int64_t max_rows; /* token rows the region's exchange buffers hold */
+  int64_t d;        /* model width (the all-reduced row length) */
+  void* peer_region[SSD_TP_MAX_RANKS]; /* region of rank r as mapped in this process */
+} SsdTpGroup;
+
+int64_t ssd_tp_region_bytes(int64_t max_rows, int64_t d);
+/* Byte offset in the region of the partial buffer, fp32 [max_rows, d] with
+ * row stride d: the row-parallel o_proj / down_proj GEMM (ssd_linear with
+ * SSD_EPI_STORE_F32) writes this rank's partial sums there. */
+int64_t ssd_tp_partial_offset(int64_t max_rows);
+
+/* resid[t, :] += sum over ranks (in rank order) of the ranks' partials [T, d];
+ * with norm_out also the next RMSNorm's folded input, as ssd_linear's residual
+ * epilogue (bit-identical to it when world == 1). Two-shot over peer memory:
+ * each rank sums a 1/world slice of the features and stores it into every
+ * rank's region, so each rank moves 2 (world - 1) / world of the partial over
+ * NVLink. When it returns on the stream, every rank has finished reading this
+ * rank's partial (the next GEMM may overwrite it). This is the all-reduce after
+ * o_proj / down_proj (_layer_forward, ssd/models/subnetwork_draft.py:243,245)
+ * of a tensor-parallel layer, fused with the residual add. dtype: of norm_out. */
+int ssd_tp_allreduce_residual(const SsdTpGroup* group, int64_t T, float* resid, int64_t ldr,
+                              const SsdNormOut* norm_out, int dtype, uint32_t* status, void* stream);
+
+/* Vocabulary-parallel heads. w: this rank's lm_head rows [vocab_offset,
+ * vocab_offset + vocab_shard) as [vocab_shard, K]. Each rank reduces its rows,
+ * the per-row results of all ranks are merged through the regions, and every
+ * rank receives the global outputs of ssd_head_argmax (lowest global index on
+ * ties) / ssd_head_topk (log-softmax over all ranks' rows; vocab_ids maps
+ * global row indices to tokens, NULL = identity). T <= max_rows. */
+int ssd_tp_head_argmax(const SsdTpGroup* group, const void* x, int64_t ldx, int64_t T, int64_t K, const void* w,
+                       int64_t vocab_shard, int64_t vocab_offset, int32_t* out_idx, float* out_max, float* out_gap,
+                       int dtype, void* workspace, int64_t workspace_bytes, const SsdRowNorm* in_norm,
+                       uint32_t* status, void* stream);
+int ssd_tp_head_topk(const SsdTpGroup* group, const void* x, int64_t ldx, int64_t T, int64_t K, const void* w,
+                     int64_t vocab_shard, int64_t vocab_offset, const int64_t* vocab_ids, int64_t k, int32_t* out_tok,
+                     float* out_logprob, int dtype, void* workspace, int64_t workspace_bytes,
+                     const SsdRowNorm* in_norm, uint32_t* status, void* stream);
+
+/* Seeded synthetic weights: out[i, j] = scale * std * N(0, 1) for the block
+ * [row0, row0 + rows) x [col0, col0 + cols) of a global matrix with full_cols
+ * columns; element (gi, gj) depends only on (seed, stream_id,
+ * gi * full_cols + gj) (Philox4x32-10, Box-Muller), so a tensor-parallel
+ * shard of a global matrix is generated on its own rank. out: [rows, ld]. */
+int ssd_fill_normal(void* out, int64_t rows, int64_t cols, int64_t ld, int64_t row0, int64_t col0, int64_t full_cols,
+                    uint64_t seed, uint64_t stream_id, float std, float scale, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

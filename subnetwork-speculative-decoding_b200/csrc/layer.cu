@@ -92,7 +92,10 @@ __global__ void rmsnorm_kernel(const float* x, int64_t d, int64_t ldx, const T* 
 
 // ------------------------------------------------------------ head reducers
 // Merge the per-tile {max1, idx1, max2} records of each row.
-__global__ void argmax_reduce_kernel(const float* part, int tiles, int32_t* out_idx, float* out_max, float* out_gap) {
+// rec_out (tensor parallel): instead of the outputs, write this shard's
+// record {max1, idx1 + idx_offset, max2} per row for the cross-rank merge.
+__global__ void argmax_reduce_kernel(const float* part, int tiles, int32_t* out_idx, float* out_max, float* out_gap,
+                                     float* rec_out, int idx_offset) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
@@ -142,6 +145,12 @@ __global__ void argmax_reduce_kernel(const float* part, int tiles, int32_t* out_
         m2 = fmaxf(m2, s1[w]);
       }
     }
+    if (rec_out) {
+      rec_out[(int64_t)t * 3] = m1;
+      rec_out[(int64_t)t * 3 + 1] = __int_as_float(i1 == INT32_MAX ? INT32_MAX : i1 + idx_offset);
+      rec_out[(int64_t)t * 3 + 2] = m2;
+      return;
+    }
     out_idx[t] = i1;
     if (out_max) out_max[t] = m1;
     if (out_gap) out_gap[t] = m1 - m2;
@@ -150,8 +159,11 @@ __global__ void argmax_reduce_kernel(const float* part, int tiles, int32_t* out_
 
 // Merge per-tile {max, sumexp, val[k], idx[k]} records: global log-sum-exp and
 // the k best (value desc, index asc); emits tokens through vocab_ids.
+// rec_out (tensor parallel): instead of the outputs, write this shard's
+// merged record {max, sumexp, val[k], idx[k] + idx_offset} per row (the
+// per-tile record format) for the cross-rank merge.
 __global__ void topk_reduce_kernel(const float* part, int tiles, int k, const int64_t* vocab_ids, int32_t* out_tok,
-                                   float* out_lp) {
+                                   float* out_lp, float* rec_out, int idx_offset) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
@@ -191,6 +203,10 @@ __global__ void topk_reduce_kernel(const float* part, int tiles, int k, const in
   }
   __syncthreads();
   const float lse = M + logf(red[0]);
+  if (rec_out && threadIdx.x == 0) {
+    rec_out[(int64_t)t * rec] = M;
+    rec_out[(int64_t)t * rec + 1] = red[0];
+  }
   for (int i = threadIdx.x; i < tiles && i < 1024; i += blockDim.x) head[i] = 0;
   __syncthreads();
   // k rounds: every thread proposes the best head among its tiles
@@ -233,9 +249,14 @@ __global__ void topk_reduce_kernel(const float* part, int tiles, int k, const in
           bt = s_tile[w];
         }
       if (bt >= 0) head[bt] += 1;
-      const int tok = (bi == INT32_MAX) ? -1 : (vocab_ids ? (int)vocab_ids[bi] : bi);
-      out_tok[(int64_t)t * k + q] = tok;
-      out_lp[(int64_t)t * k + q] = (bi == INT32_MAX) ? -INFINITY : bv - lse;
+      if (rec_out) {
+        rec_out[(int64_t)t * rec + 2 + q] = bv;
+        rec_out[(int64_t)t * rec + 2 + k + q] = __int_as_float(bi == INT32_MAX ? INT32_MAX : bi + idx_offset);
+      } else {
+        const int tok = (bi == INT32_MAX) ? -1 : (vocab_ids ? (int)vocab_ids[bi] : bi);
+        out_tok[(int64_t)t * k + q] = tok;
+        out_lp[(int64_t)t * k + q] = (bi == INT32_MAX) ? -INFINITY : bv - lse;
+      }
     }
     __syncthreads();
   }
@@ -414,7 +435,7 @@ int ssd_head_argmax(const void* x, int64_t ldx, int64_t T, int64_t K, const void
                        T * tiles * 3 * 4);
   if (rc) return rc;
   return launch_kernel("argmax_reduce_kernel", argmax_reduce_kernel, dim3((unsigned)T), dim3(256), 0, s, 1, 1, e.part,
-                       (int)tiles, out_idx, out_max, out_gap);
+                       (int)tiles, out_idx, out_max, out_gap, (float*)nullptr, 0);
 }
 
 int ssd_head_topk(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w, int64_t vocab,
@@ -440,7 +461,7 @@ int ssd_head_topk(const void* x, int64_t ldx, int64_t T, int64_t K, const void* 
                        T * tiles * rec * 4);
   if (rc) return rc;
   return launch_kernel("topk_reduce_kernel", topk_reduce_kernel, dim3((unsigned)T), dim3(256), 0, s, 1, 1, e.part,
-                       (int)tiles, (int)k, vocab_ids, out_tok, out_logprob);
+                       (int)tiles, (int)k, vocab_ids, out_tok, out_logprob, (float*)nullptr, 0);
 }
 
 }  // extern "C"

@@ -31,20 +31,6 @@ struct WarpParams {
   float log_z;   // log of the kept mass normaliser (relative to exp((l - m) / T))
 };
 
-// ------------------------------------------------------------------- Philox
-__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
-#pragma unroll
-  for (int r = 0; r < 10; ++r) {
-    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
-    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
-    c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
-    k.x += 0x9E3779B9u;
-    k.y += 0xBB67AE85u;
-  }
-  return c;
-}
-// Uniform in the open interval (0, 1) from 24 random bits.
-__device__ __forceinline__ float u01(uint32_t x) { return (static_cast<float>(x >> 8) + 0.5f) * (1.0f / 16777216.0f); }
 __device__ __forceinline__ float uniform(uint64_t seed, uint32_t round, uint32_t row, uint32_t idx, uint32_t stream) {
   const uint4 r = philox4x32_10(make_uint4(round, row, idx, stream),
                                 make_uint2(static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32)));

@@ -34,6 +34,15 @@ class SsdRowNorm(C.Structure):
     _fields_ = [("ssq", P), ("ld", I64), ("parts", I64), ("d", I64), ("eps", F32)]
 
 
+TP_MAX_RANKS = 8
+
+
+class SsdTpGroup(C.Structure):
+    """include/ssd_b200.h SsdTpGroup: a tensor-parallel group's exchange regions."""
+    _fields_ = [("rank", C.c_int32), ("world", C.c_int32), ("max_rows", I64), ("d", I64),
+                ("peer_region", P * TP_MAX_RANKS)]
+
+
 # name -> (restype, argtypes); mirrors include/ssd_b200.h
 SIGNATURES: dict[str, tuple] = {
     "ssd_version": (I32, []),
@@ -64,6 +73,12 @@ SIGNATURES: dict[str, tuple] = {
     "ssd_sample_token": (I32, [P, I64, F32, F32, P, P, I64, I64, P, P, P]),
     "ssd_tree_walk_sample": (I32, [P, I64, P, P, P, P, P, P, I64, P, I64, P, I64, P, I64, I64, P, P, P, P, P, P, P,
                                    P, P, P, P, P]),
+    "ssd_tp_region_bytes": (I64, [I64, I64]),
+    "ssd_tp_partial_offset": (I64, [I64]),
+    "ssd_tp_allreduce_residual": (I32, [P, I64, P, I64, P, I32, P, P]),
+    "ssd_tp_head_argmax": (I32, [P, P, I64, I64, I64, P, I64, I64, P, P, P, I32, P, I64, P, P, P]),
+    "ssd_tp_head_topk": (I32, [P, P, I64, I64, I64, P, I64, I64, P, I64, P, P, I32, P, I64, P, P, P]),
+    "ssd_fill_normal": (I32, [P, I64, I64, I64, I64, I64, I64, C.c_uint64, C.c_uint64, F32, F32, I32, P]),
 }
 
 _lib = None
@@ -111,8 +126,9 @@ def check(rc: int, what: str) -> None:
 
 
 # Kernels each entry point launches (host-only queries launch none).
-KERNELS_PER_CALL = {"ssd_head_argmax": 2, "ssd_head_topk": 2}
-_HOST_ONLY = {"ssd_version", "ssd_last_error", "ssd_device_sm_count", "ssd_workspace_bytes"}
+KERNELS_PER_CALL = {"ssd_head_argmax": 2, "ssd_head_topk": 2, "ssd_tp_head_argmax": 3, "ssd_tp_head_topk": 3}
+_HOST_ONLY = {"ssd_version", "ssd_last_error", "ssd_device_sm_count", "ssd_workspace_bytes", "ssd_tp_region_bytes",
+              "ssd_tp_partial_offset"}
 _launches = 0
 
 

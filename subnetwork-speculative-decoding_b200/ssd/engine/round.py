@@ -146,8 +146,8 @@ class _Decoder:
         """First generated token from the last prompt row into argmax[0]
         (_first_token, speculative.py:81-84; greedy here). rn: the folded
         final RMSNorm of xn, if any."""
-        ops.head_argmax(xn, self.w.lm_head, self.argmax[:1], ws, out_max=self.amax[:1], out_gap=self.gap[:1],
-                        in_norm=rn)
+        R.head_argmax(self.w, xn, self.w.lm_head, self.argmax[:1], ws, out_max=self.amax[:1], out_gap=self.gap[:1],
+                      in_norm=rn)
 
     def _capture(self, fn) -> torch.cuda.CUDAGraph:
         g = torch.cuda.CUDAGraph()
@@ -189,8 +189,8 @@ class TargetStep(_Decoder):
 
     def _next_token(self, xn: torch.Tensor, rn=None) -> None:
         """Next token into argmax[0]: lm_head fused with the argmax."""
-        ops.head_argmax(xn, self.w.lm_head, self.argmax[:1], self.ws, out_max=self.amax[:1], out_gap=self.gap[:1],
-                        in_norm=rn)
+        R.head_argmax(self.w, xn, self.w.lm_head, self.argmax[:1], self.ws, out_max=self.amax[:1],
+                      out_gap=self.gap[:1], in_norm=rn)
 
     def run(self, n_steps: int, use_graph: bool = True) -> None:
         if use_graph:
@@ -270,7 +270,7 @@ class GreedyRound(_Decoder):
         """k children per draft row (TreeDrafter._propose, tree_drafter.py:124-132
         for greedy): the draft head fused with a log-softmax top-k. `row0` is
         the row's index among the round's draft rows (0 = root)."""
-        ops.head_topk(xn, self.head_w, k, out_tok, out_lp, self.ws, vocab_ids=self.vocab_ids, in_norm=rn)
+        R.head_topk(self.w, xn, self.head_w, k, out_tok, out_lp, self.ws, vocab_ids=self.vocab_ids, in_norm=rn)
 
     def verify_phase(self) -> None:
         """verify_inputs + target forward + greedy_verify (verify.py:32-57)."""
@@ -286,8 +286,8 @@ class GreedyRound(_Decoder):
         """Target head over root + tree rows, then the acceptance walk
         (greedy_verify, verify.py:45-57): lm_head fused with the argmax."""
         p, st, w = self.plan, self.state, self.w
-        ops.head_argmax(xn, w.lm_head, self.argmax[: p.rows], self.ws, out_max=self.amax[: p.rows],
-                        out_gap=self.gap[: p.rows], in_norm=rn)
+        R.head_argmax(w, xn, w.lm_head, self.argmax[: p.rows], self.ws, out_max=self.amax[: p.rows],
+                      out_gap=self.gap[: p.rows], in_norm=rn)
         ops.tree_walk_greedy(self.tree, self.argmax, st[SEQ:SEQ + 1], self.accepted, st[N_ACC:N_ACC + 1],
                              st[BONUS:BONUS + 1], self.keep_slots, st[N_KEEP:N_KEEP + 1], p.n_verify)
 

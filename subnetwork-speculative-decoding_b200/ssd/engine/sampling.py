@@ -60,6 +60,8 @@ class _SamplingState:
             raise ValueError("sampling engines need temperature > 0")
         if not 0 < top_p <= 1:
             raise ValueError("top_p must be in (0, 1]")
+        if self.w.tp is not None:
+            raise NotImplementedError("sampling (temperature > 0) is not supported with tensor parallelism")
         dev, V = self.device, self.w.V
         self.temperature, self.top_p = float(temperature), float(top_p)
         self.seed_buf = torch.zeros(1, dtype=torch.int64, device=dev)

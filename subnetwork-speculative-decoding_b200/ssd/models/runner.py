@@ -52,6 +52,8 @@ class ModelWeights:
         self.F = cfg.intermediate_size
         self.V = cfg.vocab_size
         self.L = cfg.num_hidden_layers
+        self.tp = None  # tensor-parallel group (ssd.engine.tp.attach)
+        self.vocab_offset = 0  # first lm_head row of this rank's shard
         self.embed = inner.embed_tokens.weight
         self.lm_head = base.lm_head.weight
         self.norm = inner.norm.weight
@@ -332,15 +334,47 @@ def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm
         ops.tree_attention(scratch.q[:T], kc, vc, w.H, w.Hkv, w.hd, fwd.prefix_len, scratch.attn[:T], ws,
                            spec_base=fwd.spec_base if fwd.use_mask else None,
                            spec_mask=fwd.mask if fwd.use_mask else None, kv_bound=kv_bound, T=T)
-        ops.linear(scratch.attn[:T], [lw.o], ws, epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=out_for(k + 1))
+        _residual_linear(w, scratch.attn[:T], lw.o, ws, resid, out_for(k + 1), T)
         hid = scratch.hid(w.dtype, w.F, 0)[:T, : w.F]
         ops.linear(xg, [lw.gate, lw.up], ws, epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid, in_norm=in_for(k + 1))
-        ops.linear(hid, [lw.down], ws, epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=out_for(k + 2))
+        _residual_linear(w, hid, lw.down, ws, resid, out_for(k + 2), T)
         k += 2
     if pre_norm_bridge is not None:
         _bridge_folded(pre_norm_bridge, scratch, T, ws, xg, in_for(k), out_for(k + 1))
         k += 1
     assert k == len(norms) - 1
+
+
+def _residual_linear(w: ModelWeights, x, weight, ws: ops.Workspace, resid, norm_out, T: int) -> None:
+    """resid += x @ weight^T (+ the next folded norm input). Tensor parallel:
+    weight is this rank's input-feature slice; its partial goes to the
+    group's exchange buffer and ssd_tp_allreduce_residual sums the ranks'."""
+    if w.tp is None:
+        ops.linear(x, [weight], ws, epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=norm_out)
+        return
+    w.tp.check_rows(T)
+    ops.linear(x, [weight], ws, epilogue=L.EPI_STORE_F32, out=w.tp.partial[:T])
+    ops.tp_allreduce_residual(w.tp, T, resid, ws, norm_out=norm_out, dtype=w.dtype)
+
+
+def head_argmax(w: ModelWeights, x, weight, out_idx, ws: ops.Workspace, out_max=None, out_gap=None,
+                in_norm=None) -> None:
+    """lm_head fused with the per-row argmax (vocabulary-parallel when w.tp)."""
+    if w.tp is None:
+        ops.head_argmax(x, weight, out_idx, ws, out_max=out_max, out_gap=out_gap, in_norm=in_norm)
+    else:
+        ops.tp_head_argmax(w.tp, x, weight, w.vocab_offset, out_idx, ws, out_max=out_max, out_gap=out_gap,
+                           in_norm=in_norm)
+
+
+def head_topk(w: ModelWeights, x, weight, k: int, out_tok, out_lp, ws: ops.Workspace, vocab_ids=None,
+              in_norm=None) -> None:
+    """lm_head fused with the per-row log-softmax top-k (vocabulary-parallel when w.tp)."""
+    if w.tp is None:
+        ops.head_topk(x, weight, k, out_tok, out_lp, ws, vocab_ids=vocab_ids, in_norm=in_norm)
+    else:
+        ops.tp_head_topk(w.tp, x, weight, w.vocab_offset, k, out_tok, out_lp, ws, vocab_ids=vocab_ids,
+                         in_norm=in_norm)
 
 
 def _bridge_folded(bridge, scratch: Scratch, T: int, ws: ops.Workspace, xg, rn, nout) -> None:
@@ -381,6 +415,8 @@ def run_stack_auto(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm_b
     """The engines' forward: folded norms for bf16, standalone ones for fp32."""
     if folds_norms(w):
         run_stack_folded(w, layer_indices, pre_layer_bridges, pre_norm_bridge, fwd, T, cache, scratch, ws, kv_bound)
+    elif w.tp is not None:
+        raise NotImplementedError("tensor parallelism runs the bf16 path only")
     else:
         run_stack(w, layer_indices, pre_layer_bridges, pre_norm_bridge, fwd, T, cache, scratch, ws, kv_bound)
 

@@ -117,6 +117,8 @@ class SubnetworkDraftModel(nn.Module):
         if token_ids is None:
             self.vocab_ids = self._sub_head = None
             return
+        if getattr(self._base_model, "_ssd_tp_shard", None) is not None:
+            raise NotImplementedError("a draft vocabulary subset is not supported on a tensor-parallel shard")
         w = self.base.lm_head.weight
         self.vocab_ids = token_ids.to(device=w.device, dtype=torch.int64)
         self._sub_head = w.detach().index_select(0, self.vocab_ids).contiguous()
@@ -186,6 +188,9 @@ class SubnetworkDraftModel(nn.Module):
             raise NotImplementedError("output_layer_inputs is a training tap, not part of the B200 path")
         if input_ids is None and inputs_embeds is None:
             raise ValueError("pass input_ids or inputs_embeds")
+        if self.weights.tp is not None:
+            raise NotImplementedError("tensor-parallel shards run through the decode engines "
+                                      "(SpeculativeGenerator.generate / autoregressive_generate)")
         bsz, q_len = (input_ids.shape if input_ids is not None else inputs_embeds.shape[:2])
         if past_key_values is not None and bsz != 1:
             raise ValueError("the cached B200 path serves batch size 1")

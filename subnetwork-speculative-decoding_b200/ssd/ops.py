@@ -263,3 +263,35 @@ def tree_walk_sample(tree, tlogits, tparams, dlogits, dparams, draft_rows: int, 
            _p(dlogits), dlogits.stride(0), _p(dparams), draft_rows, dlogits.shape[1], _p(vocab_ids), _p(seed),
            _p(round_), _p(p_scratch), _p(q_scratch), _p(accepted), _p(n_accepted), _p(bonus), _p(keep_slots),
            _p(n_keep), _p(status), _stream())
+
+
+# ------------------------------------------------------------ tensor parallel
+def fill_normal(out: torch.Tensor, row0: int, col0: int, full_cols: int, seed: int, stream_id: int, std: float,
+                scale: float = 1.0) -> None:
+    """out (2-D, contiguous rows) <- block [row0:, col0:] of a seeded N(0, std^2) * scale global matrix."""
+    t = out if out.dim() == 2 else out.view(1, -1)
+    L.call("ssd_fill_normal", _p(t), t.shape[0], t.shape[1], t.stride(0), row0, col0, full_cols,
+           seed & (2 ** 64 - 1), stream_id & (2 ** 64 - 1), float(std), float(scale), dtype_code(t.dtype), _stream())
+
+
+def tp_allreduce_residual(group, T: int, resid: torch.Tensor, ws: Workspace, norm_out: Optional[NormOut] = None,
+                          dtype: torch.dtype = torch.bfloat16) -> None:
+    """resid[:T] += all-reduced partials of the group (see ssd_tp_allreduce_residual)."""
+    L.call("ssd_tp_allreduce_residual", group.ref(), T, _p(resid), resid.stride(0), _c(norm_out), dtype_code(dtype),
+           _p(ws.status), _stream())
+
+
+def tp_head_argmax(group, x, w_shard, vocab_offset: int, out_idx, ws: Workspace, out_max=None, out_gap=None,
+                   T: Optional[int] = None, in_norm: Optional[RowNorm] = None) -> None:
+    T = x.shape[0] if T is None else T
+    L.call("ssd_tp_head_argmax", group.ref(), _p(x), x.stride(0), T, w_shard.shape[1], _p(w_shard), w_shard.shape[0],
+           vocab_offset, _p(out_idx), _p(out_max), _p(out_gap), dtype_code(w_shard.dtype), ws.ptr, ws.nbytes,
+           _c(in_norm), _p(ws.status), _stream())
+
+
+def tp_head_topk(group, x, w_shard, vocab_offset: int, k: int, out_tok, out_lp, ws: Workspace, vocab_ids=None,
+                 T: Optional[int] = None, in_norm: Optional[RowNorm] = None) -> None:
+    T = x.shape[0] if T is None else T
+    L.call("ssd_tp_head_topk", group.ref(), _p(x), x.stride(0), T, w_shard.shape[1], _p(w_shard), w_shard.shape[0],
+           vocab_offset, _p(vocab_ids), k, _p(out_tok), _p(out_lp), dtype_code(w_shard.dtype), ws.ptr, ws.nbytes,
+           _c(in_norm), _p(ws.status), _stream())
