@@ -51,8 +51,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3"])
-    ap.add_argument("--sequences", type=int, default=N_SEQUENCES)
+    ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3", "c4"],
+                    help="c4 = the 70B configuration, tensor parallel over all ranks")
+    ap.add_argument("--sequences", type=int, default=None,
+                    help=f"sequences per step (default {N_SEQUENCES}; 1 for c4)")
+    ap.add_argument("--layers", type=int, default=None, help="override the model's layer count (c4 smoke runs)")
     ap.add_argument("--max-new", type=int, default=None, help="override new tokens per sequence")
     ap.add_argument("--prompt-len", type=int, default=None, help="override the prompt length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -131,6 +134,33 @@ def model_bytes(w, layers=None, bridges=(), head_rows=None) -> float:
     return float(total)
 
 
+def is_tp(spec) -> bool:
+    """The 70B configuration runs tensor parallel over all ranks."""
+    return spec.model == "llama3_70b"
+
+
+def build_tp(spec, dev, rank: int, world: int, max_rows: int, layers=None):
+    """This rank's shard of the 70B configuration, its tensor-parallel group
+    attached (weights drawn per shard on the device from the seed)."""
+    import torch
+
+    from ssd.config import BridgeConfig, DraftingConfig
+    from ssd.engine import tp
+    from ssd.engine.speculative import TargetRunner
+    from ssd.models import SubnetworkDraftModel
+
+    over = {} if layers is None else {"num_hidden_layers": layers}
+    draft_layers = spec.draft_layers if layers is None else [0, layers // 2, layers - 1]
+    base = tp.build_tp_base(spec.model, spec.seed, spec.dtype, dev, rank, world, plant_layers=draft_layers,
+                            plant_scale=spec.plant_scale, **over)
+    tp.attach(base, tp.TPGroup(base.config.hidden_size, max_rows, dev))
+    target = TargetRunner(base)
+    draft = SubnetworkDraftModel(base, draft_layers, BridgeConfig(hidden_dim=spec.bridge_hidden))
+    tp.init_bridges_device_(draft.bridges, spec.seed, spec.bridge_in_std, spec.bridge_out_std)
+    draft.bridges.to(spec.dtype)
+    return base, target, draft, DraftingConfig(**spec.drafting)
+
+
 def build(spec, dev):
     import torch
 
@@ -183,7 +213,7 @@ NCU_DRAM_BYTES_8B_33 = {"qkv": 50707200 + 35584, "o_proj": 34445312 + 7680, "gat
 def gemm_traffic_per_launch(w, rows: int):
     """Measured DRAM bytes per average launch of the verify GEMM mix (4 per
     layer + lm_head), for the 8B shape at 33 rows only (else None)."""
-    if (w.d, w.F, w.V, w.L, rows) != (4096, 14336, 128256, 32, 33):
+    if (w.d, w.F, w.V, w.L, rows) != (4096, 14336, 128256, 32, 33) or w.tp is not None:
         return None
     t = NCU_DRAM_BYTES_8B_33
     return (sum(t[k] for k in ("qkv", "o_proj", "gate_up", "down")) * w.L + t["lm_head_argmax"]) / (4 * w.L + 1)
@@ -209,6 +239,7 @@ def gemm_roofline(w, rows: int, dev) -> dict:
     resid = torch.zeros(rows, w.d, dtype=torch.float32, device=dev)
     idx = torch.empty(rows, dtype=torch.int32, device=dev)
     es = 2 if w.dtype == torch.bfloat16 else 4
+    head_rows = w.lm_head.shape[0]  # this rank's vocabulary shard under tensor parallelism
     kinds = {
         "qkv": (lambda lw: ops.linear(x_d, [lw.q, lw.k, lw.v], ws, out=q_out),
                 (w.H + 2 * w.Hkv) * w.hd * w.d * es + rows * w.d * es + rows * (w.H + 2 * w.Hkv) * w.hd * es),
@@ -260,14 +291,17 @@ def gemm_roofline(w, rows: int, dev) -> dict:
     f.use_mask = True
     q_in = (torch.randn(rows, w.H * w.hd, generator=g, device=dev) * 0.5).to(w.dtype)
     a_out = torch.empty_like(q_in)
-    xn = torch.empty(rows, w.d, dtype=w.dtype, device=dev)
     kv_bytes = ctx * w.Hkv * w.hd * 2 * es
     extra = {
         "attention": (lambda li: ops.tree_attention(q_in, kc[li, 0], kc[li, 1], w.H, w.Hkv, w.hd, f.prefix_len, a_out,
                                                     ws, spec_base=f.spec_base, spec_mask=f.mask, kv_bound=ctx + 64),
                       kv_bytes + 2 * rows * w.H * w.hd * es),
-        "rmsnorm": (lambda li: ops.rmsnorm(resid, w.layers[li].ln1, 1e-5, xn), rows * w.d * (4 + es) + w.d * es),
     }
+    if w.tp is not None:
+        # the fused all-reduce + residual of a row-parallel output: bytes that
+        # cross NVLink into each rank (the other ranks' fp32 partial rows)
+        nv = (w.tp.world - 1) * rows * w.d * 4
+        extra["tp_allreduce"] = (lambda li: ops.tp_allreduce_residual(w.tp, li % 2, rows, resid, ws), nv)
     for name, (fn, nbytes) in extra.items():
         for li in range(2):
             fn(li)
@@ -289,12 +323,14 @@ def gemm_roofline(w, rows: int, dev) -> dict:
         out[name] = {"us": t * 1e6, "gbs": nbytes / t / 1e9, "bytes": nbytes}
     del kc
     # lm_head + argmax over the full vocabulary (1 GB, > L2)
+    from ssd.models import runner as R
+
     graph = torch.cuda.CUDAGraph()
-    ops.head_argmax(x_d, w.lm_head, idx, ws)
+    R.head_argmax(w, x_d, w.lm_head, idx, ws)
     torch.cuda.synchronize(dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.graph(graph, stream=s):
-        ops.head_argmax(x_d, w.lm_head, idx, ws)
+        R.head_argmax(w, x_d, w.lm_head, idx, ws)
     torch.cuda.current_stream(dev).wait_stream(s)
     graph.replay()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -304,7 +340,7 @@ def gemm_roofline(w, rows: int, dev) -> dict:
     e1.record()
     torch.cuda.synchronize(dev)
     t = e0.elapsed_time(e1) / 1e3 / 5
-    nb = w.V * w.d * es + rows * w.d * es
+    nb = head_rows * w.d * es + rows * w.d * es
     out["lm_head_argmax"] = {"us": t * 1e6, "gbs": nb / t / 1e9, "bytes": nb}
     total_b += nb
     total_t += t
@@ -378,9 +414,14 @@ def workload_config(args, spec, world: int) -> dict:
     P = args.prompt_len or spec.prompt_len
     max_new = args.max_new or spec.max_new_tokens
     planted = f" planted x{spec.plant_scale}" if spec.plant_scale else ""
-    return {"workload": f"{args.workload}: {spec.model}{planted}, draft {spec.draft_layers}, tree {spec.drafting}, "
-                        f"prompt {P}, {max_new} new tokens, {args.sequences} sequences split over ranks",
-            "global_batch": 1, "seq_len": P + max_new, "parallelism": f"dp{world} (independent sequences)",
+    layers = f", {args.layers} layers" if getattr(args, "layers", None) else ""
+    if is_tp(spec):
+        split, par = f"{args.sequences} sequence(s), each on all ranks", f"tp{world} (tensor parallel)"
+    else:
+        split, par = f"{args.sequences} sequences split over ranks", f"dp{world} (independent sequences)"
+    return {"workload": f"{args.workload}: {spec.model}{layers}{planted}, draft {spec.draft_layers}, "
+                        f"tree {spec.drafting}, prompt {P}, {max_new} new tokens, {split}",
+            "global_batch": 1, "seq_len": P + max_new, "parallelism": par,
             "l2": "weights exceed L2 between rounds (no flush needed)"}
 
 
@@ -392,6 +433,12 @@ def reference_arm(args) -> None:
     from ssd import synthetic as S
 
     spec = S.CONFIGS[args.workload]
+    if is_tp(spec):
+        print(json.dumps({"impl": "reference", "unavailable": "the 70B configuration in fp32 needs ~280 GB of host "
+                                                              "memory: infeasible for the CPU port"}), flush=True)
+        return
+    if args.sequences is None:
+        args.sequences = N_SEQUENCES
     t0 = time.time()
     _, target, draft = build_oracle(spec)
     build_s = time.time() - t0
@@ -504,15 +551,24 @@ def main() -> None:
     from ssd.engine.speculative import SpeculativeGenerator, _finish
 
     spec = S.CONFIGS[args.workload]
+    tp_run = is_tp(spec)
+    if args.sequences is None:
+        args.sequences = 1 if tp_run else N_SEQUENCES
     P = args.prompt_len or spec.prompt_len
     max_new = args.max_new or spec.max_new_tokens
     t_build = time.time()
-    base, target, draft, cfg = build(spec, dev)
+    if tp_run:
+        base, target, draft, cfg = build_tp(spec, dev, rank, world, max_rows=P + 64, layers=args.layers)
+    else:
+        base, target, draft, cfg = build(spec, dev)
     w = target.weights
     seqs = [S.make_prompt(spec.seed + i, P, w.V) for i in range(args.sequences)]
     from ssd.engine import dp
 
-    mine = dp.shard(seqs, rank, world)
+    # data parallel: each rank decodes its share; tensor parallel: every rank
+    # takes part in every sequence (tokens counted once)
+    mine = seqs if tp_run else dp.shard(seqs, rank, world)
+    job_sum = (lambda x: x) if tp_run else (lambda x: sync_sum(x, world))
     cap = cache_capacity(P, max_new, TreePlan(cfg))
     eng = GreedyRound(target, draft, cfg, target.new_cache(cap), max_new)
     plan_rows = eng.plan.rows
@@ -567,7 +623,7 @@ def main() -> None:
             accs += acc
             rounds += len(acc)
     clk = clocks.stop()
-    n_tok_all = sync_sum(n_tok, world)
+    n_tok_all = job_sum(n_tok)
     per_step = t_total / args.steps
     value = n_tok_all / t_total
     gpu_launches = int(getattr(eng, "launches_per_round", 0) * rounds)
@@ -595,7 +651,7 @@ def main() -> None:
             torch.cuda.synchronize(dev)
             t_ar += sync_max(e0.elapsed_time(e1) / 1e3, world)
             n_ar += len(_finish(out, set(), max_new)[0])
-        ar_value = sync_sum(n_ar, world) / t_ar
+        ar_value = job_sum(n_ar) / t_ar
         del ar
 
     # end to end through the public API (pinned host prompt -> host tokens)
@@ -613,14 +669,18 @@ def main() -> None:
         t_e2e += sync_max(time.perf_counter() - t0, world)
         n_e2e += len(res.tokens)
     d2h = getattr(e2e_engine, "d2h_bytes", 0) - d2h0
-    e2e_value = sync_sum(n_e2e, world) / t_e2e
+    e2e_value = job_sum(n_e2e) / t_e2e
 
     # kernel roofline of the dominant kernel (tcgen05 GEMM, verify forward)
     peaks = measured_peaks()
-    roof = gemm_roofline(w, plan_rows, dev) if rank == 0 else None
+    # (tensor parallel: every rank runs it, the all-reduce needs all ranks)
+    roof = gemm_roofline(w, plan_rows, dev) if (rank == 0 or tp_run) else None
 
     cb = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if tp_run:
+        cb = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+              "sample": "not run: the 70B configuration in fp32 needs ~280 GB of host memory (infeasible on CPU)"}
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             cb = cpu_baseline(spec, base=base, draft=draft)
         except MemoryError as exc:
@@ -628,13 +688,14 @@ def main() -> None:
                   "sample": f"not run: {exc}"}
 
     if rank == 0:
-        tgt_bytes = model_bytes(w)
-        d_bytes = model_bytes(w, spec.draft_layers, list(draft.bridges.values()),
+        # per GPU: under tensor parallelism w holds this rank's shard
+        tgt_bytes = model_bytes(w, head_rows=w.lm_head.shape[0])
+        d_bytes = model_bytes(w, draft.layer_indices, list(draft.bridges.values()),
                               head_rows=draft.head_weight().shape[0])
         kv_tok = 2 * w.L * w.Hkv * w.hd * (2 if w.dtype == torch.bfloat16 else 4)
         mean_acc = sum(accs) / max(1, len(accs))
         ctx = P + max_new / 2
-        round_bytes = cfg.depth * d_bytes + tgt_bytes + ctx * kv_tok * (1 + cfg.depth * len(spec.draft_layers) / w.L)
+        round_bytes = cfg.depth * d_bytes + tgt_bytes + ctx * kv_tok * (1 + cfg.depth * len(draft.layer_indices) / w.L)
         ar_bytes = tgt_bytes + ctx * kv_tok
         bw = peaks["hbm_gbs"] * 1e9
         line = {

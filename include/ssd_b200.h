@@ -318,21 +318,21 @@ typedef struct SsdTpGroup {
 } SsdTpGroup;
 
 int64_t ssd_tp_region_bytes(int64_t max_rows, int64_t d);
-/* Byte offset in the region of the partial buffer, fp32 [max_rows, d] with
- * row stride d: the row-parallel o_proj / down_proj GEMM (ssd_linear with
- * SSD_EPI_STORE_F32) writes this rank's partial sums there. */
-int64_t ssd_tp_partial_offset(int64_t max_rows);
+/* Byte offset in the region of partial buffer `parity` (0 or 1), fp32
+ * [max_rows, d] with row stride d: the row-parallel o_proj / down_proj GEMM
+ * (ssd_linear with SSD_EPI_STORE_F32) writes this rank's partial sums there. */
+int64_t ssd_tp_partial_offset(int64_t max_rows, int64_t d, int parity);
 
-/* resid[t, :] += sum over ranks (in rank order) of the ranks' partials [T, d];
- * with norm_out also the next RMSNorm's folded input, as ssd_linear's residual
- * epilogue (bit-identical to it when world == 1). Two-shot over peer memory:
- * each rank sums a 1/world slice of the features and stores it into every
- * rank's region, so each rank moves 2 (world - 1) / world of the partial over
- * NVLink. When it returns on the stream, every rank has finished reading this
- * rank's partial (the next GEMM may overwrite it). This is the all-reduce after
+/* resid[t, :] += sum over ranks (in rank order) of the ranks' partials
+ * [T, d] in buffer `parity`; with norm_out also the next RMSNorm's folded
+ * input, as ssd_linear's residual epilogue (bit-identical to it when
+ * world == 1). One-shot over peer memory: each rank reads the other ranks'
+ * partials over NVLink after one meeting of the ranks. Consecutive calls must
+ * alternate parity (a rank overwrites a partial buffer only two calls later,
+ * when every rank has finished reading it). This is the all-reduce after
  * o_proj / down_proj (_layer_forward, ssd/models/subnetwork_draft.py:243,245)
  * of a tensor-parallel layer, fused with the residual add. dtype: of norm_out. */
-int ssd_tp_allreduce_residual(const SsdTpGroup* group, int64_t T, float* resid, int64_t ldr,
+int ssd_tp_allreduce_residual(const SsdTpGroup* group, int parity, int64_t T, float* resid, int64_t ldr,
                               const SsdNormOut* norm_out, int dtype, uint32_t* status, void* stream);
 
 /* Vocabulary-parallel heads. w: this rank's lm_head rows [vocab_offset,

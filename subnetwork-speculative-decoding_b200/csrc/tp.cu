@@ -12,19 +12,24 @@
 //   flags   [2 channels][2 phases][kTpMaxBlocks][8 sources] u32
 //   epochs  [2 channels][kTpMaxBlocks] u32   (this rank's own counters)
 //   records [max_rows][kTpRecFloats] f32     (head merge input)
-//   partial [max_rows][d] f32                (row-parallel GEMM output)
-//   sum     [max_rows][d] f32                (all-reduced rows)
+//   partial [2 parities][max_rows][d] f32    (row-parallel GEMM output)
 //
 // Synchronisation: block b of a kernel meets block b of the same kernel on
 // every other rank. Each block counts its uses in its epoch counter (the same
 // sequence on every rank), stores the epoch into flags[ch][phase][b][me] of
-// every rank (release, system scope) and polls its own flags[ch][phase][b][*]
-// (acquire) until every source has reached the epoch. Polls are bounded: on
+// every rank and polls its own flags[ch][phase][b][*] until every source has
+// reached the epoch (system-scope accesses; see tp_meet). Polls are bounded: on
 // timeout the block sets the status timeout bit and goes on (results are then
 // garbage but no GPU waits forever). Flags only grow, so they never need a
 // reset. Blocks wait only on blocks of other GPUs, and each kernel's blocks
 // fit on the GPU together, so a wait cannot block the block it waits for.
 // No multicast objects or multicast loads are used.
+//
+// All-reduce buffer reuse: consecutive all-reduce calls alternate the two
+// partial buffers. A rank signals a call only after all its earlier kernels
+// have completed (programmatic-launch wait first), so when any rank passes the
+// meeting of call k + 1, every rank has finished reading the partials of call
+// k; the GEMM of call k + 2, which overwrites them, comes later still.
 #include "gemm.cuh"
 #include "host.cuh"
 
@@ -45,11 +50,8 @@ __host__ __device__ inline int64_t tp_rec_offset() { return tp_align(kTpFlagByte
 __host__ __device__ inline int64_t tp_part_offset(int64_t max_rows) {
   return tp_align(tp_rec_offset() + max_rows * kTpRecFloats * 4);
 }
-__host__ __device__ inline int64_t tp_sum_offset(int64_t max_rows, int64_t d) {
-  return tp_align(tp_part_offset(max_rows) + max_rows * d * 4);
-}
 __host__ __device__ inline int64_t tp_region_bytes(int64_t max_rows, int64_t d) {
-  return tp_align(tp_sum_offset(max_rows, d) + max_rows * d * 4);
+  return tp_align(tp_part_offset(max_rows) + 2 * max_rows * d * 4);
 }
 
 // Kernel-side view of a group.
@@ -65,12 +67,12 @@ __device__ __forceinline__ uint32_t* tp_flag(uint8_t* region, int ch, int phase,
 __device__ __forceinline__ uint32_t* tp_epoch(uint8_t* region, int ch, int b) {
   return reinterpret_cast<uint32_t*>(region + kTpFlagBytes) + (int64_t)ch * kTpMaxBlocks + b;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -83,102 +85,98 @@ __device__ __forceinline__ uint32_t tp_next_epoch(const TpDev& g, int ch, int b)
   return v;
 }
 
-// Block-wide meeting of block b with its counterparts on every rank. Every
-// thread's earlier global (and peer) stores are visible to the peers' blocks
-// after their meeting, and theirs to this block. Returns false on timeout.
+// Block-wide meeting of block b with its counterparts on every rank. Thread
+// p (< world) signals rank p and waits for rank p's signal, so the peers are
+// polled in parallel. What the meetings order is always either data written
+// by kernels that completed before this one started (the programmatic-launch
+// wait comes first), or loads whose values this block has already consumed;
+// so the flags are relaxed system-scope accesses: no release fence per block
+// (a system fence costs microseconds and serialises the blocks of an SM).
+// Peer data read after a meeting is loaded with L1 bypassed (__ldcg).
+// Returns false on timeout.
 __device__ bool tp_meet(const TpDev& g, int ch, int phase, int b, uint32_t epoch, uint32_t* status) {
-  __shared__ int s_ok;
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int p = 0; p < g.world; ++p) st_release_sys(tp_flag(g.region[p], ch, phase, b, g.rank), epoch);
-    int ok = 1;
-    for (int p = 0; p < g.world && ok; ++p) {
-      const uint32_t* f = tp_flag(g.region[g.rank], ch, phase, b, p);
-      uint32_t it = 0;
-      while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
-        if (++it > kTpSpinLimit) {
-          report_error(status, kErrWaitTimeout);
-          ok = 0;
-          break;
-        }
-        __nanosleep(64);
+  int ok = 1;
+  if (threadIdx.x < g.world) {
+    const int p = threadIdx.x;
+    st_relaxed_sys(tp_flag(g.region[p], ch, phase, b, g.rank), epoch);
+    const uint32_t* f = tp_flag(g.region[g.rank], ch, phase, b, p);
+    uint32_t it = 0;
+    while ((int32_t)(ld_relaxed_sys(f) - epoch) < 0) {
+      if (++it > kTpSpinLimit) {
+        report_error(status, kErrWaitTimeout);
+        ok = 0;
+        break;
       }
+      __nanosleep(20);
     }
-    s_ok = ok;
   }
-  __syncthreads();
-  return s_ok != 0;
+  return __syncthreads_and(ok) != 0;
 }
 
 // ------------------------------------------------- all-reduce + residual
-// Block b owns 128 features `piece` of every rank's 1/world slice for tokens
-// [t0, t1). Phase 0: all partials written. Then it sums its own slice's piece
-// over the ranks (rank order: the same bits on every rank) and stores the
-// sums into every rank's sum buffer. Phase 1: all sums stored (and all reads
-// of this rank's partials done, so the next GEMM may overwrite them). Then it
-// adds the sums of the world pieces it received to the residual and writes
-// the folded RMSNorm input and per-tile sums of squares, bit-identical to
-// ssd_linear's residual epilogue.
+// One-shot: block b owns the 128-feature tile `tile` of tokens [t0, t1).
+// After one meeting (every rank's partial of this parity is complete) it
+// reads the tile from every rank's partial (peer loads over NVLink), sums in
+// rank order (the same bits on every rank), adds the sum to the residual and
+// writes the folded RMSNorm input and the tile's sums of squares,
+// bit-identical to ssd_linear's residual epilogue. Four tokens per pass: their
+// loads are in flight together and warp u reduces token u's squares.
 template <typename T>
-__global__ void __launch_bounds__(kTpThreads) tp_allreduce_kernel(TpDev g, int T_rows, int pieces, int tpb,
+__global__ void __launch_bounds__(kTpThreads) tp_allreduce_kernel(TpDev g, int parity, int T_rows, int tiles, int tpb,
                                                                   float* resid, int64_t ldr, SsdNormOut no,
                                                                   uint32_t* status) {
-  __shared__ float s_sq[kTpThreads];
-  const int b = blockIdx.x, tid = threadIdx.x;
-  const int piece = b % pieces, grp = b / pieces;
-  const int t0 = grp * tpb, t1 = min(T_rows, t0 + tpb);
-  const int64_t d = g.d, S = d / g.world;
-  pdl_wait();  // the partials come from the preceding GEMM
+  constexpr int kU = 4;
+  __shared__ float s_sq[kU][kTpThreads];
   __shared__ uint32_t s_epoch;
+  const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = b % tiles, grp = b / tiles;
+  const int t0 = grp * tpb, t1 = min(T_rows, t0 + tpb);
+  const int64_t d = g.d, n = (int64_t)tile * 128 + tid;
+  pdl_wait();  // the partials come from the preceding GEMM
   if (tid == 0) s_epoch = tp_next_epoch(g, kTpChanAllReduce, b);
   __syncthreads();
-  const uint32_t epoch = s_epoch;
-  tp_meet(g, kTpChanAllReduce, 0, b, epoch, status);
+  tp_meet(g, kTpChanAllReduce, 0, b, s_epoch, status);
+  pdl_trigger();
+  const int64_t po = tp_part_offset(g.max_rows) + (int64_t)parity * g.max_rows * d * 4;
   const float* part[kTpMaxRanks];
-  float* sum[kTpMaxRanks];
-  const int64_t po = tp_part_offset(g.max_rows), so = tp_sum_offset(g.max_rows, d);
 #pragma unroll
-  for (int p = 0; p < kTpMaxRanks; ++p) {
+  for (int p = 0; p < kTpMaxRanks; ++p)
     part[p] = p < g.world ? reinterpret_cast<const float*>(g.region[p] + po) : nullptr;
-    sum[p] = p < g.world ? reinterpret_cast<float*>(g.region[p] + so) : nullptr;
-  }
-  {
-    const int64_t n = (int64_t)g.rank * S + (int64_t)piece * 128 + tid;
-    for (int t = t0; t < t1; ++t) {
-      float v[kTpMaxRanks];
+  const T* w = static_cast<const T*>(no.weight);
+  const float wn = w ? to_f32<T>(w[n]) : 0.f;
+  for (int tb = t0; tb < t1; tb += kU) {
+    float v[kU][kTpMaxRanks], rv[kU];
 #pragma unroll
-      for (int p = 0; p < kTpMaxRanks; ++p) v[p] = p < g.world ? part[p][(int64_t)t * d + n] : 0.f;
+    for (int u = 0; u < kU; ++u) {
+      const int t = tb + u;
+#pragma unroll
+      for (int p = 0; p < kTpMaxRanks; ++p)
+        v[u][p] = (t < t1 && p < g.world) ? __ldcg(part[p] + (int64_t)t * d + n) : 0.f;
+      rv[u] = t < t1 ? resid[(int64_t)t * ldr + n] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int t = tb + u;
       float acc = 0.f;
 #pragma unroll
       for (int p = 0; p < kTpMaxRanks; ++p)
-        if (p < g.world) acc += v[p];
-#pragma unroll
-      for (int p = 0; p < kTpMaxRanks; ++p)
-        if (p < g.world) sum[p][(int64_t)t * d + n] = acc;
-    }
-  }
-  tp_meet(g, kTpChanAllReduce, 1, b, epoch, status);
-  pdl_trigger();
-  const float* mine = sum[g.rank];
-  const T* w = static_cast<const T*>(no.weight);
-  for (int q = 0; q < g.world; ++q) {
-    const int64_t n = (int64_t)q * S + (int64_t)piece * 128 + tid;
-    const int tile = (int)(n / 128);
-    const float wn = w ? to_f32<T>(w[n]) : 0.f;
-    for (int t = t0; t < t1; ++t) {
-      const float rn = resid[(int64_t)t * ldr + n] + mine[(int64_t)t * d + n];
-      resid[(int64_t)t * ldr + n] = rn;
-      if (!w) continue;
-      static_cast<T*>(no.out)[(int64_t)t * no.ldo + n] = from_f32<T>(rn * wn);
-      s_sq[tid] = rn * rn;
-      __syncthreads();
-      if (tid < 32) {
-        const float s = warp_sum((s_sq[tid] + s_sq[tid + 32]) + (s_sq[tid + 64] + s_sq[tid + 96]));
-        if (tid == 0) no.ssq[(int64_t)t * no.ld_ssq + tile] = s;
+        if (p < g.world) acc += v[u][p];
+      const float rn = rv[u] + acc;
+      if (t < t1) {
+        resid[(int64_t)t * ldr + n] = rn;
+        if (w) static_cast<T*>(no.out)[(int64_t)t * no.ldo + n] = from_f32<T>(rn * wn);
       }
-      __syncthreads();
+      s_sq[u][tid] = rn * rn;
     }
+    if (!w) continue;
+    __syncthreads();
+    if (warp < kU && tb + warp < t1) {
+      const float* q = s_sq[warp];
+      const float s = warp_sum((q[lane] + q[lane + 32]) + (q[lane + 64] + q[lane + 96]));
+      if (lane == 0) no.ssq[(int64_t)(tb + warp) * no.ld_ssq + tile] = s;
+    }
+    __syncthreads();
   }
 }
 
@@ -198,7 +196,7 @@ __global__ void tp_argmax_merge_kernel(TpDev g, int32_t* out_idx, float* out_max
   const int64_t ro = tp_rec_offset();
   if (threadIdx.x < g.world * 3) {
     const int p = threadIdx.x / 3, j = threadIdx.x % 3;
-    s_rec[threadIdx.x] = reinterpret_cast<const float*>(g.region[p] + ro)[(int64_t)t * 3 + j];
+    s_rec[threadIdx.x] = __ldcg(reinterpret_cast<const float*>(g.region[p] + ro) + (int64_t)t * 3 + j);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -238,7 +236,7 @@ __global__ void tp_topk_merge_kernel(TpDev g, int k, const int64_t* vocab_ids, i
   const int64_t ro = tp_rec_offset();
   for (int i = threadIdx.x; i < g.world * rec; i += blockDim.x) {
     const int p = i / rec, j = i % rec;
-    s_rec[i] = reinterpret_cast<const float*>(g.region[p] + ro)[(int64_t)t * rec + j];
+    s_rec[i] = __ldcg(reinterpret_cast<const float*>(g.region[p] + ro) + (int64_t)t * rec + j);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -332,40 +330,43 @@ int64_t ssd_tp_region_bytes(int64_t max_rows, int64_t d) {
   return tp_region_bytes(max_rows, d);
 }
 
-int64_t ssd_tp_partial_offset(int64_t max_rows) { return max_rows < 1 ? -1 : tp_part_offset(max_rows); }
+int64_t ssd_tp_partial_offset(int64_t max_rows, int64_t d, int parity) {
+  if (max_rows < 1 || d < 1 || parity < 0 || parity > 1) return -1;
+  return tp_part_offset(max_rows) + parity * max_rows * d * 4;
+}
 
-int ssd_tp_allreduce_residual(const SsdTpGroup* grp, int64_t T, float* resid, int64_t ldr,
+int ssd_tp_allreduce_residual(const SsdTpGroup* grp, int parity, int64_t T, float* resid, int64_t ldr,
                               const SsdNormOut* norm_out, int dtype, uint32_t* status, void* stream) {
   TpDev g;
   if (const int rc = tp_dev(grp, &g, "ssd_tp_allreduce_residual")) return rc;
   if (T < 1 || T > g.max_rows) return fail(SSD_ERR_INVALID, "ssd_tp_allreduce_residual: T = %lld outside 1..%lld",
                                            (long long)T, (long long)g.max_rows);
   if (!resid || ldr < g.d) return fail(SSD_ERR_INVALID, "ssd_tp_allreduce_residual: bad residual");
-  if (g.d % (128LL * g.world))
-    return fail(SSD_ERR_UNSUPPORTED, "ssd_tp_allreduce_residual: d = %lld is not a multiple of 128 x world",
-                (long long)g.d);
+  if (g.d % 128)
+    return fail(SSD_ERR_UNSUPPORTED, "ssd_tp_allreduce_residual: d = %lld is not a multiple of 128", (long long)g.d);
+  if (parity != 0 && parity != 1) return fail(SSD_ERR_INVALID, "ssd_tp_allreduce_residual: parity must be 0 or 1");
   if (dtype != SSD_BF16 && dtype != SSD_F32) return fail(SSD_ERR_INVALID, "ssd_tp_allreduce_residual: bad dtype");
   SsdNormOut no{};
   if (norm_out) {
     no = *norm_out;
     if (!no.weight || !no.out || !no.ssq) return fail(SSD_ERR_INVALID, "ssd_tp_allreduce_residual: partial norm_out");
   }
-  const int pieces = (int)(g.d / g.world / 128);
+  const int tiles = (int)(g.d / 128);
   // about four blocks per SM in all, each over a run of tokens
   const int target = 4 * device_sms();
-  int groups = target / pieces;
+  int groups = target / tiles;
   if (groups < 1) groups = 1;
   if (groups > T) groups = (int)T;
   const int tpb = (int)((T + groups - 1) / groups);
   groups = (int)((T + tpb - 1) / tpb);
-  const int blocks = pieces * groups;
+  const int blocks = tiles * groups;
   if (blocks > kTpMaxBlocks) return fail(SSD_ERR_UNSUPPORTED, "ssd_tp_allreduce_residual: too many blocks");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SSD_BF16)
     return launch_kernel("tp_allreduce_kernel", tp_allreduce_kernel<bf16>, dim3(blocks), dim3(kTpThreads), 0, s, 1, 1,
-                         g, (int)T, pieces, tpb, resid, ldr, no, status);
+                         g, parity, (int)T, tiles, tpb, resid, ldr, no, status);
   return launch_kernel("tp_allreduce_kernel", tp_allreduce_kernel<float>, dim3(blocks), dim3(kTpThreads), 0, s, 1, 1,
-                       g, (int)T, pieces, tpb, resid, ldr, no, status);
+                       g, parity, (int)T, tiles, tpb, resid, ldr, no, status);
 }
 
 int ssd_tp_head_argmax(const SsdTpGroup* grp, const void* x, int64_t ldx, int64_t T, int64_t K, const void* w,

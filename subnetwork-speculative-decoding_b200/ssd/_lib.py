@@ -74,8 +74,8 @@ SIGNATURES: dict[str, tuple] = {
     "ssd_tree_walk_sample": (I32, [P, I64, P, P, P, P, P, P, I64, P, I64, P, I64, P, I64, I64, P, P, P, P, P, P, P,
                                    P, P, P, P, P]),
     "ssd_tp_region_bytes": (I64, [I64, I64]),
-    "ssd_tp_partial_offset": (I64, [I64]),
-    "ssd_tp_allreduce_residual": (I32, [P, I64, P, I64, P, I32, P, P]),
+    "ssd_tp_partial_offset": (I64, [I64, I64, I32]),
+    "ssd_tp_allreduce_residual": (I32, [P, I32, I64, P, I64, P, I32, P, P]),
     "ssd_tp_head_argmax": (I32, [P, P, I64, I64, I64, P, I64, I64, P, P, P, I32, P, I64, P, P, P]),
     "ssd_tp_head_topk": (I32, [P, P, I64, I64, I64, P, I64, I64, P, I64, P, P, I32, P, I64, P, P, P]),
     "ssd_fill_normal": (I32, [P, I64, I64, I64, I64, I64, I64, C.c_uint64, C.c_uint64, F32, F32, I32, P]),

@@ -59,8 +59,8 @@ class TPGroup:
         self.rank = dist.get_rank(group) if group is not None else 0
         if self.world > L.TP_MAX_RANKS:
             raise ValueError(f"tensor parallelism supports at most {L.TP_MAX_RANKS} ranks")
-        if d % (128 * self.world):
-            raise ValueError(f"model width {d} is not a multiple of 128 x {self.world} ranks")
+        if d % 128:
+            raise ValueError(f"model width {d} is not a multiple of 128")
         self.d, self.max_rows = int(d), int(max_rows)
         self.device = torch.device(device)
         lib = L.load()
@@ -81,8 +81,12 @@ class TPGroup:
             torch.cuda.synchronize(self.device)
             dist.barrier(group)  # every region is zeroed before any rank writes a flag into it
         self.region = region
-        off = int(lib.ssd_tp_partial_offset(self.max_rows))
-        self.partial = region[off:off + self.max_rows * self.d * 4].view(torch.float32).view(self.max_rows, self.d)
+        n = self.max_rows * self.d * 4
+        self.partials = []
+        for parity in (0, 1):
+            off = int(lib.ssd_tp_partial_offset(self.max_rows, self.d, parity))
+            self.partials.append(region[off:off + n].view(torch.float32).view(self.max_rows, self.d))
+        self._calls = 0  # all-reduce calls issued since begin()
         arr = (C.c_void_p * L.TP_MAX_RANKS)(*ptrs, *([None] * (L.TP_MAX_RANKS - len(ptrs))))
         self._struct = L.SsdTpGroup(self.rank, self.world, self.max_rows, self.d, arr)
 
@@ -92,6 +96,22 @@ class TPGroup:
     def check_rows(self, T: int) -> None:
         if T > self.max_rows:
             raise RuntimeError(f"tensor-parallel exchange holds {self.max_rows} rows, the forward has {T}")
+
+    # Consecutive all-reduce calls must alternate the partial buffers, in the
+    # order the GPU runs them, across forwards and CUDA graphs alike: every
+    # forward starts at parity 0 (begin) and issues an even number of calls
+    # (two per layer), so any concatenation of forwards alternates.
+    def begin(self) -> None:
+        self._calls = 0
+
+    def next_parity(self) -> int:
+        p = self._calls & 1
+        self._calls += 1
+        return p
+
+    def end(self) -> None:
+        if self._calls & 1:
+            raise RuntimeError("a tensor-parallel forward issued an odd number of all-reduce calls")
 
 
 # ------------------------------------------------------------ shard layout

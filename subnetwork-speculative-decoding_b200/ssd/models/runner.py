@@ -321,6 +321,8 @@ def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm
     out_for = lambda k: ops.NormOut(norms[k][0], xg, ssq)
     in_for = lambda k: ops.RowNorm(ssq, parts, d, norms[k][1])
     ops.embed(fwd.ids[:T], w.embed, resid, ws, norm_out=out_for(0))
+    if w.tp is not None:
+        w.tp.begin()
     k = 0
     for slot, li in enumerate(layer_indices):
         b = pre_layer_bridges[slot]
@@ -343,6 +345,8 @@ def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm
         _bridge_folded(pre_norm_bridge, scratch, T, ws, xg, in_for(k), out_for(k + 1))
         k += 1
     assert k == len(norms) - 1
+    if w.tp is not None:
+        w.tp.end()
 
 
 def _residual_linear(w: ModelWeights, x, weight, ws: ops.Workspace, resid, norm_out, T: int) -> None:
@@ -353,8 +357,9 @@ def _residual_linear(w: ModelWeights, x, weight, ws: ops.Workspace, resid, norm_
         ops.linear(x, [weight], ws, epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=norm_out)
         return
     w.tp.check_rows(T)
-    ops.linear(x, [weight], ws, epilogue=L.EPI_STORE_F32, out=w.tp.partial[:T])
-    ops.tp_allreduce_residual(w.tp, T, resid, ws, norm_out=norm_out, dtype=w.dtype)
+    parity = w.tp.next_parity()
+    ops.linear(x, [weight], ws, epilogue=L.EPI_STORE_F32, out=w.tp.partials[parity][:T])
+    ops.tp_allreduce_residual(w.tp, parity, T, resid, ws, norm_out=norm_out, dtype=w.dtype)
 
 
 def head_argmax(w: ModelWeights, x, weight, out_idx, ws: ops.Workspace, out_max=None, out_gap=None,

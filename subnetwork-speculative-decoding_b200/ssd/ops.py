@@ -274,11 +274,11 @@ def fill_normal(out: torch.Tensor, row0: int, col0: int, full_cols: int, seed: i
            seed & (2 ** 64 - 1), stream_id & (2 ** 64 - 1), float(std), float(scale), dtype_code(t.dtype), _stream())
 
 
-def tp_allreduce_residual(group, T: int, resid: torch.Tensor, ws: Workspace, norm_out: Optional[NormOut] = None,
-                          dtype: torch.dtype = torch.bfloat16) -> None:
-    """resid[:T] += all-reduced partials of the group (see ssd_tp_allreduce_residual)."""
-    L.call("ssd_tp_allreduce_residual", group.ref(), T, _p(resid), resid.stride(0), _c(norm_out), dtype_code(dtype),
-           _p(ws.status), _stream())
+def tp_allreduce_residual(group, parity: int, T: int, resid: torch.Tensor, ws: Workspace,
+                          norm_out: Optional[NormOut] = None, dtype: torch.dtype = torch.bfloat16) -> None:
+    """resid[:T] += all-reduced partials (buffer `parity`) of the group (see ssd_tp_allreduce_residual)."""
+    L.call("ssd_tp_allreduce_residual", group.ref(), parity, T, _p(resid), resid.stride(0), _c(norm_out),
+           dtype_code(dtype), _p(ws.status), _stream())
 
 
 def tp_head_argmax(group, x, w_shard, vocab_offset: int, out_idx, ws: Workspace, out_max=None, out_gap=None,

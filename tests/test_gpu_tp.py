@@ -77,10 +77,10 @@ def test_one_rank_allreduce_residual_matches_fused_epilogue():
     fused_s, tp_s = torch.zeros(T, parts, device=dev), torch.zeros(T, parts, device=dev)
     ops.linear(x, [w], ws, epilogue=L.EPI_RESIDUAL, resid=fused_r, norm_out=ops.NormOut(wn, fused_x, fused_s))
     grp = _single_group(d, 64)
-    for _ in range(3):  # repeated calls advance the epochs
+    for i in range(4):  # repeated calls advance the epochs and alternate the buffers
         tp_r.copy_(resid0)
-        ops.linear(x, [w], ws, epilogue=L.EPI_STORE_F32, out=grp.partial[:T])
-        ops.tp_allreduce_residual(grp, T, tp_r, ws, norm_out=ops.NormOut(wn, tp_x, tp_s))
+        ops.linear(x, [w], ws, epilogue=L.EPI_STORE_F32, out=grp.partials[i % 2][:T])
+        ops.tp_allreduce_residual(grp, i % 2, T, tp_r, ws, norm_out=ops.NormOut(wn, tp_x, tp_s))
     torch.cuda.synchronize()
     ws.check_status()
     assert torch.equal(tp_r, fused_r)
