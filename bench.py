@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--prompt-len", type=int, default=None, help="override the prompt length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ar", action="store_true", help="skip the target-only baseline")
+    ap.add_argument("--sweep", choices=["c5"], default=None,
+                    help="c5: tree-attention and KV-compaction sweep (ctx x tree nodes) on one GPU, then exit")
     ap.add_argument("--ncu-case", choices=["gemm", "gemm_mix", "attention"], default=None,
                     help="run one small launch set of a kernel for an ncu capture, then exit")
     return ap.parse_args()
@@ -526,6 +528,124 @@ def ncu_case(args, dev) -> None:
     print(json.dumps({"ncu_case": args.ncu_case, "ok": True}))
 
 
+def c5_tree(nodes: int, depth: int, seed: int) -> list[int]:
+    """Random tree of `nodes` nodes and depth `depth` below the root (node 0):
+    depth d holds about nodes/depth nodes (at least one), each with a random
+    parent at depth d - 1. Returns parents (root: -1)."""
+    import random
+
+    rng = random.Random(seed)
+    per = [max(1, nodes // depth + (1 if d < nodes % depth else 0)) for d in range(depth)]
+    while sum(per) > nodes:
+        per[per.index(max(per))] -= 1
+    parents, prev = [-1], [0]
+    for d in range(depth):
+        cur = []
+        for _ in range(per[d]):
+            parents.append(rng.choice(prev))
+            cur.append(len(parents) - 1)
+        prev = cur
+    return parents
+
+
+def c5_sweep(args, dev) -> None:
+    """tree attention at the 8B shape over a cache of
+    committed positions K/V ~ N(0, 1) (seed 4), ctx x tree nodes, plus the KV
+    compaction of an accepted path. Each cell times 32 launches (one per
+    layer's cache, > L2 in total) captured in a CUDA graph, CUDA events
+    around 5 replays."""
+    import torch
+
+    from ssd import ops
+    from ssd.models.runner import ForwardInputs
+
+    H, Hkv, hd, L = 32, 8, 128, 32
+    ctxs, node_counts, depth = [1024, 4096, 16384, 32768], [8, 24, 64], 6
+    slack = 128
+    max_len = max(ctxs) + slack
+    g = torch.Generator(device=dev).manual_seed(4)
+    buf = torch.empty(L, 2, Hkv, max_len, hd, dtype=torch.bfloat16, device=dev)
+    for li in range(L):
+        buf[li].normal_(generator=g)
+    peaks = measured_peaks()
+    cells = []
+    ws = ops.Workspace(dev, 128, 1, 128)
+    s = torch.cuda.Stream(device=dev)
+    for n in node_counts:
+        parents = c5_tree(n, depth, 4)
+        rows = len(parents)
+        words = (rows + 63) // 64
+        f = ForwardInputs(rows, dev, words)
+        bits = torch.zeros(rows, words, dtype=torch.int64)
+        for r in range(rows):
+            a = r
+            while a >= 0:
+                w_, b_ = divmod(a, 64)
+                bits[r, w_] |= (1 << b_) if b_ < 63 else -(1 << 63)
+                a = parents[a]
+        f.mask[:rows].copy_(bits)
+        q = torch.randn(rows, H * hd, generator=g, device=dev).bfloat16()
+        out = torch.empty_like(q)
+        for ctx in ctxs:
+            f.prefix_len.fill_(ctx)
+            f.spec_base.fill_(ctx)
+
+            def run():
+                for li in range(L):
+                    ops.tree_attention(q, buf[li, 0], buf[li, 1], H, Hkv, hd, f.prefix_len, out, ws,
+                                       spec_base=f.spec_base, spec_mask=f.mask, kv_bound=ctx + rows, T=rows)
+
+            run()
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.graph(graph, stream=s):
+                run()
+            torch.cuda.current_stream(dev).wait_stream(s)
+            graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(5):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            t = e0.elapsed_time(e1) / 1e3 / (5 * L)
+            nbytes = (ctx + rows) * Hkv * hd * 2 * 2 + 2 * rows * H * hd * 2
+            cells.append({"ctx": ctx, "nodes": n, "rows": rows, "us": t * 1e6, "gbs": nbytes / t / 1e9,
+                          "frac": nbytes / t / 1e9 / peaks["hbm_gbs"], "bytes": nbytes})
+            del graph
+    ws.check_status()
+    # KV compaction of an accepted path of depth + 1 positions over all layers
+    keep = torch.tensor([0] + list(range(2, 2 + depth)), dtype=torch.int32, device=dev)
+    start = torch.tensor([max(ctxs) - 1], dtype=torch.int32, device=dev)
+    n_keep = torch.tensor([depth + 1], dtype=torch.int32, device=dev)
+
+    def comp():
+        for _ in range(L):
+            ops.kv_compact(buf, start, keep, n_keep, max_keep=depth + 1)
+
+    comp()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.graph(graph, stream=s):
+        comp()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = e0.elapsed_time(e1) / 1e3 / (5 * L)
+    cbytes = 2 * (depth + 1) * L * 2 * Hkv * hd * 2
+    print(json.dumps({"sweep": "c5", "shape": "8B (H 32, Hkv 8, hd 128), 32 layer caches, K/V ~ N(0,1) seed 4",
+                      "attention": cells,
+                      "compaction": {"kept": depth + 1, "us": t * 1e6, "gbs": cbytes / t / 1e9, "bytes": cbytes},
+                      "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"]}), flush=True)
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
@@ -541,6 +661,9 @@ def main() -> None:
     dev = torch.device("cuda", local)
     if args.ncu_case:
         ncu_case(args, dev)
+        return
+    if args.sweep == "c5":
+        c5_sweep(args, dev)
         return
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
