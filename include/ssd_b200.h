@@ -177,8 +177,9 @@ int ssd_head_topk(const void* x, int64_t ldx, int64_t T, int64_t K, const void* 
  * k children each from topk_tok / topk_lp [n_frontier, k] (tokens < 0 or
  * -inf log-probs are missing candidates). Candidates are ordered by
  * descending cumulative score (fp64, ties keep frontier order then rank) and
- * the first `width` (all if width <= 0) are appended at index *n_nodes,
- * which is advanced; their indices go to next_frontier. If `fed`, the level
+ * the first `width` (all if width <= 0) are appended at index *n_nodes
+ * (at index 0 for level 0, which starts a new tree), which is advanced;
+ * their indices go to next_frontier. If `fed`, the level
  * is the input of the next draft forward and its ids / positions
  * (root_pos + level + 1) / cache slots (root_pos + 1 + level_slot_offset + j)
  * / prefix length (root_pos + 1) / ancestor bitmask over spec slots starting

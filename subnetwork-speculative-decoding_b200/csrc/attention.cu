@@ -700,13 +700,17 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
 // M = 128 tcgen05 tile; rows past the group are zero) x one key slice.
 // Warp 0 streams the slice's 64-key K and V blocks by TMA (128-byte swizzle,
 // straight from the cache rows) into a kTcAttnStages ring. Warp 1 (one
-// lane) issues S = Q K^T into one of two TMEM S buffers and O += P V into a
-// TMEM O accumulator (V read MN-major as stored). Warps 2..5 own one query
-// row per thread (= TMEM lane): they load S, apply the tree mask, run the
-// online softmax in base 2 with a lazy reference max (P = 2^(s - m_ref)
-// stays below 2^8, so O is rescaled only when a row's max grows by more than
-// 8), write P as bf16 into shared memory for the P V product and, at the
-// end, read O back. Partials of the key slices merge as in the mma.sync
+// lane) issues S = Q K^T into one of two TMEM S buffers and O += P V into
+// one of two TMEM O accumulators (V read MN-major as stored). On long slices
+// two softmax warpgroups split the key blocks: warps 2..5 take the even blocks
+// (S, P and O buffers 0), warps 6..9 the odd ones (buffers 1), so each SM
+// sub-partition runs two softmax warps; on short slices warps 2..5 take every
+// block (S and P buffers alternate, one O accumulator). A softmax thread owns one query row (= TMEM lane):
+// it loads S, applies the tree mask, runs the online softmax in base 2 with a
+// lazy reference max (P = 2^(s - m_ref) stays below 2^8, so O is rescaled
+// only when a row's max grows by more than 8) and writes P as bf16 into
+// shared memory for the P V product. At the end the two warpgroups combine
+// their (max, sum, O) states of each row; each writes half of the columns. Partials of the key slices merge as in the mma.sync
 // kernel: pushed into the merging CTA of the cluster, or through global
 // memory for long contexts.
 // 2^x on the special-function unit (PTX ex2.approx.ftz.f32; 2^-inf = +0).
@@ -717,8 +721,12 @@ __device__ __forceinline__ float ex2_fast(float x) {
 }
 constexpr int kTcAttnStages = 4;
 constexpr int kTcAttnMaxTok = 129;  // token rows spanned by 128 query rows (keeps the metadata 8-byte aligned)
-constexpr int kTcAttnThreads = 192;
+constexpr int kTcAttnThreads = 320;  // TMA warp, MMA warp, two softmax warpgroups
 constexpr float kLazyRescale = 8.f;  // log2 headroom of P before O is rescaled
+// Key blocks per CTA from which the second softmax warpgroup takes the odd
+// blocks (below it warps 2..5 take every block and accumulator 1 stays unused:
+// short slices are bound by the CTA's set-up and merge, not by the softmax).
+constexpr int kTcTwoGroupsMinBlocks = 12;
 
 struct AttnMaps {
   CUtensorMap k;  // [n_kv * max_slots, hd] bf16, box {64, 64}
@@ -794,11 +802,11 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
       mbar_init(&p_free[i], 1);
     }
     mbar_init(o_full, 1);
-    mbar_init(q_ready, 5);  // warps 1..5 have staged their Q rows
+    mbar_init(q_ready, kTcAttnThreads / 32 - 1);  // warps 1.. have staged their Q rows
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -824,6 +832,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   const int k_lo = split * slice;
   const int k_hi = min(k_lo + slice, need_end);
   const int nblocks = k_hi > k_lo ? (k_hi - k_lo + KB - 1) / KB : 0;
+  const bool two = nblocks >= kTcTwoGroupsMinBlocks;  // CTA-uniform
   const uint32_t qs_s = smem_u32(qs), ring_s = smem_u32(ring), ps_s = smem_u32(ps);
   if (warp >= 1) {
     // Q rows (A operand, K-major, 128-byte swizzle; rows past Mg are zero),
@@ -840,11 +849,14 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(q_ready);
   }
-  const uint32_t tm_o = tmem + 128;  // O accumulator columns [128, 128 + HD)
+  // TMEM columns: S buffers [0, 64) and [64, 128), O accumulators of the
+  // even and odd key blocks at [128, 128 + HD) and [256, 256 + HD)
+  const uint32_t tm_o = tmem + 128;
 
-  // softmax-side state (warps 2..5)
+  // softmax-side state (warps 2..9): warpgroup wg takes key blocks wg, wg + 2, ...
   const int q = warp & 3;
   const int r = q * 32 + lane;  // query row of this thread = TMEM lane
+  const int wg = warp >= 6 ? 1 : 0;
   const bool row_ok = warp >= 2 && r < Mg;
   float m_ref = -INFINITY, l = 0.f;
 
@@ -899,8 +911,9 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
         const uint32_t pb = ps_s + (j & 1) * Lay::P_BYTES;
 #pragma unroll
         for (int kk = 0; kk < KB / 16; ++kk)
-          umma_bf16(tm_o, sdesc_k_sw128(pb + kk * 32), sdesc_mn_sw128(vb + kk * 2048, Lay::KV_REGION, 1024), id_pv,
-                    (j > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16(tm_o + (two ? (j & 1) * 128 : 0), sdesc_k_sw128(pb + kk * 32),
+                    sdesc_mn_sw128(vb + kk * 2048, Lay::KV_REGION, 1024), id_pv,
+                    (j > (two ? 1 : 0) || kk > 0) ? 1u : 0u);
         umma_commit(&p_free[j & 1]);
         umma_commit(&kv_empty[j % kTcAttnStages]);
       };
@@ -935,7 +948,9 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     const float sc = a.scale * 1.4426950408889634f;  // base 2
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     bool bad = false;
-    for (int b = 0; b < nblocks; ++b) {
+    const uint32_t tm_ow = tm_o + (two ? wg * 128 : 0);
+    const int b0 = two ? wg : (wg == 0 ? 0 : nblocks), bstep = two ? 2 : 1;
+    for (int b = b0; b < nblocks; b += bstep) {
       const int sbuf = b & 1;
       bad = !mbar_wait(&s_full[sbuf], (b >> 1) & 1) || *abort_flag;
       if (__any_sync(0xffffffffu, bad)) {
@@ -968,19 +983,20 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
       if (__any_sync(0xffffffffu, grow)) {
         const float m_new = grow ? bm : m_ref;
         const float alpha = (!grow || m_ref == -INFINITY) ? (grow ? 0.f : 1.f) : exp2f(m_ref - m_new);
-        if (b > 0) {
-          // O holds earlier blocks: rescale it once P V of block b - 1 is done
-          const bool w_ok = mbar_wait(&p_free[(b - 1) & 1], ((b - 1) >> 1) & 1);
+        if (b >= bstep) {
+          // this warpgroup's O holds earlier blocks: rescale it once P V of
+          // its previous block b - bstep is done
+          const int pb = b - bstep;
+          const bool w_ok = mbar_wait(&p_free[pb & 1], (pb >> 1) & 1);
           if (!w_ok) report_error(a.status, kErrWaitTimeout);
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < HD / 64; ++c) {
-            float ov[64];
-            tmem_ld64(tm_o + lane_base + c * 64, ov);
+          for (int c = 0; c < HD; c += 16) {
+            float ov[16];
+            tmem_ld16(tm_ow + lane_base + c, ov);
 #pragma unroll
-            for (int i = 0; i < 64; ++i) ov[i] *= alpha;
-#pragma unroll
-            for (int i = 0; i < 64; i += 16) tmem_st16(tm_o + lane_base + c * 64 + i, ov + i);
+            for (int i = 0; i < 16; ++i) ov[i] *= alpha;
+            tmem_st16(tm_ow + lane_base + c, ov);
           }
           tmem_wait_st();
         }
@@ -1014,33 +1030,60 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     }
     (void)bad;
   }
-  // ---- results: warps 2..5 read their O rows
-  float o[HD];
+  // ---- results: the two softmax warpgroups combine their states of each
+  // row (base 2) and each reads half of the O columns of both accumulators
+  constexpr int HH = HD / 2;
+  float ov[HH];
 #pragma unroll
-  for (int i = 0; i < HD; ++i) o[i] = 0.f;
+  for (int i = 0; i < HH; ++i) ov[i] = 0.f;
+  float Mrow = -INFINITY, Lrow = 0.f;
+  const int c0 = wg * HH;
   if (warp >= 2) {
     const bool w_ok = mbar_wait(o_full, 0);
     if (!w_ok) report_error(a.status, kErrWaitTimeout);
     tc_fence_after();
-    if (nblocks > 0 && w_ok && !*abort_flag) {
+    float* s_ml = reinterpret_cast<float*>(ps);  // the P buffers are free once every P V retired
+    s_ml[(wg * 128 + r) * 2] = m_ref;
+    s_ml[(wg * 128 + r) * 2 + 1] = l;
+    named_bar_sync(3, kTcAttnThreads - 64);
+    const float m0 = s_ml[r * 2], l0 = s_ml[r * 2 + 1];
+    const float m1 = s_ml[(128 + r) * 2], l1 = s_ml[(128 + r) * 2 + 1];
+    Mrow = fmaxf(m0, m1);
+    const float a0 = m0 == -INFINITY ? 0.f : exp2f(m0 - Mrow);
+    const float a1 = m1 == -INFINITY ? 0.f : exp2f(m1 - Mrow);
+    Lrow = a0 * l0 + a1 * l1;
+    // accumulator 0 holds data once a block ran, accumulator 1 once two did
+    if (__all_sync(0xffffffffu, nblocks > 0 && w_ok && !*abort_flag)) {
+      const uint32_t lb = static_cast<uint32_t>(q * 32) << 16;
 #pragma unroll
-      for (int c = 0; c < HD / 64; ++c) tmem_ld64(tm_o + (static_cast<uint32_t>(q * 32) << 16) + c * 64, o + c * 64);
+      for (int i = 0; i < HH; i += 16) {
+        float x[16], y[16];
+        tmem_ld16(tm_o + lb + c0 + i, x);
+        if (two && nblocks > 1) {
+          tmem_ld16(tm_o + 128 + lb + c0 + i, y);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) y[k] = 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 16; ++k) ov[i + k] = a0 * x[k] + a1 * y[k];
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
   bf16* outp = static_cast<bf16*>(a.out);
   if (P == 1) {
     if (row_ok) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float inv = Lrow > 0.f ? 1.f / Lrow : 0.f;
       const int qr = q0 + r;
-      bf16* op = outp + (int64_t)(qr / a.G) * a.ldo + (int64_t)(h * a.G + qr % a.G) * HD;
+      bf16* op = outp + (int64_t)(qr / a.G) * a.ldo + (int64_t)(h * a.G + qr % a.G) * HD + c0;
 #pragma unroll
-      for (int d = 0; d < HD; d += 2) *reinterpret_cast<uint32_t*>(op + d) = pack_bf16(o[d] * inv, o[d + 1] * inv);
+      for (int d = 0; d < HH; d += 2) *reinterpret_cast<uint32_t*>(op + d) = pack_bf16(ov[d] * inv, ov[d + 1] * inv);
     }
     return;
   }
@@ -1091,9 +1134,10 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
       const int owner = r % ns, j = r / ns;
       const uint32_t base = dsmem_map(smem_u32(recv), static_cast<uint32_t>(owner)) +
                             (uint32_t)(((split * owned + j) * rec) * 4);
-      dsmem_st4(base, m_ref, l, 0.f, 0.f);
+      if (wg == 0) dsmem_st4(base, Mrow, Lrow, 0.f, 0.f);
 #pragma unroll
-      for (int d = 0; d < HD; d += 4) dsmem_st4(base + (uint32_t)(4 + d) * 4, o[d], o[d + 1], o[d + 2], o[d + 3]);
+      for (int d = 0; d < HH; d += 4)
+        dsmem_st4(base + (uint32_t)(4 + c0 + d) * 4, ov[d], ov[d + 1], ov[d + 2], ov[d + 3]);
     }
     cluster_sync_all();
     const int n_own = Mg > split ? (Mg - split + ns - 1) / ns : 0;
@@ -1103,30 +1147,70 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     }
     return;
   }
-  // Long contexts: records in the global workspace slot of (row group, slice).
+  // Long contexts: records in the global workspace slot of (row group,
+  // slice); attn_merge_kernel combines the slices of every row in parallel.
   float* recs = a.part + ((int64_t)blk * a.n_splits + split) * a.rows_per_group * rec;
   if (row_ok) {
     float* pr = recs + (int64_t)r * rec;
-    pr[0] = m_ref;
-    pr[1] = l;
+    if (wg == 0) {
+      pr[0] = Mrow;
+      pr[1] = Lrow;
+    }
 #pragma unroll
-    for (int d = 0; d < HD; d += 2) *reinterpret_cast<float2*>(pr + 4 + d) = make_float2(o[d], o[d + 1]);
+    for (int d = 0; d < HH; d += 2) *reinterpret_cast<float2*>(pr + 4 + c0 + d) = make_float2(ov[d], ov[d + 1]);
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const uint32_t prev = atomicAdd(&a.counters[kAttnCounterBase + blk], 1u);
-    s_misc[2] = (prev == (uint32_t)(a.n_splits - 1)) ? 1 : 0;
+}
+
+// Merge of the key-slice records written by attn_tc_kernel (long contexts):
+// one warp per query row, all rows of all row groups in parallel. Slices
+// combine in a fixed order (max, then weighted sums in slice order), lane l
+// owning columns l * HD/32 ...; the same arithmetic as the in-kernel merges.
+template <int HD>
+__global__ void __launch_bounds__(256) attn_merge_kernel(const AttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int DPL = HD / 32;
+  const int blk = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rr = blockIdx.y * 8 + warp;
+  const int h = blk / a.groups, gr = blk % a.groups;
+  const int M = a.T * a.G;
+  const int q0 = gr * a.rows_per_group;
+  const int Mg = min(a.rows_per_group, M - q0);
+  if (rr >= Mg) return;
+  const int P = a.n_splits, rec = mma_rec(HD);
+  const float* base = a.part + (int64_t)blk * P * a.rows_per_group * rec + (int64_t)rr * rec;
+  const int64_t sstride = (int64_t)a.rows_per_group * rec;
+  float ms = -INFINITY, ls = 0.f;
+  if (lane < P) {
+    ms = base[lane * sstride];
+    ls = base[lane * sstride + 1];
   }
-  __syncthreads();
-  if (!s_misc[2]) return;
-  __threadfence();
-  const float* gbase = a.part + (int64_t)blk * a.n_splits * a.rows_per_group * rec;
-  for (int rr = warp; rr < Mg; rr += nwarps) {
-    auto at = [&](int pp, int f) { return __ldcg(gbase + ((int64_t)pp * a.rows_per_group + rr) * rec + f); };
-    merge_row(rr, at);
+  const float Mx = warp_max(ms);
+  const float wgt = (ms == -INFINITY || Mx == -INFINITY) ? 0.f : exp2f(ms - Mx);
+  const float L = warp_sum(ls * wgt);
+  float acc[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+  for (int p0 = 0; p0 < P; p0 += 16) {
+    float v[16][DPL];
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) v[u][i] = (p0 + u < P) ? base[(p0 + u) * sstride + 4 + lane * DPL + i] : 0.f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const float ws = __shfl_sync(0xffffffffu, wgt, (p0 + u) & 31);
+      if (p0 + u < P) {
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[i] = fmaf(ws, v[u][i], acc[i]);
+      }
+    }
   }
-  if (threadIdx.x == 0) a.counters[kAttnCounterBase + blk] = 0u;
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const int qr = q0 + rr;
+  bf16* op = static_cast<bf16*>(a.out) + (int64_t)(qr / a.G) * a.ldo + (int64_t)(h * a.G + qr % a.G) * HD + lane * DPL;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) op[i] = f2bf(acc[i] * inv);
 }
 
 // Clusters of `s` CTAs (one row group's key slices) that can be resident at
@@ -1277,16 +1361,15 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
       allow_max_dynamic_smem(kern);
       set = true;
     }
+    // One CTA per SM: up to 8 slices merge in a cluster for <= 8k keys;
+    // beyond, one wave of slices (blocks x slices <= SMs) and a separate
+    // merge kernel.
     int64_t splits = sms / blocks;
     const int64_t by_len = (kv_bound + 255) / 256;
     if (splits > by_len) splits = by_len;
     if (kv_bound <= 8 * 1024) {
       if (splits > kMaxAttnClusterSplits) splits = kMaxAttnClusterSplits;
       while (splits > 1 && attn_resident_clusters_tc(kern, (int)splits, smem, kTcAttnThreads) < blocks) --splits;
-    } else {
-      int64_t want = (2 * sms) / blocks;
-      if (want > by_len) want = by_len;
-      if (want > splits) splits = want;
     }
     if (splits > kMaxPartials) splits = kMaxPartials;
     if (splits < 1) splits = 1;
@@ -1301,8 +1384,12 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
       a.counters = static_cast<uint32_t*>(workspace);
       a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
     }
-    return launch_kernel("attn_tc_kernel", kern, dim3((unsigned)blocks, (unsigned)a.n_splits), dim3(kTcAttnThreads),
-                         smem, s, 1u, a.cluster_merge ? (unsigned)a.n_splits : 1u, maps, a);
+    rc = launch_kernel("attn_tc_kernel", kern, dim3((unsigned)blocks, (unsigned)a.n_splits), dim3(kTcAttnThreads),
+                       smem, s, 1u, a.cluster_merge ? (unsigned)a.n_splits : 1u, maps, a);
+    if (rc || a.n_splits == 1 || a.cluster_merge) return rc;
+    const dim3 mgrid((unsigned)blocks, (unsigned)((a.rows_per_group + 7) / 8));
+    return head_dim == 128 ? launch_kernel("attn_merge_kernel", attn_merge_kernel<128>, mgrid, dim3(256), 0, s, 1, 1, a)
+                           : launch_kernel("attn_merge_kernel", attn_merge_kernel<64>, mgrid, dim3(256), 0, s, 1, 1, a);
   }
   if (dtype == SSD_BF16 && (head_dim == 64 || head_dim == 128)) {
     // Tensor-core path: all query rows of a KV head in as few CTAs as

@@ -35,7 +35,7 @@ __global__ void level_prune_kernel(const int32_t* topk_tok, const float* topk_lp
   __shared__ int s_base;
   pdl_wait();
   pdl_trigger();
-  if (threadIdx.x == 0) s_base = *n_nodes;
+  if (threadIdx.x == 0) s_base = level == 0 ? 0 : *n_nodes;  // level 0 starts a new tree
   __syncthreads();
   const int base = s_base;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {

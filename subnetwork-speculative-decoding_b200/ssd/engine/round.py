@@ -252,7 +252,6 @@ class GreedyRound(_Decoder):
         ops.causal_prep(st[SEQ:SEQ + 1], 1, st[ROOT_TOK:ROOT_TOK + 1], self.fwd_root)
         xn, rn = self._draft_forward(self.fwd_root, 1)
         self._propose(xn, 0, 1, p.branch[0], self.topk_tok[0], self.topk_lp[0], rn)
-        self.tree.n_nodes.zero_()
         for d in range(p.depth):
             frontier = self.root_frontier if d == 0 else self.level_nodes[d - 1]
             n_front = 1 if d == 0 else p.level_sizes[d - 1]

@@ -212,3 +212,19 @@ def test_c1_full_size_fp32_matches_reference():
         ids, spec.max_new_tokens, set())
     assert sd.tokens == g["ar"]
     assert sd.accepted_per_round == g["accepted_per_round"]
+
+
+def test_generate_batch_greedy_matches_reference(tiny, base32):
+    """generate_batch (ssd/data/generate_selfdistill.py:64-108): each row's greedy
+    continuation equals the reference's recorded decode of that prompt; rows of
+    different lengths; EOS cuts a row after the first EOS."""
+    from ssd.data.generate_selfdistill import generate_batch
+
+    target = TargetRunner(base32)
+    prompts = [list(p) for p in tiny["prompts"]]
+    rows = generate_batch(target, prompts, 40, {-1}, 0.0, 1.0, pad_id=0)
+    assert rows == [ref[:40] for ref in tiny["ar"]]
+    eos = tiny["ar"][0][5]
+    cut = generate_batch(target, prompts[:1], 40, {eos}, 0.0, 1.0, pad_id=0)[0]
+    assert cut == tiny["ar"][0][: tiny["ar"][0].index(eos) + 1]
+    assert generate_batch(target, [], 8, set(), 0.0, 1.0, pad_id=0) == []

@@ -235,7 +235,9 @@ def attention_ref(q, kc, vc, prefix, spec_base, mask, H, Hkv, hd):
 @pytest.mark.parametrize("H,Hkv,hd,ctx,T,tree", [(32, 8, 128, 2048, 33, True), (4, 2, 16, 40, 5, True),
                                                   (32, 8, 64, 300, 1, False), (8, 8, 128, 5000, 9, True),
                                                   (64, 8, 128, 700, 33, True), (16, 2, 128, 16384, 17, True),
-                                                  (32, 8, 128, 130, 40, False), (8, 4, 64, 1000, 16, True)])
+                                                  (32, 8, 128, 130, 40, False), (8, 4, 64, 1000, 16, True),
+                                                  (32, 8, 128, 32768, 9, True), (32, 8, 128, 20000, 60, True),
+                                                  (16, 4, 64, 12000, 25, True)])
 def test_tree_attention(ops, ws, dtype, H, Hkv, hd, ctx, T, tree):
     torch.manual_seed(0)
     S = ctx + 80
