@@ -80,23 +80,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
       const uint32_t tx = kABytes + g.BN * kChunkK * 2;
+      // A tile = kTileM / a_box weight boxes (one 128-row box when every
+      // segment starts on a tile boundary, 64 + 64 rows for gate/up pairs,
+      // else four 32-row boxes); the 128-byte swizzle repeats every 8 rows,
+      // so stacked boxes give the same layout as one.
+      const int nA = kTileM / g.a_box;
       auto load_a = [&](int i) {
         uint8_t* a = smem + (i % g.stages) * stage_bytes;
         const int kx = (kc0 + i) * kChunkK;
-#pragma unroll
-        for (int grp = 0; grp < 4; ++grp) {
+        for (int grp = 0; grp < nA; ++grp) {
           int seg, row;
           if (g.layout == SSD_SEG_PAIRS) {
-            seg = grp >> 1;
-            row = tile_m * 64 + (grp & 1) * 32;
+            if (g.a_box == 64) {
+              seg = grp;
+              row = tile_m * 64;
+            } else {
+              seg = grp >> 1;
+              row = tile_m * 64 + (grp & 1) * 32;
+            }
           } else {
-            const int n = tile_m * kTileM + grp * 32;
+            const int n = tile_m * kTileM + grp * g.a_box;
             seg = 0;
             for (int q = 1; q < g.n_seg; ++q)
               if (n >= g.seg_start[q]) seg = q;
             row = n - g.seg_start[seg];  // rows past the segment end are zero-filled by TMA
           }
-          tma_load_2d(a + grp * 32 * 128, &maps.w[seg], &full[i % g.stages], kx, row, pol_w);
+          tma_load_2d(a + grp * g.a_box * 128, &maps.w[seg], &full[i % g.stages], kx, row, pol_w);
         }
       };
       auto load_b = [&](int i) {
@@ -815,6 +824,15 @@ int tc_ctas_per_sm(int tiles_m, int kchunks, bool head, int sms) {
 
 }  // namespace
 
+// Weight boxes of the cluster kernel: whole-tile boxes unless SSD_GEMM_BOX=32.
+static bool big_boxes() {
+  static const bool v = [] {
+    const char* e = getenv("SSD_GEMM_BOX");
+    return !(e && e[0] == '3');
+  }();
+  return v;
+}
+
 int tma_map_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_outer,
                     CUtensorMap* out) {
   return get_map(base, inner, outer, row_stride_bytes, box_outer, out);
@@ -890,7 +908,7 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
     // every segment starts on a tile boundary, 64 + 64 for gate/up pairs),
     // else four 32-row boxes.
     g.a_box = 32;
-    if (sk) {
+    if (sk || big_boxes()) {
       if (layout == SSD_SEG_PAIRS) {
         g.a_box = 64;
       } else {
@@ -898,6 +916,8 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
         for (int i = 1; i < n_seg; ++i) aligned = aligned && (g.seg_start[i] % kTileM == 0);
         if (aligned) g.a_box = 128;
       }
+      for (int i = 0; i < n_seg; ++i)  // boxes no taller than any segment
+        if (rows[i] < g.a_box) g.a_box = 32;
     }
     TcMaps maps;
     for (int i = 0; i < n_seg; ++i) {
