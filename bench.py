@@ -208,8 +208,8 @@ def barrier(world: int) -> None:
 # target at 33 rows, from `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum`
 # (cold L2) of `python bench.py --ncu-case gemm_mix` on a B200; the summary and
 # command are in profiles/tc_gemm_verify_mix_8b.md.
-NCU_DRAM_BYTES_8B_33 = {"qkv": 50707200 + 35584, "o_proj": 34445312 + 7680, "gate_up": 235248640 + 2761216,
-                        "down": 119024128 + 2936832, "lm_head_argmax": 1051216896 + 12325376}
+NCU_DRAM_BYTES_8B_33 = {"qkv": 50719744 + 172288, "o_proj": 34450432 + 0, "gate_up": 235283968 + 2875904,
+                        "down": 119016192 + 3048448, "lm_head_argmax": 1051037696 + 10976000}
 
 
 def gemm_traffic_per_launch(w, rows: int):
