@@ -50,6 +50,9 @@ enum { SSD_ACT_NONE = 0, SSD_ACT_SILU = 1, SSD_ACT_GELU = 2, SSD_ACT_RELU = 3 };
 enum { SSD_SEG_CONCAT = 0, SSD_SEG_PAIRS = 1 };
 
 int ssd_version(void);
+/* Kernels this library has launched (or recorded into a CUDA graph being
+ * captured) in this process so far, all threads and devices together. */
+int64_t ssd_launch_count(void);
 const char* ssd_last_error(void);
 int ssd_device_sm_count(int device);
 

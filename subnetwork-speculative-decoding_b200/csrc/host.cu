@@ -1,5 +1,6 @@
 // Host helpers: thread-local error text, launch checks, device properties,
 // driver entry points.
+#include <atomic>
 #include <mutex>
 #include <string.h>
 
@@ -17,9 +18,12 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+static std::atomic<int64_t> g_launches{0};
+
 int check_launch(const char* what) {
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return fail(SSD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   return SSD_OK;
 }
 
@@ -61,6 +65,8 @@ TensorMapEncodeFn tensor_map_encoder() {
 extern "C" {
 
 int ssd_version(void) { return 1; }
+
+int64_t ssd_launch_count(void) { return ssd::g_launches.load(std::memory_order_relaxed); }
 
 const char* ssd_last_error(void) { return ssd::g_err; }
 

@@ -311,7 +311,6 @@ int ssd_embed(const int32_t* ids, int64_t T, const void* table, int64_t vocab, i
                          static_cast<const bf16*>(table), vocab, d, resid, no, status);
   else
     return fail(SSD_ERR_UNSUPPORTED, "ssd_embed: dtype %d", dtype);
-  return check_launch("embed_kernel");
 }
 
 int ssd_rmsnorm(const float* x, int64_t T, int64_t d, int64_t ldx, const void* weight, float eps, void* out,
@@ -326,7 +325,6 @@ int ssd_rmsnorm(const float* x, int64_t T, int64_t d, int64_t ldx, const void* w
                          static_cast<const bf16*>(weight), eps, static_cast<bf16*>(out), ldo);
   else
     return fail(SSD_ERR_UNSUPPORTED, "ssd_rmsnorm: dtype %d", dtype);
-  return check_launch("rmsnorm_kernel");
 }
 
 // Copies the C ABI's RMSNorm-folding arguments into the epilogue arguments.

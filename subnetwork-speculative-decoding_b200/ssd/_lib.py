@@ -46,6 +46,7 @@ class SsdTpGroup(C.Structure):
 # name -> (restype, argtypes); mirrors include/ssd_b200.h
 SIGNATURES: dict[str, tuple] = {
     "ssd_version": (I32, []),
+    "ssd_launch_count": (I64, []),
     "ssd_last_error": (C.c_char_p, []),
     "ssd_device_sm_count": (I32, [I32]),
     "ssd_workspace_bytes": (I64, [I64, I64, I64]),
@@ -125,20 +126,11 @@ def check(rc: int, what: str) -> None:
     raise SSDError(text)
 
 
-# Kernels each entry point launches (host-only queries launch none).
-KERNELS_PER_CALL = {"ssd_head_argmax": 2, "ssd_head_topk": 2, "ssd_tp_head_argmax": 3, "ssd_tp_head_topk": 3}
-_HOST_ONLY = {"ssd_version", "ssd_last_error", "ssd_device_sm_count", "ssd_workspace_bytes", "ssd_tp_region_bytes",
-              "ssd_tp_partial_offset"}
-_launches = 0
-
-
 def launch_count() -> int:
-    """Kernels launched (or captured into a graph) through this binding so far."""
-    return _launches
+    """Kernels the library launched (or captured into a graph) so far, counted
+    by the library itself at every launch."""
+    return int(load().ssd_launch_count())
 
 
 def call(name: str, *args) -> None:
-    global _launches
     check(getattr(load(), name)(*args), name)
-    if name not in _HOST_ONLY:
-        _launches += KERNELS_PER_CALL.get(name, 1)
