@@ -782,11 +782,9 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   const int t_first = q0 / a.G;
   const int ntok = (q0 + Mg - 1) / a.G - t_first + 1;
   const int P = a.n_splits;
-  pdl_wait();
-  pdl_trigger();
-  const int sb = a.spec_base ? a.spec_base[0] : 0;
-  const int mw = a.mask ? a.mask_words : 0;
 
+  // Set-up that reads nothing an earlier kernel writes runs before the
+  // programmatic-launch wait: barriers, TMEM, tensor-map prefetch.
   if (threadIdx.x == 0) {
     s_misc[0] = 0;
     s_misc[1] = INT32_MAX;
@@ -809,10 +807,18 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&maps.k);
+    tma_prefetch_desc(&maps.v);
+  }
   tc_fence_before();
   __syncthreads();  // barriers, TMEM and the meta accumulators are initialised
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // Q, the new K/V rows and the row metadata come from earlier kernels
+  pdl_trigger();
+  const int sb = a.spec_base ? a.spec_base[0] : 0;
+  const int mw = a.mask ? a.mask_words : 0;
   for (int i = threadIdx.x; i < ntok; i += blockDim.x) {
     const int t = t_first + i;
     const int pl = a.prefix_len[t];
@@ -862,8 +868,6 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
 
   if (warp == 0) {
     if (lane == 0 && nblocks > 0) {
-      tma_prefetch_desc(&maps.k);
-      tma_prefetch_desc(&maps.v);
       const uint64_t pol = l2_policy_evict_first();
       int issued = 0;
       for (int b = 0; b < nblocks; ++b) {

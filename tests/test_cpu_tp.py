@@ -58,3 +58,22 @@ def test_stream_ids_are_stable_and_distinct():
     assert a == tp.stream_id("model.layers.0.mlp.up_proj.weight")
     assert a != tp.stream_id("model.layers.0.mlp.gate_proj.weight")
     assert 0 <= a < 2 ** 64
+
+
+def test_allreduce_parity_alternates_and_checks_even_forwards():
+    """Consecutive all-reduce calls alternate the two partial buffers; every
+    forward restarts at parity 0 and must issue an even number of calls, so
+    forwards (and CUDA graphs of forwards) concatenate without two
+    consecutive calls on one buffer."""
+    g = tp.TPGroup.__new__(tp.TPGroup)  # host bookkeeping only, no device region
+    seq = []
+    for n_layers in (3, 1, 2):
+        g.begin()
+        for _ in range(2 * n_layers):
+            seq.append(g.next_parity())
+        g.end()
+    assert all(a != b for a, b in zip(seq, seq[1:]))
+    g.begin()
+    g.next_parity()
+    with pytest.raises(RuntimeError):
+        g.end()
