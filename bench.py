@@ -51,8 +51,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3", "c4"],
-                    help="c4 = the 70B configuration, tensor parallel over all ranks")
+    ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3", "c3_sample", "c4"],
+                    help="c3_sample = c3 with temperature 0.7 / top_p 0.9; "
+                         "c4 = the 70B configuration, tensor parallel over all ranks")
     ap.add_argument("--sequences", type=int, default=None,
                     help=f"sequences per step (default {N_SEQUENCES}; 1 for c4)")
     ap.add_argument("--layers", type=int, default=None, help="override the model's layer count (c4 smoke runs)")
@@ -693,11 +694,20 @@ def main() -> None:
     mine = seqs if tp_run else dp.shard(seqs, rank, world)
     job_sum = (lambda x: x) if tp_run else (lambda x: sync_sum(x, world))
     cap = cache_capacity(P, max_new, TreePlan(cfg))
-    eng = GreedyRound(target, draft, cfg, target.new_cache(cap), max_new)
+    sampled = cfg.temperature != 0
+    if sampled:  # multi-candidate speculative sampling, seeded per sequence below
+        from ssd.engine.sampling import SampledRound, SampledTargetStep
+
+        eng = SampledRound(target, draft, cfg, target.new_cache(cap), max_new, spec.seed)
+    else:
+        eng = GreedyRound(target, draft, cfg, target.new_cache(cap), max_new)
+    seq_seed = {id(ids): spec.seed * 1000 + i for i, ids in enumerate(seqs)}
     plan_rows = eng.plan.rows
     build_s = time.time() - t_build
 
     def decode(ids, phase_acc=None):
+        if sampled:
+            eng.set_seed(seq_seed[id(ids)])
         eng.prefill(ids.to(dev))
         torch.cuda.synchronize(dev)
         barrier(world)
@@ -754,7 +764,10 @@ def main() -> None:
     # target-only baseline on the same sequences (one pass)
     ar_value = None
     if not args.no_ar:
-        ar = TargetStep(target, target.new_cache(cap), max_new)
+        if sampled:
+            ar = SampledTargetStep(target, target.new_cache(cap), max_new, cfg.temperature, cfg.top_p, spec.seed)
+        else:
+            ar = TargetStep(target, target.new_cache(cap), max_new)
         t_ar, n_ar = 0.0, 0
         for j, ids in enumerate(mine):
             ar.prefill(ids.to(dev))

@@ -71,6 +71,21 @@ __device__ __forceinline__ float key_float(uint32_t k) {
 
 // Warp parameters of one row (all threads of the block). `red` >= 32 floats,
 // `hist` 256 x u64, `sel` 4 u64 of shared memory.
+// hist[bin] += v for every lane with `valid`, with one shared-memory atomic
+// per distinct bin in the warp: the lanes of a bin add their values exactly
+// (24-bit halves through integer warp reductions; v < 2^48) and the group's
+// lowest lane adds the sum. Logit rows put most keys into a handful of bins,
+// where one atomic per element would serialise. Integer sums, so the result
+// does not depend on the grouping. All 32 lanes must call it together.
+__device__ __forceinline__ void hist_add_warp(unsigned long long* hist, uint32_t bin, unsigned long long v,
+                                              bool valid) {
+  const unsigned peers = __match_any_sync(0xffffffffu, valid ? bin : 0xffffffffu);
+  const unsigned lo = __reduce_add_sync(peers, static_cast<unsigned>(v & 0xffffffull));
+  const unsigned hi = __reduce_add_sync(peers, static_cast<unsigned>(v >> 24));
+  if (valid && (threadIdx.x & 31) == static_cast<unsigned>(__ffs(peers) - 1))
+    atomicAdd(&hist[bin], (static_cast<unsigned long long>(hi) << 24) + lo);
+}
+
 __device__ WarpParams row_warp(const float* row, int V, float temperature, float top_p, float* red,
                                unsigned long long* hist, unsigned long long* sel) {
   WarpParams P;
@@ -94,14 +109,16 @@ __device__ WarpParams row_warp(const float* row, int V, float temperature, float
     const int shift = 24 - 8 * level;
     for (int b = threadIdx.x; b < 256; b += kSampThreads) hist[b] = 0ull;
     __syncthreads();
-    for (int i = threadIdx.x; i < V; i += kSampThreads) {
-      const float l = row[i];
+    // Every thread runs the same number of passes (whole warps stay
+    // converged for the warp-level aggregation in hist_add_warp).
+    for (int base = 0; base < V; base += kSampThreads) {
+      const int i = base + threadIdx.x;
+      const float l = i < V ? row[i] : -INFINITY;
       const uint32_t k = order_key(l);
-      if (level == 0 || (k >> (shift + 8)) == prefix) {
-        const unsigned long long fp =
-            static_cast<unsigned long long>((double)expf((l - P.m) * P.inv_t) * scale);
-        atomicAdd(&hist[(k >> shift) & 255u], fp);
-      }
+      const bool in = i < V && (level == 0 || (k >> (shift + 8)) == prefix);
+      const unsigned long long fp =
+          in ? static_cast<unsigned long long>((double)expf((l - P.m) * P.inv_t) * scale) : 0ull;
+      hist_add_warp(hist, (k >> shift) & 255u, fp, in);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
