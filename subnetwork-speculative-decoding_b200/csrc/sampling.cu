@@ -183,6 +183,13 @@ __global__ void warp_probs_kernel(const float* logits, int64_t ld, int V, const 
 // Gumbel top-k (sampling without replacement, in draw order) per row over
 // the warped distribution; tokens through vocab_ids. Missing draws (support
 // < k) get token -1 and log-prob -inf. RNG counter: (round, row_id[row], i, 0).
+// Gumbel top-k of one row, split over a cluster of `gridDim.y` CTAs: CTA
+// (cluster rank) s takes the vocabulary slice [s * len, (s + 1) * len), finds
+// its k best keys (key desc, index asc) and pushes them into rank 0's shared
+// memory; rank 0 merges the sorted slice lists. Keys and tie rules are those
+// of a single pass over the whole row, so the draws do not depend on the
+// split.
+constexpr int kGumbelMaxSlices = 8;
 __global__ void __launch_bounds__(kSampThreads) gumbel_topk_kernel(const float* logits, int64_t ld, int V,
                                                                    const WarpParams* params, int k,
                                                                    const int64_t* vocab_ids, const uint64_t* seed,
@@ -191,8 +198,13 @@ __global__ void __launch_bounds__(kSampThreads) gumbel_topk_kernel(const float* 
   __shared__ float s_key[kSampWarps];
   __shared__ int s_idx[kSampWarps];
   __shared__ int s_own[kSampWarps];
+  __shared__ float c_key[kGumbelMaxSlices * kMaxK];  // rank 0: every slice's list
+  __shared__ int c_idx[kGumbelMaxSlices * kMaxK];
   pdl_wait();
   pdl_trigger();
+  const int slices = gridDim.y, sl = blockIdx.y;  // cluster (1, slices): rank = sl
+  const int len = (V + slices - 1) / slices;
+  const int i0 = sl * len, i1 = min(V, i0 + len);
   const float* row = logits + (int64_t)blockIdx.x * ld;
   const WarpParams P = params[blockIdx.x];
   const uint64_t sd = seed[0];
@@ -206,7 +218,7 @@ __global__ void __launch_bounds__(kSampThreads) gumbel_topk_kernel(const float* 
     kk[j] = -INFINITY;
     ki[j] = INT32_MAX;
   }
-  for (int i = threadIdx.x; i < V; i += kSampThreads) {
+  for (int i = i0 + threadIdx.x; i < i1; i += kSampThreads) {
     const float lp = warped_lp(P, row[i]);
     if (lp == -INFINITY) continue;
     const float g = -logf(-logf(uniform(sd, rnd, row_id, static_cast<uint32_t>(i), 0u)));
@@ -222,6 +234,9 @@ __global__ void __launch_bounds__(kSampThreads) gumbel_topk_kernel(const float* 
       ki[j] = i;
     }
   }
+  // this slice's k best, in order, into rank 0's candidate lists
+  const uint32_t ck0 = slices > 1 ? dsmem_map(smem_u32(c_key), 0u) : 0u;
+  const uint32_t ci0 = slices > 1 ? dsmem_map(smem_u32(c_idx), 0u) : 0u;
   int head = 0;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int q = 0; q < k; ++q) {
@@ -255,11 +270,38 @@ __global__ void __launch_bounds__(kSampThreads) gumbel_topk_kernel(const float* 
       }
     if (threadIdx.x == go) ++head;
     if (threadIdx.x == 0) {
-      const bool ok = gk != -INFINITY;
-      out_tok[(int64_t)blockIdx.x * k + q] = ok ? (vocab_ids ? (int)vocab_ids[gi] : gi) : -1;
-      out_lp[(int64_t)blockIdx.x * k + q] = ok ? warped_lp(P, row[gi]) : -INFINITY;
+      if (slices > 1) {
+        const uint32_t off = static_cast<uint32_t>((sl * kMaxK + q) * 4);
+        dsmem_st(ck0 + off, gk);
+        dsmem_st(ci0 + off, __int_as_float(gi));
+      } else {
+        c_key[q] = gk;
+        c_idx[q] = gi;
+      }
     }
     __syncthreads();
+  }
+  if (slices > 1) cluster_sync_all();  // every slice's list is in rank 0's shared memory
+  if (sl != 0 || threadIdx.x != 0) return;
+  int hd[kGumbelMaxSlices];
+  for (int j = 0; j < kGumbelMaxSlices; ++j) hd[j] = 0;
+  for (int q = 0; q < k; ++q) {
+    float gk = -INFINITY;
+    int gi = INT32_MAX, gs = -1;
+    for (int j = 0; j < slices; ++j) {
+      if (hd[j] >= k) continue;
+      const float ck = c_key[j * kMaxK + hd[j]];
+      const int cix = c_idx[j * kMaxK + hd[j]];
+      if (ck > gk || (ck == gk && cix < gi)) {
+        gk = ck;
+        gi = cix;
+        gs = j;
+      }
+    }
+    if (gs >= 0) ++hd[gs];
+    const bool ok = gk != -INFINITY;
+    out_tok[(int64_t)blockIdx.x * k + q] = ok ? (vocab_ids ? (int)vocab_ids[gi] : gi) : -1;
+    out_lp[(int64_t)blockIdx.x * k + q] = ok ? warped_lp(P, row[gi]) : -INFINITY;
   }
 }
 
@@ -510,8 +552,13 @@ int ssd_gumbel_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, co
                     int32_t* out_tok, float* out_logprob, void* stream) {
   if (k < 1 || k > kMaxK) return fail(SSD_ERR_UNSUPPORTED, "ssd_gumbel_topk: k must be 1..16");
   if (!seed) return fail(SSD_ERR_INVALID, "ssd_gumbel_topk: seed is NULL");
-  return launch_kernel("gumbel_topk_kernel", gumbel_topk_kernel, dim3((unsigned)rows), dim3(kSampThreads), 0,
-                       static_cast<cudaStream_t>(stream), 1, 1, logits, ld, (int)V,
+  if (rows <= 0 || rows > 65535 || V <= 0) return fail(SSD_ERR_INVALID, "ssd_gumbel_topk: bad shape");
+  // a cluster of up to 8 CTAs per row, each over >= 4096 logits
+  int slices = (int)((V + 4095) / 4096);
+  if (slices > kGumbelMaxSlices) slices = kGumbelMaxSlices;
+  return launch_kernel("gumbel_topk_kernel", gumbel_topk_kernel, dim3((unsigned)rows, (unsigned)slices),
+                       dim3(kSampThreads), 0, static_cast<cudaStream_t>(stream), 1, (unsigned)slices, logits, ld,
+                       (int)V,
                        static_cast<const WarpParams*>(params), (int)k, vocab_ids, seed, round, (int)row_base, out_tok,
                        out_logprob);
 }

@@ -374,3 +374,24 @@ def test_sampled_tree_build_api(v8):
             np.testing.assert_allclose(tree.scores[k] - base_s, np.log(float(tree.child_q[par][tree.tokens[k]])),
                                        rtol=1e-4, atol=1e-4)
     assert len(tree) <= sum(TreeDrafter(draft, cfg).max_nodes_per_level())
+
+
+def test_gumbel_topk_split_over_a_cluster_matches_one_pass():
+    """Rows longer than 4096 logits are split over a cluster of CTAs and
+    merged; padding a row with -inf logits (outside every nucleus) moves it
+    onto that path but must not change a single draw."""
+    rows, V, k = 5, 4096, 8
+    logits = _logit_rows(rows, V, 2.0, 11)
+    padded = torch.full((rows, 32768), float("-inf"), dtype=torch.float32, device=DEV)
+    padded[:, :V] = logits
+    seed = torch.tensor([99], dtype=torch.int64, device=DEV)
+    out = []
+    for x in (logits, padded):
+        prm = _params(x, 0.7, 0.9)
+        tok = torch.empty(rows, k, dtype=torch.int32, device=DEV)
+        lp = torch.empty(rows, k, dtype=torch.float32, device=DEV)
+        ops.gumbel_topk(x, prm, k, seed, None, 3, tok, lp)
+        out.append((tok.cpu(), lp.cpu()))
+    assert torch.equal(out[0][0], out[1][0])
+    assert torch.equal(out[0][1], out[1][1])
+    assert (out[0][0] >= 0).all()
