@@ -56,6 +56,9 @@ class SyntheticSpec:
 
 
 CONFIGS: dict[str, SyntheticSpec] = {
+    # a seconds-long configuration for smoke runs of the command line
+    "tiny": SyntheticSpec("tiny", 0, torch.float32, [0, 3, 5], None, prompt_len=16, max_new_tokens=16,
+                          drafting=dict(depth=3, branch=[2, 2, 1])),
     "c1": SyntheticSpec("llama32_1b", 0, torch.float32, [0, 7, 15], 4096, None, prompt_len=128, max_new_tokens=64,
                         drafting=dict(depth=4, branch=1)),
     "c2": SyntheticSpec("llama32_1b", 1, torch.bfloat16, [0, 7, 15], 4096, 0.05, prompt_len=512, max_new_tokens=256,

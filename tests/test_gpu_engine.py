@@ -228,3 +228,19 @@ def test_generate_batch_greedy_matches_reference(tiny, base32):
     cut = generate_batch(target, prompts[:1], 40, {eos}, 0.0, 1.0, pad_id=0)[0]
     assert cut == tiny["ar"][0][: tiny["ar"][0].index(eos) + 1]
     assert generate_batch(target, [], 8, set(), 0.0, 1.0, pad_id=0) == []
+
+
+def test_ssd_run_command_line_on_a_synthetic_model(capsys):
+    """ssd-run end to end (--synthetic tiny: seeded fp32 random weights, no
+    checkpoint or tokenizer): greedy speculative output equals the target-only
+    output and the acceptance report is printed."""
+    from ssd.cli import run
+
+    run.main(["--synthetic", "tiny", "--prompt", "hello world", "--max-new-tokens", "12", "--no-warmup"])
+    out = capsys.readouterr().out
+    assert "=== speculative: 12 tokens ===" in out
+    assert "greedy output identical to AR: True" in out
+    assert "accept rate by depth:" in out
+    run.main(["--synthetic", "tiny", "--prompt", "hello world", "--max-new-tokens", "5", "--mode", "target",
+              "--no-warmup"])
+    assert "=== target: 5 tokens" in capsys.readouterr().out
