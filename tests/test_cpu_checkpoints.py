@@ -77,3 +77,19 @@ def test_checkpoint_discovery_order(base, tmp_path):
     want = _expected(base)
     for k, v in draft.bridges.state_dict().items():
         assert torch.equal(v, want[k]), k
+
+
+def test_top_vocab_matches_reference_subset():
+    """ssd.data.token_freq.top_vocab (token_freq.py:49-55) gives the subset the
+    reference chose for the recorded vocab-subset run (tests/golden/tiny.json)."""
+    import json
+
+    from ssd.data.token_freq import top_vocab
+
+    gold = json.loads((Path(__file__).parent / "golden" / "tiny.json").read_text())["vocab_subset"]
+    sub = top_vocab(torch.arange(128).flip(0), 40, always={127})
+    assert sub.tolist() == gold["ids"]
+    # ties keep the stable descending-count order; forced ids count toward the size
+    counts = torch.tensor([5, 9, 9, 1, 9, 0])
+    assert top_vocab(counts, 3).tolist() == [1, 2, 4]
+    assert top_vocab(counts, 3, always={5}).tolist() == [1, 2, 5]
