@@ -35,6 +35,13 @@ import tempfile
 import time
 from datetime import timedelta
 
+if "--impl" in sys.argv and "reference" in sys.argv:
+    # The CPU arm uses every host thread for numpy's BLAS, whatever
+    # OMP_NUM_THREADS torchrun set (it sets 1): the BLAS reads these once, when
+    # numpy is first imported, so they are set before any import loads it.
+    for _v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[_v] = str(os.cpu_count() or 1)
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "subnetwork-speculative-decoding_b200")
 for _p in (PKG, ROOT):
@@ -61,6 +68,8 @@ def parse():
     ap.add_argument("--prompt-len", type=int, default=None, help="override the prompt length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ar", action="store_true", help="skip the target-only baseline")
+    ap.add_argument("--no-sample", action="store_true", help="skip the sampled (c3_sample) leg of the c3 line")
+    ap.add_argument("--no-tp", action="store_true", help="skip the 70B tensor-parallel leg of multi-GPU runs")
     ap.add_argument("--sweep", choices=["c5"], default=None,
                     help="c5: tree-attention and KV-compaction sweep (ctx x tree nodes) on one GPU, then exit")
     ap.add_argument("--ncu-case", choices=["gemm", "gemm_mix", "attention"], default=None,
@@ -352,6 +361,18 @@ def gemm_roofline(w, rows: int, dev) -> dict:
 
 
 # ------------------------------------------------------------- CPU baseline
+def _blas_threads(n: int) -> int:
+    """Set numpy's BLAS to n threads at run time (threadpoolctl); returns the
+    threads it reports afterwards."""
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+
+        threadpool_limits(n)
+        return max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except ImportError:
+        return int(os.environ.get("OPENBLAS_NUM_THREADS", "1"))
+
+
 def build_oracle(spec, base=None, draft=None):
     """The oracle (numpy restatement of the reference path) in fp32 on the
     host with the GPU arm's exact weights: the workload's bf16 weights are
@@ -366,6 +387,7 @@ def build_oracle(spec, base=None, draft=None):
     from oracle.model import bridges_from_module, weights_from_hf
 
     torch.set_num_threads(os.cpu_count() or 1)
+    _blas_threads(os.cpu_count() or 1)
     if base is None:
         dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
         base, _, draft, _ = build(spec, dev)
@@ -378,18 +400,22 @@ def build_oracle(spec, base=None, draft=None):
     return base, target, odraft
 
 
-CPU_SAMPLE = dict(prompt_len=64, n_tokens=6)
+# A bounded CPU sample: speculative decode of n_tokens after a prompt of
+# prompt_len (the GPU arm decodes 256 after 2048); warm-up samples are short.
+CPU_SAMPLE = dict(prompt_len=512, n_tokens=24)
+CPU_WARMUP_SAMPLE = dict(prompt_len=64, n_tokens=4)
 
 
-def oracle_step(spec, target, draft, seq: int) -> tuple[int, float, list]:
-    """One bounded sample: speculative decode of CPU_SAMPLE tokens after a
-    short prompt of sequence `seq`. Returns (decoded tokens, decode seconds,
+def oracle_step(spec, target, draft, seq: int, sample=None) -> tuple[int, float, list]:
+    """One bounded sample: speculative decode of `sample` tokens after a
+    prompt of sequence `seq`. Returns (decoded tokens, decode seconds,
     committed per round); the prefill is excluded like the GPU arm's."""
     import oracle as O
     from ssd import synthetic as S
 
-    ids = S.make_prompt(spec.seed + seq, CPU_SAMPLE["prompt_len"], target.conf["vocab"])[0].tolist()
-    res = O.speculative_generate(target, draft, dict(spec.drafting), ids, CPU_SAMPLE["n_tokens"], set())
+    sample = sample or CPU_SAMPLE
+    ids = S.make_prompt(spec.seed + seq, sample["prompt_len"], target.conf["vocab"])[0].tolist()
+    res = O.speculative_generate(target, draft, dict(spec.drafting), ids, sample["n_tokens"], set())
     return len(res["tokens"]) - 1, res["decode_s"], res["accepted_per_round"]
 
 
@@ -407,7 +433,7 @@ def cpu_baseline(spec, steps: int = 1, base=None, draft=None) -> dict:
     for s in range(steps):
         dn, dt, da = oracle_step(spec, target, odraft, s)
         n, t, acc = n + dn, t + dt, acc + da
-    return {"value": n / t, "unit": "tok/s", "cores": os.cpu_count() or 1, "kind": "port",
+    return {"value": n / t, "unit": "tok/s", "cores": _blas_threads(os.cpu_count() or 1), "kind": "port",
             "sample": cpu_sample_text(spec, steps) + f"; setup {build_s:.0f}s",
             "mean_accepted": sum(acc) / max(1, len(acc))}
 
@@ -446,13 +472,13 @@ def reference_arm(args) -> None:
     _, target, draft = build_oracle(spec)
     build_s = time.time() - t0
     for i in range(args.warmup):
-        oracle_step(spec, target, draft, i)
+        oracle_step(spec, target, draft, i, CPU_WARMUP_SAMPLE)
     n, t, acc = 0, 0.0, []
     for i in range(args.steps):
         dn, dt, da = oracle_step(spec, target, draft, args.warmup + i)
         n, t, acc = n + dn, t + dt, acc + da
     value = n / t
-    cores = os.cpu_count() or 1
+    cores = _blas_threads(os.cpu_count() or 1)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
@@ -647,6 +673,189 @@ def c5_sweep(args, dev) -> None:
                       "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"]}), flush=True)
 
 
+def decode_timed(eng, ids, dev, world: int, max_new: int, seed=None, phase_acc=None):
+    """Prefill one sequence (untimed), then its decode timed with CUDA events
+    on the launching stream between a barrier + synchronize on both sides.
+    Returns (tokens, committed per round, seconds: max over ranks). With
+    `phase_acc`, per-phase device time is accumulated from events recorded
+    between the round's phases."""
+    import torch
+
+    from ssd.engine.speculative import _finish
+
+    if seed is not None:
+        eng.set_seed(seed)
+    eng.prefill(ids.to(dev))
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    if phase_acc is not None:  # the launch-list capture (ncu --profile-from-start off) sees decode only
+        torch.cuda.profiler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    evs = []
+    e0.record()
+    out = eng.tokens()
+    while not _finish(out, set(), max_new)[1]:
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if phase_acc is not None else None
+        eng.run_round(True, ev)
+        if ev is not None:
+            evs.append(ev)
+        out = eng.tokens()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    if phase_acc is not None:
+        torch.cuda.profiler.stop()
+        for ev in evs:
+            for i, name in enumerate(eng.PHASES):
+                phase_acc[name] = phase_acc.get(name, 0.0) + ev[i].elapsed_time(ev[i + 1]) / 1e3
+    t = sync_max(e0.elapsed_time(e1) / 1e3, world)
+    barrier(world)
+    return _finish(out, set(), max_new)[0], eng.committed_per_round(), t
+
+
+def ar_timed(ar, ids, dev, world: int, max_new: int, seed=None, warm: bool = False):
+    """Target-only decode of one sequence, timed like decode_timed."""
+    import torch
+
+    from ssd.engine.speculative import _finish
+
+    if seed is not None:
+        ar.set_seed(seed)
+    ar.prefill(ids.to(dev))
+    torch.cuda.synchronize(dev)
+    if warm:  # capture the step graph outside the timed region
+        ar.run(2)
+        ar.prefill(ids.to(dev))
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    out = ar.tokens()
+    while not _finish(out, set(), max_new)[1]:
+        ar.run(max(1, min(4, max_new - len(out))))
+        out = ar.tokens()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = sync_max(e0.elapsed_time(e1) / 1e3, world)
+    return _finish(out, set(), max_new)[0], t
+
+
+def first_divergence(a, b):
+    for i, (x, y) in enumerate(zip(a, b)):
+        if x != y:
+            return i
+    return None if len(a) == len(b) else min(len(a), len(b))
+
+
+def roofline_bounds(w, draft, cfg, P: int, max_new: int, mean_acc: float, bw: float) -> dict:
+    """Weight+KV HBM bound per GPU: a round reads the draft weights once per
+    level and the target once, plus the KV of the layers it runs; an AR token
+    reads the target once plus its KV (w holds this rank's shard under tensor
+    parallelism)."""
+    import torch
+
+    tgt_bytes = model_bytes(w, head_rows=w.lm_head.shape[0])
+    d_bytes = model_bytes(w, draft.layer_indices, list(draft.bridges.values()), head_rows=draft.head_weight().shape[0])
+    kv_tok = 2 * w.L * w.Hkv * w.hd * (2 if w.dtype == torch.bfloat16 else 4)
+    ctx = P + max_new / 2
+    round_bytes = cfg.depth * d_bytes + tgt_bytes + ctx * kv_tok * (1 + cfg.depth * len(draft.layer_indices) / w.L)
+    ar_bytes = tgt_bytes + ctx * kv_tok
+    return {"sd_tok_s_bound": bw * mean_acc / round_bytes, "ar_tok_s_bound": bw / ar_bytes,
+            "round_bytes": round_bytes, "ar_token_bytes": ar_bytes}
+
+
+def sampled_leg(target, draft, mine, dev, world: int, P: int, max_new: int, job_sum) -> dict:
+    """BASELINE config 3 at temperature 0.7 / top_p 0.9 (multi-candidate
+    speculative sampling) on the same weights and sequences: one warm-up
+    sequence, then every sequence of this rank once, and the sampled
+    target-only decode of the same sequences."""
+    from ssd import synthetic as S
+    from ssd.config import DraftingConfig
+    from ssd.engine.round import TreePlan, cache_capacity
+    from ssd.engine.sampling import SampledRound, SampledTargetStep
+
+    spec = S.CONFIGS["c3_sample"]
+    cfg = DraftingConfig(**spec.drafting)
+    cap = cache_capacity(P, max_new, TreePlan(cfg))
+    eng = SampledRound(target, draft, cfg, target.new_cache(cap), max_new, spec.seed)
+    seeds = [spec.seed * 1000 + i for i in range(len(mine))]
+    decode_timed(eng, mine[0], dev, world, max_new, seeds[0])
+    phases: dict = {}
+    t_sd, n_sd, accs = 0.0, 0, []
+    for ids, sd_seed in zip(mine, seeds):
+        toks, acc, t = decode_timed(eng, ids, dev, world, max_new, sd_seed, phases)
+        t_sd, n_sd, accs = t_sd + t, n_sd + len(toks), accs + acc
+    del eng
+    ar = SampledTargetStep(target, target.new_cache(cap), max_new, cfg.temperature, cfg.top_p, spec.seed)
+    t_ar, n_ar = 0.0, 0
+    for j, (ids, sd_seed) in enumerate(zip(mine, seeds)):
+        toks, t = ar_timed(ar, ids, dev, world, max_new, sd_seed, warm=j == 0)
+        t_ar, n_ar = t_ar + t, n_ar + len(toks)
+    del ar
+    value, ar_value = job_sum(n_sd) / t_sd, job_sum(n_ar) / t_ar
+    rounds = max(1, len(accs))
+    return {"workload": "c3_sample: c3 with temperature 0.7, top_p 0.9 (same weights, tree and sequences)",
+            "value": value, "unit": "tok/s", "ar_value": ar_value, "speedup_vs_ar": value / ar_value,
+            "mean_accepted": sum(accs) / rounds,
+            "phase_ms_per_round": {k: v / rounds * 1e3 for k, v in phases.items()}}
+
+
+def tp_leg(args, dev, rank: int, world: int) -> dict:
+    """BASELINE config 4 (70B, tensor parallel over all `world` ranks, full 80
+    layers, 4096-token prompt, 128 new tokens, greedy): one warm-up decode,
+    then `steps` timed decodes of the sequence; target-only decode of the same
+    sequence; every rank must hold the same tokens, and speculative tokens
+    must equal target-only tokens."""
+    import torch
+
+    from ssd import synthetic as S
+    from ssd.engine import dp
+    from ssd.engine.round import GreedyRound, TargetStep, TreePlan, cache_capacity
+
+    spec = S.CONFIGS["c4"]
+    P, max_new = spec.prompt_len, spec.max_new_tokens
+    t0 = time.time()
+    base, target, draft, cfg = build_tp(spec, dev, rank, world, max_rows=P + 64)
+    build_s = time.time() - t0
+    w = target.weights
+    ids = S.make_prompt(spec.seed, P, w.V)
+    cap = cache_capacity(P, max_new, TreePlan(cfg))
+    eng = GreedyRound(target, draft, cfg, target.new_cache(cap), max_new)
+    decode_timed(eng, ids, dev, world, max_new)
+    phases: dict = {}
+    t_sd, n_sd, accs, sd_tokens = 0.0, 0, [], None
+    for _ in range(max(1, args.steps)):
+        toks, acc, t = decode_timed(eng, ids, dev, world, max_new, None, phases)
+        t_sd, n_sd, accs, sd_tokens = t_sd + t, n_sd + len(toks), accs + acc, toks
+    rows = eng.plan.rows
+    del eng
+    ar = TargetStep(target, target.new_cache(cap), max_new)
+    ar_tokens, t_ar = ar_timed(ar, ids, dev, world, max_new, warm=True)
+    del ar
+    roof = gemm_roofline(w, rows, dev)
+    everyone = dp.gather_lists(sd_tokens, world)
+    rounds = max(1, len(accs))
+    mean_acc = sum(accs) / rounds
+    value, ar_value = n_sd / t_sd, len(ar_tokens) / t_ar
+    bw = measured_peaks()["hbm_gbs"] * 1e9
+    bounds = roofline_bounds(w, draft, cfg, P, max_new, mean_acc, bw)
+    pt = roof["per_type"]
+    out = {"workload": f"c4: {spec.model} planted x{spec.plant_scale}, draft {spec.draft_layers}, tree {spec.drafting}, "
+                       f"prompt {P}, {max_new} new tokens, tensor parallel over {world} GPUs",
+           "tp": world, "value": value, "unit": "tok/s", "ar_value": ar_value, "speedup_vs_ar": value / ar_value,
+           "mean_accepted": mean_acc, "phase_ms_per_round": {k: v / rounds * 1e3 for k, v in phases.items()},
+           "ranks_agree": all(t == everyone[0] for t in everyone),
+           "sd_equals_ar": sd_tokens == ar_tokens, "first_divergence": first_divergence(sd_tokens, ar_tokens),
+           "allreduce_us": pt.get("tp_allreduce", {}).get("us"),
+           "verify_gemm_us": {k: v["us"] for k, v in pt.items()},
+           "verify_gemm_mix_gbs": roof["gbs"],
+           "weight_kv_roofline": {**bounds, "sd_frac": value / bounds["sd_tok_s_bound"],
+                                  "ar_frac": ar_value / bounds["ar_tok_s_bound"]},
+           "build_s": build_s}
+    del base, target, draft, w
+    torch.cuda.empty_cache()
+    return out
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
@@ -672,7 +881,7 @@ def main() -> None:
     from ssd import _lib
     from ssd import synthetic as S
     from ssd.engine.round import GreedyRound, TargetStep, TreePlan, cache_capacity
-    from ssd.engine.speculative import SpeculativeGenerator, _finish
+    from ssd.engine.speculative import SpeculativeGenerator
 
     spec = S.CONFIGS[args.workload]
     tp_run = is_tp(spec)
@@ -701,43 +910,14 @@ def main() -> None:
         eng = SampledRound(target, draft, cfg, target.new_cache(cap), max_new, spec.seed)
     else:
         eng = GreedyRound(target, draft, cfg, target.new_cache(cap), max_new)
-    seq_seed = {id(ids): spec.seed * 1000 + i for i, ids in enumerate(seqs)}
+    seq_seed = [spec.seed * 1000 + i for i in range(len(mine))] if sampled else [None] * len(mine)
     plan_rows = eng.plan.rows
     build_s = time.time() - t_build
 
-    def decode(ids, phase_acc=None):
-        if sampled:
-            eng.set_seed(seq_seed[id(ids)])
-        eng.prefill(ids.to(dev))
-        torch.cuda.synchronize(dev)
-        barrier(world)
-        if phase_acc is not None:  # timed: the launch-list capture (ncu --profile-from-start off) sees decode only
-            torch.cuda.profiler.start()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        evs = []
-        e0.record()
-        out = eng.tokens()
-        while not _finish(out, set(), max_new)[1]:
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if phase_acc is not None else None
-            eng.run_round(True, ev)
-            if ev is not None:
-                evs.append(ev)
-            out = eng.tokens()
-        e1.record()
-        torch.cuda.synchronize(dev)
-        if phase_acc is not None:
-            torch.cuda.profiler.stop()
-            for ev in evs:
-                for i, name in enumerate(eng.PHASES):
-                    phase_acc[name] = phase_acc.get(name, 0.0) + ev[i].elapsed_time(ev[i + 1]) / 1e3
-        t = sync_max(e0.elapsed_time(e1) / 1e3, world)
-        barrier(world)
-        return _finish(out, set(), max_new)[0], eng.committed_per_round(), t
-
     # warm-up (captures the graphs)
     for _ in range(args.warmup):
-        for ids in mine:
-            decode(ids)
+        for ids, sd_seed in zip(mine, seq_seed):
+            decode_timed(eng, ids, dev, world, max_new, sd_seed)
     # timed
     try:
         pr = torch.cuda.get_device_properties(dev)
@@ -745,72 +925,76 @@ def main() -> None:
     except (AttributeError, TypeError, ValueError):
         pci = None
     clocks = ClockSampler(local, pci)
-    launches0 = _lib.launch_count()
     phases: dict = {}
     t_total, n_tok, accs, rounds = 0.0, 0, [], 0
+    sd_tokens = [None] * len(mine)
     for _ in range(args.steps):
-        for ids in mine:
-            toks, acc, t = decode(ids, phases)
+        for j, (ids, sd_seed) in enumerate(zip(mine, seq_seed)):
+            toks, acc, t = decode_timed(eng, ids, dev, world, max_new, sd_seed, phases)
             t_total += t
             n_tok += len(toks)
             accs += acc
             rounds += len(acc)
+            sd_tokens[j] = toks
     clk = clocks.stop()
     n_tok_all = job_sum(n_tok)
     per_step = t_total / args.steps
     value = n_tok_all / t_total
     gpu_launches = int(getattr(eng, "launches_per_round", 0) * rounds)
+    del eng
 
-    # target-only baseline on the same sequences (one pass)
-    ar_value = None
+    # target-only baseline on the same sequences (one pass); greedy runs also
+    # check that speculative decoding reproduced target-only decoding
+    ar_value, parity = None, None
     if not args.no_ar:
         if sampled:
             ar = SampledTargetStep(target, target.new_cache(cap), max_new, cfg.temperature, cfg.top_p, spec.seed)
         else:
             ar = TargetStep(target, target.new_cache(cap), max_new)
-        t_ar, n_ar = 0.0, 0
-        for j, ids in enumerate(mine):
-            ar.prefill(ids.to(dev))
-            torch.cuda.synchronize(dev)
-            if j == 0:
-                ar.run(2)
-                ar.prefill(ids.to(dev))
-                torch.cuda.synchronize(dev)
-            barrier(world)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            out = ar.tokens()
-            while not _finish(out, set(), max_new)[1]:
-                ar.run(max(1, min(4, max_new - len(out))))
-                out = ar.tokens()
-            e1.record()
-            torch.cuda.synchronize(dev)
-            t_ar += sync_max(e0.elapsed_time(e1) / 1e3, world)
-            n_ar += len(_finish(out, set(), max_new)[0])
+        t_ar, n_ar, diverged = 0.0, 0, []
+        for j, (ids, sd_seed) in enumerate(zip(mine, seq_seed)):
+            toks, t = ar_timed(ar, ids, dev, world, max_new, sd_seed, warm=j == 0)
+            t_ar += t
+            n_ar += len(toks)
+            if not sampled:
+                i = first_divergence(sd_tokens[j], toks)
+                if i is not None:
+                    diverged.append({"sequence": rank + j * world if not tp_run else j, "step": i})
         ar_value = job_sum(n_ar) / t_ar
         del ar
+        if not sampled:
+            all_div = [d for part in dp.gather_lists(diverged, world) for d in part]
+            parity = {"sd_equals_ar": not all_div, "first_divergence": all_div or None,
+                      "sequences": args.sequences * args.steps if tp_run else args.sequences,
+                      "check": "greedy speculative tokens == target-only tokens, every timed sequence"}
 
     # end to end through the public API (pinned host prompt -> host tokens)
     gen = SpeculativeGenerator(base, draft, cfg, target)
-    gen.generate(mine[0].pin_memory(), max_new, set())  # capture
+    gen.generate(mine[0].pin_memory(), max_new, set(), seed=seq_seed[0])  # capture
     t_e2e, n_e2e = 0.0, 0
     e2e_engine = gen.engine()
     d2h0 = getattr(e2e_engine, "d2h_bytes", 0)
-    for ids in mine:
+    for ids, sd_seed in zip(mine, seq_seed):
         pinned = ids.pin_memory()
         torch.cuda.synchronize(dev)
         barrier(world)
         t0 = time.perf_counter()
-        res = gen.generate(pinned, max_new, set())
+        res = gen.generate(pinned, max_new, set(), seed=sd_seed)
         t_e2e += sync_max(time.perf_counter() - t0, world)
         n_e2e += len(res.tokens)
     d2h = getattr(e2e_engine, "d2h_bytes", 0) - d2h0
     e2e_value = job_sum(n_e2e) / t_e2e
+    del gen, e2e_engine
 
     # kernel roofline of the dominant kernel (tcgen05 GEMM, verify forward)
     peaks = measured_peaks()
     # (tensor parallel: every rank runs it, the all-reduce needs all ranks)
     roof = gemm_roofline(w, plan_rows, dev) if (rank == 0 or tp_run) else None
+
+    # the sampled variant of the default workload, same weights and sequences
+    sample_line = None
+    if args.workload == "c3" and not args.no_sample:
+        sample_line = sampled_leg(target, draft, mine, dev, world, P, max_new, job_sum)
 
     cb = None
     if tp_run:
@@ -823,17 +1007,19 @@ def main() -> None:
             cb = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
                   "sample": f"not run: {exc}"}
 
+    mean_acc = sum(accs) / max(1, len(accs))
+    bw = peaks["hbm_gbs"] * 1e9
+    bounds = roofline_bounds(w, draft, cfg, P, max_new, mean_acc, bw)
+    traffic = gemm_traffic_per_launch(w, plan_rows)
+    # the bounds are per GPU: data-parallel aggregates are divided by the ranks
+    per_gpu = 1 if tp_run else world
+    tp_line = None
+    if world > 1 and not tp_run and not args.no_tp:
+        del base, target, draft, w
+        torch.cuda.empty_cache()
+        tp_line = tp_leg(args, dev, rank, world)
+
     if rank == 0:
-        # per GPU: under tensor parallelism w holds this rank's shard
-        tgt_bytes = model_bytes(w, head_rows=w.lm_head.shape[0])
-        d_bytes = model_bytes(w, draft.layer_indices, list(draft.bridges.values()),
-                              head_rows=draft.head_weight().shape[0])
-        kv_tok = 2 * w.L * w.Hkv * w.hd * (2 if w.dtype == torch.bfloat16 else 4)
-        mean_acc = sum(accs) / max(1, len(accs))
-        ctx = P + max_new / 2
-        round_bytes = cfg.depth * d_bytes + tgt_bytes + ctx * kv_tok * (1 + cfg.depth * len(draft.layer_indices) / w.L)
-        ar_bytes = tgt_bytes + ctx * kv_tok
-        bw = peaks["hbm_gbs"] * 1e9
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong",
@@ -843,13 +1029,13 @@ def main() -> None:
             "mean_accepted": mean_acc,
             "ar_value": ar_value,
             "speedup_vs_ar": (value / ar_value) if ar_value else None,
+            "parity": parity,
             "phase_ms_per_round": {k: v / max(1, rounds) * 1e3 for k, v in phases.items()},
             "weight_kv_roofline": {
-                "sd_tok_s_bound": bw * mean_acc / round_bytes, "ar_tok_s_bound": bw / ar_bytes,
-                "sd_frac": value / (bw * mean_acc / round_bytes),
-                "ar_frac": (ar_value / (bw / ar_bytes)) if ar_value else None,
-                "round_bytes": round_bytes, "ar_token_bytes": ar_bytes, "peak_gbs": peaks["hbm_gbs"],
-                "peak_source": peaks["source"]},
+                **bounds, "per_gpu_value": value / per_gpu,
+                "sd_frac": value / per_gpu / bounds["sd_tok_s_bound"],
+                "ar_frac": (ar_value / per_gpu / bounds["ar_tok_s_bound"]) if ar_value else None,
+                "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"]},
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": int(sum(x.numel() * 8 for x in mine)),
                     "d2h_bytes_per_step": int(d2h),
                     "note": "SpeculativeGenerator.generate per sequence: H2D prompt, prefill, decode, D2H tokens"},
@@ -857,7 +1043,7 @@ def main() -> None:
             "roofline": {"kernel": "tc_gemm_kernel (verify-forward GEMM mix + lm_head argmax)", "bound": "hbm",
                          "achieved": roof["gbs"] if roof else None, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": (roof["gbs"] / peaks["hbm_gbs"]) if roof else None,
-                         "traffic": gemm_traffic_per_launch(w, plan_rows),
+                         "traffic": traffic,
                          "algorithmic_bytes_per_launch": (roof["bytes"] / roof["launches"]) if roof else None,
                          "peak_source": peaks["source"],
                          "per_type": roof["per_type"] if roof else None},
@@ -865,6 +1051,10 @@ def main() -> None:
             "clocks": clk,
             "build_s": build_s,
         }
+        if sample_line is not None:
+            line["c3_sample"] = sample_line
+        if tp_line is not None:
+            line["tp70b"] = tp_line
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -118,9 +118,11 @@ int ssd_linear(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, cons
  * with no allocator, code that must avoid the allocator's synchronisation).
  * No counterpart in the reference: it is an addition of this library.
  * Same arguments and results as ssd_linear; its split-K scratch is a fixed
- * 12 MiB array inside the library that every GPU loading the library keeps
- * until exit. Limit: T <= 64 rows for bf16, T <= 16 for fp32; larger calls
- * fail with SSD_ERR_UNSUPPORTED. Every call shares that array: calls that
+ * 20 MiB array inside the library that every GPU loading the library keeps
+ * until exit. Limit: T <= 64 token rows (bf16 or fp32); on a GPU of up to
+ * 148 SMs every such call fits the array. Larger calls, and any shape whose
+ * split-K scratch on this GPU exceeds the array, fail with
+ * SSD_ERR_UNSUPPORTED before launching. Every call shares that array: calls that
  * overlap on the GPU race, so keep them ordered on one stream. The first call
  * on a device looks up the array's address and should come before any stream
  * capture. Allocates nothing. */
@@ -227,11 +229,13 @@ int ssd_tree_walk_greedy(const int32_t* n_nodes, int64_t max_nodes, const int32_
  * keep_slots[j] moves to slot start[0] + j. Each thread owns one 16-byte
  * group of one (layer, K/V, head) row across all kept slots and reads them
  * all before writing, so overlapping source/destination slots are safe.
+ * A keep list longer than max_keep or naming a slot outside the cache copies
+ * nothing and sets status bit 2 (bad index), if `status` is given.
  * Strides are in elements. Replaces KVCache.keep_positions
  * (ssd/engine/kv_cache.py:54-70). */
 int ssd_kv_compact(void* cache, int64_t n_layers, int64_t layer_stride, int64_t kv_stride, int64_t n_kv_heads,
                    int64_t head_stride, int64_t head_dim, const int32_t* start, const int32_t* keep_slots,
-                   const int32_t* n_keep, int64_t max_keep, int dtype, void* stream);
+                   const int32_t* n_keep, int64_t max_keep, int dtype, uint32_t* status, void* stream);
 
 /* Commit one round: append the accepted tokens + bonus to out_tokens at
  * *n_out, advance *seq_len by 1 + accepted, make the bonus the new root and
@@ -322,6 +326,11 @@ typedef struct SsdTpGroup {
 } SsdTpGroup;
 
 int64_t ssd_tp_region_bytes(int64_t max_rows, int64_t d);
+/* Polls a tensor-parallel meeting makes before it gives up, sets status bit 1
+ * (timeout) and lets the kernel finish; 0 restores the default (2^22 polls,
+ * about half a second). Applies to calls issued after it; returns the previous
+ * limit. A lower limit lets a caller detect a rank that never arrives sooner. */
+uint32_t ssd_tp_set_spin_limit(uint32_t polls);
 /* Byte offset in the region of partial buffer `parity` (0 or 1), fp32
  * [max_rows, d] with row stride d: the row-parallel o_proj / down_proj GEMM
  * (ssd_linear with SSD_EPI_STORE_F32) writes this rank's partial sums there. */

@@ -838,6 +838,54 @@ int tma_map_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t r
   return get_map(base, inner, outer, row_stride_bytes, box_outer, out);
 }
 
+// Token tiling and K split of a GEMM: BN, tiles_n, splits, stages, plus the
+// stream-K grid when that variant is enabled. Shared by launch_gemm and
+// gemm_workspace_need so a size query always matches the launch.
+struct SplitPlan {
+  int BN = 0, tiles_n = 0, splits = 1, stages = 0;
+  bool sk = false;
+  int64_t sk_ctas = 0;
+};
+
+static SplitPlan plan_splits(int64_t T, int tiles_m, int kchunks, bool head, int dtype, int sms) {
+  SplitPlan p;
+  if (dtype == SSD_BF16) {
+    p.BN = round_bn(T);
+    p.tiles_n = (int)((T + p.BN - 1) / p.BN);
+    const int per_sm = tc_ctas_per_sm(tiles_m, kchunks, head, sms);
+    p.splits = (p.tiles_n == 1 && !head) ? choose_cluster_splits(tiles_m, kchunks, per_sm * sms) : 1;
+    p.stages = tc_stages(p.BN, per_sm);
+    p.sk = p.tiles_n == 1 && p.BN <= 128 && sk_enabled();
+    if (p.sk) {
+      const int64_t W = (int64_t)tiles_m * kchunks;
+      p.sk_ctas = (int64_t)sms * sk_ctas_per_sm();
+      if (p.sk_ctas > W) p.sk_ctas = W;
+    }
+  } else {
+    p.BN = kSimtBN;
+    p.tiles_n = (int)((T + kSimtBN - 1) / kSimtBN);
+    // Same split for every decode-sized T (<= kSimtInvariantRows), so rows are
+    // bit-identical whatever the batch; larger (prefill) batches do not split.
+    p.splits = (T <= kSimtInvariantRows && !head) ? choose_splits(tiles_m, kchunks, 4 * sms) : 1;
+  }
+  return p;
+}
+
+static int64_t plan_workspace_bytes(const SplitPlan& p, int tiles_m) {
+  if (p.sk) return kCounterBytes + 2 * p.sk_ctas * kTileM * p.BN * 4;
+  if (p.splits <= 1) return 0;
+  return kCounterBytes + (int64_t)tiles_m * p.tiles_n * p.splits * p.BN * kTileM * 4;
+}
+
+int64_t gemm_workspace_need(int64_t T, int64_t K, int n_seg, const int64_t* rows, int layout, bool head, int dtype) {
+  if (T <= 0 || K <= 0 || n_seg < 1 || n_seg > 3) return -1;
+  int64_t N = 0;
+  for (int i = 0; i < n_seg; ++i) N += rows[i];
+  const int tiles_m = (int)(layout == SSD_SEG_PAIRS ? (rows[0] + 63) / 64 : (N + kTileM - 1) / kTileM);
+  const int kchunks = (int)((K + kChunkK - 1) / kChunkK);
+  return plan_workspace_bytes(plan_splits(T, tiles_m, kchunks, head, dtype, device_sms()), tiles_m);
+}
+
 int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, const void* const* w,
                 const int64_t* rows, int layout, const EpiArgs& e, int dtype, void* workspace,
                 int64_t workspace_bytes, uint32_t* status, cudaStream_t stream, int64_t partial_offset_bytes) {
@@ -871,22 +919,13 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
   const int sms = device_sms();
   const bool head = (e.kind == EPI_ARGMAX || e.kind == EPI_TOPK);
 
-  if (dtype == SSD_BF16) {
-    if (K % 8) return fail(SSD_ERR_UNSUPPORTED, "bf16 GEMM needs K % 8 == 0");
-    g.BN = round_bn(T);
-    g.tiles_n = (int)((T + g.BN - 1) / g.BN);
-    const int per_sm = tc_ctas_per_sm(g.tiles_m, g.kchunks, head, sms);
-    g.splits = (g.tiles_n == 1 && !head) ? choose_cluster_splits(g.tiles_m, g.kchunks, per_sm * sms) : 1;
-    g.stages = tc_stages(g.BN, per_sm);
-  } else if (dtype == SSD_F32) {
-    g.BN = kSimtBN;
-    g.tiles_n = (int)((T + kSimtBN - 1) / kSimtBN);
-    // Same split for every decode-sized T (<= kSimtInvariantRows), so rows are
-    // bit-identical whatever the batch; larger (prefill) batches do not split.
-    g.splits = (T <= kSimtInvariantRows && !head) ? choose_splits(g.tiles_m, g.kchunks, 4 * sms) : 1;
-  } else {
-    return fail(SSD_ERR_UNSUPPORTED, "dtype %d", dtype);
-  }
+  if (dtype != SSD_BF16 && dtype != SSD_F32) return fail(SSD_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (dtype == SSD_BF16 && K % 8) return fail(SSD_ERR_UNSUPPORTED, "bf16 GEMM needs K % 8 == 0");
+  const SplitPlan plan = plan_splits(T, g.tiles_m, g.kchunks, head, dtype, sms);
+  g.BN = plan.BN;
+  g.tiles_n = plan.tiles_n;
+  g.splits = plan.splits;
+  g.stages = plan.stages;
 
   const int64_t tiles = (int64_t)g.tiles_m * g.tiles_n;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -903,7 +942,7 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
   dim3 grid(g.tiles_m * g.splits, g.tiles_n);
 
   if (dtype == SSD_BF16) {
-    const bool sk = g.tiles_n == 1 && g.BN <= 128 && sk_enabled();
+    const bool sk = plan.sk;
     // Stream-K: one TMA box per weight segment a tile touches (128 rows when
     // every segment starts on a tile boundary, 64 + 64 for gate/up pairs),
     // else four 32-row boxes.
@@ -929,9 +968,7 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
     if (rc) return rc;
     set_tc_attributes();
     if (sk) {
-      const int64_t W = (int64_t)g.tiles_m * g.kchunks;
-      int64_t G = (int64_t)sms * sk_ctas_per_sm();
-      if (G > W) G = W;
+      const int64_t G = plan.sk_ctas;
       if (g.tiles_m > kMaxCounters / 2) return fail(SSD_ERR_WORKSPACE, "too many weight tiles");
       const int64_t need = kCounterBytes + partial_offset_bytes + 2 * G * kTileM * g.BN * 4;
       if (!workspace || need > workspace_bytes)

@@ -50,6 +50,12 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
                 const int64_t* rows, int layout, const EpiArgs& epi, int dtype, void* workspace,
                 int64_t workspace_bytes, uint32_t* status, cudaStream_t stream, int64_t partial_offset_bytes);
 
+// Workspace bytes (split counters + split-K partials) that launch_gemm needs
+// for this shape on the current device with no partial offset: 0 when the GEMM
+// does not split, -1 for invalid arguments. `head` = an lm_head epilogue
+// (argmax / top-k records), which never splits.
+int64_t gemm_workspace_need(int64_t T, int64_t K, int n_seg, const int64_t* rows, int layout, bool head, int dtype);
+
 constexpr int64_t kMaxCounters = 1 << 16;
 constexpr int64_t kCounterBytes = kMaxCounters * 4;
 

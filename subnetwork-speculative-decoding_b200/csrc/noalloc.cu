@@ -29,9 +29,14 @@
 
 namespace ssd {
 
-// 12 MiB: the split counters plus split-K partials for any decode-sized call
-// (T <= 64 token rows: at most 2 CTAs per SM, each a 128 x 64 fp32 tile).
-constexpr int64_t kNoAllocScratchBytes = 12LL << 20;
+// 20 MiB: the split counters (256 KiB) plus the split-K partials of any call
+// of up to 64 token rows on a GPU of up to 148 SMs. A split GEMM runs at most
+// 4 CTAs per SM (tiles x splits <= 4 x SMs), each with one 128-row fp32
+// partial tile of at most 64 token columns: 4 x 148 x 128 x 64 x 4 bytes =
+// 18.5 MiB (the opt-in stream-K variant needs the same: 2 x 2 x SMs tiles).
+// fp32 weights use 4-token tiles, so 64 rows need the same bound.
+// Each call computes its exact need first and refuses what does not fit.
+constexpr int64_t kNoAllocScratchBytes = 20LL << 20;
 constexpr int kNoAllocMaxRows = 64;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
@@ -66,13 +71,16 @@ extern "C" int ssd_linear_noalloc(const void* x, int64_t ldx, int64_t T, int64_t
                                   const int64_t* rows, const void* const* bias, int seg_layout, int epilogue, int act,
                                   void* out, int64_t ldo, float* resid, int64_t ldr, int dtype, uint32_t* status,
                                   void* stream) {
-  // fp32 (CUDA-core) tiles hold 4 tokens, so their split partials per row
-  // are 4x larger: 16 rows fit the same scratch.
-  const int max_rows = dtype == SSD_F32 ? kNoAllocMaxRows / 4 : kNoAllocMaxRows;
-  if (T <= 0 || T > max_rows)
+  if (T <= 0 || T > kNoAllocMaxRows)
     return fail(SSD_ERR_UNSUPPORTED, "ssd_linear_noalloc: T = %lld token rows is outside 1..%d (its fixed %lld-byte "
                 "scratch holds decode-sized calls only; use ssd_linear with a workspace)",
-                (long long)T, max_rows, (long long)kNoAllocScratchBytes);
+                (long long)T, kNoAllocMaxRows, (long long)kNoAllocScratchBytes);
+  if (!w || !rows || n_seg < 1 || n_seg > 3) return fail(SSD_ERR_INVALID, "ssd_linear_noalloc: bad weight segments");
+  const int64_t need = gemm_workspace_need(T, K, n_seg, rows, seg_layout, false, dtype);
+  if (need > kNoAllocScratchBytes)
+    return fail(SSD_ERR_UNSUPPORTED, "ssd_linear_noalloc: this shape needs %lld bytes of split-K scratch on this GPU, "
+                "more than the fixed %lld-byte array; use ssd_linear with a workspace",
+                (long long)need, (long long)kNoAllocScratchBytes);
   void* scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;

@@ -17,10 +17,11 @@
 // Synchronisation: block b of a kernel meets block b of the same kernel on
 // every other rank. Each block counts its uses in its epoch counter (the same
 // sequence on every rank), stores the epoch into flags[ch][phase][b][me] of
-// every rank and polls its own flags[ch][phase][b][*] until every source has
-// reached the epoch (system-scope accesses; see tp_meet). Polls are bounded: on
-// timeout the block sets the status timeout bit and goes on (results are then
-// garbage but no GPU waits forever). Flags only grow, so they never need a
+// every rank with a system-scope release and polls its own
+// flags[ch][phase][b][*] with system-scope acquires until every source has
+// reached the epoch (see tp_meet). Polls are bounded (ssd_tp_set_spin_limit):
+// on timeout the block sets the status timeout bit and goes on (results are
+// then garbage but no GPU waits forever). Flags only grow, so they never need a
 // reset. Blocks wait only on blocks of other GPUs, and each kernel's blocks
 // fit on the GPU together, so a wait cannot block the block it waits for.
 // No multicast objects or multicast loads are used.
@@ -30,6 +31,8 @@
 // have completed (programmatic-launch wait first), so when any rank passes the
 // meeting of call k + 1, every rank has finished reading the partials of call
 // k; the GEMM of call k + 2, which overwrites them, comes later still.
+#include <atomic>
+
 #include "gemm.cuh"
 #include "host.cuh"
 
@@ -39,7 +42,7 @@ constexpr int kTpMaxRanks = SSD_TP_MAX_RANKS;
 constexpr int kTpMaxBlocks = 1024;
 constexpr int kTpRecFloats = 2 + 2 * 16;  // largest head record: top-k with k = 16
 constexpr int kTpChanAllReduce = 0, kTpChanHead = 1;
-constexpr uint32_t kTpSpinLimit = 1u << 22;  // polls of ~100 ns: ~0.4 s and more
+constexpr uint32_t kTpSpinLimit = 1u << 22;  // default polls of ~100 ns: ~0.4 s and more
 constexpr int kTpThreads = 128;
 
 constexpr int64_t kTpFlagBytes = 2LL * 2 * kTpMaxBlocks * kTpMaxRanks * 4;
@@ -59,6 +62,7 @@ struct TpDev {
   uint8_t* region[kTpMaxRanks];
   int rank, world;
   int64_t max_rows, d;
+  uint32_t spin_limit;  // polls before a meeting gives up
 };
 
 __device__ __forceinline__ uint32_t* tp_flag(uint8_t* region, int ch, int phase, int b, int src) {
@@ -67,12 +71,12 @@ __device__ __forceinline__ uint32_t* tp_flag(uint8_t* region, int ch, int phase,
 __device__ __forceinline__ uint32_t* tp_epoch(uint8_t* region, int ch, int b) {
   return reinterpret_cast<uint32_t*>(region + kTpFlagBytes) + (int64_t)ch * kTpMaxBlocks + b;
 }
-__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -87,23 +91,25 @@ __device__ __forceinline__ uint32_t tp_next_epoch(const TpDev& g, int ch, int b)
 
 // Block-wide meeting of block b with its counterparts on every rank. Thread
 // p (< world) signals rank p and waits for rank p's signal, so the peers are
-// polled in parallel. What the meetings order is always either data written
-// by kernels that completed before this one started (the programmatic-launch
-// wait comes first), or loads whose values this block has already consumed;
-// so the flags are relaxed system-scope accesses: no release fence per block
-// (a system fence costs microseconds and serialises the blocks of an SM).
-// Peer data read after a meeting is loaded with L1 bypassed (__ldcg).
+// polled in parallel. What a meeting orders is either data written by kernels
+// that completed before this one started (the programmatic-launch wait comes
+// first, so those writes are visible to this thread) or loads whose values
+// this block has already consumed (the __syncthreads below orders them before
+// the signalling thread's store). The signal is a system-scope release store,
+// which is cumulative: everything this thread has observed is ordered before
+// it. The poll is a system-scope acquire load, so the peer data read after
+// the meeting (with L1 bypassed, __ldcg) is at least as new as the signal.
 // Returns false on timeout.
 __device__ bool tp_meet(const TpDev& g, int ch, int phase, int b, uint32_t epoch, uint32_t* status) {
   __syncthreads();
   int ok = 1;
   if (threadIdx.x < g.world) {
     const int p = threadIdx.x;
-    st_relaxed_sys(tp_flag(g.region[p], ch, phase, b, g.rank), epoch);
+    st_release_sys(tp_flag(g.region[p], ch, phase, b, g.rank), epoch);
     const uint32_t* f = tp_flag(g.region[g.rank], ch, phase, b, p);
     uint32_t it = 0;
-    while ((int32_t)(ld_relaxed_sys(f) - epoch) < 0) {
-      if (++it > kTpSpinLimit) {
+    while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
+      if (++it > g.spin_limit) {
         report_error(status, kErrWaitTimeout);
         ok = 0;
         break;
@@ -297,6 +303,8 @@ __global__ void fill_normal_kernel(T* out, int64_t rows, int64_t cols, int64_t l
 }
 
 namespace {
+std::atomic<uint32_t> g_tp_spin_limit{kTpSpinLimit};
+
 int tp_dev(const SsdTpGroup* g, TpDev* out, const char* who) {
   if (!g) return fail(SSD_ERR_INVALID, "%s: group is NULL", who);
   if (g->world < 1 || g->world > kTpMaxRanks || g->rank < 0 || g->rank >= g->world)
@@ -309,6 +317,7 @@ int tp_dev(const SsdTpGroup* g, TpDev* out, const char* who) {
   out->world = g->world;
   out->max_rows = g->max_rows;
   out->d = g->d;
+  out->spin_limit = g_tp_spin_limit.load(std::memory_order_relaxed);
   return SSD_OK;
 }
 }  // namespace
@@ -328,6 +337,10 @@ extern "C" {
 int64_t ssd_tp_region_bytes(int64_t max_rows, int64_t d) {
   if (max_rows < 1 || d < 1) return -1;
   return tp_region_bytes(max_rows, d);
+}
+
+uint32_t ssd_tp_set_spin_limit(uint32_t polls) {
+  return g_tp_spin_limit.exchange(polls ? polls : kTpSpinLimit);
 }
 
 int64_t ssd_tp_partial_offset(int64_t max_rows, int64_t d, int parity) {

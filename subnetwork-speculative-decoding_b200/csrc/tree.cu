@@ -240,11 +240,13 @@ __global__ void tree_walk_greedy_kernel(const int32_t* n_nodes, int max_n, const
 
 // One thread per (layer, K/V, head, 16-byte group of head_dim): read every
 // kept slot first, then write, so overlapping source/destination slots of the
-// same slice can never be clobbered.
+// same slice can never be clobbered. A keep list that does not fit (more than
+// max_keep entries, or a slot outside the cache) copies nothing and sets the
+// status word's bad-index bit, which the host turns into an error.
 template <typename VEC>
 __global__ void kv_compact_kernel(uint8_t* cache, int64_t n_layers, int64_t layer_stride_b, int64_t kv_stride_b,
                                   int64_t n_kv, int64_t head_stride_b, int64_t row_bytes, const int32_t* start,
-                                  const int32_t* keep_slots, const int32_t* n_keep, int max_keep) {
+                                  const int32_t* keep_slots, const int32_t* n_keep, int max_keep, uint32_t* status) {
   constexpr int kMaxKeep = 32;
   pdl_wait();
   pdl_trigger();
@@ -252,12 +254,16 @@ __global__ void kv_compact_kernel(uint8_t* cache, int64_t n_layers, int64_t laye
   const int64_t total = n_layers * 2 * n_kv * groups;
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (tid >= total) return;
-  const int nk = min(min(*n_keep, max_keep), kMaxKeep);
+  const int nk_req = *n_keep;
+  const int nk = min(min(nk_req, max_keep), kMaxKeep);
   const int s0 = start[0];
   const int64_t n_slots = head_stride_b / row_bytes;
-  if (s0 < 0 || s0 + nk > n_slots) return;
-  for (int j = 0; j < nk; ++j)
-    if (keep_slots[j] < 0 || keep_slots[j] >= n_slots) return;
+  bool bad = nk_req < 0 || nk_req > max_keep || s0 < 0 || s0 + nk > n_slots;
+  for (int j = 0; j < nk && !bad; ++j) bad = keep_slots[j] < 0 || keep_slots[j] >= n_slots;
+  if (bad) {
+    if (tid == 0) report_error(status, kErrBadIndex);
+    return;
+  }
   const int64_t g = tid % groups;
   const int64_t h = (tid / groups) % n_kv;
   const int64_t kv = (tid / (groups * n_kv)) % 2;
@@ -372,7 +378,7 @@ int ssd_tree_walk_greedy(const int32_t* n_nodes, int64_t max_nodes, const int32_
 
 int ssd_kv_compact(void* cache, int64_t n_layers, int64_t layer_stride, int64_t kv_stride, int64_t n_kv_heads,
                    int64_t head_stride, int64_t head_dim, const int32_t* start, const int32_t* keep_slots,
-                   const int32_t* n_keep, int64_t max_keep, int dtype, void* stream) {
+                   const int32_t* n_keep, int64_t max_keep, int dtype, uint32_t* status, void* stream) {
   if (max_keep <= 0 || max_keep > 32) return fail(SSD_ERR_UNSUPPORTED, "ssd_kv_compact: max_keep must be 1..32");
   const int64_t es = dtype == SSD_F32 ? 4 : 2;
   const int64_t row_bytes = head_dim * es;
@@ -382,7 +388,7 @@ int ssd_kv_compact(void* cache, int64_t n_layers, int64_t layer_stride, int64_t 
   const unsigned blocks = (unsigned)((total + 255) / 256);
   return launch_kernel("kv_compact_kernel", kv_compact_kernel<uint4>, dim3(blocks), dim3(256), 0,
       static_cast<cudaStream_t>(stream), 1, 1, static_cast<uint8_t*>(cache), n_layers, layer_stride * es, kv_stride * es, n_kv_heads, head_stride * es,
-      row_bytes, start, keep_slots, n_keep, (int)max_keep);
+      row_bytes, start, keep_slots, n_keep, (int)max_keep, status);
 }
 
 int ssd_round_commit(const int32_t* n_accepted, const int32_t* accepted, const int32_t* tokens,

@@ -65,7 +65,7 @@ SIGNATURES: dict[str, tuple] = {
     "ssd_tree_prune": (I32, [P, I64, P, P, P, P, P, P, I64, P]),
     "ssd_verify_prep": (I32, [P, I64, P, P, P, P, P, P, P, P, P, P, P, I64, P, P]),
     "ssd_tree_walk_greedy": (I32, [P, I64, P, P, P, P, P, P, P, P, P, P, P]),
-    "ssd_kv_compact": (I32, [P, I64, I64, I64, I64, I64, I64, P, P, P, I64, I32, P]),
+    "ssd_kv_compact": (I32, [P, I64, I64, I64, I64, I64, I64, P, P, P, I64, I32, P, P]),
     "ssd_round_commit": (I32, [P, P, P, P, P, P, P, P, I64, P, P, P]),
     "ssd_causal_prep": (I32, [P, I64, P, P, P, P, P, P]),
     "ssd_warp_params": (I32, [P, I64, I64, I64, F32, F32, P, P]),
@@ -76,6 +76,7 @@ SIGNATURES: dict[str, tuple] = {
                                    P, P, P, P, P]),
     "ssd_tp_region_bytes": (I64, [I64, I64]),
     "ssd_tp_partial_offset": (I64, [I64, I64, I32]),
+    "ssd_tp_set_spin_limit": (C.c_uint32, [C.c_uint32]),
     "ssd_tp_allreduce_residual": (I32, [P, I32, I64, P, I64, P, I32, P, P]),
     "ssd_tp_head_argmax": (I32, [P, P, I64, I64, I64, P, I64, I64, P, P, P, I32, P, I64, P, P, P]),
     "ssd_tp_head_topk": (I32, [P, P, I64, I64, I64, P, I64, I64, P, I64, P, P, I32, P, I64, P, P, P]),

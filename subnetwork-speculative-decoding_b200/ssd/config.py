@@ -100,25 +100,37 @@ class DraftingConfig:
     draft_vocab: Optional[int] = None
 
     def per_depth(self, value: Optional[IntOrList], name: str) -> list[Optional[int]]:
-        if value is None or isinstance(value, int):
-            return [value] * self.depth
-        if len(value) != self.depth:
-            raise ValueError(f"drafting.{name} has {len(value)} entries but depth={self.depth}")
-        return list(value)
+        """One entry per tree level: a scalar (or None) repeats, a list must
+        name every level."""
+        if isinstance(value, (list, tuple)):
+            if len(value) != self.depth:
+                raise ValueError(f"drafting.{name}: {len(value)} values given for depth {self.depth}")
+            return list(value)
+        return [value for _ in range(self.depth)]
 
     def validate(self) -> None:
-        if self.depth < 1:
-            raise ValueError("drafting.depth must be >= 1")
-        if any(b is None or b < 1 for b in self.per_depth(self.branch, "branch")):
-            raise ValueError("drafting.branch entries must be >= 1")
-        if any(w is not None and w < 1 for w in self.per_depth(self.width, "width")):
-            raise ValueError("drafting.width entries must be >= 1")
-        if self.max_nodes is not None and self.max_nodes < 1:
-            raise ValueError("drafting.max_nodes must be >= 1")
-        if self.draft_vocab is not None and self.draft_vocab < 1:
-            raise ValueError("drafting.draft_vocab must be >= 1 (or null)")
-        if not 0.0 < self.top_p <= 1.0 or self.temperature < 0:
-            raise ValueError("need temperature >= 0 and 0 < top_p <= 1")
+        """Reject trees the drafter cannot build (ValueError, as the reference)."""
+
+        def at_least_one(v) -> bool:
+            return isinstance(v, int) and v >= 1
+
+        if not at_least_one(self.depth):
+            raise ValueError(f"drafting.depth must be at least 1, got {self.depth!r}")
+        problems = []
+        if not all(at_least_one(b) for b in self.per_depth(self.branch, "branch")):
+            problems.append(f"every branch entry must be at least 1 (branch={self.branch!r})")
+        if not all(x is None or at_least_one(x) for x in self.per_depth(self.width, "width")):
+            problems.append(f"every width entry must be at least 1 or null (width={self.width!r})")
+        for name in ("max_nodes", "draft_vocab"):
+            v = getattr(self, name)
+            if v is not None and not at_least_one(v):
+                problems.append(f"{name} must be at least 1 or null ({name}={v!r})")
+        if self.temperature < 0:
+            problems.append(f"temperature must be >= 0 (temperature={self.temperature!r})")
+        if not 0.0 < self.top_p <= 1.0:
+            problems.append(f"top_p must lie in (0, 1] (top_p={self.top_p!r})")
+        if problems:
+            raise ValueError("drafting: " + "; ".join(problems))
 
 
 @dataclass
@@ -155,16 +167,32 @@ class TrainingConfig:
     online: OnlineConfig = field(default_factory=OnlineConfig)
 
 
-def _build(cls, raw: Optional[dict], where: str):
-    raw = raw or {}
-    unknown = set(raw) - {f.name for f in fields(cls)}
-    if unknown:
-        raise ValueError(f"unknown keys in {where}: {sorted(unknown)}")
-    return cls(**raw)
+# Nested sections: (parent dataclass, field) -> the dataclass its mapping builds.
+_NESTED: dict = {}
+
+
+def _section(cls, raw: Any, path: str):
+    """Build dataclass `cls` from a YAML mapping. Keys the schema does not
+    define are an error (a typo must not silently fall back to a default);
+    nested sections are built the same way, recursively."""
+    if raw is None:
+        raw = {}
+    if not isinstance(raw, dict):
+        raise ValueError(f"{path}: expected a mapping, got {type(raw).__name__}")
+    names = {f.name for f in fields(cls)}
+    extra = sorted(k for k in raw if k not in names)
+    if extra:
+        raise ValueError(f"{path}: unknown key(s) {extra}")
+    kwargs = {}
+    for key, value in raw.items():
+        sub = _NESTED.get((cls, key))
+        kwargs[key] = _section(sub, value, f"{path}.{key}") if sub is not None else value
+    return cls(**kwargs)
 
 
 def profile_name(layers: list[int]) -> str:
-    return "L" + "-".join(str(i) for i in layers)
+    """Name of a layer profile, e.g. [0, 7, 15] -> "L0-7-15"."""
+    return "L" + "-".join(map(str, layers))
 
 
 @dataclass
@@ -178,56 +206,47 @@ class SSDConfig:
 
     @classmethod
     def from_yaml(cls, path: str | Path) -> "SSDConfig":
-        with open(path) as f:
-            raw = yaml.safe_load(f) or {}
-        return cls.from_dict(raw)
+        return cls.from_dict(yaml.safe_load(Path(path).read_text()) or {})
 
     @classmethod
     def from_dict(cls, raw: dict) -> "SSDConfig":
-        unknown = set(raw) - {f.name for f in fields(cls)}
-        if unknown:
-            raise ValueError(f"unknown top-level config sections: {sorted(unknown)}")
-        layers = raw.get("draft_layers")
-        if not isinstance(layers, list) or not all(isinstance(i, int) for i in layers):
-            raise ValueError("draft_layers must be a list of 0-based layer indices, e.g. [0, 7, 15]")
-        tr = dict(raw.get("training") or {})
-        training = _build(
-            TrainingConfig,
-            {
-                **{k: v for k, v in tr.items() if k not in ("stage1", "stage2", "online")},
-                "stage1": _build(Stage1Config, tr.get("stage1"), "training.stage1"),
-                "stage2": _build(Stage2Config, tr.get("stage2"), "training.stage2"),
-                "online": _build(OnlineConfig, tr.get("online"), "training.online"),
-            },
-            "training",
-        )
-        drafting = _build(DraftingConfig, raw.get("drafting"), "drafting")
-        drafting.validate()
-        return cls(
-            model=_build(ModelConfig, raw.get("model"), "model"),
-            draft_layers=layers,
-            bridge=_build(BridgeConfig, raw.get("bridge"), "bridge"),
-            drafting=drafting,
-            data=_build(DataConfig, raw.get("data"), "data"),
-            training=training,
-        )
+        """Parse a whole config. draft_layers is required (0-based indices);
+        the drafting section is validated on load."""
+        layers = raw.get("draft_layers") if isinstance(raw, dict) else None
+        if not (isinstance(layers, list) and all(isinstance(i, int) and not isinstance(i, bool) for i in layers)):
+            raise ValueError(f"draft_layers must be a list of 0-based layer indices such as [0, 7, 15], "
+                             f"got {layers!r}")
+        cfg = _section(cls, raw, "config")
+        cfg.drafting.validate()
+        return cfg
 
     def validate_against(self, num_hidden_layers: int) -> None:
+        """Check draft_layers against the base model's depth."""
         validate_layer_indices(self.draft_layers, num_hidden_layers)
 
     def to_dict(self) -> dict[str, Any]:
         return asdict(self)
 
 
+_NESTED.update({
+    (SSDConfig, "model"): ModelConfig, (SSDConfig, "bridge"): BridgeConfig,
+    (SSDConfig, "drafting"): DraftingConfig, (SSDConfig, "data"): DataConfig,
+    (SSDConfig, "training"): TrainingConfig, (TrainingConfig, "stage1"): Stage1Config,
+    (TrainingConfig, "stage2"): Stage2Config, (TrainingConfig, "online"): OnlineConfig,
+})
+
+
 def validate_layer_indices(layer_indices: list[int], num_hidden_layers: int) -> list[int]:
+    """The selected base layers as ints: non-empty, strictly increasing and
+    inside 0..num_hidden_layers-1 (ValueError otherwise)."""
     idx = [int(i) for i in layer_indices]
-    if not idx:
-        raise ValueError("layer_indices must be non-empty")
-    if any(b <= a for a, b in zip(idx, idx[1:])):
-        raise ValueError(f"layer_indices must be strictly increasing, got {idx}")
-    if idx[0] < 0 or idx[-1] >= num_hidden_layers:
-        raise ValueError(
-            f"layer_indices {idx} out of range for a model with {num_hidden_layers} layers "
-            f"(valid: 0..{num_hidden_layers - 1}; indices are 0-based)"
-        )
+    if len(idx) == 0:
+        raise ValueError("layer_indices is empty: select at least one base layer")
+    for prev, cur in zip(idx, idx[1:]):
+        if cur <= prev:
+            raise ValueError(f"layer_indices must increase strictly: {prev} is followed by {cur} in {idx}")
+    outside = [i for i in idx if not 0 <= i < num_hidden_layers]
+    if outside:
+        raise ValueError(f"layer_indices {outside} lie outside 0..{num_hidden_layers - 1} "
+                         f"(0-based indices into a model of {num_hidden_layers} layers)")
     return idx

@@ -294,7 +294,7 @@ class GreedyRound(_Decoder):
         """keep_positions + append accepted + bonus (speculative.py:165-172)."""
         st = self.state
         ops.kv_compact(self.cache.buf, st[SEQ:SEQ + 1], self.keep_slots, st[N_KEEP:N_KEEP + 1],
-                       max_keep=self.plan.depth + 1)
+                       max_keep=self.plan.depth + 1, status=self.ws.status)
         ops.round_commit(st[N_ACC:N_ACC + 1], self.accepted, self.tree.tokens, st[BONUS:BONUS + 1], st[SEQ:SEQ + 1],
                          st[ROOT_TOK:ROOT_TOK + 1], self.out_tokens, st[N_OUT:N_OUT + 1], self.round_log,
                          self.ws.status)

@@ -250,7 +250,9 @@ def sample_verify_device(tree, target_logits: torch.Tensor, temperature: float, 
     return accepted[:na].tolist(), int(bonus.item())
 
 
-def _timed_decode(eng, dev, input_ids, run, done):
+def _timed_decode(eng, dev, input_ids, run, done, clock=None):
+    """Prefill, then `run` until `done`; times {prefill, decode}, or with a
+    PhaseClock {prefill, draft, verify, bookkeeping}."""
     times: dict[str, float] = {}
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
@@ -262,8 +264,13 @@ def _timed_decode(eng, dev, input_ids, run, done):
     while not done(out):
         run(len(out))
         out = eng.tokens()
+        if clock is not None:
+            clock.collect()
     torch.cuda.synchronize(dev)
-    times["decode"] = time.perf_counter() - t0
+    if clock is None:
+        times["decode"] = time.perf_counter() - t0
+    else:
+        clock.finish(times, time.perf_counter() - t0)
     eng.ws.check_status()
     eng.cache.seq_len = int(eng.state[SEQ].item())
     return out, times
@@ -294,7 +301,7 @@ def sampled_speculative(gen, input_ids: torch.Tensor, max_new_tokens: int, eos_i
                         seed: Optional[int] = None, use_graph: bool = True, max_cache: Optional[int] = None):
     """SpeculativeGenerator.generate with temperature > 0 (speculative.py:132-174)."""
     from ssd.engine.round import cache_capacity
-    from ssd.engine.speculative import GenerationResult, _engine_cache, _finish
+    from ssd.engine.speculative import GenerationResult, PhaseClock, _engine_cache, _finish
 
     cfg = gen.cfg
     dev = gen.target.weights.device
@@ -304,8 +311,9 @@ def sampled_speculative(gen, input_ids: torch.Tensor, max_new_tokens: int, eos_i
     eng = _engine_cache(gen, key, lambda: SampledRound(gen.target, gen.draft, cfg, gen.target.new_cache(cap),
                                                        max_new_tokens, 0))
     eng.set_seed(seed_from(seed))
-    out, times = _timed_decode(eng, dev, input_ids, lambda n: eng.run_round(use_graph),
-                               lambda out: _finish(out, eos_ids, max_new_tokens)[1])
+    clock = PhaseClock(eng.PHASES)
+    out, times = _timed_decode(eng, dev, input_ids, lambda n: eng.run_round(use_graph, clock.round_events()),
+                               lambda out: _finish(out, eos_ids, max_new_tokens)[1], clock)
     acc = eng.committed_per_round()
     return GenerationResult(tokens=_finish(out, eos_ids, max_new_tokens)[0], times=times, accepted_per_round=acc,
                             tree_sizes=[gen.plan.n_verify] * len(acc))

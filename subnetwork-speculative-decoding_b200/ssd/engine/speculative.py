@@ -63,6 +63,40 @@ def _sync(dev) -> None:
     torch.cuda.synchronize(dev)
 
 
+class PhaseClock:
+    """Per-phase times of the round loop for GenerationResult.times (the
+    reference's draft / verify / bookkeeping totals, speculative.py:149-171).
+    Each round's phases are bracketed by CUDA events on the launching stream;
+    they are read after the round's committed tokens (a stream-synchronising
+    read), so the clock adds no synchronisation of its own. Host time of the
+    loop not covered by device phases (token reads, the Python loop) is
+    counted as bookkeeping, so the phases add up to the decode wall time."""
+
+    def __init__(self, phases):
+        self.phases = tuple(phases)
+        self.events = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.phases) + 1)]
+        self.totals = {p: 0.0 for p in self.phases}
+        self.armed = False
+
+    def collect(self) -> None:
+        """Add the last round's phase times (its events have completed)."""
+        if self.armed:
+            for i, p in enumerate(self.phases):
+                self.totals[p] += self.events[i].elapsed_time(self.events[i + 1]) / 1e3
+        self.armed = False
+
+    def round_events(self):
+        self.armed = True
+        return self.events
+
+    def finish(self, times: dict, wall: float) -> None:
+        self.collect()
+        times.update(self.totals)
+        rest = wall - sum(self.totals.values())
+        if rest > 0 and "bookkeeping" in times:
+            times["bookkeeping"] += rest
+
+
 @torch.no_grad()
 def autoregressive_generate(target: TargetRunner, input_ids: torch.Tensor, max_new_tokens: int, eos_ids: set[int],
                             temperature: float = 0.0, top_p: float = 1.0, seed: Optional[int] = None,
@@ -144,13 +178,15 @@ class SpeculativeGenerator:
         eng.prefill(input_ids.to(dev))
         _sync(dev)
         times["prefill"] = time.perf_counter() - t0
+        clock = PhaseClock(eng.PHASES)
         t0 = time.perf_counter()
         out = eng.tokens()
         while not _finish(out, eos_ids, max_new_tokens)[1]:
-            eng.run_round(use_graph)
+            eng.run_round(use_graph, clock.round_events())
             out = eng.tokens()
+            clock.collect()
         _sync(dev)
-        times["decode"] = time.perf_counter() - t0
+        clock.finish(times, time.perf_counter() - t0)
         eng.ws.check_status()
         eng.cache.seq_len = int(eng.state[0].item())
         acc = eng.committed_per_round()

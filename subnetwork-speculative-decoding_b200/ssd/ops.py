@@ -195,11 +195,12 @@ def tree_walk_greedy(tree, argmax, root_pos, accepted, n_accepted, bonus, keep_s
            _p(root_pos), _p(accepted), _p(n_accepted), _p(bonus), _p(keep_slots), _p(n_keep), _stream())
 
 
-def kv_compact(cache: torch.Tensor, start, keep_slots, n_keep, max_keep: int) -> None:
-    """cache: [L, 2, n_kv, max_slots, head_dim]."""
+def kv_compact(cache: torch.Tensor, start, keep_slots, n_keep, max_keep: int, status=None) -> None:
+    """cache: [L, 2, n_kv, max_slots, head_dim]. A keep list that does not fit
+    sets the bad-index bit of `status` (a workspace's status word)."""
     Ln, _, n_kv, _, hd = cache.shape
     L.call("ssd_kv_compact", _p(cache), Ln, cache.stride(0), cache.stride(1), n_kv, cache.stride(2), hd, _p(start),
-           _p(keep_slots), _p(n_keep), max_keep, dtype_code(cache.dtype), _stream())
+           _p(keep_slots), _p(n_keep), max_keep, dtype_code(cache.dtype), _p(status), _stream())
 
 
 def round_commit(n_accepted, accepted, tokens, bonus, seq_len, root_token, out_tokens, n_out, round_log,

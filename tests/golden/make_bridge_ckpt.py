@@ -2,7 +2,7 @@
 (ssd/models/subnetwork_draft.py:455-466), for the format test in
 tests/test_cpu_checkpoints.py.
 
-    python tests/golden/make_bridge_ckpt.py [--ref /root/reference]
+    python tests/golden/make_bridge_ckpt.py --ref PATH_TO_REFERENCE   (or set SSD_REFERENCE)
 
 Base: this repo's seeded tiny Llama (synthetic.py, loaded by path so it does not
 clash with the reference's `ssd` package). Draft layers [0, 3, 5] give the
@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import argparse
 import importlib.util
+import os
 import sys
 from pathlib import Path
 
@@ -25,7 +26,8 @@ LAYERS = [0, 3, 5]
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("SSD_REFERENCE"), required="SSD_REFERENCE" not in os.environ,
+                    help="path of the reference checkout (default: $SSD_REFERENCE)")
     args = ap.parse_args()
     spec = importlib.util.spec_from_file_location("ssd_synthetic", SYN_PATH)
     syn = importlib.util.module_from_spec(spec)

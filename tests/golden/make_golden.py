@@ -1,9 +1,9 @@
 """Generate golden fixtures by running the REFERENCE implementation.
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--skip-1b]
+    python tests/golden/make_golden.py --ref PATH_TO_REFERENCE [--skip-1b]
 
-Needs the reference checkout (importable as `ssd`) and runs on the CPU in
-fp32. Weights come from this repo's seeded synthetic builder
+Needs the reference checkout (importable as `ssd`; `--ref`, or the
+SSD_REFERENCE environment variable) and runs on the CPU in fp32. Weights come from this repo's seeded synthetic builder
 (subnetwork-speculative-decoding_b200/ssd/synthetic.py, loaded by path so it
 does not clash with the reference's `ssd` package); a checksum of every model
 is stored so a host whose CPU RNG differs is detected instead of silently
@@ -18,8 +18,9 @@ Outputs (tests/golden/):
   c1.json    - BASELINE config 1 (Llama-3.2-1B shape, fp32, seed 0): prompt,
                target-only greedy tokens with top-2 gaps, SD chain tokens.
   c2ref.json - config-2 model (seed 1, planted, bf16-rounded weights) run in
-               fp32 by the reference: greedy AR tokens + top-2 gaps, the
-               reference for the bf16 tier.
+               fp32 by the reference: greedy AR tokens + top-2 gaps, and per
+               step the top-8 logits (values, ids) and the logits at 64 fixed
+               probe ids: the reference for the bf16 tier.
 """
 
 from __future__ import annotations
@@ -53,23 +54,32 @@ TREES = {
 }
 
 
-def ref_ar_with_gaps(target, ids, n, eos=frozenset()):
+def ref_ar_with_gaps(target, ids, n, eos=frozenset(), probe=None, record=None):
     """The reference's autoregressive_generate loop (ssd/engine/speculative.py:101-122),
     run step by step through the reference TargetRunner to also record each
-    step's top-2 logit gap."""
+    step's top-2 logit gap. With `record` (a dict), each step's top-8 logits
+    (values and ids) and the logits at the `probe` ids are appended to it."""
     import torch
 
     cache = target.new_cache(ids.shape[1] + n + 1)
+
+    def note(logits):
+        top = logits.float().topk(8)
+        gaps.append(float(top.values[0] - top.values[1]))
+        if record is not None:
+            record.setdefault("top_values", []).append([float(v) for v in top.values])
+            record.setdefault("top_ids", []).append([int(i) for i in top.indices])
+            record.setdefault("probe_logits", []).append([float(logits[j]) for j in probe])
+
     with torch.no_grad():
+        gaps = []
         logits = target(ids, past_key_values=cache, logits_to_keep=1).logits[0, -1]
-        out, gaps = [int(logits.argmax())], []
-        top = logits.float().topk(2).values
-        gaps.append(float(top[0] - top[1]))
+        out = [int(logits.argmax())]
+        note(logits)
         while len(out) < n:
             logits = target(torch.tensor([[out[-1]]]), past_key_values=cache).logits[0, -1]
             out.append(int(logits.argmax()))
-            top = logits.float().topk(2).values
-            gaps.append(float(top[0] - top[1]))
+            note(logits)
     return out, gaps
 
 
@@ -216,16 +226,19 @@ def make_c2ref(syn, out_path: Path, n_new: int = 48):
             p.copy_(p.bfloat16().float())
     target = TargetRunner(base)
     ids = syn.make_prompt(spec.seed, spec.prompt_len, base.config.vocab_size)
-    ar, gaps = ref_ar_with_gaps(target, ids, n_new)
+    probe = torch.randperm(base.config.vocab_size, generator=torch.Generator().manual_seed(11))[:64].tolist()
+    rec: dict = {}
+    ar, gaps = ref_ar_with_gaps(target, ids, n_new, probe=probe, record=rec)
     res = dict(config="c2", checksum=syn.weights_checksum(base), prompt=ids[0].tolist(), ar=ar, gaps=gaps,
-               note="weights rounded to bf16, evaluated by the reference in fp32")
+               probe_ids=probe, **rec, note="weights rounded to bf16, evaluated by the reference in fp32")
     out_path.write_text(json.dumps(res))
     print(f"wrote {out_path}")
 
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--ref", default=os.environ.get("SSD_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("SSD_REFERENCE"), required="SSD_REFERENCE" not in os.environ,
+                    help="path of the reference checkout (default: $SSD_REFERENCE)")
     ap.add_argument("--skip-1b", action="store_true")
     ap.add_argument("--only", choices=["tiny", "c1", "c2ref"])
     a = ap.parse_args()

@@ -39,7 +39,7 @@ def test_library_rejects_bad_arguments_without_gpu():
         L.call("ssd_tree_attention", None, 0, 1, 3, 2, 16, None, None, 0, 0, None, None, None, 0, 0, None, 0, 0,
                None, 0, None, None)
     with pytest.raises(L.SSDError):
-        L.call("ssd_kv_compact", None, 1, 1, 1, 1, 1, 64, None, None, None, 99, 1, None)
+        L.call("ssd_kv_compact", None, 1, 1, 1, 1, 1, 64, None, None, None, 99, 1, None, None)
 
 
 YAML = """
@@ -140,3 +140,43 @@ def test_forward_inputs_mask_conversion():
     assert fi.mask[:T, 0].tolist() == [0, 0b001, 0b010, 0b101]
     fi.fill(torch.tensor([5, 6]), torch.tensor([6, 7]), past, None)
     assert fi.prefix_len[:2].tolist() == [past + 1, past + 2] and not fi.use_mask
+
+
+def _random_tree(seed: int, n: int, vocab: int = 50):
+    """A random draft tree in the drafter's storage order (parents first),
+    siblings ranked in proposal order."""
+    import random
+
+    from ssd.engine.tree_drafter import ROOT, DraftTree
+
+    rng = random.Random(seed)
+    t = DraftTree()
+    n_kids: dict = {}
+    for i in range(n):
+        parent = rng.choice([ROOT] + list(range(i))) if i else ROOT
+        t.tokens.append(rng.randrange(vocab))
+        t.parents.append(parent)
+        t.depths.append(1 if parent == ROOT else t.depths[parent] + 1)
+        t.scores.append(-rng.random())
+        t.ranks.append(n_kids.get(parent, 0))
+        t.draft_pos.append(i)
+        n_kids[parent] = n_kids.get(parent, 0) + 1
+    return t
+
+
+@pytest.mark.parametrize("seed,n,past", [(0, 1, 0), (1, 7, 5), (2, 24, 13), (3, 32, 100)])
+def test_verify_inputs_match_oracle(seed, n, past):
+    """verify_inputs (verify.py:32-42): ids, positions and the bool mask equal
+    the oracle's ancestor-walk restatement on random trees."""
+    import numpy as np
+
+    from oracle import tree as OT
+    from ssd.engine.verify import verify_inputs
+
+    t = _random_tree(seed, n)
+    ot = OT.DraftTree(tokens=list(t.tokens), parents=list(t.parents), depths=list(t.depths), scores=list(t.scores),
+                      ranks=list(t.ranks), draft_pos=list(t.draft_pos))
+    ids, pos, mask = verify_inputs(t, 9, past, past, "cpu")
+    rids, rpos, rmask = OT.verify_inputs(ot, 9, past, past)
+    assert ids[0].tolist() == rids and pos[0].tolist() == rpos
+    assert np.array_equal(mask.numpy(), rmask)

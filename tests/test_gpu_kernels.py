@@ -281,9 +281,29 @@ def test_kv_compact(ops, dtype, keep):
     ks = torch.tensor(keep, dtype=torch.int32, device=DEV)
     st = torch.tensor([start], dtype=torch.int32, device=DEV)
     nk = torch.tensor([len(keep)], dtype=torch.int32, device=DEV)
-    ops.kv_compact(cache, st, ks, nk, max_keep=8)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.kv_compact(cache, st, ks, nk, max_keep=8, status=status)
     torch.cuda.synchronize()
     assert torch.equal(cache, ref)
+    assert int(status.item()) == 0
+
+
+def test_kv_compact_rejects_a_keep_list_that_does_not_fit(ops):
+    """A keep list naming a slot past the cache, or longer than max_keep,
+    copies nothing and sets the status word's bad-index bit."""
+    cache = _rand(2, 2, 2, 16, 64, dtype=torch.bfloat16, seed=28)
+    ref = cache.clone()
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    i32 = dict(dtype=torch.int32, device=DEV)
+    ops.kv_compact(cache, torch.tensor([4], **i32), torch.tensor([5, 16], **i32), torch.tensor([2], **i32),
+                   max_keep=4, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 2 and torch.equal(cache, ref)
+    status.zero_()
+    ops.kv_compact(cache, torch.tensor([4], **i32), torch.tensor([5, 6, 7], **i32), torch.tensor([3], **i32),
+                   max_keep=2, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 2 and torch.equal(cache, ref)
 
 
 @pytest.mark.parametrize("name,over", [("tiny", {}), ("llama32_1b", dict(num_hidden_layers=2, vocab_size=4096))])
@@ -325,3 +345,33 @@ def test_folded_rmsnorm_matches_standalone(name, over):
     scale = ref.abs().max()
     assert (got - ref).abs().max() <= 2e-2 * scale, ((got - ref).abs().max(), scale)
     assert (got.argmax(-1) == ref.argmax(-1)).float().mean() >= 0.8
+
+
+@pytest.mark.parametrize("seed,n", [(0, 1), (1, 6), (2, 24), (3, 32)])
+def test_greedy_verify_matches_oracle(seed, n):
+    """greedy_verify (verify.py:45-57) on the device tree walk: accepted path
+    and bonus equal the oracle's on random trees whose target rows often pick
+    a child's token (deep walks), including duplicate sibling tokens, where
+    the first child in rank order must win."""
+    import random
+
+    import numpy as np
+
+    from oracle import tree as OT
+    from ssd.engine.verify import greedy_verify
+    from test_cpu_host import _random_tree
+
+    V = 50
+    t = _random_tree(seed, n, vocab=8)  # few distinct tokens: sibling duplicates
+    rng = random.Random(seed + 100)
+    logits = np.random.default_rng(seed).standard_normal((n + 1, V)).astype(np.float32)
+    kids = t.children()
+    for row in range(n + 1):
+        ch = kids.get(row - 1, [])
+        if ch and rng.random() < 0.8:
+            logits[row, t.tokens[rng.choice(ch)]] = 10.0
+    ot = OT.DraftTree(tokens=list(t.tokens), parents=list(t.parents), depths=list(t.depths), scores=list(t.scores),
+                      ranks=list(t.ranks), draft_pos=list(t.draft_pos))
+    want = OT.greedy_verify(ot, logits)
+    got = greedy_verify(t, torch.tensor(logits, device=DEV))
+    assert got == (want[0], want[1])

@@ -8,6 +8,7 @@ equal the single-GPU run except at near-ties, and every rank must hold the
 same tokens.
 """
 
+import ctypes as C
 import json
 import os
 import socket
@@ -115,6 +116,47 @@ def test_one_rank_heads_match_full_heads():
         assert torch.equal(u, v)
     assert torch.equal(ta, tb)
     assert torch.equal(la, lb)
+
+
+def test_meeting_with_a_rank_that_never_arrives_times_out():
+    """Failure detection without a fault: a two-rank group whose second region
+    is a plain local buffer that no process ever signals stands for a rank
+    that never arrives. With the spin limit lowered, the all-reduce's meeting
+    gives up, the kernel returns, the status word carries the timeout bit and
+    Workspace.check_status raises; the context stays usable (a one-rank
+    all-reduce afterwards completes cleanly)."""
+    from ssd import _lib as L
+    from ssd import ops
+
+    dev = _dev()
+    d, rows, T = 1024, 8, 4
+    lib = L.load()
+    nbytes = int(lib.ssd_tp_region_bytes(rows, d))
+    mine = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    phantom = torch.zeros(nbytes, dtype=torch.uint8, device=dev)  # nobody writes its flags
+    ptrs = (C.c_void_p * L.TP_MAX_RANKS)(mine.data_ptr(), phantom.data_ptr(), *([None] * (L.TP_MAX_RANKS - 2)))
+    grp = L.SsdTpGroup(0, 2, rows, d, ptrs)
+    resid = torch.ones(T, d, device=dev)
+    ws = ops.Workspace(dev, 64, 1)
+    stream = torch.cuda.current_stream().cuda_stream
+    prev = lib.ssd_tp_set_spin_limit(2000)
+    try:
+        L.call("ssd_tp_allreduce_residual", C.byref(grp), 0, T, resid.data_ptr(), d, None, L.SSD_F32,
+               ws.status.data_ptr(), stream)
+        torch.cuda.synchronize()
+    finally:
+        assert lib.ssd_tp_set_spin_limit(prev) == 2000
+    assert int(ws.status.item()) & 1, "the meeting did not report its timeout"
+    with pytest.raises(RuntimeError, match="timed out"):
+        ws.check_status()
+    assert int(ws.status.item()) == 0
+    # the device is still usable: a one-rank group meets itself at once
+    one = _single_group(d, rows)
+    one.partials[0][:T].fill_(2.0)
+    ops.tp_allreduce_residual(one, 0, T, resid, ws)
+    torch.cuda.synchronize()
+    ws.check_status()
+    assert torch.equal(resid, torch.full_like(resid, 3.0))
 
 
 def test_one_rank_engine_matches_unsharded_engine():

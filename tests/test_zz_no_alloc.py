@@ -20,17 +20,18 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda:0")
 
 
-def _args(x, w, out=None, resid=None, epilogue=3):
+def _args(x, ws_, out=None, resid=None, epilogue=3, layout=0):
     from ssd import _lib as L
     from ssd import ops
 
-    wp = (C.c_void_p * 3)(w.data_ptr(), None, None)
-    rows = (C.c_int64 * 3)(w.shape[0], 0, 0)
+    ws_ = list(ws_)
+    wp = (C.c_void_p * 3)(*[w.data_ptr() for w in ws_], *([None] * (3 - len(ws_))))
+    rows = (C.c_int64 * 3)(*[w.shape[0] for w in ws_], *([0] * (3 - len(ws_))))
     bp = (C.c_void_p * 3)(None, None, None)
-    return [x.data_ptr(), x.stride(0), x.shape[0], x.shape[1], 1, wp, rows, bp, L.SEG_CONCAT, epilogue, 0,
+    return [x.data_ptr(), x.stride(0), x.shape[0], x.shape[1], len(ws_), wp, rows, bp, layout, epilogue, 0,
             out.data_ptr() if out is not None else None, out.stride(0) if out is not None else 0,
             resid.data_ptr() if resid is not None else None, resid.stride(0) if resid is not None else 0,
-            ops.dtype_code(w.dtype)]
+            ops.dtype_code(ws_[0].dtype)]
 
 
 def _noalloc(x, w, status, **kw):
@@ -46,31 +47,49 @@ def _with_workspace(x, w, ws, **kw):
            torch.cuda.current_stream().cuda_stream)
 
 
-@pytest.mark.parametrize("dtype,T,N,K", [(torch.bfloat16, 33, 4096, 4096), (torch.bfloat16, 1, 14336, 4096),
-                                         (torch.float32, 7, 2048, 2048)])
-def test_noalloc_matches_workspace_entry_point(dtype, T, N, K):
+# (dtype, T, weight segments [(rows, K)], layout): decode-sized calls at the
+# largest documented row count (64) for every Llama-3-8B projection shape
+# (q/k/v as three segments, o_proj, gate/up as a pair, down, a 128k-row
+# vocabulary head), a verify-sized call, a 1-row call and fp32 calls.
+SHAPES = [
+    (torch.bfloat16, 33, [(4096, 4096)], 0),
+    (torch.bfloat16, 1, [(14336, 4096)], 0),
+    (torch.bfloat16, 64, [(4096, 4096), (1024, 4096), (1024, 4096)], 0),
+    (torch.bfloat16, 64, [(4096, 4096)], 0),
+    (torch.bfloat16, 64, [(14336, 4096), (14336, 4096)], 1),
+    (torch.bfloat16, 64, [(4096, 14336)], 0),
+    (torch.bfloat16, 64, [(128256, 4096)], 0),
+    (torch.float32, 7, [(2048, 2048)], 0),
+    (torch.float32, 64, [(2048, 8192)], 0),
+]
+
+
+@pytest.mark.parametrize("dtype,T,segs,layout", SHAPES)
+def test_noalloc_matches_workspace_entry_point(dtype, T, segs, layout):
     from ssd import ops
 
     ws = ops.Workspace(DEV, max_rows=64, vocab=1, max_head_rows=1)
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
     g = torch.Generator(device=DEV).manual_seed(7)
-    w = (torch.randn(N, K, generator=g, device=DEV) * 0.02).to(dtype)
+    K = segs[0][1]
+    w = [(torch.randn(n, k, generator=g, device=DEV) * 0.02).to(dtype) for n, k in segs]
+    N = sum(n for n, _ in segs)
     for call in range(2):  # two calls in a row, different inputs
         x = torch.randn(T, K, generator=g, device=DEV).to(dtype)
         ref = torch.empty(T, N, dtype=torch.float32, device=DEV)
         got = torch.full((T, N), float("nan"), dtype=torch.float32, device=DEV)
-        _with_workspace(x, w, ws, out=ref)
-        _noalloc(x, w, status, out=got)
+        _with_workspace(x, w, ws, out=ref, layout=layout)
+        _noalloc(x, w, status, out=got, layout=layout)
         torch.cuda.synchronize()
         assert int(status.item()) == 0
         torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-5)
-        # and the residual epilogue on the same call pattern
-        r0 = torch.randn(T, N, generator=g, device=DEV)
-        r_ref, r_got = r0.clone(), r0.clone()
-        _with_workspace(x, w, ws, resid=r_ref, epilogue=1)
-        _noalloc(x, w, status, resid=r_got, epilogue=1)
-        torch.cuda.synchronize()
-        torch.testing.assert_close(r_got, r_ref, rtol=1e-4, atol=1e-5)
+        if len(w) == 1:  # and the residual epilogue on the same call pattern
+            r0 = torch.randn(T, N, generator=g, device=DEV)
+            r_ref, r_got = r0.clone(), r0.clone()
+            _with_workspace(x, w, ws, resid=r_ref, epilogue=1)
+            _noalloc(x, w, status, resid=r_got, epilogue=1)
+            torch.cuda.synchronize()
+            torch.testing.assert_close(r_got, r_ref, rtol=1e-4, atol=1e-5)
 
 
 def test_noalloc_rejects_oversized_calls():
@@ -81,4 +100,4 @@ def test_noalloc_rejects_oversized_calls():
     x = torch.zeros(65, 128, dtype=torch.bfloat16, device=DEV)
     out = torch.empty(65, 256, dtype=torch.float32, device=DEV)
     with pytest.raises(L.SSDError, match="outside 1..64"):
-        _noalloc(x, w, status, out=out)
+        _noalloc(x, [w], status, out=out)
