@@ -74,6 +74,8 @@ def parse():
                     help="c5: tree-attention and KV-compaction sweep (ctx x tree nodes) on one GPU, then exit")
     ap.add_argument("--ncu-case", choices=["gemm", "gemm_mix", "attention"], default=None,
                     help="run one small launch set of a kernel for an ncu capture, then exit")
+    ap.add_argument("--rows", type=int, default=None, help="query token rows of the attention ncu case (33)")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the time-to-first-token measurement")
     return ap.parse_args()
 
 
@@ -130,8 +132,35 @@ def measured_peaks() -> dict:
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d.get("bf16_tflops", 1590.0)),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def prefill_timing(eng, w, ids, dev, reps: int = 3) -> dict:
+    """Time to first token of the engine's prefill (the whole prompt through
+    the target, causal, first token from the last row), CUDA events around
+    `reps` prefills after one warm-up. FLOPs: 2 x (layer weights) x P + the
+    head row + causal attention 2 x 2 x P^2/2 x H x hd per layer; roofline
+    against the measured bf16 tensor peak."""
+    import torch
+
+    eng.prefill(ids.to(dev))
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        eng.prefill(ids.to(dev))
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = e0.elapsed_time(e1) / 1e3 / reps
+    P = int(ids.numel())
+    layer_params = (w.H * w.hd + 2 * w.Hkv * w.hd) * w.d + w.H * w.hd * w.d + 3 * w.d * w.F
+    flops = 2.0 * layer_params * w.L * P + 2.0 * w.d * w.V + 2.0 * 2.0 * P * P / 2 * w.H * w.hd * w.L
+    peak = measured_peaks()
+    return {"prompt": P, "ms": t * 1e3, "tok_s": P / t, "tflops": flops / t / 1e12,
+            "frac_of_bf16_peak": flops / t / 1e12 / peak["bf16_tflops"], "peak_tflops": peak["bf16_tflops"],
+            "peak_source": peak["source"], "bound": "tensor"}
 
 
 def model_bytes(w, layers=None, bridges=(), head_rows=None) -> float:
@@ -537,7 +566,8 @@ def ncu_case(args, dev) -> None:
     else:
         from ssd.models.runner import ForwardInputs
 
-        H, Hkv, hd, T = 32, 8, 128, 33
+        H, Hkv, hd = 32, 8, 128
+        T = args.rows or 33
         ctx = args.prompt_len or 16384
         ws = ops.Workspace(dev, 64, 1, 64)
         kc = torch.randn(Hkv, ctx + 64, hd, device=dev).bfloat16()
@@ -667,10 +697,64 @@ def c5_sweep(args, dev) -> None:
     torch.cuda.synchronize(dev)
     t = e0.elapsed_time(e1) / 1e3 / (5 * L)
     cbytes = 2 * (depth + 1) * L * 2 * Hkv * hd * 2
+    del graph, buf
+    torch.cuda.empty_cache()
+    control = c5_control(dev, args)
     print(json.dumps({"sweep": "c5", "shape": "8B (H 32, Hkv 8, hd 128), 32 layer caches, K/V ~ N(0,1) seed 4",
                       "attention": cells,
                       "compaction": {"kept": depth + 1, "us": t * 1e6, "gbs": cbytes / t / 1e9, "bytes": cbytes},
+                      "control": control,
                       "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"]}), flush=True)
+
+
+def c5_control(dev, args) -> dict:
+    """BASELINE config 5's control run: the Llama-3-8B shape (bf16, seed 4,
+    no planting) with draft_layers = all 32 layers and no bridges, so every
+    drafted token is the target's own greedy choice up to rounding near-ties:
+    the maximum-commit-rate path of the C3 tree (depth 6, branch
+    [4,2,2,1,1,1], max_nodes 32), 2048-token prompt, 256 new tokens, against
+    target-only decoding of the same sequence; plus time to first token at
+    1k / 2k / 4k prompts on the same model."""
+    import torch
+
+    from ssd import synthetic as S
+    from ssd.config import DraftingConfig
+    from ssd.engine.round import GreedyRound, TargetStep, TreePlan, cache_capacity
+    from ssd.engine.speculative import TargetRunner
+    from ssd.models import SubnetworkDraftModel
+
+    c3 = S.CONFIGS["c3"]
+    P, max_new = c3.prompt_len, c3.max_new_tokens
+    base = S.build_base_model(c3.model, 4, torch.bfloat16, dev, gen_device="cuda")
+    target = TargetRunner(base)
+    draft = SubnetworkDraftModel(base, list(range(base.config.num_hidden_layers)))
+    assert not draft.bridges
+    cfg = DraftingConfig(**c3.drafting)
+    ids = S.make_prompt(4, P, base.config.vocab_size)
+    cap = cache_capacity(P, max_new, TreePlan(cfg))
+    eng = GreedyRound(target, draft, cfg, target.new_cache(cap), max_new)
+    decode_timed(eng, ids, dev, 1, max_new)
+    phases: dict = {}
+    toks, acc, t = decode_timed(eng, ids, dev, 1, max_new, None, phases)
+    del eng
+    ar = TargetStep(target, target.new_cache(cap), max_new)
+    ar_toks, t_ar = ar_timed(ar, ids, dev, 1, max_new, warm=True)
+    del ar
+    prefills = []
+    for plen in (1024, 2048, 4096):
+        tstep = TargetStep(target, target.new_cache(cache_capacity(plen, 8)), 8)
+        prefills.append(prefill_timing(tstep, target.weights, S.make_prompt(4, plen, base.config.vocab_size), dev))
+        del tstep
+    del base, target, draft
+    torch.cuda.empty_cache()
+    rounds = max(1, len(acc))
+    return {"workload": "c5 control: 8B shape, draft = all 32 layers, no bridges, c3 tree, prompt 2048, 256 tokens",
+            "value": len(toks) / t, "unit": "tok/s", "mean_accepted": sum(acc) / rounds,
+            "max_committed": cfg.depth + 1, "ar_value": len(ar_toks) / t_ar,
+            "speedup_vs_ar": (len(toks) / t) / (len(ar_toks) / t_ar),
+            "sd_equals_ar": toks == ar_toks, "first_divergence": first_divergence(toks, ar_toks),
+            "phase_ms_per_round": {k: v / rounds * 1e3 for k, v in phases.items()},
+            "prefill": prefills}
 
 
 def decode_timed(eng, ids, dev, world: int, max_new: int, seed=None, phase_acc=None):
@@ -737,6 +821,15 @@ def ar_timed(ar, ids, dev, world: int, max_new: int, seed=None, warm: bool = Fal
     torch.cuda.synchronize(dev)
     t = sync_max(e0.elapsed_time(e1) / 1e3, world)
     return _finish(out, set(), max_new)[0], t
+
+
+def ar_gap_at(ar, ids, dev, step: int) -> float:
+    """Top-2 logit gap of the target-only decode of `ids` at decode step
+    `step` (0 = the token after the prompt), one graph step at a time."""
+    ar.prefill(ids.to(dev))
+    for _ in range(step):
+        ar.run(1)
+    return float(ar.gap[0])
 
 
 def first_divergence(a, b):
@@ -830,6 +923,8 @@ def tp_leg(args, dev, rank: int, world: int) -> dict:
     del eng
     ar = TargetStep(target, target.new_cache(cap), max_new)
     ar_tokens, t_ar = ar_timed(ar, ids, dev, world, max_new, warm=True)
+    div = first_divergence(sd_tokens, ar_tokens)
+    div_gap = ar_gap_at(ar, ids, dev, div) if div is not None and div < len(ar_tokens) else None
     del ar
     roof = gemm_roofline(w, rows, dev)
     everyone = dp.gather_lists(sd_tokens, world)
@@ -844,7 +939,7 @@ def tp_leg(args, dev, rank: int, world: int) -> dict:
            "tp": world, "value": value, "unit": "tok/s", "ar_value": ar_value, "speedup_vs_ar": value / ar_value,
            "mean_accepted": mean_acc, "phase_ms_per_round": {k: v / rounds * 1e3 for k, v in phases.items()},
            "ranks_agree": all(t == everyone[0] for t in everyone),
-           "sd_equals_ar": sd_tokens == ar_tokens, "first_divergence": first_divergence(sd_tokens, ar_tokens),
+           "sd_equals_ar": sd_tokens == ar_tokens, "first_divergence": div, "ar_gap_at_divergence": div_gap,
            "allreduce_us": pt.get("tp_allreduce", {}).get("us"),
            "verify_gemm_us": {k: v["us"] for k, v in pt.items()},
            "verify_gemm_mix_gbs": roof["gbs"],
@@ -959,14 +1054,21 @@ def main() -> None:
             if not sampled:
                 i = first_divergence(sd_tokens[j], toks)
                 if i is not None:
-                    diverged.append({"sequence": rank + j * world if not tp_run else j, "step": i})
+                    diverged.append({"sequence": rank + j * world if not tp_run else j, "step": i, "j": j})
         ar_value = job_sum(n_ar) / t_ar
-        del ar
         if not sampled:
+            # untimed: the target-only decode's own top-2 logit gap at each
+            # divergence step (a flip between the verify forward's and the
+            # single-row forward's rounding needs a near-tie there)
+            for d in diverged:
+                d["ar_gap"] = ar_gap_at(ar, mine[d.pop("j")], dev, d["step"])
             all_div = [d for part in dp.gather_lists(diverged, world) for d in part]
-            parity = {"sd_equals_ar": not all_div, "first_divergence": all_div or None,
+            parity = {"sd_equals_ar": not all_div, "divergences": all_div or None,
+                      "max_gap_at_divergence": max((d["ar_gap"] for d in all_div), default=None),
                       "sequences": args.sequences * args.steps if tp_run else args.sequences,
-                      "check": "greedy speculative tokens == target-only tokens, every timed sequence"}
+                      "check": "greedy speculative tokens == target-only tokens, every timed sequence; at a "
+                               "divergence, the target-only decode's top-2 logit gap at that step"}
+        del ar
 
     # end to end through the public API (pinned host prompt -> host tokens)
     gen = SpeculativeGenerator(base, draft, cfg, target)
@@ -985,6 +1087,13 @@ def main() -> None:
     d2h = getattr(e2e_engine, "d2h_bytes", 0) - d2h0
     e2e_value = job_sum(n_e2e) / t_e2e
     del gen, e2e_engine
+
+    # time to first token: the prefill of the first sequence
+    prefill = None
+    if not sampled and not args.no_prefill:
+        tstep = TargetStep(target, target.new_cache(cap), max_new)
+        prefill = prefill_timing(tstep, w, mine[0], dev)
+        del tstep
 
     # kernel roofline of the dominant kernel (tcgen05 GEMM, verify forward)
     peaks = measured_peaks()
@@ -1051,6 +1160,8 @@ def main() -> None:
             "clocks": clk,
             "build_s": build_s,
         }
+        if prefill is not None:
+            line["prefill"] = prefill
         if sample_line is not None:
             line["c3_sample"] = sample_line
         if tp_line is not None:

@@ -74,12 +74,16 @@ def test_noalloc_matches_workspace_entry_point(dtype, T, segs, layout):
     K = segs[0][1]
     w = [(torch.randn(n, k, generator=g, device=DEV) * 0.02).to(dtype) for n, k in segs]
     N = sum(n for n, _ in segs)
+    # the gate/up pair runs with its SwiGLU epilogue (bf16 [T, F] out), the
+    # only epilogue of the pair layout; everything else stores fp32
+    pair = layout == 1
+    epi, odt, ncol = (2, dtype, N // 2) if pair else (3, torch.float32, N)
     for call in range(2):  # two calls in a row, different inputs
         x = torch.randn(T, K, generator=g, device=DEV).to(dtype)
-        ref = torch.empty(T, N, dtype=torch.float32, device=DEV)
-        got = torch.full((T, N), float("nan"), dtype=torch.float32, device=DEV)
-        _with_workspace(x, w, ws, out=ref, layout=layout)
-        _noalloc(x, w, status, out=got, layout=layout)
+        ref = torch.empty(T, ncol, dtype=odt, device=DEV)
+        got = torch.full((T, ncol), float("nan"), dtype=odt, device=DEV)
+        _with_workspace(x, w, ws, out=ref, layout=layout, epilogue=epi)
+        _noalloc(x, w, status, out=got, layout=layout, epilogue=epi)
         torch.cuda.synchronize()
         assert int(status.item()) == 0
         torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-5)
