@@ -278,8 +278,23 @@ int ssd_gumbel_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, co
                     const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round, int64_t row_base,
                     int32_t* out_tok, float* out_logprob, void* stream);
 
-/* One token drawn from warp(logits[0..V)) into out[0] (scratch: V floats).
- * Replaces _first_token's sampling branch (ssd/engine/speculative.py:81-84). */
+/* Fused ssd_warp_params + ssd_gumbel_topk: each row is split over a
+ * thread-block cluster of up to 8 CTAs (slices staged in shared memory,
+ * reductions combined in rank order). Writes the rows' warp parameters to
+ * params_out (may be NULL when k > 0) and, for k >= 1, the same draws as
+ * ssd_gumbel_topk with those parameters (RNG counters (round, row_base + r,
+ * i, 0)); out_logprob may be NULL. k = 0 computes the parameters only.
+ * V <= 131072. Replaces the sampling branch of TreeDrafter._propose
+ * (tree_drafter.py:134-145) and warp_probs (:34-45) for the verify rows. */
+int ssd_warp_sample_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, float temperature, float top_p,
+                         int64_t k, const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round,
+                         int64_t row_base, void* params_out, int32_t* out_tok, float* out_logprob, void* stream);
+
+/* One token drawn from warp(logits[0..V)) into out[0]: a Gumbel-max draw on
+ * one cluster (RNG counters (round, row_id, i, stream_id)); rows longer than
+ * 131072 use one CTA and an inverse-CDF draw over `scratch` (V floats, may be
+ * NULL otherwise). Replaces _first_token's sampling branch
+ * (ssd/engine/speculative.py:81-84). */
 int ssd_sample_token(const float* logits, int64_t V, float temperature, float top_p, const uint64_t* seed,
                      const int32_t* round, int64_t row_id, int64_t stream_id, float* scratch, int32_t* out,
                      void* stream);
@@ -292,8 +307,12 @@ int ssd_sample_token(const float* logits, int64_t V, float temperature, float to
  * root, row draft_pos - root_pos for a fed node) over the draft vocabulary
  * (vocab_ids, NULL = the first Vd ids). target_params / draft_params are
  * ssd_warp_params of the target rows [rows, ldt] and the draft_rows draft
- * rows [draft_rows, ldd]. p_scratch / q_scratch: V floats each. Outputs as
- * ssd_tree_walk_greedy. Replaces sample_verify (ssd/engine/verify.py:60-95). */
+ * rows [draft_rows, ldd]. Runs on one cluster of up to 8 CTAs that keep
+ * their vocabulary slices of p and q in shared memory; the bonus is a
+ * Gumbel-max draw from p (counters (round, cur + 1, i, 2)). p_scratch /
+ * q_scratch (V floats each) are used only for V > 131072 (one CTA) and may be
+ * NULL otherwise. Outputs as ssd_tree_walk_greedy. Replaces sample_verify
+ * (ssd/engine/verify.py:60-95). */
 int ssd_tree_walk_sample(const int32_t* n_nodes, int64_t max_nodes, const int32_t* tokens, const int32_t* parents,
                          const int32_t* ranks, const int32_t* draft_pos, const int32_t* root_pos,
                          const float* target_logits, int64_t ldt, const void* target_params, int64_t V,

@@ -182,6 +182,23 @@ __device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t saddr, uint32_t lbo,
   d |= static_cast<uint64_t>(2) << 61;
   return d;
 }
+// 32 lanes x 32 bit, 32 consecutive columns per thread, one wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,"
+      "%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
 // 32 lanes x 32 bit, 64 consecutive columns per thread, one wait.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
   uint32_t r[64];
@@ -259,6 +276,12 @@ __device__ __forceinline__ float dsmem_ld(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ unsigned long long dsmem_ld_u64(uint32_t addr) {
+  unsigned long long v;
+  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void dsmem_st(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
@@ -318,8 +341,11 @@ __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
   }
   return c;
 }
-// Uniform in the open interval (0, 1) from 24 random bits.
-__device__ __forceinline__ float u01(uint32_t x) { return (static_cast<float>(x >> 8) + 0.5f) * (1.0f / 16777216.0f); }
+// Uniform in the open interval (0, 1) from 23 random bits: (k + 1/2) / 2^23
+// for k < 2^23, every value exactly representable, the largest 1 - 2^-24 (a
+// 24-bit version rounds its top value up to exactly 1.0 in fp32, which would
+// make a Gumbel key -log(-log(u)) infinite).
+__device__ __forceinline__ float u01(uint32_t x) { return (static_cast<float>(x >> 9) + 0.5f) * (1.0f / 8388608.0f); }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float gelu_f(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }

@@ -359,8 +359,10 @@ __device__ int draw_from(const float* w, int n, float u, float* red, float* scan
   return pick;
 }
 
-// Token ~ warp(logits row): one launch, one row. Writes the token to out[0];
-// the RNG counter is (round[0], row_id, 0, stream).
+// Token ~ warp(logits row): one launch, one row, one CTA; inverse-CDF draw
+// with RNG counter (round[0], row_id, 0, stream). ssd_sample_token draws with
+// the clustered warp_sample_kernel (Gumbel-max, counters (round[0], row_id,
+// i, stream)); this kernel serves rows too long for a cluster.
 __global__ void __launch_bounds__(kSampThreads) sample_token_kernel(const float* logits, int V, float temperature,
                                                                     float top_p, const uint64_t* seed,
                                                                     const int32_t* round, int row_id, int stream,
@@ -522,6 +524,488 @@ __global__ void __launch_bounds__(kSampThreads) sample_verify_kernel(
   }
 }
 
+// ------------------------------------------------------ cluster row kernels
+// One logit row split over a cluster of S CTAs (S <= 8, grid x = rank): CTA s
+// stages its slice [s * len, min(V, (s + 1) * len)) of the row in shared
+// memory once and every pass reads it from there. Row-wide reductions publish
+// one partial per CTA in the CTA's own slot, cross one cluster barrier, and
+// every CTA combines the S partials in rank order, so all CTAs hold the same
+// bits and take the same decisions. Slots come in two banks used in turn
+// (one counter per kernel): a bank is rewritten two exchanges later, after a
+// barrier that every reader of its previous contents has passed. Each kernel
+// ends with a cluster barrier, so no CTA exits while a peer may still read
+// its shared memory.
+constexpr int kRowMaxSlices = 8;
+constexpr int kRowSliceMax = 16384;  // staged floats per CTA (64 KB)
+
+struct RowExchange {
+  float* fslot;               // [2][2] floats: (value, index bits) per bank
+  unsigned long long* hslot;  // [2][256] histogram bins per bank
+  float* gath;                // [2 * kRowMaxSlices] gathered partials
+  unsigned long long* ghist;  // [256] combined histogram
+  int S;
+  int n;  // exchanges so far
+};
+
+// Row-wide max (is_max) or sum of a CTA-uniform value v, in rank order.
+__device__ float row_allreduce(RowExchange& x, float v, bool is_max) {
+  float* slot = x.fslot + (x.n & 1) * 2;
+  if (threadIdx.x == 0) slot[0] = v;
+  cluster_sync_all();
+  if (threadIdx.x < x.S) x.gath[threadIdx.x] = dsmem_ld(dsmem_map(smem_u32(slot), threadIdx.x));
+  __syncthreads();
+  float r = is_max ? -INFINITY : 0.f;
+  for (int t = 0; t < x.S; ++t) r = is_max ? fmaxf(r, x.gath[t]) : r + x.gath[t];
+  __syncthreads();  // gath is reused by the next exchange
+  ++x.n;
+  return r;
+}
+
+// Row-wide best (key desc, index asc) of CTA-uniform (key, idx) pairs.
+__device__ void row_allbest(RowExchange& x, float& key, int& idx) {
+  float* slot = x.fslot + (x.n & 1) * 2;
+  if (threadIdx.x == 0) {
+    slot[0] = key;
+    slot[1] = __int_as_float(idx);
+  }
+  cluster_sync_all();
+  if (threadIdx.x < x.S) {
+    const uint32_t a = dsmem_map(smem_u32(slot), threadIdx.x);
+    x.gath[2 * threadIdx.x] = dsmem_ld(a);
+    x.gath[2 * threadIdx.x + 1] = dsmem_ld(a + 4);
+  }
+  __syncthreads();
+  float bk = -INFINITY;
+  int bi = INT32_MAX;
+  for (int t = 0; t < x.S; ++t) {
+    const float k = x.gath[2 * t];
+    const int i = __float_as_int(x.gath[2 * t + 1]);
+    if (k > bk || (k == bk && i < bi)) {
+      bk = k;
+      bi = i;
+    }
+  }
+  __syncthreads();
+  ++x.n;
+  key = bk;
+  idx = bi;
+}
+
+// Warp parameters of the row whose slice is staged in xs[0, n): max,
+// kept-mass normaliser and, for top_p < 1, the nucleus threshold by the same
+// 4-level radix select as row_warp with the bins summed over the cluster
+// (integer masses, so the sums do not depend on the split).
+__device__ WarpParams cluster_row_warp(const float* xs, int n, float temperature, float top_p, float* red,
+                                       RowExchange& x, unsigned long long* sel) {
+  WarpParams P;
+  P.inv_t = 1.0f / temperature;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += kSampThreads) mx = fmaxf(mx, xs[i]);
+  P.m = row_allreduce(x, block_max(mx, red), true);
+  float z = 0.f;
+  for (int i = threadIdx.x; i < n; i += kSampThreads) z += expf((xs[i] - P.m) * P.inv_t);
+  const float Z = row_allreduce(x, block_sum(z, red), false);
+  if (!(top_p < 1.0f)) {
+    P.lambda = -INFINITY;
+    P.log_z = logf(Z);
+    return P;
+  }
+  const double scale = 281474976710656.0 / (double)Z;  // 2^48 / Z
+  const unsigned long long target = static_cast<unsigned long long>((double)top_p * 281474976710656.0);
+  uint32_t prefix = 0;
+  unsigned long long mass_gt = 0;
+  for (int level = 0; level < 4; ++level) {
+    const int shift = 24 - 8 * level;
+    unsigned long long* hist = x.hslot + (x.n & 1) * 256;
+    for (int b = threadIdx.x; b < 256; b += kSampThreads) hist[b] = 0ull;
+    __syncthreads();
+    for (int base = 0; base < n; base += kSampThreads) {
+      const int i = base + threadIdx.x;
+      const float l = i < n ? xs[i] : -INFINITY;
+      const uint32_t k = order_key(l);
+      const bool in = i < n && (level == 0 || (k >> (shift + 8)) == prefix);
+      const unsigned long long fp =
+          in ? static_cast<unsigned long long>((double)expf((l - P.m) * P.inv_t) * scale) : 0ull;
+      hist_add_warp(hist, (k >> shift) & 255u, fp, in);
+    }
+    cluster_sync_all();  // every CTA's bins are complete
+    for (int b = threadIdx.x; b < 256; b += kSampThreads) {
+      unsigned long long t = 0ull;
+      for (int r = 0; r < x.S; ++r) t += dsmem_ld_u64(dsmem_map(smem_u32(hist + b), r));
+      x.ghist[b] = t;
+    }
+    ++x.n;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      // lowest non-empty bin whose mass strictly above it is <= top_p
+      unsigned long long S = mass_gt, sel_S = mass_gt;
+      int sb = -1;
+      for (int b = 255; b >= 0; --b) {
+        if (x.ghist[b] == 0ull) continue;
+        if (S > target) break;
+        sb = b;
+        sel_S = S;
+        S += x.ghist[b];
+      }
+      if (sb < 0) sb = 255;  // unreachable for a finite row
+      sel[0] = (static_cast<unsigned long long>(prefix) << 8) | static_cast<unsigned>(sb);
+      sel[1] = sel_S;
+    }
+    __syncthreads();
+    prefix = static_cast<uint32_t>(sel[0]);
+    mass_gt = sel[1];
+    __syncthreads();
+  }
+  P.lambda = key_float(prefix);
+  float zk = 0.f;
+  for (int i = threadIdx.x; i < n; i += kSampThreads) {
+    const float l = xs[i];
+    if (l >= P.lambda) zk += expf((l - P.m) * P.inv_t);
+  }
+  P.log_z = logf(row_allreduce(x, block_sum(zk, red), false));
+  return P;
+}
+
+// Fused warp parameters + Gumbel top-k of each row (grid (S, rows), cluster
+// (S, 1)): the parameters of row r go to params_out[r] (if given) and its k
+// draws without replacement, in draw order, to out_tok / out_lp[r * k ...]
+// (k = 0: parameters only). The draws equal gumbel_topk_kernel's for the same
+// parameters: keys lp + Gumbel with RNG counter (round, row_base + r, i,
+// stream), ties to the lower index, tokens through vocab_ids.
+__global__ void __launch_bounds__(kSampThreads, 1) warp_sample_kernel(
+    const float* logits, int64_t ld, int V, float temperature, float top_p, int k, const int64_t* vocab_ids,
+    const uint64_t* seed, const int32_t* round, int row_base, int stream, WarpParams* params_out, int32_t* out_tok,
+    float* out_lp) {
+  extern __shared__ float xs[];
+  __shared__ float red[32];
+  __shared__ float fslot[4];
+  __shared__ unsigned long long hslot[512];
+  __shared__ unsigned long long ghist[256];
+  __shared__ float gath[2 * kRowMaxSlices];
+  __shared__ unsigned long long sel[4];
+  __shared__ float s_key[kSampWarps];
+  __shared__ int s_idx[kSampWarps];
+  __shared__ int s_own[kSampWarps];
+  __shared__ float c_key[kRowMaxSlices * kMaxK];  // rank 0: every slice's list
+  __shared__ int c_idx[kRowMaxSlices * kMaxK];
+  const int S = gridDim.x, s = blockIdx.x, r = blockIdx.y;
+  const int len = (V + S - 1) / S;
+  const int i0 = s * len, n = max(0, min(V, i0 + len) - i0);
+  const float* row = logits + (int64_t)r * ld;
+  pdl_wait();
+  pdl_trigger();
+  for (int i = threadIdx.x; i < n; i += kSampThreads) xs[i] = row[i0 + i];
+  __syncthreads();
+  RowExchange x{fslot, hslot, gath, ghist, S, 0};
+  const WarpParams P = cluster_row_warp(xs, n, temperature, top_p, red, x, sel);
+  if (s == 0 && threadIdx.x == 0 && params_out) params_out[r] = P;
+  if (k <= 0) {
+    cluster_sync_all();  // peers may still read this CTA's exchange slot
+    return;
+  }
+  const uint64_t sd = seed[0];
+  const uint32_t rnd = static_cast<uint32_t>(round ? round[0] : 0);
+  const uint32_t row_id = static_cast<uint32_t>(row_base + r);
+  float kk[kMaxK];
+  int ki[kMaxK];
+#pragma unroll
+  for (int j = 0; j < kMaxK; ++j) {
+    kk[j] = -INFINITY;
+    ki[j] = INT32_MAX;
+  }
+  for (int i = threadIdx.x; i < n; i += kSampThreads) {
+    const float lp = warped_lp(P, xs[i]);
+    if (lp == -INFINITY) continue;
+    const int gi = i0 + i;
+    const float g = -logf(-logf(uniform(sd, rnd, row_id, static_cast<uint32_t>(gi), static_cast<uint32_t>(stream))));
+    const float key = lp + g;
+    if (key > kk[k - 1] || (key == kk[k - 1] && gi < ki[k - 1])) {
+      int j = k - 1;
+      while (j > 0 && (key > kk[j - 1] || (key == kk[j - 1] && gi < ki[j - 1]))) {
+        kk[j] = kk[j - 1];
+        ki[j] = ki[j - 1];
+        --j;
+      }
+      kk[j] = key;
+      ki[j] = gi;
+    }
+  }
+  // this slice's k best, in order, into rank 0's candidate lists
+  const uint32_t ck0 = dsmem_map(smem_u32(c_key), 0u);
+  const uint32_t ci0 = dsmem_map(smem_u32(c_idx), 0u);
+  int head = 0;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int q = 0; q < k; ++q) {
+    float bk = head < k ? kk[head] : -INFINITY;
+    int bi = head < k ? ki[head] : INT32_MAX;
+    int own = threadIdx.x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const int oo = __shfl_xor_sync(0xffffffffu, own, o);
+      if (ok > bk || (ok == bk && oi < bi)) {
+        bk = ok;
+        bi = oi;
+        own = oo;
+      }
+    }
+    if (lane == 0) {
+      s_key[w] = bk;
+      s_idx[w] = bi;
+      s_own[w] = own;
+    }
+    __syncthreads();
+    float gk = -INFINITY;
+    int gi = INT32_MAX, go = -1;
+    for (int j = 0; j < kSampWarps; ++j)
+      if (s_key[j] > gk || (s_key[j] == gk && s_idx[j] < gi)) {
+        gk = s_key[j];
+        gi = s_idx[j];
+        go = s_own[j];
+      }
+    if (threadIdx.x == go) ++head;
+    if (threadIdx.x == 0) {
+      const uint32_t off = static_cast<uint32_t>((s * kMaxK + q) * 4);
+      dsmem_st(ck0 + off, gk);
+      dsmem_st(ci0 + off, __int_as_float(gi));
+    }
+    __syncthreads();
+  }
+  cluster_sync_all();  // every slice's list is in rank 0's shared memory
+  if (s != 0 || threadIdx.x != 0) return;
+  int hd[kRowMaxSlices];
+  for (int j = 0; j < kRowMaxSlices; ++j) hd[j] = 0;
+  for (int q = 0; q < k; ++q) {
+    float gk = -INFINITY;
+    int gi = INT32_MAX, gs = -1;
+    for (int j = 0; j < S; ++j) {
+      if (hd[j] >= k) continue;
+      const float ck = c_key[j * kMaxK + hd[j]];
+      const int cix = c_idx[j * kMaxK + hd[j]];
+      if (ck > gk || (ck == gk && cix < gi)) {
+        gk = ck;
+        gi = cix;
+        gs = j;
+      }
+    }
+    if (gs >= 0) ++hd[gs];
+    const bool ok = gk != -INFINITY;
+    out_tok[(int64_t)r * k + q] = ok ? (vocab_ids ? (int)vocab_ids[gi] : gi) : -1;
+    if (out_lp) out_lp[(int64_t)r * k + q] = ok ? warped_lp(P, row[gi]) : -INFINITY;
+  }
+}
+
+// Multi-candidate speculative sampling without replacement over the device
+// tree, on a cluster of S CTAs (grid (S, 1)): CTA s keeps its vocabulary
+// slice of the current p and q in shared memory. Every CTA runs the walk;
+// decisions use point values read from the owning CTA and sums combined in
+// rank order, so all CTAs decide alike. Same inputs and RNG counters as
+// sample_verify_kernel for the acceptance tests ((round, cur + 1, child, 1));
+// the bonus token is a Gumbel-max draw from the current p with counters
+// (round, cur + 1, i, 2) (the same distribution as an inverse-CDF draw).
+__global__ void __launch_bounds__(kSampThreads, 1) sample_verify_cluster_kernel(
+    const int32_t* n_nodes, int max_nodes, const int32_t* tokens, const int32_t* parents, const int32_t* ranks,
+    const int32_t* draft_pos, const int32_t* root_pos, const float* tlogits, int64_t ldt, const WarpParams* tparams,
+    int V, const float* dlogits, int64_t ldd, const WarpParams* dparams, int draft_rows, int Vd,
+    const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round, int32_t* accepted, int32_t* n_accepted,
+    int32_t* bonus, int32_t* keep_slots, int32_t* n_keep, uint32_t* status) {
+  extern __shared__ float dyn[];
+  __shared__ float red[32];
+  __shared__ float fslot[4];
+  __shared__ float gath[2 * kRowMaxSlices];
+  __shared__ int kids[64];
+  __shared__ int s_nk;
+  __shared__ float s_pt[2];
+  __shared__ float s_key[kSampWarps];
+  __shared__ int s_idx[kSampWarps];
+  const int S = gridDim.x, s = blockIdx.x;
+  const int len = (V + S - 1) / S;
+  const int i0 = s * len, nl = max(0, min(V, i0 + len) - i0);
+  float* ps = dyn;
+  float* qs = dyn + len;
+  pdl_wait();
+  pdl_trigger();
+  RowExchange x{fslot, nullptr, gath, nullptr, S, 0};
+  const int n = min(*n_nodes, max_nodes);
+  const int c0 = root_pos[0];
+  const uint64_t sd = seed[0];
+  const uint32_t rnd = static_cast<uint32_t>(round ? round[0] : 0);
+  const bool lead = s == 0 && threadIdx.x == 0;
+  int cur = -1, na = 0;
+  if (lead) keep_slots[0] = c0;
+  for (int step = 0; step <= n; ++step) {
+    // p = warp(target row of cur), this CTA's slice
+    const float* trow = tlogits + (int64_t)(cur + 1) * ldt;
+    const WarpParams PT = tparams[cur + 1];
+    for (int i = threadIdx.x; i < nl; i += kSampThreads) {
+      const float lp = warped_lp(PT, trow[i0 + i]);
+      ps[i] = lp == -INFINITY ? 0.f : expf(lp);
+    }
+    // children of cur in rank order (ties by index)
+    if (threadIdx.x == 0) {
+      int m = 0;
+      for (int i = 0; i < n && m < 64; ++i)
+        if (parents[i] == cur) kids[m++] = i;
+      for (int a = 1; a < m; ++a) {
+        const int c = kids[a];
+        int b = a - 1;
+        while (b >= 0 && ranks[kids[b]] > ranks[c]) {
+          kids[b + 1] = kids[b];
+          --b;
+        }
+        kids[b + 1] = c;
+      }
+      s_nk = m;
+    }
+    __syncthreads();
+    const int nk = s_nk;
+    int chosen = -1;
+    if (nk > 0) {
+      const int drow = cur < 0 ? 0 : draft_pos[cur] - c0;
+      if (drow < 0 || drow >= draft_rows) {
+        if (lead) report_error(status, kErrBadIndex);
+        break;
+      }
+      // q over this slice of the full vocabulary (0 outside the draft vocabulary)
+      const float* dr = dlogits + (int64_t)drow * ldd;
+      const WarpParams PD = dparams[drow];
+      if (vocab_ids) {
+        for (int i = threadIdx.x; i < nl; i += kSampThreads) qs[i] = 0.f;
+        __syncthreads();
+        for (int j = threadIdx.x; j < Vd; j += kSampThreads) {
+          const int64_t v = vocab_ids[j];
+          if (v >= i0 && v < i0 + nl) {
+            const float lp = warped_lp(PD, dr[j]);
+            qs[v - i0] = lp == -INFINITY ? 0.f : expf(lp);
+          }
+        }
+      } else {
+        for (int i = threadIdx.x; i < nl; i += kSampThreads) {
+          const float lp = i0 + i < Vd ? warped_lp(PD, dr[i0 + i]) : -INFINITY;
+          qs[i] = lp == -INFINITY ? 0.f : expf(lp);
+        }
+      }
+      cluster_sync_all();  // every slice of p and q is complete
+      float zp = 1.f, zq = 1.f;  // p / zp and q / zq are the current distributions
+      for (int ci = 0; ci < nk; ++ci) {
+        const int c = kids[ci];
+        const int tok = tokens[c];
+        const bool in = tok >= 0 && tok < V;
+        const int owner = in ? tok / len : 0, off = in ? tok - owner * len : 0;
+        if (threadIdx.x == 0) {
+          s_pt[0] = in ? dsmem_ld(dsmem_map(smem_u32(ps + off), owner)) : 0.f;
+          s_pt[1] = in ? dsmem_ld(dsmem_map(smem_u32(qs + off), owner)) : 0.f;
+        }
+        __syncthreads();
+        const float qx = s_pt[1] / zq;
+        const float px = s_pt[0] / zp;
+        __syncthreads();
+        if (!(qx > 0.f)) continue;
+        const float u = uniform(sd, rnd, static_cast<uint32_t>(cur + 1), static_cast<uint32_t>(ci), 1u);
+        if (u < fminf(1.f, px / qx)) {
+          chosen = c;
+          break;
+        }
+        // reject: p <- max(p - q, 0) renormalised, only if that has mass
+        float rs = 0.f;
+        for (int i = threadIdx.x; i < nl; i += kSampThreads) rs += fmaxf(ps[i] / zp - qs[i] / zq, 0.f);
+        const float R = row_allreduce(x, block_sum(rs, red), false);
+        if (R > 0.f) {
+          for (int i = threadIdx.x; i < nl; i += kSampThreads) ps[i] = fmaxf(ps[i] / zp - qs[i] / zq, 0.f);
+          zp = R;
+        }
+        // q <- q without x, renormalised; stop when nothing is left (every
+        // peer's read of q[x] came before the exchange barrier above)
+        __syncthreads();
+        if (in && owner == s && threadIdx.x == 0) qs[off] = 0.f;
+        __syncthreads();
+        float qsum = 0.f;
+        for (int i = threadIdx.x; i < nl; i += kSampThreads) qsum += qs[i];
+        const float Q = row_allreduce(x, block_sum(qsum, red), false);
+        if (!(Q > 0.f)) break;
+        zq = Q;
+      }
+      cluster_sync_all();  // no peer reads this step's p or q any more
+      if (chosen >= 0) {
+        if (lead) {
+          accepted[na] = chosen;
+          keep_slots[1 + na] = c0 + 1 + chosen;
+        }
+        ++na;
+        cur = chosen;
+        continue;
+      }
+    }
+    // bonus ~ p: Gumbel-max over the slice, then over the cluster
+    float bk = -INFINITY;
+    int bi = INT32_MAX;
+    for (int i = threadIdx.x; i < nl; i += kSampThreads) {
+      const float w = ps[i];
+      if (!(w > 0.f)) continue;
+      const int gi = i0 + i;
+      const float key =
+          logf(w) - logf(-logf(uniform(sd, rnd, static_cast<uint32_t>(cur + 1), static_cast<uint32_t>(gi), 2u)));
+      if (key > bk || (key == bk && gi < bi)) {
+        bk = key;
+        bi = gi;
+      }
+    }
+    const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ok > bk || (ok == bk && oi < bi)) {
+        bk = ok;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      s_key[wp] = bk;
+      s_idx[wp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float gk = -INFINITY;
+      int gi = INT32_MAX;
+      for (int j = 0; j < kSampWarps; ++j)
+        if (s_key[j] > gk || (s_key[j] == gk && s_idx[j] < gi)) {
+          gk = s_key[j];
+          gi = s_idx[j];
+        }
+      s_key[0] = gk;
+      s_idx[0] = gi;
+    }
+    __syncthreads();
+    float gk = s_key[0];
+    int gi = s_idx[0];
+    row_allbest(x, gk, gi);
+    cluster_sync_all();  // peers may still read this CTA's exchange slot
+    if (lead) {
+      *bonus = gi == INT32_MAX ? 0 : gi;
+      *n_accepted = na;
+      *n_keep = na + 1;
+    }
+    return;
+  }
+  cluster_sync_all();
+  if (lead) {
+    *bonus = 0;
+    *n_accepted = na;
+    *n_keep = na + 1;
+  }
+}
+
+// Cluster size for a row of V logits: slices of at least 2048 and at most
+// kRowSliceMax floats, at most 8 CTAs. 0 = the row is too long.
+static int row_slices(int64_t V) {
+  int S = (int)((V + 2047) / 2048);
+  if (S > kRowMaxSlices) S = kRowMaxSlices;
+  if (S < 1) S = 1;
+  return (V + S - 1) / S > kRowSliceMax ? 0 : S;
+}
+
 }  // namespace ssd
 
 using namespace ssd;
@@ -563,14 +1047,53 @@ int ssd_gumbel_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, co
                        out_logprob);
 }
 
+int ssd_warp_sample_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, float temperature, float top_p,
+                         int64_t k, const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round,
+                         int64_t row_base, void* params_out, int32_t* out_tok, float* out_logprob, void* stream) {
+  if (rows <= 0 || rows > 65535 || V <= 0 || !logits || ld < V || !(temperature > 0.f) || !(top_p > 0.f) ||
+      top_p > 1.f)
+    return fail(SSD_ERR_INVALID, "ssd_warp_sample_topk: need rows, V > 0, temperature > 0, 0 < top_p <= 1");
+  if (k < 0 || k > kMaxK) return fail(SSD_ERR_UNSUPPORTED, "ssd_warp_sample_topk: k must be 0..16");
+  if (k > 0 && (!seed || !out_tok)) return fail(SSD_ERR_INVALID, "ssd_warp_sample_topk: NULL seed or output");
+  if (k == 0 && !params_out) return fail(SSD_ERR_INVALID, "ssd_warp_sample_topk: nothing to compute");
+  const int S = row_slices(V);
+  if (S == 0)
+    return fail(SSD_ERR_UNSUPPORTED, "ssd_warp_sample_topk: V = %lld exceeds %d", (long long)V,
+                kRowMaxSlices * kRowSliceMax);
+  const size_t smem = (size_t)((V + S - 1) / S) * 4;
+  static bool set = false;
+  if (!set) {
+    allow_max_dynamic_smem(warp_sample_kernel);
+    set = true;
+  }
+  return launch_kernel("warp_sample_kernel", warp_sample_kernel, dim3((unsigned)S, (unsigned)rows), dim3(kSampThreads),
+                       smem, static_cast<cudaStream_t>(stream), (unsigned)S, 1u, logits, ld, (int)V, temperature,
+                       top_p, (int)k, vocab_ids, seed, round, (int)row_base, 0, static_cast<WarpParams*>(params_out),
+                       out_tok, out_logprob);
+}
+
 int ssd_sample_token(const float* logits, int64_t V, float temperature, float top_p, const uint64_t* seed,
                      const int32_t* round, int64_t row_id, int64_t stream_id, float* scratch, int32_t* out,
                      void* stream) {
-  if (V <= 0 || !(temperature > 0.f) || !(top_p > 0.f) || top_p > 1.f || !seed || !scratch || !out)
+  if (V <= 0 || !(temperature > 0.f) || !(top_p > 0.f) || top_p > 1.f || !seed || !out)
     return fail(SSD_ERR_INVALID, "ssd_sample_token: bad arguments");
-  return launch_kernel("sample_token_kernel", sample_token_kernel, dim3(1), dim3(kSampThreads), 0,
-                       static_cast<cudaStream_t>(stream), 1, 1, logits, (int)V, temperature, top_p, seed, round,
-                       (int)row_id, (int)stream_id, scratch, out);
+  const int S = row_slices(V);
+  if (S == 0) {  // rows too long for a cluster's shared memory: one CTA over global scratch
+    if (!scratch) return fail(SSD_ERR_INVALID, "ssd_sample_token: scratch needed for V = %lld", (long long)V);
+    return launch_kernel("sample_token_kernel", sample_token_kernel, dim3(1), dim3(kSampThreads), 0,
+                         static_cast<cudaStream_t>(stream), 1, 1, logits, (int)V, temperature, top_p, seed, round,
+                         (int)row_id, (int)stream_id, scratch, out);
+  }
+  const size_t smem = (size_t)((V + S - 1) / S) * 4;
+  static bool set = false;
+  if (!set) {
+    allow_max_dynamic_smem(warp_sample_kernel);
+    set = true;
+  }
+  return launch_kernel("warp_sample_kernel", warp_sample_kernel, dim3((unsigned)S, 1u), dim3(kSampThreads), smem,
+                       static_cast<cudaStream_t>(stream), (unsigned)S, 1u, logits, (int64_t)V, (int)V, temperature,
+                       top_p, 1, static_cast<const int64_t*>(nullptr), seed, round, (int)row_id, (int)stream_id,
+                       static_cast<WarpParams*>(nullptr), out, static_cast<float*>(nullptr));
 }
 
 int ssd_tree_walk_sample(const int32_t* n_nodes, int64_t max_nodes, const int32_t* tokens, const int32_t* parents,
@@ -580,16 +1103,32 @@ int ssd_tree_walk_sample(const int32_t* n_nodes, int64_t max_nodes, const int32_
                          int64_t Vd, const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round,
                          float* p_scratch, float* q_scratch, int32_t* accepted, int32_t* n_accepted, int32_t* bonus,
                          int32_t* keep_slots, int32_t* n_keep, uint32_t* status, void* stream) {
-  if (max_nodes < 0 || max_nodes > 4096 || V <= 0 || Vd <= 0 || draft_rows <= 0 || !seed || !p_scratch ||
-      !q_scratch || !target_params || !draft_params)
+  if (max_nodes < 0 || max_nodes > 4096 || V <= 0 || Vd <= 0 || draft_rows <= 0 || !seed || !target_params ||
+      !draft_params)
     return fail(SSD_ERR_INVALID, "ssd_tree_walk_sample: bad arguments");
   if (!vocab_ids && Vd > V) return fail(SSD_ERR_INVALID, "ssd_tree_walk_sample: draft vocabulary exceeds V");
-  return launch_kernel("sample_verify_kernel", sample_verify_kernel, dim3(1), dim3(kSampThreads), 0,
-                       static_cast<cudaStream_t>(stream), 1, 1, n_nodes, (int)max_nodes, tokens, parents, ranks,
-                       draft_pos, root_pos, target_logits, ldt, static_cast<const WarpParams*>(target_params), (int)V,
-                       draft_logits, ldd, static_cast<const WarpParams*>(draft_params), (int)draft_rows, (int)Vd,
-                       vocab_ids, seed, round, p_scratch, q_scratch, accepted, n_accepted, bonus, keep_slots, n_keep,
-                       status);
+  const int S = row_slices(V);
+  if (S == 0) {  // vocabularies beyond the cluster's shared memory: one CTA over global scratch
+    if (!p_scratch || !q_scratch) return fail(SSD_ERR_INVALID, "ssd_tree_walk_sample: scratch needed for this V");
+    return launch_kernel("sample_verify_kernel", sample_verify_kernel, dim3(1), dim3(kSampThreads), 0,
+                         static_cast<cudaStream_t>(stream), 1, 1, n_nodes, (int)max_nodes, tokens, parents, ranks,
+                         draft_pos, root_pos, target_logits, ldt, static_cast<const WarpParams*>(target_params),
+                         (int)V, draft_logits, ldd, static_cast<const WarpParams*>(draft_params), (int)draft_rows,
+                         (int)Vd, vocab_ids, seed, round, p_scratch, q_scratch, accepted, n_accepted, bonus,
+                         keep_slots, n_keep, status);
+  }
+  const size_t smem = (size_t)((V + S - 1) / S) * 8;  // p and q slices
+  static bool set = false;
+  if (!set) {
+    allow_max_dynamic_smem(sample_verify_cluster_kernel);
+    set = true;
+  }
+  return launch_kernel("sample_verify_cluster_kernel", sample_verify_cluster_kernel, dim3((unsigned)S, 1u),
+                       dim3(kSampThreads), smem, static_cast<cudaStream_t>(stream), (unsigned)S, 1u, n_nodes,
+                       (int)max_nodes, tokens, parents, ranks, draft_pos, root_pos, target_logits, ldt,
+                       static_cast<const WarpParams*>(target_params), (int)V, draft_logits, ldd,
+                       static_cast<const WarpParams*>(draft_params), (int)draft_rows, (int)Vd, vocab_ids, seed, round,
+                       accepted, n_accepted, bonus, keep_slots, n_keep, status);
 }
 
 }  // extern "C"

@@ -121,15 +121,14 @@ class SampledRound(_SamplingState, GreedyRound):
         rows = self.dlogits[row0:row0 + T]
         prm = self.dparams[row0:row0 + T]
         ops.linear(xn, [self.head_w], self.ws, epilogue=L.EPI_STORE_F32, out=rows, T=T, in_norm=rn)
-        ops.warp_params(rows, self.temperature, self.top_p, prm)
-        ops.gumbel_topk(rows, prm, k, self.seed_buf, self.round_log[0:1], row0, out_tok, out_lp,
-                        vocab_ids=self.vocab_ids)
+        ops.warp_sample_topk(rows, self.temperature, self.top_p, prm, k, self.seed_buf, self.round_log[0:1], row0,
+                             out_tok, out_lp, vocab_ids=self.vocab_ids)
 
     def _walk(self, xn, rn=None) -> None:
         """sample_verify (verify.py:60-95) on the device."""
         p, st = self.plan, self.state
         ops.linear(xn, [self.w.lm_head], self.ws, epilogue=L.EPI_STORE_F32, out=self.tlogits, T=p.rows, in_norm=rn)
-        ops.warp_params(self.tlogits, self.temperature, self.top_p, self.tparams)
+        ops.warp_sample_topk(self.tlogits, self.temperature, self.top_p, self.tparams)
         ops.tree_walk_sample(self.tree, self.tlogits, self.tparams, self.dlogits, self.dparams, self.draft_rows,
                              self.seed_buf, self.round_log[0:1], self.p_scratch, self.q_scratch, st[SEQ:SEQ + 1],
                              self.accepted, st[N_ACC:N_ACC + 1], st[BONUS:BONUS + 1], self.keep_slots,

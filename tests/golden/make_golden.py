@@ -20,7 +20,12 @@ Outputs (tests/golden/):
   c2ref.json - config-2 model (seed 1, planted, bf16-rounded weights) run in
                fp32 by the reference: greedy AR tokens + top-2 gaps, and per
                step the top-8 logits (values, ids) and the logits at 64 fixed
-               probe ids: the reference for the bf16 tier.
+               probe ids: the reference for the bf16 tier. Section "bf16":
+               the reference's own bf16 run of the same model (its modules
+               in torch.bfloat16): its free-running greedy tokens and gaps,
+               and its logits at the same ids teacher-forced on the fp32
+               tokens, i.e. how far the reference's own bf16 arithmetic lands
+               from its fp32 decode.
 """
 
 from __future__ import annotations
@@ -231,6 +236,20 @@ def make_c2ref(syn, out_path: Path, n_new: int = 48):
     ar, gaps = ref_ar_with_gaps(target, ids, n_new, probe=probe, record=rec)
     res = dict(config="c2", checksum=syn.weights_checksum(base), prompt=ids[0].tolist(), ar=ar, gaps=gaps,
                probe_ids=probe, **rec, note="weights rounded to bf16, evaluated by the reference in fp32")
+    # the reference's own bf16 arithmetic on the same weights
+    base = base.to(torch.bfloat16)
+    target = TargetRunner(base)
+    ar16, gaps16 = ref_ar_with_gaps(target, ids, n_new)
+    cache = target.new_cache(ids.shape[1] + n_new + 1)
+    with torch.no_grad():
+        rows = [target(ids, past_key_values=cache, logits_to_keep=1).logits[0, -1].float()]
+        for t in ar[:-1]:
+            rows.append(target(torch.tensor([[t]]), past_key_values=cache).logits[0, -1].float())
+    res["bf16"] = dict(ar=ar16, gaps=gaps16,
+                       tf_top_values=[[float(r[j]) for j in rec["top_ids"][i]] for i, r in enumerate(rows)],
+                       tf_probe_logits=[[float(r[j]) for j in probe] for r in rows],
+                       tf_argmax=[int(r.argmax()) for r in rows],
+                       note="the reference's modules in torch.bfloat16 (CPU); tf_* teacher-forced on the fp32 tokens")
     out_path.write_text(json.dumps(res))
     print(f"wrote {out_path}")
 

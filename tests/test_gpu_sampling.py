@@ -395,3 +395,131 @@ def test_gumbel_topk_split_over_a_cluster_matches_one_pass():
     assert torch.equal(out[0][0], out[1][0])
     assert torch.equal(out[0][1], out[1][1])
     assert (out[0][0] >= 0).all()
+
+
+# ------------------------------------------------- clustered row kernels
+@pytest.mark.parametrize("V,top_p", [(8, 0.9), (32768, 1.0), (32768, 0.9), (128256, 0.9), (128256, 0.5)])
+def test_fused_warp_sample_matches_separate_kernels(V, top_p):
+    """ssd_warp_sample_topk (one cluster per row, up to 8 CTAs) gives the
+    warp parameters of ssd_warp_params (max and nucleus threshold exactly,
+    log Z to fp32 rounding) and the draws of ssd_gumbel_topk with them."""
+    rows, k, T = 6, 4, 0.7
+    logits = _logit_rows(rows, V, 2.0, V + 17)
+    seed = torch.tensor([321], dtype=torch.int64, device=DEV)
+    rnd = torch.tensor([5], dtype=torch.int32, device=DEV)
+    ref_p = _params(logits, T, top_p)
+    ref_t = torch.empty(rows, k, dtype=torch.int32, device=DEV)
+    ref_l = torch.empty(rows, k, dtype=torch.float32, device=DEV)
+    ops.gumbel_topk(logits, ref_p, k, seed, rnd, 7, ref_t, ref_l)
+    got_p = ops.warp_params_buffer(rows, DEV)
+    got_t = torch.empty_like(ref_t)
+    got_l = torch.empty_like(ref_l)
+    ops.warp_sample_topk(logits, T, top_p, got_p, k, seed, rnd, 7, got_t, got_l)
+    only_p = ops.warp_params_buffer(rows, DEV)
+    ops.warp_sample_topk(logits, T, top_p, only_p)  # k = 0: parameters only
+    torch.cuda.synchronize()
+    a, b = ref_p.cpu().numpy(), got_p.cpu().numpy()
+    np.testing.assert_array_equal(a[:, 0], b[:, 0])  # max
+    np.testing.assert_array_equal(a[:, 2], b[:, 2])  # nucleus threshold
+    np.testing.assert_allclose(a[:, 3], b[:, 3], rtol=1e-5, atol=1e-6)  # log Z
+    assert torch.equal(got_p, only_p)
+    assert torch.equal(ref_t, got_t)
+    torch.testing.assert_close(got_l, ref_l, rtol=1e-5, atol=1e-5)
+
+
+def test_clustered_tree_walk_first_token_is_target_distributed():
+    """The rejection walk on a cluster (V = 20000: 8 CTAs, vocabulary slices
+    of 2500): candidates and mass spread over different slices, so point
+    values come from other CTAs and the bonus is a cluster-wide Gumbel-max
+    (all other tokens carry ~1e-29 of the mass, which the draw must never
+    pick). The first committed token must be distributed as p_root and the
+    second, given an accepted first, as that child's target row."""
+    V_small, V = 6, 20000
+    spread = np.array([5, 2600, 7777, 10001, 15000, 19999])  # one id per slice region
+    rng = np.random.default_rng(3)
+    tl = rng.normal(size=(V_small + 1, V_small)) * 1.2
+    dl = rng.normal(size=(V_small + 1, V_small)) * 1.2
+    T, top_p = 0.9, 1.0
+    p_root = oracle_warp(tl[0], T, top_p)
+    q_root = oracle_warp(dl[0], T, top_p)
+    q_child = [oracle_warp(dl[1 + t], T, top_p) for t in range(V_small)]
+
+    def widen(row):  # small row -> V-wide logits with the mass on `spread`
+        out = np.full(V, -60.0)
+        out[spread] = row
+        return out
+
+    def widen_q(q):
+        out = np.zeros(V)
+        out[spread] = q
+        return torch.tensor(out, dtype=torch.float32)
+
+    gen = torch.Generator().manual_seed(0)
+    n = 1500
+    firsts = np.zeros(V_small)
+    pairs = np.zeros((V_small, V_small))
+    back = {int(v): i for i, v in enumerate(spread)}
+    for _ in range(n):
+        small = _rand_tree_from_q(q_root, q_child, [3, 2], rng)
+        tree = DraftTree(tokens=[int(spread[t]) for t in small.tokens], parents=small.parents, depths=small.depths,
+                         ranks=small.ranks, scores=small.scores, draft_pos=small.draft_pos)
+        tree.child_q[-1] = widen_q(q_root)
+        for par in range(len(small)):
+            if small.depths[par] == 1:
+                tree.child_q[par] = widen_q(q_child[small.tokens[par]])
+        rows = [widen(tl[0])] + [widen(tl[1 + small.tokens[i]]) if small.depths[i] == 1 else widen(tl[0])
+                                 for i in range(len(small))]
+        logits = torch.tensor(np.stack(rows), dtype=torch.float32)
+        acc, bonus = SP.sample_verify_device(tree, logits, T, top_p, gen)
+        assert bonus in back, f"bonus {bonus} drawn outside the support"
+        toks = [back[tree.tokens[i]] for i in acc] + [back[bonus]]
+        firsts[toks[0]] += 1
+        if len(toks) > 1 and small.depths[acc[0]] == 1:
+            pairs[toks[0], toks[1]] += 1
+    assert chi2_pvalue(firsts, p_root) > P_MIN
+    exact = np.array([p_root[a] * oracle_warp(tl[1 + a], T, top_p) for a in range(V_small)])
+    exact *= pairs.sum(1, keepdims=True) / np.maximum(exact.sum(1, keepdims=True), 1e-300)
+    assert chi2_pvalue(pairs, exact / pairs.sum()) > P_MIN
+
+
+# ------------------------------------------- draws against the Philox oracle
+@pytest.mark.parametrize("V", [100, 20000, 128256])
+def test_sample_token_draws_match_the_philox_oracle(V):
+    """ssd_sample_token is a Gumbel-max draw: the device's token equals the
+    oracle's argmax of log p + Gumbel(seed, round, row, i, stream) for every
+    seed (same Philox4x32-10 counters; keys compared in float64)."""
+    from oracle import philox
+
+    T, top_p = 0.8, 0.9
+    logits = _logit_rows(1, V, 2.0, V + 5)[0]
+    p = oracle_warp(logits.cpu().double().numpy(), T, top_p)
+    lp = np.where(p > 0, np.log(np.maximum(p, 1e-300)), -np.inf)
+    out = torch.empty(1, dtype=torch.int32, device=DEV)
+    mism = 0
+    for s in range(48):
+        seed = torch.tensor([1000 + s], dtype=torch.int64, device=DEV)
+        rnd = torch.tensor([s % 5], dtype=torch.int32, device=DEV)
+        ops.sample_token(logits, T, top_p, seed, rnd, 7, 3, None, out)
+        want = philox.gumbel_topk(lp, 1, 1000 + s, s % 5, 7, 3)[0]
+        mism += int(int(out.item()) != want)
+    assert mism == 0
+
+
+def test_fused_topk_draws_match_the_philox_oracle():
+    """ssd_warp_sample_topk's k draws without replacement per row equal the
+    oracle's Gumbel top-k with the same counters (row id = row_base + r)."""
+    from oracle import philox
+
+    rows, V, k, T, top_p = 4, 32768, 4, 0.7, 0.9
+    logits = _logit_rows(rows, V, 2.0, 77)
+    seed = torch.tensor([4242], dtype=torch.int64, device=DEV)
+    rnd = torch.tensor([3], dtype=torch.int32, device=DEV)
+    prm = ops.warp_params_buffer(rows, DEV)
+    tok = torch.empty(rows, k, dtype=torch.int32, device=DEV)
+    lpo = torch.empty(rows, k, dtype=torch.float32, device=DEV)
+    ops.warp_sample_topk(logits, T, top_p, prm, k, seed, rnd, 11, tok, lpo)
+    tok = tok.cpu().numpy()
+    for r in range(rows):
+        p = oracle_warp(logits[r].cpu().double().numpy(), T, top_p)
+        lp = np.where(p > 0, np.log(np.maximum(p, 1e-300)), -np.inf)
+        assert tok[r].tolist() == philox.gumbel_topk(lp, k, 4242, 3, 11 + r, 0)

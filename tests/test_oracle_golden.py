@@ -163,3 +163,16 @@ def test_c1_fixture_prompt_and_checksum_format():
     assert len(g["prompt"]) == 128 and len(g["ar"]) == 64
     assert g["prompt"] == S.make_prompt(0, 128, 128256)[0].tolist()
     assert g["sd"] == g["ar"], "the reference's own SD must equal its AR (greedy identity)"
+
+
+def test_philox_known_answers():
+    """The oracle's Philox4x32-10 against the published known-answer vectors
+    of the Random123 distribution (philox4x32, 10 rounds)."""
+    from oracle.philox import philox4x32_10
+
+    out = philox4x32_10((0, 0, 0, 0), (0, 0))
+    assert [int(x) for x in out] == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
+    out = philox4x32_10((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF))
+    assert [int(x) for x in out] == [0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD]
+    out = philox4x32_10((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0))
+    assert [int(x) for x in out] == [0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1]
