@@ -144,14 +144,17 @@ int ssd_qkv_rope(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w
                  int64_t workspace_bytes, const SsdRowNorm* in_norm, uint32_t* status, void* stream);
 
 /* Tree attention over the shared cache (split-KV, GQA). Row t attends cache
- * slots [0, prefix_len[t]) and, if spec_mask is given, slot spec_base[0] + j
+ * slots [prefix_start[t], prefix_len[t]) (prefix_start NULL: from slot 0;
+ * batched decoding gives each sequence its own slot range) and, if spec_mask
+ * is given, slot spec_base[0] + j
  * for every set bit j of spec_mask[t * mask_words + j / 64]. Scores use
  * scale = 1/sqrt(head_dim). q: [T, n_heads*head_dim]; out the same.
  * Replaces SDPA with the bool tree mask (subnetwork_draft.py:165-191,
  * 236-242; tree_drafter.py:192-196; ssd/engine/verify.py:37-41). */
 int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t n_heads, int64_t n_kv_heads,
                        int64_t head_dim, const void* k_cache, const void* v_cache, int64_t cache_head_stride,
-                       int64_t max_slots, const int32_t* prefix_len, const int32_t* spec_base,
+                       int64_t max_slots, const int32_t* prefix_len, const int32_t* prefix_start,
+                       const int32_t* spec_base,
                        const uint64_t* spec_mask, int64_t mask_words, int64_t kv_bound, void* out, int64_t ldo,
                        int dtype, void* workspace, int64_t workspace_bytes, uint32_t* status, void* stream);
 

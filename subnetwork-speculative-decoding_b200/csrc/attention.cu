@@ -1,6 +1,7 @@
 // Tree attention over the shared KV cache (split-KV "FlashDecoding" layout).
 //
-// Row t of the forward attends cache slots [0, prefix_len[t]) and every
+// Row t of the forward attends cache slots [prefix_start[t] (0 without the
+// array), prefix_len[t]) and every
 // speculative slot spec_base + j whose bit j is set in its ancestor mask. A
 // CTA owns one KV head, a group of token rows (times the GQA group of query
 // heads that share the KV head) and one contiguous slice of the key range,
@@ -31,6 +32,7 @@ struct AttnArgs {
   int64_t head_stride;
   int max_slots;
   const int32_t* prefix_len;
+  const int32_t* prefix_start;  // optional first visible slot per row (NULL = 0)
   const int32_t* spec_base;
   const uint64_t* mask;
   int mask_words;
@@ -56,6 +58,7 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const AttnArgs a) {
   float* Ps = Qs + kAttnQ * hd;              // [8][4][64]
   int* s_plen = reinterpret_cast<int*>(Ps + kAttnWarps * kAttnQPerWarp * kAttnBlock);  // [rows_per_tile]
   int* s_misc = s_plen + kAttnQ;             // [0] need_end, [1] is_last
+  int* s_pstart = s_misc + 2;                // [rows_per_tile]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x / a.row_tiles, rt = blockIdx.x % a.row_tiles;
@@ -73,6 +76,7 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const AttnArgs a) {
     const int t = row0 + i;
     const int pl = a.prefix_len[t];
     s_plen[i] = pl;
+    s_pstart[i] = a.prefix_start ? a.prefix_start[t] : 0;
     int end = pl;
     if (a.mask) {
       for (int w = a.mask_words - 1; w >= 0; --w) {
@@ -137,7 +141,7 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const AttnArgs a) {
       for (int u = 0; u < 2; ++u) {
         const int j = lane + 32 * u;
         const int slot = kb + j;
-        bool ok = j < nkeys && slot < s_plen[rl];
+        bool ok = j < nkeys && slot < s_plen[rl] && slot >= s_pstart[rl];
         if (!ok && a.mask && j < nkeys && slot >= sb) {
           const int bit = slot - sb;
           if (bit < a.mask_words * 64) ok = (a.mask[(int64_t)t * a.mask_words + (bit >> 6)] >> (bit & 63)) & 1ull;
@@ -244,11 +248,13 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const AttnArgs a) {
 // the row's ancestor mask (bit i = slot sb + i, mw words), clipped to the
 // slice end k_hi. Built with a few integer ops instead of a per-key branch.
 __device__ __forceinline__ uint64_t key_block_bits(int kb, int k_hi, int plen, const uint64_t* row_mask, int mw,
-                                                   int sb) {
+                                                   int sb, int pstart) {
   const int n_hi = min(max(k_hi - kb, 0), 64);
   const uint64_t hi = n_hi >= 64 ? ~0ull : ((1ull << n_hi) - 1ull);
   const int n_pre = min(max(plen - kb, 0), 64);
-  const uint64_t pre = n_pre >= 64 ? ~0ull : ((1ull << n_pre) - 1ull);
+  const int n_lo = min(max(pstart - kb, 0), 64);  // keys before the row's first visible slot
+  const uint64_t pre = (n_pre >= 64 ? ~0ull : ((1ull << n_pre) - 1ull)) &
+                       ~(n_lo >= 64 ? ~0ull : ((1ull << n_lo) - 1ull));
   uint64_t spec = 0ull;
   const int off = kb - sb;  // mask bit of slot kb
   if (mw > 0 && off < mw * 64 && off > -64) {
@@ -326,7 +332,7 @@ __host__ __device__ inline int ws_recv_bytes(int hd, int kw, int rows) {
 __host__ __device__ inline int ws_region_bytes(int hd, int kw, int rows) {
   return ws_ring_bytes(hd) + ws_recv_bytes(hd, kw, rows);
 }
-constexpr int kWsMeta = (kMmaMaxTok + 1) * 4 + kMmaMaxTok * 4 * 8 + 16 + 2 * kWsStages * 8 + 16;
+constexpr int kWsMeta = (kMmaMaxTok + 1) * 4 + kMmaMaxTok * 4 * 8 + 16 + 2 * kWsStages * 8 + 16 + (kMmaMaxTok + 1) * 4;
 
 template <int HD>
 __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(const AttnArgs a) {
@@ -341,6 +347,7 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
   int* s_misc = reinterpret_cast<int*>(s_mask + kMmaMaxTok * 4);           // need_end, min_plen, last, pad
   uint64_t* full = reinterpret_cast<uint64_t*>(s_misc + 4);
   uint64_t* empty = full + kWsStages;
+  int* s_pstart = reinterpret_cast<int*>(empty + kWsStages) + 4;  // [tok]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwc = a.rt * a.kw;  // consumer warps; warp nwc produces
@@ -373,6 +380,7 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
     const int t = t_first + i;
     const int pl = a.prefix_len[t];
     s_plen[i] = pl;
+    s_pstart[i] = a.prefix_start ? a.prefix_start[t] : 0;
     int end = pl;
     for (int w = 0; w < mw; ++w) {
       const uint64_t m = a.mask[(int64_t)t * mw + w];
@@ -446,6 +454,7 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
     }
     const int tok0 = ok0 ? qr0 / a.G - t_first : 0, tok1 = ok1 ? qr1 / a.G - t_first : 0;
     const int pl0 = ok0 ? s_plen[tok0] : 0, pl1 = ok1 ? s_plen[tok1] : 0;
+    const int ps0 = ok0 ? s_pstart[tok0] : 0, ps1 = ok1 ? s_pstart[tok1] : 0;
     const float sc = a.scale * 1.4426950408889634f;  // softmax in base 2
     const int mi = lane >> 3, rj = lane & 7;
     for (int b = kw; b < nblocks; b += a.kw) {
@@ -473,8 +482,8 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
       }
       // scale + mask: rows rl0 (sacc[.][0..1]) and rl1 (sacc[.][2..3]); this
       // lane holds keys nt * 8 + 2 * tq + {0, 1} of each n-tile
-      const uint64_t vb0 = ok0 ? key_block_bits(kb, k_hi, pl0, s_mask + tok0 * 4, mw, sb) >> (2 * tq) : 0ull;
-      const uint64_t vb1 = ok1 ? key_block_bits(kb, k_hi, pl1, s_mask + tok1 * 4, mw, sb) >> (2 * tq) : 0ull;
+      const uint64_t vb0 = ok0 ? key_block_bits(kb, k_hi, pl0, s_mask + tok0 * 4, mw, sb, ps0) >> (2 * tq) : 0ull;
+      const uint64_t vb1 = ok1 ? key_block_bits(kb, k_hi, pl1, s_mask + tok1 * 4, mw, sb, ps1) >> (2 * tq) : 0ull;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
@@ -751,7 +760,8 @@ struct TcAttnLayout {
   static constexpr int OFF_BM = OFF_P + 2 * P_BYTES;  // [parity][half][slot][128] block maxima
   static constexpr int BM_BYTES = 2 * 2 * 2 * 128 * 4;
   static constexpr int OFF_META = OFF_BM + BM_BYTES;
-  static constexpr int META = (kTcAttnMaxTok + 1) * 4 + kTcAttnMaxTok * 4 * 8 + 16 + (2 * kTcAttnStages + 10) * 8 + 16;
+  static constexpr int META = (kTcAttnMaxTok + 1) * 4 + kTcAttnMaxTok * 4 * 8 + 16 + (2 * kTcAttnStages + 10) * 8 + 16 +
+                              (kTcAttnMaxTok + 1) * 4;
   static constexpr int SMEM = 1024 + OFF_META + META;
 };
 
@@ -779,6 +789,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   uint64_t* o_full = p_free + 2;
   uint64_t* q_ready = o_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
+  int* s_pstart = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(tmem_slot) + 16);  // [tok]
   volatile int* abort_flag = s_misc + 3;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -832,6 +843,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     const int t = t_first + i;
     const int pl = a.prefix_len[t];
     s_plen[i] = pl;
+    s_pstart[i] = a.prefix_start ? a.prefix_start[t] : 0;
     int end = pl;
     for (int w = 0; w < mw; ++w) {
       const uint64_t m = a.mask[(int64_t)t * mw + w];
@@ -959,6 +971,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     // of its parity (no early exit), so the pair barriers always match.
     const int tok = row_ok ? (q0 + r) / a.G - t_first : 0;
     const int plen = row_ok ? s_plen[tok] : 0;
+    const int pstart = row_ok ? s_pstart[tok] : 0;
     const float sc = a.scale * 1.4426950408889634f;  // base 2
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t tm_ow = tm_o + par * 128;
@@ -984,7 +997,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[par]);
       const int kb = k_lo + b * KB;
-      const uint64_t vbits = (row_ok && !bad) ? key_block_bits(kb, k_hi, plen, s_mask + tok * 4, mw, sb) : 0ull;
+      const uint64_t vbits = (row_ok && !bad) ? key_block_bits(kb, k_hi, plen, s_mask + tok * 4, mw, sb, pstart) : 0ull;
       const uint32_t vh = static_cast<uint32_t>(vbits >> (half * 32));
       float bmx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
@@ -1349,6 +1362,7 @@ using namespace ssd;
 extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t n_heads, int64_t n_kv_heads,
                                   int64_t head_dim, const void* k_cache, const void* v_cache,
                                   int64_t cache_head_stride, int64_t max_slots, const int32_t* prefix_len,
+                                  const int32_t* prefix_start,
                                   const int32_t* spec_base, const uint64_t* spec_mask, int64_t mask_words,
                                   int64_t kv_bound, void* out, int64_t ldo, int dtype, void* workspace,
                                   int64_t workspace_bytes, uint32_t* status, void* stream) {
@@ -1371,6 +1385,7 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
   a.head_stride = cache_head_stride;
   a.max_slots = (int)max_slots;
   a.prefix_len = prefix_len;
+  a.prefix_start = prefix_start;
   a.spec_base = spec_mask ? spec_base : nullptr;
   a.mask = spec_mask;
   a.mask_words = (int)mask_words;
@@ -1522,7 +1537,7 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
   a.counters = static_cast<uint32_t*>(workspace);
   a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
   const size_t smem = (size_t)(2 * kAttnBlock * (head_dim + 1) + kAttnQ * head_dim +
-                               kAttnWarps * kAttnQPerWarp * kAttnBlock) * 4 + (kAttnQ + 2) * 4;
+                               kAttnWarps * kAttnQPerWarp * kAttnBlock) * 4 + (2 * kAttnQ + 2) * 4;
   dim3 grid((unsigned)blocks, (unsigned)a.n_splits);
   if (dtype == SSD_F32) {
     static bool set = false;

@@ -56,8 +56,8 @@ SIGNATURES: dict[str, tuple] = {
     "ssd_linear_noalloc": (I32, [P, I64, I64, I64, I32, P, P, P, I32, I32, I32, P, I64, P, I64, I32, P, P]),
     "ssd_qkv_rope": (I32, [P, I64, I64, I64, P, P, P, I64, I64, I64, P, P, I64, P, P, P, P, I64, I64, P, I64, I32,
                            P, I64, P, P, P]),
-    "ssd_tree_attention": (I32, [P, I64, I64, I64, I64, I64, P, P, I64, I64, P, P, P, I64, I64, P, I64, I32, P, I64,
-                                 P, P]),
+    "ssd_tree_attention": (I32, [P, I64, I64, I64, I64, I64, P, P, I64, I64, P, P, P, P, I64, I64, P, I64, I32, P,
+                                 I64, P, P]),
     "ssd_head_argmax": (I32, [P, I64, I64, I64, P, I64, P, P, P, I32, P, I64, P, P, P]),
     "ssd_head_topk": (I32, [P, I64, I64, I64, P, I64, P, I64, P, P, I32, P, I64, P, P, P]),
     "ssd_level_prune": (I32, [P, P, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, I64, P, I32, I64, P, P, P, P, P,

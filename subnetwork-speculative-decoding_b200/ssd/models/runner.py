@@ -111,7 +111,9 @@ class ModelWeights:
 class ForwardInputs:
     """Device-side inputs of one forward over up to `cap` rows: token ids,
     RoPE positions, cache slots written, contiguous prefix length per row and
-    the ancestor bitmask over speculative slots starting at spec_base."""
+    the ancestor bitmask over speculative slots starting at spec_base; for
+    batched forwards (several sequences, each in its own slot range) also the
+    first visible slot per row (prefix_start, else None: slot 0)."""
 
     def __init__(self, cap: int, device, mask_words: int = 2):
         self.cap = cap
@@ -124,6 +126,7 @@ class ForwardInputs:
         self.spec_base = torch.zeros(1, **i32)
         self.mask = torch.zeros(cap, mask_words, dtype=torch.int64, device=device)
         self.use_mask = False
+        self.prefix_start = None
 
     def fill(self, ids, positions, past: int, tree_mask: Optional[torch.Tensor]) -> None:
         """Host-side fill for the API path (reference mask semantics of
@@ -264,7 +267,7 @@ def run_layer(w: ModelWeights, li: int, fwd: ForwardInputs, T: int, cache, scrat
                  scratch.q[:T], ws, T=T)
     ops.tree_attention(scratch.q[:T], kc, vc, w.H, w.Hkv, w.hd, fwd.prefix_len, scratch.attn[:T], ws,
                        spec_base=fwd.spec_base if fwd.use_mask else None, spec_mask=fwd.mask if fwd.use_mask else None,
-                       kv_bound=kv_bound, T=T)
+                       kv_bound=kv_bound, T=T, prefix_start=fwd.prefix_start)
     ops.linear(scratch.attn[:T], [lw.o], ws, epilogue=L.EPI_RESIDUAL, resid=resid)
     ops.rmsnorm(resid, lw.ln2, lw.eps2, xn)
     hid = scratch.hid(w.dtype, w.F, 0)[:T, : w.F]
@@ -335,7 +338,8 @@ def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm
                      scratch.q[:T], ws, T=T, in_norm=in_for(k))
         ops.tree_attention(scratch.q[:T], kc, vc, w.H, w.Hkv, w.hd, fwd.prefix_len, scratch.attn[:T], ws,
                            spec_base=fwd.spec_base if fwd.use_mask else None,
-                           spec_mask=fwd.mask if fwd.use_mask else None, kv_bound=kv_bound, T=T)
+                           spec_mask=fwd.mask if fwd.use_mask else None, kv_bound=kv_bound, T=T,
+                           prefix_start=fwd.prefix_start)
         _residual_linear(w, scratch.attn[:T], lw.o, ws, resid, out_for(k + 1), T)
         hid = scratch.hid(w.dtype, w.F, 0)[:T, : w.F]
         ops.linear(xg, [lw.gate, lw.up], ws, epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid, in_norm=in_for(k + 1))

@@ -146,12 +146,15 @@ def qkv_rope(x, wq, wk, wv, n_heads, n_kv, head_dim, cos, sin, positions, slots,
 
 
 def tree_attention(q, k_cache, v_cache, n_heads, n_kv, head_dim, prefix_len, out, ws: Workspace, *,
-                   spec_base=None, spec_mask=None, kv_bound: int = 0, T: Optional[int] = None) -> None:
+                   spec_base=None, spec_mask=None, kv_bound: int = 0, T: Optional[int] = None,
+                   prefix_start=None) -> None:
+    """Row t attends slots [prefix_start[t] (0 if None), prefix_len[t]) plus its
+    speculative mask bits (ssd_tree_attention)."""
     T = q.shape[0] if T is None else T
     mw = spec_mask.shape[-1] if spec_mask is not None else 0
     L.call("ssd_tree_attention", _p(q), q.stride(0), T, n_heads, n_kv, head_dim, _p(k_cache), _p(v_cache),
-           k_cache.stride(0), k_cache.shape[1], _p(prefix_len), _p(spec_base), _p(spec_mask), mw, kv_bound, _p(out),
-           out.stride(0), dtype_code(q.dtype), ws.ptr, ws.nbytes, _p(ws.status), _stream())
+           k_cache.stride(0), k_cache.shape[1], _p(prefix_len), _p(prefix_start), _p(spec_base), _p(spec_mask), mw,
+           kv_bound, _p(out), out.stride(0), dtype_code(q.dtype), ws.ptr, ws.nbytes, _p(ws.status), _stream())
 
 
 def head_argmax(x, w, out_idx, ws: Workspace, out_max=None, out_gap=None, T: Optional[int] = None,

@@ -36,8 +36,8 @@ def test_library_exports_every_declared_symbol():
 def test_library_rejects_bad_arguments_without_gpu():
     """Argument validation happens on the host, before any launch."""
     with pytest.raises(ValueError):
-        L.call("ssd_tree_attention", None, 0, 1, 3, 2, 16, None, None, 0, 0, None, None, None, 0, 0, None, 0, 0,
-               None, 0, None, None)
+        L.call("ssd_tree_attention", None, 0, 1, 3, 2, 16, None, None, 0, 0, None, None, None, None, 0, 0, None, 0,
+               0, None, 0, None, None)
     with pytest.raises(L.SSDError):
         L.call("ssd_kv_compact", None, 1, 1, 1, 1, 1, 64, None, None, None, 99, 1, None, None)
 

@@ -207,15 +207,16 @@ def test_gemm_batch_invariance(ops, ws, dtype):
         assert torch.equal(one[0], full[t]), f"row {t} differs between T=1 and T={T}"
 
 
-def attention_ref(q, kc, vc, prefix, spec_base, mask, H, Hkv, hd):
-    """Explicit per-row masked softmax attention in fp64."""
+def attention_ref(q, kc, vc, prefix, spec_base, mask, H, Hkv, hd, start=None):
+    """Explicit per-row masked softmax attention in fp64 (row t sees slots
+    [start[t], prefix[t]) plus its mask bits)."""
     T = q.shape[0]
     G = H // Hkv
     out = torch.zeros(T, H * hd, dtype=torch.float64, device=DEV)
     S = kc.shape[1]
     for t in range(T):
         valid = torch.zeros(S, dtype=torch.bool, device=DEV)
-        valid[: int(prefix[t])] = True
+        valid[int(start[t]) if start is not None else 0: int(prefix[t])] = True
         if mask is not None:
             for b in range(mask.shape[1] * 64):
                 if (int(mask[t, b // 64].item()) >> (b % 64)) & 1:
@@ -265,6 +266,33 @@ def test_tree_attention(ops, ws, dtype, H, Hkv, hd, ctx, T, tree):
     ws.check_status()
     ref = attention_ref(q, kc, vc, prefix.cpu(), ctx, mask.cpu() if mask is not None else None,
                         H, Hkv, hd)
+    tol = dict(rtol=2e-2, atol_frac=1e-2) if dtype == torch.bfloat16 else dict(rtol=1e-4, atol_frac=1e-5)
+    _close(out, ref, **tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("H,Hkv,hd,B,region,T_per", [(32, 8, 128, 4, 700, 1), (32, 8, 128, 8, 2304, 1),
+                                                     (32, 8, 64, 3, 300, 2), (32, 8, 128, 6, 1000, 4)])
+def test_tree_attention_per_row_slot_ranges(ops, ws, dtype, H, Hkv, hd, B, region, T_per):
+    """Batched decoding: B sequences share one cache, sequence b in slots
+    [b * region, (b + 1) * region); each row sees only its own sequence's
+    slots [prefix_start, prefix_len). Covers the mma.sync kernel (<= 16 rows per
+    KV head), the tcgen05 kernel (more) and the fp32 kernel."""
+    T = B * T_per
+    S = B * region
+    kc = _rand(Hkv, S, hd, dtype=dtype, seed=31)
+    vc = _rand(Hkv, S, hd, dtype=dtype, seed=32)
+    q = _rand(T, H * hd, dtype=dtype, seed=33)
+    g = torch.Generator().manual_seed(5)
+    lens = torch.randint(region // 4, region - T_per, (B,), generator=g)
+    start = torch.tensor([b * region for b in range(B) for _ in range(T_per)], dtype=torch.int32)
+    prefix = torch.tensor([b * region + int(lens[b]) + j + 1 for b in range(B) for j in range(T_per)],
+                          dtype=torch.int32)
+    out = torch.empty(T, H * hd, dtype=dtype, device=DEV)
+    ops.tree_attention(q, kc, vc, H, Hkv, hd, prefix.to(DEV), out, ws, kv_bound=S, prefix_start=start.to(DEV))
+    torch.cuda.synchronize()
+    ws.check_status()
+    ref = attention_ref(q, kc, vc, prefix, None, None, H, Hkv, hd, start=start)
     tol = dict(rtol=2e-2, atol_frac=1e-2) if dtype == torch.bfloat16 else dict(rtol=1e-4, atol_frac=1e-5)
     _close(out, ref, **tol)
 
