@@ -287,11 +287,16 @@ int ssd_gumbel_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, co
  * params_out (may be NULL when k > 0) and, for k >= 1, the same draws as
  * ssd_gumbel_topk with those parameters (RNG counters (round, row_base + r,
  * i, 0)); out_logprob may be NULL. k = 0 computes the parameters only.
- * V <= 131072. Replaces the sampling branch of TreeDrafter._propose
- * (tree_drafter.py:134-145) and warp_probs (:34-45) for the verify rows. */
+ * keep_top > 0 first restricts each row to its keep_top largest logits (ties
+ * at the boundary kept), then applies temperature and top_p within them, as
+ * sample_next does for batched generation (ssd/data/generate_selfdistill.py:
+ * 51-61, keep_top = 64); 0 = the full row. V <= 131072. Replaces the sampling
+ * branch of TreeDrafter._propose (tree_drafter.py:134-145) and warp_probs
+ * (:34-45) for the verify rows. */
 int ssd_warp_sample_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, float temperature, float top_p,
-                         int64_t k, const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round,
-                         int64_t row_base, void* params_out, int32_t* out_tok, float* out_logprob, void* stream);
+                         int64_t keep_top, int64_t k, const int64_t* vocab_ids, const uint64_t* seed,
+                         const int32_t* round, int64_t row_base, void* params_out, int32_t* out_tok,
+                         float* out_logprob, void* stream);
 
 /* One token drawn from warp(logits[0..V)) into out[0]: a Gumbel-max draw on
  * one cluster (RNG counters (round, row_id, i, stream_id)); rows longer than

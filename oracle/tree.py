@@ -42,6 +42,17 @@ def warp_probs(logits: np.ndarray, temperature: float, top_p: float) -> np.ndarr
     return p
 
 
+def top_k_warp(logits: np.ndarray, k: int, temperature: float, top_p: float) -> np.ndarray:
+    """The distribution sample_next draws from at temperature > 0
+    (ssd/data/generate_selfdistill.py:51-61): the k largest logits of the row,
+    warp_probs over them, zero elsewhere. 1-D rows."""
+    x = np.asarray(logits, dtype=np.float64)
+    idx = np.argsort(-x, kind="stable")[:k]
+    out = np.zeros_like(x)
+    out[idx] = warp_probs(x[idx], temperature, top_p)
+    return out
+
+
 @dataclass
 class DraftTree:
     """DraftTree (tree_drafter.py:48-95)."""

@@ -591,29 +591,19 @@ __device__ void row_allbest(RowExchange& x, float& key, int& idx) {
   idx = bi;
 }
 
-// Warp parameters of the row whose slice is staged in xs[0, n): max,
-// kept-mass normaliser and, for top_p < 1, the nucleus threshold by the same
-// 4-level radix select as row_warp with the bins summed over the cluster
-// (integer masses, so the sums do not depend on the split).
-__device__ WarpParams cluster_row_warp(const float* xs, int n, float temperature, float top_p, float* red,
-                                       RowExchange& x, unsigned long long* sel) {
-  WarpParams P;
-  P.inv_t = 1.0f / temperature;
-  float mx = -INFINITY;
-  for (int i = threadIdx.x; i < n; i += kSampThreads) mx = fmaxf(mx, xs[i]);
-  P.m = row_allreduce(x, block_max(mx, red), true);
-  float z = 0.f;
-  for (int i = threadIdx.x; i < n; i += kSampThreads) z += expf((xs[i] - P.m) * P.inv_t);
-  const float Z = row_allreduce(x, block_sum(z, red), false);
-  if (!(top_p < 1.0f)) {
-    P.lambda = -INFINITY;
-    P.log_z = logf(Z);
-    return P;
-  }
-  const double scale = 281474976710656.0 / (double)Z;  // 2^48 / Z
-  const unsigned long long target = static_cast<unsigned long long>((double)top_p * 281474976710656.0);
+// Cluster-wide radix select over the order keys of the staged slice: four
+// 8-bit levels; at each level every CTA histograms the keys that share the
+// prefix found so far (weight(l) per key: 1 to select by count, a 2^48
+// fixed-point mass to select by probability mass), the bins are summed over
+// the cluster (integers, so the sums do not depend on the split) and the
+// selected bin is the lowest whose weight strictly above it stays <= target
+// (by mass) or, counting, the bin holding the target-th largest key. Only
+// keys >= floor_key take part. Returns the selected key.
+template <typename Weight>
+__device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_key, unsigned long long target,
+                                         bool by_count, Weight weight, RowExchange& x, unsigned long long* sel) {
   uint32_t prefix = 0;
-  unsigned long long mass_gt = 0;
+  unsigned long long above = 0;
   for (int level = 0; level < 4; ++level) {
     const int shift = 24 - 8 * level;
     unsigned long long* hist = x.hslot + (x.n & 1) * 256;
@@ -623,10 +613,8 @@ __device__ WarpParams cluster_row_warp(const float* xs, int n, float temperature
       const int i = base + threadIdx.x;
       const float l = i < n ? xs[i] : -INFINITY;
       const uint32_t k = order_key(l);
-      const bool in = i < n && (level == 0 || (k >> (shift + 8)) == prefix);
-      const unsigned long long fp =
-          in ? static_cast<unsigned long long>((double)expf((l - P.m) * P.inv_t) * scale) : 0ull;
-      hist_add_warp(hist, (k >> shift) & 255u, fp, in);
+      const bool in = i < n && k >= floor_key && (level == 0 || (k >> (shift + 8)) == prefix);
+      hist_add_warp(hist, (k >> shift) & 255u, in ? weight(l) : 0ull, in);
     }
     cluster_sync_all();  // every CTA's bins are complete
     for (int b = threadIdx.x; b < 256; b += kSampThreads) {
@@ -637,15 +625,22 @@ __device__ WarpParams cluster_row_warp(const float* xs, int n, float temperature
     ++x.n;
     __syncthreads();
     if (threadIdx.x == 0) {
-      // lowest non-empty bin whose mass strictly above it is <= top_p
-      unsigned long long S = mass_gt, sel_S = mass_gt;
+      unsigned long long S = above, sel_S = above;
       int sb = -1;
       for (int b = 255; b >= 0; --b) {
-        if (x.ghist[b] == 0ull) continue;
-        if (S > target) break;
-        sb = b;
-        sel_S = S;
-        S += x.ghist[b];
+        const unsigned long long hb = x.ghist[b];
+        if (hb == 0ull) continue;
+        if (by_count) {
+          sb = b;
+          sel_S = S;
+          if (S + hb >= target) break;
+          S += hb;
+        } else {
+          if (S > target) break;
+          sb = b;
+          sel_S = S;
+          S += hb;
+        }
       }
       if (sb < 0) sb = 255;  // unreachable for a finite row
       sel[0] = (static_cast<unsigned long long>(prefix) << 8) | static_cast<unsigned>(sb);
@@ -653,10 +648,47 @@ __device__ WarpParams cluster_row_warp(const float* xs, int n, float temperature
     }
     __syncthreads();
     prefix = static_cast<uint32_t>(sel[0]);
-    mass_gt = sel[1];
+    above = sel[1];
     __syncthreads();
   }
-  P.lambda = key_float(prefix);
+  return prefix;
+}
+
+// Warp parameters of the row whose slice is staged in xs[0, n): max,
+// kept-mass normaliser and the smallest kept logit. keep_top > 0 first keeps
+// only the keep_top largest logits (ties at the boundary all kept); top_p < 1
+// then keeps the nucleus of what remains, by the same radix select as
+// row_warp with the bins summed over the cluster.
+__device__ WarpParams cluster_row_warp(const float* xs, int n, int V, float temperature, float top_p, int keep_top,
+                                       float* red, RowExchange& x, unsigned long long* sel) {
+  WarpParams P;
+  P.inv_t = 1.0f / temperature;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += kSampThreads) mx = fmaxf(mx, xs[i]);
+  P.m = row_allreduce(x, block_max(mx, red), true);
+  uint32_t floor_key = 0;
+  float lam_k = -INFINITY;
+  if (keep_top > 0 && keep_top < V) {
+    floor_key = cluster_radix_select(xs, n, 0u, static_cast<unsigned long long>(keep_top), true,
+                                     [](float) { return 1ull; }, x, sel);
+    lam_k = key_float(floor_key);
+  }
+  float z = 0.f;
+  for (int i = threadIdx.x; i < n; i += kSampThreads)
+    if (xs[i] >= lam_k) z += expf((xs[i] - P.m) * P.inv_t);
+  const float Z = row_allreduce(x, block_sum(z, red), false);
+  if (!(top_p < 1.0f)) {
+    P.lambda = lam_k;
+    P.log_z = logf(Z);
+    return P;
+  }
+  const double scale = 281474976710656.0 / (double)Z;  // 2^48 / Z
+  const unsigned long long target = static_cast<unsigned long long>((double)top_p * 281474976710656.0);
+  const float m = P.m, inv_t = P.inv_t;
+  const uint32_t key = cluster_radix_select(
+      xs, n, floor_key, target, false,
+      [=](float l) { return static_cast<unsigned long long>((double)expf((l - m) * inv_t) * scale); }, x, sel);
+  P.lambda = key_float(key);
   float zk = 0.f;
   for (int i = threadIdx.x; i < n; i += kSampThreads) {
     const float l = xs[i];
@@ -673,7 +705,8 @@ __device__ WarpParams cluster_row_warp(const float* xs, int n, float temperature
 // parameters: keys lp + Gumbel with RNG counter (round, row_base + r, i,
 // stream), ties to the lower index, tokens through vocab_ids.
 __global__ void __launch_bounds__(kSampThreads, 1) warp_sample_kernel(
-    const float* logits, int64_t ld, int V, float temperature, float top_p, int k, const int64_t* vocab_ids,
+    const float* logits, int64_t ld, int V, float temperature, float top_p, int keep_top, int k,
+    const int64_t* vocab_ids,
     const uint64_t* seed, const int32_t* round, int row_base, int stream, WarpParams* params_out, int32_t* out_tok,
     float* out_lp) {
   extern __shared__ float xs[];
@@ -697,7 +730,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) warp_sample_kernel(
   for (int i = threadIdx.x; i < n; i += kSampThreads) xs[i] = row[i0 + i];
   __syncthreads();
   RowExchange x{fslot, hslot, gath, ghist, S, 0};
-  const WarpParams P = cluster_row_warp(xs, n, temperature, top_p, red, x, sel);
+  const WarpParams P = cluster_row_warp(xs, n, V, temperature, top_p, keep_top, red, x, sel);
   if (s == 0 && threadIdx.x == 0 && params_out) params_out[r] = P;
   if (k <= 0) {
     cluster_sync_all();  // peers may still read this CTA's exchange slot
@@ -1048,8 +1081,10 @@ int ssd_gumbel_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, co
 }
 
 int ssd_warp_sample_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, float temperature, float top_p,
-                         int64_t k, const int64_t* vocab_ids, const uint64_t* seed, const int32_t* round,
-                         int64_t row_base, void* params_out, int32_t* out_tok, float* out_logprob, void* stream) {
+                         int64_t keep_top, int64_t k, const int64_t* vocab_ids, const uint64_t* seed,
+                         const int32_t* round, int64_t row_base, void* params_out, int32_t* out_tok,
+                         float* out_logprob, void* stream) {
+  if (keep_top < 0) return fail(SSD_ERR_INVALID, "ssd_warp_sample_topk: keep_top must be >= 0");
   if (rows <= 0 || rows > 65535 || V <= 0 || !logits || ld < V || !(temperature > 0.f) || !(top_p > 0.f) ||
       top_p > 1.f)
     return fail(SSD_ERR_INVALID, "ssd_warp_sample_topk: need rows, V > 0, temperature > 0, 0 < top_p <= 1");
@@ -1068,8 +1103,8 @@ int ssd_warp_sample_topk(const float* logits, int64_t ld, int64_t rows, int64_t 
   }
   return launch_kernel("warp_sample_kernel", warp_sample_kernel, dim3((unsigned)S, (unsigned)rows), dim3(kSampThreads),
                        smem, static_cast<cudaStream_t>(stream), (unsigned)S, 1u, logits, ld, (int)V, temperature,
-                       top_p, (int)k, vocab_ids, seed, round, (int)row_base, 0, static_cast<WarpParams*>(params_out),
-                       out_tok, out_logprob);
+                       top_p, (int)(keep_top < V ? keep_top : 0), (int)k, vocab_ids, seed, round, (int)row_base, 0,
+                       static_cast<WarpParams*>(params_out), out_tok, out_logprob);
 }
 
 int ssd_sample_token(const float* logits, int64_t V, float temperature, float top_p, const uint64_t* seed,
@@ -1092,7 +1127,7 @@ int ssd_sample_token(const float* logits, int64_t V, float temperature, float to
   }
   return launch_kernel("warp_sample_kernel", warp_sample_kernel, dim3((unsigned)S, 1u), dim3(kSampThreads), smem,
                        static_cast<cudaStream_t>(stream), (unsigned)S, 1u, logits, (int64_t)V, (int)V, temperature,
-                       top_p, 1, static_cast<const int64_t*>(nullptr), seed, round, (int)row_id, (int)stream_id,
+                       top_p, 0, 1, static_cast<const int64_t*>(nullptr), seed, round, (int)row_id, (int)stream_id,
                        static_cast<WarpParams*>(nullptr), out, static_cast<float*>(nullptr));
 }
 

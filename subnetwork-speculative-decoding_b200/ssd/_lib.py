@@ -71,7 +71,7 @@ SIGNATURES: dict[str, tuple] = {
     "ssd_warp_params": (I32, [P, I64, I64, I64, F32, F32, P, P]),
     "ssd_warp_probs": (I32, [P, I64, I64, I64, P, P, I64, P]),
     "ssd_gumbel_topk": (I32, [P, I64, I64, I64, P, I64, P, P, P, I64, P, P, P]),
-    "ssd_warp_sample_topk": (I32, [P, I64, I64, I64, F32, F32, I64, P, P, P, I64, P, P, P, P]),
+    "ssd_warp_sample_topk": (I32, [P, I64, I64, I64, F32, F32, I64, I64, P, P, P, I64, P, P, P, P]),
     "ssd_sample_token": (I32, [P, I64, F32, F32, P, P, I64, I64, P, P, P]),
     "ssd_tree_walk_sample": (I32, [P, I64, P, P, P, P, P, P, I64, P, I64, P, I64, P, I64, I64, P, P, P, P, P, P, P,
                                    P, P, P, P, P]),

@@ -253,14 +253,15 @@ def gumbel_topk(logits: torch.Tensor, params: torch.Tensor, k: int, seed: torch.
 def warp_sample_topk(logits: torch.Tensor, temperature: float, top_p: float, params_out: Optional[torch.Tensor],
                      k: int = 0, seed: Optional[torch.Tensor] = None, round_: Optional[torch.Tensor] = None,
                      row_base: int = 0, out_tok: Optional[torch.Tensor] = None, out_lp: Optional[torch.Tensor] = None,
-                     vocab_ids=None, rows: Optional[int] = None) -> None:
+                     vocab_ids=None, rows: Optional[int] = None, keep_top: int = 0) -> None:
     """Fused warp parameters + k Gumbel draws per row on one cluster per row
-    (ssd_warp_sample_topk; k = 0: parameters only)."""
+    (ssd_warp_sample_topk; k = 0: parameters only; keep_top > 0: only the
+    keep_top largest logits of a row take part)."""
     rows = logits.shape[0] if rows is None else rows
     if logits.dtype != torch.float32 or (params_out is not None and params_out.shape[0] < rows):
         raise ValueError("warp_sample_topk: fp32 logits and a params buffer of >= rows records")
     L.call("ssd_warp_sample_topk", _p(logits), logits.stride(0), rows, logits.shape[1], float(temperature),
-           float(top_p), k, _p(vocab_ids), _p(seed), _p(round_), row_base, _p(params_out), _p(out_tok), _p(out_lp),
+           float(top_p), keep_top, k, _p(vocab_ids), _p(seed), _p(round_), row_base, _p(params_out), _p(out_tok), _p(out_lp),
            _stream())
 
 

@@ -236,6 +236,35 @@ def test_generate_batch_greedy_matches_reference(tiny, base32):
     assert generate_batch(target, [], 8, set(), 0.0, 1.0, pad_id=0) == []
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_batched_decoder_matches_single_sequence_decodes(dtype):
+    """One forward per step over several sequences, each in its own cache
+    slot range: every row decodes as the sequence alone does, up to a
+    near-tie of the single-sequence decode's top-2 gap (fp32: < 1e-4, where
+    only the attention's split layout differs; bf16: < 2e-2), with prompts of
+    different lengths."""
+    from ssd.engine.batch import BatchDecoder
+    from ssd.engine.round import TargetStep, cache_capacity
+
+    base = S.build_base_model("llama32_1b", 7, dtype, DEV, gen_device="cuda", num_hidden_layers=2, vocab_size=4096)
+    target = TargetRunner(base)
+    prompts = [S.make_prompt(30 + b, n, 4096)[0].tolist() for b, n in enumerate([5, 40, 17, 130, 64, 9])]
+    n_new = 24
+    dec = BatchDecoder(target, len(prompts), 256, sum(map(len, prompts)))
+    rows = dec.generate(prompts, n_new, set())
+    for p, row in zip(prompts, rows):
+        eng = TargetStep(target, target.new_cache(cache_capacity(len(p), n_new)), n_new)
+        eng.prefill(torch.tensor([p], device=DEV))
+        gaps = [float(eng.gap[0])]
+        for _ in range(n_new - 1):
+            eng.run(1)
+            gaps.append(float(eng.gap[0]))
+        single = eng.tokens()
+        i = next((j for j, (a, b) in enumerate(zip(row, single)) if a != b), None)
+        tie = 1e-4 if dtype == torch.float32 else 2e-2
+        assert i is None or gaps[i] < tie, (i, gaps[i] if i is not None else None)
+
+
 def test_ssd_run_command_line_on_a_synthetic_model(capsys):
     """ssd-run end to end (--synthetic tiny: seeded fp32 random weights, no
     checkpoint or tokenizer): greedy speculative output equals the target-only

@@ -523,3 +523,41 @@ def test_fused_topk_draws_match_the_philox_oracle():
         p = oracle_warp(logits[r].cpu().double().numpy(), T, top_p)
         lp = np.where(p > 0, np.log(np.maximum(p, 1e-300)), -np.inf)
         assert tok[r].tolist() == philox.gumbel_topk(lp, k, 4242, 3, 11 + r, 0)
+
+
+@pytest.mark.parametrize("V,top_p", [(1000, 1.0), (1000, 0.8), (128256, 0.9)])
+def test_keep_top_warp_matches_sample_next(V, top_p):
+    """keep_top = 64 (batched generation): the warped distribution equals the
+    reference's sample_next one, the 64 largest logits warped by temperature
+    and top_p (oracle.tree.top_k_warp, generate_selfdistill.py:51-61)."""
+    from oracle.tree import top_k_warp
+
+    rows, T = 4, 0.8
+    logits = _logit_rows(rows, V, 2.0, V + 3)
+    prm = ops.warp_params_buffer(rows, DEV)
+    ops.warp_sample_topk(logits, T, top_p, prm, keep_top=64)
+    probs = torch.empty_like(logits)
+    ops.warp_probs(logits, prm, probs)
+    got = probs.cpu().double().numpy()
+    for r in range(rows):
+        want = top_k_warp(logits[r].cpu().double().numpy(), 64, T, top_p)
+        assert np.array_equal(got[r] > 0, want > 0)
+        np.testing.assert_allclose(got[r], want, rtol=2e-4, atol=1e-7)
+
+
+def test_generate_batch_sampled_rows_are_target_distributed(v8):
+    """generate_batch at temperature > 0: rows of one batch are independent
+    draws; the joint of each row's first two tokens matches exact warped
+    target sampling (the 8-token vocabulary is below the 64-logit cut)."""
+    from ssd.data.generate_selfdistill import generate_batch
+
+    base, oracle_target = v8
+    target = TargetRunner(base)
+    prompt = [2, 6, 1]
+    counts = np.zeros((8, 8))
+    for s in range(1000):
+        rows = generate_batch(target, [prompt] * 4, 2, {-1}, 0.9, 0.85, 0,
+                              generator=torch.Generator().manual_seed(10_000 + s))
+        for r in rows:
+            counts[r[0], r[1]] += 1
+    assert chi2_pvalue(counts, _exact_joint(oracle_target, prompt, 0.9, 0.85, 2)) > P_MIN
