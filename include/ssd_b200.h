@@ -85,13 +85,6 @@ typedef struct SsdRowNorm {
   float eps;
 } SsdRowNorm;
 
-/* Bulk L2 prefetch of [ptr, ptr + bytes) (16-byte aligned) on the stream:
- * warms the L2 cache with the weights a later GEMM streams. The launch waits
- * for its predecessor before it completes, so stream order is kept for every
- * later kernel, but lets its successor start early. A performance hint with
- * no counterpart in the reference. */
-int ssd_l2_prefetch(const void* ptr, int64_t bytes, void* stream);
-
 /* Embedding gather: resid[t, :] = table[ids[t], :] (fp32 out).
  * Replaces base.embed_tokens(input_ids), ssd/models/subnetwork_draft.py:290-291. */
 int ssd_embed(const int32_t* ids, int64_t T, const void* table, int64_t vocab, int64_t d, int dtype,

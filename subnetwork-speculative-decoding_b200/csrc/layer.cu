@@ -266,28 +266,6 @@ __global__ void topk_reduce_kernel(const float* part, int tiles, int k, const in
 
 using namespace ssd;
 
-// Warm L2 with the weights the next GEMM will stream: each lane issues
-// bulk L2 prefetches (no shared memory, no registers held) over its share of
-// [p, p + bytes), then the kernel waits for its predecessor like any other
-// launch, so everything after it still sees the predecessor complete. Its
-// trigger comes before its wait: the next kernel may start its prologue
-// (and its own weight prefetch) while the kernel before this one drains,
-// and the prefetches fill the HBM idle time of that drain and of the
-// latency-bound launches in between (the tree attention after q/k/v).
-constexpr int64_t kPrefetchChunk = 64 * 1024;
-__global__ void __launch_bounds__(32) l2_prefetch_kernel(const uint8_t* p, int64_t bytes) {
-  const int64_t chunks = (bytes + kPrefetchChunk - 1) / kPrefetchChunk;
-  for (int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x; c < chunks; c += (int64_t)gridDim.x * 32) {
-    const int64_t off = c * kPrefetchChunk;
-    const int64_t n = min(kPrefetchChunk, bytes - off) & ~int64_t(15);
-    if (n > 0)
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + off), "r"(static_cast<uint32_t>(n))
-                   : "memory");
-  }
-  pdl_trigger();
-  pdl_wait();
-}
-
 extern "C" {
 
 int64_t ssd_workspace_bytes(int64_t max_rows, int64_t max_head_rows, int64_t vocab) {
@@ -313,17 +291,6 @@ int64_t ssd_workspace_bytes(int64_t max_rows, int64_t max_head_rows, int64_t voc
   int64_t body = heads + splitk;
   body = body > attn ? body : attn;
   return kCounterBytes + body;
-}
-
-int ssd_l2_prefetch(const void* ptr, int64_t bytes, void* stream) {
-  if (!ptr || bytes < 0) return fail(SSD_ERR_INVALID, "ssd_l2_prefetch: bad arguments");
-  if (reinterpret_cast<uintptr_t>(ptr) % 16) return fail(SSD_ERR_INVALID, "ssd_l2_prefetch: pointer not 16-byte aligned");
-  if (bytes < 16) return SSD_OK;
-  const int64_t chunks = (bytes + kPrefetchChunk - 1) / kPrefetchChunk;
-  int64_t blocks = (chunks + 31) / 32;
-  if (blocks > device_sms()) blocks = device_sms();
-  return launch_kernel("l2_prefetch_kernel", l2_prefetch_kernel, dim3((unsigned)blocks), dim3(32), 0,
-                       static_cast<cudaStream_t>(stream), 1, 1, static_cast<const uint8_t*>(ptr), bytes);
 }
 
 int ssd_embed(const int32_t* ids, int64_t T, const void* table, int64_t vocab, int64_t d, int dtype, float* resid,

@@ -51,7 +51,6 @@ SIGNATURES: dict[str, tuple] = {
     "ssd_device_sm_count": (I32, [I32]),
     "ssd_workspace_bytes": (I64, [I64, I64, I64]),
     "ssd_embed": (I32, [P, I64, P, I64, I64, I32, P, P, P, P]),
-    "ssd_l2_prefetch": (I32, [P, I64, P]),
     "ssd_rmsnorm": (I32, [P, I64, I64, I64, P, F32, P, I64, I32, P]),
     "ssd_linear": (I32, [P, I64, I64, I64, I32, P, P, P, I32, I32, I32, P, I64, P, I64, I32, P, I64, P, P, P, P]),
     "ssd_linear_noalloc": (I32, [P, I64, I64, I64, I32, P, P, P, I32, I32, I32, P, I64, P, I64, I32, P, P]),

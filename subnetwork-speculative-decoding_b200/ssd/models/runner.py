@@ -311,19 +311,6 @@ def _norm_chain(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm_brid
     return out
 
 
-# Decode-sized forwards warm L2 with the next small GEMM's weights (o_proj
-# during the attention, the next layer's q/k/v after down_proj); at most this
-# many bytes per prefetch (L2: 126 MB).
-PREFETCH_BYTES = 48 << 20
-
-
-def l2_prefetch_enabled() -> bool:
-    """SSD_L2_PREFETCH=0 turns the L2 weight prefetch off (A/B timing)."""
-    import os
-
-    return os.environ.get("SSD_L2_PREFETCH", "1") != "0"
-
-
 def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm_bridge, fwd: ForwardInputs, T: int,
                      cache, scratch: Scratch, ws: ops.Workspace, kv_bound: int) -> None:
     """run_stack with every RMSNorm folded into the neighbouring kernels (bf16).
@@ -331,7 +318,6 @@ def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm
     norm's folded input for final_norm_folded."""
     norms = _norm_chain(w, layer_indices, pre_layer_bridges, pre_norm_bridge)
     parts, d = norm_parts(w), w.d
-    prefetch = l2_prefetch_enabled() and T <= 64 and w.tp is None
     xg = scratch.xn(w.dtype, d)[:T, :d]
     ssq = scratch.ssq[:T]
     resid = scratch.resid[:T]
@@ -350,8 +336,6 @@ def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm
         kc, vc = cache.layer(li)
         ops.qkv_rope(xg, lw.q, lw.k, lw.v, w.H, w.Hkv, w.hd, w.rope_cos, w.rope_sin, fwd.positions, fwd.slots, kc, vc,
                      scratch.q[:T], ws, T=T, in_norm=in_for(k))
-        if prefetch:  # o_proj's weights into L2 while the attention runs
-            ops.l2_prefetch([lw.o], PREFETCH_BYTES)
         ops.tree_attention(scratch.q[:T], kc, vc, w.H, w.Hkv, w.hd, fwd.prefix_len, scratch.attn[:T], ws,
                            spec_base=fwd.spec_base if fwd.use_mask else None,
                            spec_mask=fwd.mask if fwd.use_mask else None, kv_bound=kv_bound, T=T,
@@ -360,9 +344,6 @@ def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm
         hid = scratch.hid(w.dtype, w.F, 0)[:T, : w.F]
         ops.linear(xg, [lw.gate, lw.up], ws, epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid, in_norm=in_for(k + 1))
         _residual_linear(w, hid, lw.down, ws, resid, out_for(k + 2), T)
-        if prefetch and slot + 1 < len(layer_indices) and pre_layer_bridges[slot + 1] is None:
-            nw = w.layers[layer_indices[slot + 1]]  # the next layer's q/k/v weights
-            ops.l2_prefetch([nw.q, nw.k, nw.v], PREFETCH_BYTES)
         k += 2
     if pre_norm_bridge is not None:
         _bridge_folded(pre_norm_bridge, scratch, T, ws, xg, in_for(k), out_for(k + 1))

@@ -135,21 +135,6 @@ def linear(x: torch.Tensor, weights: Sequence[torch.Tensor], ws: Workspace, *, b
            dtype_code(weights[0].dtype), ws.ptr, ws.nbytes, _c(in_norm), _c(norm_out), _p(ws.status), _stream())
 
 
-def l2_prefetch(tensors, max_bytes: Optional[int] = None) -> None:
-    """Warm L2 with the leading bytes of each tensor (ssd_l2_prefetch), in
-    order, up to max_bytes in all."""
-    left = max_bytes
-    for t in tensors:
-        n = t.numel() * t.element_size()
-        if left is not None:
-            n = min(n, left)
-            left -= n
-        if n >= 16:
-            L.call("ssd_l2_prefetch", _p(t), n, _stream())
-        if left is not None and left <= 0:
-            break
-
-
 def qkv_rope(x, wq, wk, wv, n_heads, n_kv, head_dim, cos, sin, positions, slots, k_cache, v_cache, q_out,
              ws: Workspace, T: Optional[int] = None, in_norm: Optional[RowNorm] = None) -> None:
     """k_cache/v_cache: [n_kv, max_slots, head_dim] views of one layer."""
