@@ -708,26 +708,20 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
 // bf16, head_dim 64 or 128. A CTA = one KV head x up to 128 query rows (one
 // M = 128 tcgen05 tile; rows past the group are zero) x one key slice.
 // Warp 0 streams the slice's 64-key K and V blocks by TMA (128-byte swizzle,
-// straight from the cache rows) into a kTcAttnStages ring. Warp 1 (one lane)
-// issues S = Q K^T into one of two TMEM S buffers and O += P V into one of two
-// TMEM O accumulators (V read MN-major as stored): block b uses S buffer,
-// P buffer and O accumulator b & 1 (its parity).
-// Sixteen softmax warps (warps 2..17) form four warpgroups: (parity, half).
-// A softmax thread owns one query row (= TMEM lane) and one half of the 64
-// scores of every block of its parity: it loads its 32 scores, applies the
-// tree mask and runs the online softmax in base 2 with a lazy reference max
-// (P = 2^(s - m_ref) stays below 2^8, so O is rescaled only when a row's max
-// grows by more than 8). The two halves of a row agree on the block max
-// through shared memory (a 64-thread named barrier per pair of warps that
-// share a TMEM lane quarter), so both scale their P with the same reference;
-// each writes its half of P (bf16) into shared memory for the P V product
-// and rescales its half of the O columns. Four softmax warps per SM
-// sub-partition keep the score pipeline fed (one warpgroup per parity left
-// each sub-partition idle on latency most of the time); the two O
-// accumulators (and their (max, sum) states) combine at the end, each
-// warpgroup emitting a quarter of the output columns. Partials of the key
-// slices merge as in the mma.sync kernel: pushed into the merging CTA of the
-// cluster, or through global memory for long contexts.
+// straight from the cache rows) into a kTcAttnStages ring. Warp 1 (one
+// lane) issues S = Q K^T into one of two TMEM S buffers and O += P V into
+// one of two TMEM O accumulators (V read MN-major as stored). On long slices
+// two softmax warpgroups split the key blocks: warps 2..5 take the even blocks
+// (S, P and O buffers 0), warps 6..9 the odd ones (buffers 1), so each SM
+// sub-partition runs two softmax warps; on short slices warps 2..5 take every
+// block (S and P buffers alternate, one O accumulator). A softmax thread owns one query row (= TMEM lane):
+// it loads S, applies the tree mask, runs the online softmax in base 2 with a
+// lazy reference max (P = 2^(s - m_ref) stays below 2^8, so O is rescaled
+// only when a row's max grows by more than 8) and writes P as bf16 into
+// shared memory for the P V product. At the end the two warpgroups combine
+// their (max, sum, O) states of each row; each writes half of the columns. Partials of the key slices merge as in the mma.sync
+// kernel: pushed into the merging CTA of the cluster, or through global
+// memory for long contexts.
 // 2^x on the special-function unit (PTX ex2.approx.ftz.f32; 2^-inf = +0).
 __device__ __forceinline__ float ex2_fast(float x) {
   float y;
@@ -736,12 +730,12 @@ __device__ __forceinline__ float ex2_fast(float x) {
 }
 constexpr int kTcAttnStages = 4;
 constexpr int kTcAttnMaxTok = 129;  // token rows spanned by 128 query rows (keeps the metadata 8-byte aligned)
-constexpr int kTcAttnSoftWarps = 16;
-// TMA warp, MMA warp, four softmax warpgroups. 18 warps put five on one SM
-// sub-partition, whose 16K-register share caps a thread at 96 registers.
-constexpr int kTcAttnThreads = 32 * (2 + kTcAttnSoftWarps);
+constexpr int kTcAttnThreads = 320;  // TMA warp, MMA warp, two softmax warpgroups
 constexpr float kLazyRescale = 8.f;  // log2 headroom of P before O is rescaled
-constexpr int kTcAttnPairBar = 4;    // named barriers 4..11: (parity, lane quarter) pairs of softmax warps
+// Key blocks per CTA from which the second softmax warpgroup takes the odd
+// blocks (below it warps 2..5 take every block and accumulator 1 stays unused:
+// short slices are bound by the CTA's set-up and merge, not by the softmax).
+constexpr int kTcTwoGroupsMinBlocks = 12;
 
 struct AttnMaps {
   CUtensorMap k;  // [n_kv * max_slots, hd] bf16, box {64, 64}
@@ -757,9 +751,7 @@ struct TcAttnLayout {
   static constexpr int P_BYTES = 128 * 128;          // [128 rows x 64 keys] bf16
   static constexpr int OFF_RING = Q_BYTES;
   static constexpr int OFF_P = Q_BYTES + kTcAttnStages * STAGE;
-  static constexpr int OFF_BM = OFF_P + 2 * P_BYTES;  // [parity][half][slot][128] block maxima
-  static constexpr int BM_BYTES = 2 * 2 * 2 * 128 * 4;
-  static constexpr int OFF_META = OFF_BM + BM_BYTES;
+  static constexpr int OFF_META = OFF_P + 2 * P_BYTES;
   static constexpr int META = (kTcAttnMaxTok + 1) * 4 + kTcAttnMaxTok * 4 * 8 + 16 + (2 * kTcAttnStages + 10) * 8 + 16 +
                               (kTcAttnMaxTok + 1) * 4;
   static constexpr int SMEM = 1024 + OFF_META + META;
@@ -776,7 +768,6 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   uint8_t* qs = sm;
   uint8_t* ring = sm + Lay::OFF_RING;
   uint8_t* ps = sm + Lay::OFF_P;
-  float* s_bm = reinterpret_cast<float*>(sm + Lay::OFF_BM);
   int* s_plen = reinterpret_cast<int*>(sm + Lay::OFF_META);
   uint64_t* s_mask = reinterpret_cast<uint64_t*>(s_plen + kTcAttnMaxTok + 1);  // [tok][4]
   int* s_misc = reinterpret_cast<int*>(s_mask + kTcAttnMaxTok * 4);           // need_end, min_plen, last, abort
@@ -815,8 +806,8 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 8);  // the eight softmax warps of the buffer's parity
-      mbar_init(&p_full[i], 8);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
       mbar_init(&p_free[i], 1);
     }
     mbar_init(o_full, 1);
@@ -859,10 +850,11 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   const int k_lo = split * slice;
   const int k_hi = min(k_lo + slice, need_end);
   const int nblocks = k_hi > k_lo ? (k_hi - k_lo + KB - 1) / KB : 0;
+  const bool two = nblocks >= kTcTwoGroupsMinBlocks;  // CTA-uniform
   const uint32_t qs_s = smem_u32(qs), ring_s = smem_u32(ring), ps_s = smem_u32(ps);
   if (warp >= 1) {
     // Q rows (A operand, K-major, 128-byte swizzle; rows past Mg are zero),
-    // staged by warps 1.. while warp 0 already streams K/V.
+    // staged by warps 1..5 while warp 0 already streams K/V.
     const bf16* qb = static_cast<const bf16*>(a.q);
     for (int idx = threadIdx.x - 32; idx < 128 * (HD / 8); idx += kTcAttnThreads - 32) {
       const int r = idx / (HD / 8), c = idx % (HD / 8);
@@ -879,11 +871,10 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   // even and odd key blocks at [128, 128 + HD) and [256, 256 + HD)
   const uint32_t tm_o = tmem + 128;
 
-  // softmax-side state (warps 2..17): warpgroup wgi = (parity, half)
-  const int wgi = warp >= 2 ? (warp - 2) >> 2 : 0;
-  const int par = wgi >> 1, half = wgi & 1;
+  // softmax-side state (warps 2..9): warpgroup wg takes key blocks wg, wg + 2, ...
   const int q = warp & 3;
   const int r = q * 32 + lane;  // query row of this thread = TMEM lane
+  const int wg = warp >= 6 ? 1 : 0;
   const bool row_ok = warp >= 2 && r < Mg;
   float m_ref = -INFINITY, l = 0.f;
 
@@ -936,8 +927,9 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
         const uint32_t pb = ps_s + (j & 1) * Lay::P_BYTES;
 #pragma unroll
         for (int kk = 0; kk < KB / 16; ++kk)
-          umma_bf16(tm_o + (j & 1) * 128, sdesc_k_sw128(pb + kk * 32),
-                    sdesc_mn_sw128(vb + kk * 2048, Lay::KV_REGION, 1024), id_pv, (j > 1 || kk > 0) ? 1u : 0u);
+          umma_bf16(tm_o + (two ? (j & 1) * 128 : 0), sdesc_k_sw128(pb + kk * 32),
+                    sdesc_mn_sw128(vb + kk * 2048, Lay::KV_REGION, 1024), id_pv,
+                    (j > (two ? 1 : 0) || kk > 0) ? 1u : 0u);
         umma_commit(&p_free[j & 1]);
         umma_commit(&kv_empty[j % kTcAttnStages]);
       };
@@ -966,174 +958,150 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
       umma_commit(o_full);
     }
   } else {
-    // ---- softmax warps: thread = query row r, 32 scores of each block of
-    // parity `par` (keys half * 32 .. + 31). Every warp runs every iteration
-    // of its parity (no early exit), so the pair barriers always match.
+    // ---- softmax warps: thread = query row r
     const int tok = row_ok ? (q0 + r) / a.G - t_first : 0;
     const int plen = row_ok ? s_plen[tok] : 0;
     const int pstart = row_ok ? s_pstart[tok] : 0;
     const float sc = a.scale * 1.4426950408889634f;  // base 2
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    const uint32_t tm_ow = tm_o + par * 128;
-    const int pair_bar = kTcAttnPairBar + par * 4 + q;
     bool bad = false;
-    for (int b = par; b < nblocks; b += 2) {
-      const int it = b >> 1;  // the how-many-th block of this parity
-      if (!bad) bad = !mbar_wait(&s_full[par], it & 1) || *abort_flag;
-      bad = __any_sync(0xffffffffu, bad);
-      float sv[32];
-      if (!bad) {
-        tc_fence_after();
-        tmem_ld32(tmem + lane_base + par * KB + half * 32, sv);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sv[j] = 0.f;
+    const uint32_t tm_ow = tm_o + (two ? wg * 128 : 0);
+    const int b0 = two ? wg : (wg == 0 ? 0 : nblocks), bstep = two ? 2 : 1;
+    for (int b = b0; b < nblocks; b += bstep) {
+      const int sbuf = b & 1;
+      bad = !mbar_wait(&s_full[sbuf], (b >> 1) & 1) || *abort_flag;
+      if (__any_sync(0xffffffffu, bad)) {
         if (lane == 0) {
           report_error(a.status, kErrWaitTimeout);
           *abort_flag = 1;
         }
+        bad = true;
+        break;
       }
+      tc_fence_after();
+      float sv[KB];
+      tmem_ld64(tmem + lane_base + sbuf * KB, sv);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[par]);
+      if (lane == 0) mbar_arrive(&s_free[sbuf]);
       const int kb = k_lo + b * KB;
-      const uint64_t vbits = (row_ok && !bad) ? key_block_bits(kb, k_hi, plen, s_mask + tok * 4, mw, sb, pstart) : 0ull;
-      const uint32_t vh = static_cast<uint32_t>(vbits >> (half * 32));
+      const uint64_t vbits = row_ok ? key_block_bits(kb, k_hi, plen, s_mask + tok * 4, mw, sb, pstart) : 0ull;
+      const uint32_t vlo = static_cast<uint32_t>(vbits), vhi = static_cast<uint32_t>(vbits >> 32);
       float bmx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float v = ((vh >> j) & 1u) ? sv[j] * sc : -INFINITY;
+      for (int j = 0; j < KB; ++j) {
+        const bool ok = ((j < 32 ? vlo >> j : vhi >> (j - 32)) & 1u) != 0u;
+        const float v = ok ? sv[j] * sc : -INFINITY;
         sv[j] = v;
         bmx[j & 3] = fmaxf(bmx[j & 3], v);
       }
-      float bm = fmaxf(fmaxf(bmx[0], bmx[1]), fmaxf(bmx[2], bmx[3]));
-      // the two halves of the row agree on the block max (slots alternate
-      // between this parity's consecutive blocks)
-      s_bm[((par * 2 + half) * 2 + (it & 1)) * 128 + r] = bm;
-      named_bar_sync(pair_bar, 64);
-      bm = fmaxf(bm, s_bm[((par * 2 + (half ^ 1)) * 2 + (it & 1)) * 128 + r]);
+      const float bm = fmaxf(fmaxf(bmx[0], bmx[1]), fmaxf(bmx[2], bmx[3]));
       const bool grow = bm > m_ref + kLazyRescale || (m_ref == -INFINITY && bm > -INFINITY);
-      const bool any_grow = __any_sync(0xffffffffu, grow);
-      float alpha = 1.f;
-      if (any_grow) {
+      if (__any_sync(0xffffffffu, grow)) {
         const float m_new = grow ? bm : m_ref;
-        alpha = (!grow || m_ref == -INFINITY) ? (grow ? 0.f : 1.f) : exp2f(m_ref - m_new);
+        const float alpha = (!grow || m_ref == -INFINITY) ? (grow ? 0.f : 1.f) : exp2f(m_ref - m_new);
+        if (b >= bstep) {
+          // this warpgroup's O holds earlier blocks: rescale it once P V of
+          // its previous block b - bstep is done
+          const int pb = b - bstep;
+          const bool w_ok = mbar_wait(&p_free[pb & 1], (pb >> 1) & 1);
+          if (!w_ok) report_error(a.status, kErrWaitTimeout);
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < HD; c += 16) {
+            float ov[16];
+            tmem_ld16(tm_ow + lane_base + c, ov);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ov[i] *= alpha;
+            tmem_st16(tm_ow + lane_base + c, ov);
+          }
+          tmem_wait_st();
+        }
         l *= alpha;
         m_ref = m_new;
       }
-      uint32_t pk[16];
+      uint32_t pk[KB / 2];
       float lsx[4] = {0.f, 0.f, 0.f, 0.f};
       const float mr = m_ref == -INFINITY ? 0.f : m_ref;  // a row with no key yet has only -inf scores
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) {
+      for (int j = 0; j < KB; j += 2) {
         const float p0 = ex2_fast(sv[j] - mr);
         const float p1 = ex2_fast(sv[j + 1] - mr);
         lsx[(j >> 1) & 3] += p0 + p1;
         pk[j >> 1] = pack_bf16(p0, p1);
       }
       l += (lsx[0] + lsx[1]) + (lsx[2] + lsx[3]);
-      if (any_grow && b >= 2 && !bad) {
-        // this parity's O holds earlier blocks: rescale this half of its
-        // columns once P V of block b - 2 is done (before this block's P is
-        // published, so P V of block b adds onto the rescaled accumulator)
-        const int pb = b - 2;
-        if (!mbar_wait(&p_free[par], (pb >> 1) & 1)) report_error(a.status, kErrWaitTimeout);
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < HD / 2; c += 16) {
-          float ov[16];
-          tmem_ld16(tm_ow + lane_base + half * (HD / 2) + c, ov);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) ov[i] *= alpha;
-          tmem_st16(tm_ow + lane_base + half * (HD / 2) + c, ov);
-        }
-        tmem_wait_st();
-      }
-      if (b >= 2 && !bad) {
-        const bool w_ok = mbar_wait(&p_free[par], ((b - 2) >> 1) & 1);  // P V of block b - 2 read this buffer
+      if (b >= 2) {
+        const bool w_ok = mbar_wait(&p_free[sbuf], ((b - 2) >> 1) & 1);  // P V of block b - 2 read this buffer
         if (!w_ok) report_error(a.status, kErrWaitTimeout);
       }
-      uint8_t* prow = ps + par * Lay::P_BYTES + r * 128;
+      uint8_t* prow = ps + sbuf * Lay::P_BYTES + r * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<uint4*>(prow + (((half * 4 + c) ^ (r & 7)) << 4)) =
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[par]);
+      if (lane == 0) mbar_arrive(&p_full[sbuf]);
     }
+    (void)bad;
   }
-  // ---- results: combine the two parities' (max, sum, O) states of each row
-  // (base 2); warpgroup wgi owns output columns [wgi * QC, (wgi + 1) * QC)
-  // of both accumulators and emits them 16 columns at a time
-  constexpr int QC = HD / 4;
-  float Mrow = -INFINITY, Lrow = 0.f, a0 = 0.f, a1 = 0.f;
-  bool have_o = false;
-  const int c0 = wgi * QC;
+  // ---- results: the two softmax warpgroups combine their states of each
+  // row (base 2) and each reads half of the O columns of both accumulators
+  constexpr int HH = HD / 2;
+  float ov[HH];
+#pragma unroll
+  for (int i = 0; i < HH; ++i) ov[i] = 0.f;
+  float Mrow = -INFINITY, Lrow = 0.f;
+  const int c0 = wg * HH;
   if (warp >= 2) {
     const bool w_ok = mbar_wait(o_full, 0);
     if (!w_ok) report_error(a.status, kErrWaitTimeout);
     tc_fence_after();
     float* s_ml = reinterpret_cast<float*>(ps);  // the P buffers are free once every P V retired
-    s_ml[(wgi * 128 + r) * 2] = m_ref;
-    s_ml[(wgi * 128 + r) * 2 + 1] = l;
-    named_bar_sync(3, kTcAttnSoftWarps * 32);
-    // parity p: reference max shared by its two halves, sum = both halves' sums
-    const float m0 = s_ml[r * 2], l0 = s_ml[r * 2 + 1] + s_ml[(128 + r) * 2 + 1];
-    const float m1 = s_ml[(256 + r) * 2], l1 = s_ml[(256 + r) * 2 + 1] + s_ml[(384 + r) * 2 + 1];
+    s_ml[(wg * 128 + r) * 2] = m_ref;
+    s_ml[(wg * 128 + r) * 2 + 1] = l;
+    named_bar_sync(3, kTcAttnThreads - 64);
+    const float m0 = s_ml[r * 2], l0 = s_ml[r * 2 + 1];
+    const float m1 = s_ml[(128 + r) * 2], l1 = s_ml[(128 + r) * 2 + 1];
     Mrow = fmaxf(m0, m1);
-    a0 = m0 == -INFINITY ? 0.f : exp2f(m0 - Mrow);
-    a1 = m1 == -INFINITY ? 0.f : exp2f(m1 - Mrow);
+    const float a0 = m0 == -INFINITY ? 0.f : exp2f(m0 - Mrow);
+    const float a1 = m1 == -INFINITY ? 0.f : exp2f(m1 - Mrow);
     Lrow = a0 * l0 + a1 * l1;
     // accumulator 0 holds data once a block ran, accumulator 1 once two did
-    have_o = __all_sync(0xffffffffu, nblocks > 0 && w_ok && !*abort_flag);
+    if (__all_sync(0xffffffffu, nblocks > 0 && w_ok && !*abort_flag)) {
+      const uint32_t lb = static_cast<uint32_t>(q * 32) << 16;
+#pragma unroll
+      for (int i = 0; i < HH; i += 16) {
+        float x[16], y[16];
+        tmem_ld16(tm_o + lb + c0 + i, x);
+        if (two && nblocks > 1) {
+          tmem_ld16(tm_o + 128 + lb + c0 + i, y);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) y[k] = 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 16; ++k) ov[i + k] = a0 * x[k] + a1 * y[k];
+      }
+    }
   }
-  const uint32_t lb = static_cast<uint32_t>(q * 32) << 16;
-  // 16 combined output columns [c0 + i, c0 + i + 16) of this thread's row
-  auto chunk = [&](int i, float* ov) {
-    if (!have_o) {
-#pragma unroll
-      for (int k = 0; k < 16; ++k) ov[k] = 0.f;
-      return;
-    }
-    float y[16];
-    tmem_ld16(tm_o + lb + c0 + i, ov);
-    if (nblocks > 1) {
-      tmem_ld16(tm_o + 128 + lb + c0 + i, y);
-    } else {
-#pragma unroll
-      for (int k = 0; k < 16; ++k) y[k] = 0.f;
-    }
-#pragma unroll
-    for (int k = 0; k < 16; ++k) ov[k] = a0 * ov[k] + a1 * y[k];
-  };
-  auto release_tmem = [&]() {
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-      tc_fence_after();
-      tmem_dealloc(tmem, 512);
-    }
-  };
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
   bf16* outp = static_cast<bf16*>(a.out);
   if (P == 1) {
-    if (warp >= 2) {
+    if (row_ok) {
       const float inv = Lrow > 0.f ? 1.f / Lrow : 0.f;
       const int qr = q0 + r;
       bf16* op = outp + (int64_t)(qr / a.G) * a.ldo + (int64_t)(h * a.G + qr % a.G) * HD + c0;
 #pragma unroll
-      for (int i = 0; i < QC; i += 16) {
-        float ov[16];
-        chunk(i, ov);
-        if (row_ok) {
-#pragma unroll
-          for (int d = 0; d < 16; d += 2)
-            *reinterpret_cast<uint32_t*>(op + i + d) = pack_bf16(ov[d] * inv, ov[d + 1] * inv);
-        }
-      }
+      for (int d = 0; d < HH; d += 2) *reinterpret_cast<uint32_t*>(op + d) = pack_bf16(ov[d] * inv, ov[d + 1] * inv);
     }
-    release_tmem();
     return;
   }
   const int rec = mma_rec(HD);
@@ -1179,23 +1147,15 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     const int ns = a.n_splits;
     const int owned = (a.rows_per_group + ns - 1) / ns;
     float* recv = reinterpret_cast<float*>(ring);
-    if (warp >= 2) {
+    if (row_ok) {
       const int owner = r % ns, j = r / ns;
       const uint32_t base = dsmem_map(smem_u32(recv), static_cast<uint32_t>(owner)) +
                             (uint32_t)(((split * owned + j) * rec) * 4);
-      if (row_ok && wgi == 0) dsmem_st4(base, Mrow, Lrow, 0.f, 0.f);
+      if (wg == 0) dsmem_st4(base, Mrow, Lrow, 0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < QC; i += 16) {
-        float ov[16];
-        chunk(i, ov);
-        if (row_ok) {
-#pragma unroll
-          for (int d = 0; d < 16; d += 4)
-            dsmem_st4(base + (uint32_t)(4 + c0 + i + d) * 4, ov[d], ov[d + 1], ov[d + 2], ov[d + 3]);
-        }
-      }
+      for (int d = 0; d < HH; d += 4)
+        dsmem_st4(base + (uint32_t)(4 + c0 + d) * 4, ov[d], ov[d + 1], ov[d + 2], ov[d + 3]);
     }
-    release_tmem();
     cluster_sync_all();
     const int n_own = Mg > split ? (Mg - split + ns - 1) / ns : 0;
     for (int j = warp; j < n_own; j += nwarps) {
@@ -1207,24 +1167,15 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   // Long contexts: records in the global workspace slot of (row group,
   // slice); attn_merge_kernel combines the slices of every row in parallel.
   float* recs = a.part + ((int64_t)blk * a.n_splits + split) * a.rows_per_group * rec;
-  if (warp >= 2) {
+  if (row_ok) {
     float* pr = recs + (int64_t)r * rec;
-    if (row_ok && wgi == 0) {
+    if (wg == 0) {
       pr[0] = Mrow;
       pr[1] = Lrow;
     }
 #pragma unroll
-    for (int i = 0; i < QC; i += 16) {
-      float ov[16];
-      chunk(i, ov);
-      if (row_ok) {
-#pragma unroll
-        for (int d = 0; d < 16; d += 2)
-          *reinterpret_cast<float2*>(pr + 4 + c0 + i + d) = make_float2(ov[d], ov[d + 1]);
-      }
-    }
+    for (int d = 0; d < HH; d += 2) *reinterpret_cast<float2*>(pr + 4 + c0 + d) = make_float2(ov[d], ov[d + 1]);
   }
-  release_tmem();
 }
 
 // Merge of the key-slice records written by attn_tc_kernel (long contexts):
