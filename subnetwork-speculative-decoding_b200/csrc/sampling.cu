@@ -543,6 +543,7 @@ struct RowExchange {
   unsigned long long* hslot;  // [2][256] histogram bins per bank
   float* gath;                // [2 * kRowMaxSlices] gathered partials
   unsigned long long* ghist;  // [256] combined histogram
+  unsigned long long* whist;  // [kSampWarps][256] per-warp bins (radix select)
   int S;
   int n;  // exchanges so far
 };
@@ -594,8 +595,11 @@ __device__ void row_allbest(RowExchange& x, float& key, int& idx) {
 // Cluster-wide radix select over the order keys of the staged slice: four
 // 8-bit levels; at each level every CTA histograms the keys that share the
 // prefix found so far (weight(l) per key: 1 to select by count, a 2^48
-// fixed-point mass to select by probability mass), the bins are summed over
-// the cluster (integers, so the sums do not depend on the split) and the
+// fixed-point mass to select by probability mass) into one private
+// histogram per warp (a row's keys crowd into a few top-byte bins, so a
+// shared histogram serialises its updates across warps), sums the warps'
+// bins, then the bins are summed over the cluster (integers, so the sums do
+// not depend on the split or the order) and the
 // selected bin is the lowest whose weight strictly above it stays <= target
 // (by mass) or, counting, the bin holding the target-th largest key. Only
 // keys >= floor_key take part. Returns the selected key.
@@ -607,14 +611,32 @@ __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_
   for (int level = 0; level < 4; ++level) {
     const int shift = 24 - 8 * level;
     unsigned long long* hist = x.hslot + (x.n & 1) * 256;
-    for (int b = threadIdx.x; b < 256; b += kSampThreads) hist[b] = 0ull;
+    unsigned long long* mine = x.whist + (threadIdx.x >> 5) * 256;
+    for (int b = threadIdx.x; b < kSampWarps * 256; b += kSampThreads) x.whist[b] = 0ull;
     __syncthreads();
     for (int base = 0; base < n; base += kSampThreads) {
       const int i = base + threadIdx.x;
       const float l = i < n ? xs[i] : -INFINITY;
       const uint32_t k = order_key(l);
       const bool in = i < n && k >= floor_key && (level == 0 || (k >> (shift + 8)) == prefix);
-      hist_add_warp(hist, (k >> shift) & 255u, in ? weight(l) : 0ull, in);
+      // lanes of a bin add their weights exactly (24-bit halves through
+      // integer reductions) and the bin's lowest lane adds the sum to this
+      // warp's own histogram: no other warp writes it, and the leaders of one
+      // step hold distinct bins, so a plain add suffices
+      const uint32_t bin = (k >> shift) & 255u;
+      const unsigned long long v = in ? weight(l) : 0ull;
+      const unsigned peers = __match_any_sync(0xffffffffu, in ? bin : 0xffffffffu);
+      const unsigned lo = __reduce_add_sync(peers, static_cast<unsigned>(v & 0xffffffull));
+      const unsigned hi = __reduce_add_sync(peers, static_cast<unsigned>(v >> 24));
+      if (in && (threadIdx.x & 31) == static_cast<unsigned>(__ffs(peers) - 1))
+        mine[bin] += (static_cast<unsigned long long>(hi) << 24) + lo;
+      __syncwarp();
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < 256; b += kSampThreads) {
+      unsigned long long t = 0ull;
+      for (int w = 0; w < kSampWarps; ++w) t += x.whist[w * 256 + b];
+      hist[b] = t;
     }
     cluster_sync_all();  // every CTA's bins are complete
     for (int b = threadIdx.x; b < 256; b += kSampThreads) {
@@ -729,7 +751,8 @@ __global__ void __launch_bounds__(kSampThreads, 1) warp_sample_kernel(
   pdl_trigger();
   for (int i = threadIdx.x; i < n; i += kSampThreads) xs[i] = row[i0 + i];
   __syncthreads();
-  RowExchange x{fslot, hslot, gath, ghist, S, 0};
+  RowExchange x{fslot, hslot, gath, ghist, nullptr, S, 0};
+  x.whist = reinterpret_cast<unsigned long long*>(xs + ((len + 1) & ~1));
   const WarpParams P = cluster_row_warp(xs, n, V, temperature, top_p, keep_top, red, x, sel);
   if (s == 0 && threadIdx.x == 0 && params_out) params_out[r] = P;
   if (k <= 0) {
@@ -859,7 +882,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_verify_cluster_kernel(
   float* qs = dyn + len;
   pdl_wait();
   pdl_trigger();
-  RowExchange x{fslot, nullptr, gath, nullptr, S, 0};
+  RowExchange x{fslot, nullptr, gath, nullptr, nullptr, S, 0};
   const int n = min(*n_nodes, max_nodes);
   const int c0 = root_pos[0];
   const uint64_t sd = seed[0];
@@ -1030,6 +1053,13 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_verify_cluster_kernel(
   }
 }
 
+// Dynamic shared memory of warp_sample_kernel: the staged slice (padded to
+// 8 bytes) and the per-warp histograms of the radix select.
+static size_t warp_sample_smem(int64_t V, int S) {
+  const int64_t len = (V + S - 1) / S;
+  return (size_t)(((len + 1) & ~int64_t(1)) * 4 + (int64_t)kSampWarps * 256 * 8);
+}
+
 // Cluster size for a row of V logits: slices of at least 2048 and at most
 // kRowSliceMax floats, at most 8 CTAs. 0 = the row is too long.
 static int row_slices(int64_t V) {
@@ -1095,7 +1125,7 @@ int ssd_warp_sample_topk(const float* logits, int64_t ld, int64_t rows, int64_t 
   if (S == 0)
     return fail(SSD_ERR_UNSUPPORTED, "ssd_warp_sample_topk: V = %lld exceeds %d", (long long)V,
                 kRowMaxSlices * kRowSliceMax);
-  const size_t smem = (size_t)((V + S - 1) / S) * 4;
+  const size_t smem = warp_sample_smem(V, S);
   static bool set = false;
   if (!set) {
     allow_max_dynamic_smem(warp_sample_kernel);
@@ -1119,7 +1149,7 @@ int ssd_sample_token(const float* logits, int64_t V, float temperature, float to
                          static_cast<cudaStream_t>(stream), 1, 1, logits, (int)V, temperature, top_p, seed, round,
                          (int)row_id, (int)stream_id, scratch, out);
   }
-  const size_t smem = (size_t)((V + S - 1) / S) * 4;
+  const size_t smem = warp_sample_smem(V, S);
   static bool set = false;
   if (!set) {
     allow_max_dynamic_smem(warp_sample_kernel);
