@@ -318,6 +318,48 @@ def gemm_roofline(w, rows: int, dev) -> dict:
         out[name] = {"us": t * 1e6, "gbs": nbytes / t / 1e9, "bytes": nbytes}
         total_b += nbytes * w.L
         total_t += t * w.L
+    # the engines' decode path: one chained launch per layer (o_proj ->
+    # gate/up -> down -> the next layer's q/k/v, folded norms), timed the same way
+    from ssd.models import runner as R
+
+    chained = R.chain_enabled(w, rows)
+    if chained:
+        parts = R.norm_parts(w)
+        ssq = torch.zeros(rows, parts, dtype=torch.float32, device=dev)
+        xg = x_d.clone()
+
+        def layer_chain(li):
+            lw, nx = w.layers[li], w.layers[(li + 1) % w.L]
+            c = ops.GemmChain(ws, rows, True)
+            c.linear(x_a, [lw.o], epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=ops.NormOut(lw.ln2, xg, ssq))
+            c.linear(xg, [lw.gate, lw.up], epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=h_out,
+                     in_norm=ops.RowNorm(ssq, parts, w.d, lw.eps2))
+            c.linear(h_out, [lw.down], epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=ops.NormOut(nx.ln1, xg, ssq))
+            c.linear(xg, [nx.q, nx.k, nx.v], out=q_out, in_norm=ops.RowNorm(ssq, parts, w.d, nx.eps1))
+            c.flush()
+
+        for li in range(2):
+            layer_chain(li)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.graph(graph, stream=s):
+            for li in range(w.L):
+                layer_chain(li)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        for _ in range(2):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        t = e0.elapsed_time(e1) / 1e3 / (5 * w.L)
+        nbytes = sum(out[k]["bytes"] for k in ("qkv", "o_proj", "gate_up", "down"))
+        out["layer_chain"] = {"us": t * 1e6, "gbs": nbytes / t / 1e9, "bytes": nbytes}
+        total_b, total_t = nbytes * w.L, t * w.L
+        del graph
     # non-GEMM kernels of the same forward: RMSNorm and tree attention over a
     # cache of the bench context (their bytes are the activations / the KV)
     from ssd.models.runner import ForwardInputs
@@ -364,8 +406,6 @@ def gemm_roofline(w, rows: int, dev) -> dict:
         out[name] = {"us": t * 1e6, "gbs": nbytes / t / 1e9, "bytes": nbytes}
     del kc
     # lm_head + argmax over the full vocabulary (1 GB, > L2)
-    from ssd.models import runner as R
-
     graph = torch.cuda.CUDAGraph()
     R.head_argmax(w, x_d, w.lm_head, idx, ws)
     torch.cuda.synchronize(dev)
@@ -385,8 +425,8 @@ def gemm_roofline(w, rows: int, dev) -> dict:
     out["lm_head_argmax"] = {"us": t * 1e6, "gbs": nb / t / 1e9, "bytes": nb}
     total_b += nb
     total_t += t
-    return {"per_type": out, "bytes": total_b, "seconds": total_t, "launches": 4 * w.L + 1,
-            "gbs": total_b / total_t / 1e9}
+    return {"per_type": out, "bytes": total_b, "seconds": total_t, "launches": (w.L if chained else 4 * w.L) + 1,
+            "gbs": total_b / total_t / 1e9, "chained": chained}
 
 
 # ------------------------------------------------------------- CPU baseline
@@ -1149,7 +1189,9 @@ def main() -> None:
                     "d2h_bytes_per_step": int(d2h),
                     "note": "SpeculativeGenerator.generate per sequence: H2D prompt, prefill, decode, D2H tokens"},
             "gpu_launches": gpu_launches,
-            "roofline": {"kernel": "tc_gemm_kernel (verify-forward GEMM mix + lm_head argmax)", "bound": "hbm",
+            "roofline": {"kernel": ("tc_chain_kernel (one launch per layer: o_proj, gate/up, down, next q/k/v) + "
+                                    "tc_gemm_kernel lm_head argmax" if roof and roof.get("chained") else
+                                    "tc_gemm_kernel (verify-forward GEMM mix + lm_head argmax)"), "bound": "hbm",
                          "achieved": roof["gbs"] if roof else None, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": (roof["gbs"] / peaks["hbm_gbs"]) if roof else None,
                          "traffic": traffic,

@@ -143,6 +143,57 @@ int ssd_qkv_rope(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w
                  int64_t cache_head_stride, int64_t max_slots, void* q_out, int64_t ldq, int dtype, void* workspace,
                  int64_t workspace_bytes, const SsdRowNorm* in_norm, uint32_t* status, void* stream);
 
+/* One GEMM of ssd_linear_chain. With epilogue SSD_EPI_STORE, _RESIDUAL,
+ * _SWIGLU or _STORE_F32 the fields mean what the arguments of ssd_linear
+ * mean (in_norm.ssq / norm_out.weight NULL: no folding). With SSD_EPI_QKV it
+ * is ssd_qkv_rope: w = {wq, wk, wv}, rows and seg_layout are derived from
+ * the head counts, out / ldo are q_out / ldq, and the fields after norm_out
+ * carry the RoPE tables, positions, cache slots and caches. */
+enum { SSD_EPI_QKV = 16 };
+typedef struct SsdLinearArgs {
+  const void* x;
+  int64_t ldx;
+  int64_t K;
+  int32_t n_seg;
+  int32_t seg_layout;
+  const void* w[3];
+  int64_t rows[3];
+  const void* bias[3];
+  int32_t epilogue;
+  int32_t act;
+  void* out;
+  int64_t ldo;
+  float* resid;
+  int64_t ldr;
+  SsdRowNorm in_norm;
+  SsdNormOut norm_out;
+  int64_t n_heads, n_kv_heads, head_dim;
+  const float* rope_cos;
+  const float* rope_sin;
+  int64_t max_pos;
+  const int32_t* positions;
+  const int32_t* slots;
+  void* k_cache;
+  void* v_cache;
+  int64_t cache_head_stride;
+  int64_t max_slots;
+} SsdLinearArgs;
+
+/* n (1..6) dependent GEMMs over the same T token rows (bf16, T <= 64) in
+ * one persistent launch: link i may read what links < i wrote (its x, the
+ * residual, the folded-norm sums), and every link reads only data that the
+ * previous kernel in the stream or earlier links wrote. Same results as
+ * calling ssd_linear / ssd_qkv_rope for each link in turn, up to the
+ * summation order of the K splits (fixed by the weight shapes and the SM
+ * count, never by T). For the decode-time layer sequence o_proj -> gate/up
+ * -> down -> next layer's q/k/v (subnetwork_draft.py:209-246): the weights
+ * of link i + 1 stream into shared memory while link i finishes, which
+ * separate launches cannot do. Needs ssd_workspace_bytes(>= T, ...) of
+ * workspace; after a status with the timeout bit set, zero the workspace
+ * again before the next call. */
+int ssd_linear_chain(int32_t n, const SsdLinearArgs* links, int64_t T, int dtype, void* workspace,
+                     int64_t workspace_bytes, uint32_t* status, void* stream);
+
 /* Tree attention over the shared cache (split-KV, GQA). Row t attends cache
  * slots [prefix_start[t], prefix_len[t]) (prefix_start NULL: from slot 0;
  * batched decoding gives each sequence its own slot range) and, if spec_mask

@@ -740,6 +740,7 @@ constexpr int kTcTwoGroupsMinBlocks = 12;
 struct AttnMaps {
   CUtensorMap k;  // [n_kv * max_slots, hd] bf16, box {64, 64}
   CUtensorMap v;
+  CUtensorMap q;  // [T][n_heads][hd] bf16 (token stride ldq), box {64, G, 128 / G}: 128 query rows
 };
 
 template <int HD>
@@ -811,7 +812,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
       mbar_init(&p_free[i], 1);
     }
     mbar_init(o_full, 1);
-    mbar_init(q_ready, kTcAttnThreads / 32 - 1);  // warps 1.. have staged their Q rows
+    mbar_init(q_ready, 1);  // the Q boxes landed
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -821,6 +822,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&maps.k);
     tma_prefetch_desc(&maps.v);
+    tma_prefetch_desc(&maps.q);
   }
   tc_fence_before();
   __syncthreads();  // barriers, TMEM and the meta accumulators are initialised
@@ -828,6 +830,17 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // Q, the new K/V rows and the row metadata come from earlier kernels
   pdl_trigger();
+  if (warp == 0 && lane == 0) {
+    // Q rows (A operand, K-major, 128-byte swizzle): one 3-D box per 64
+    // columns lands tokens t_first.. x the head group's G heads as rows
+    // r = token * G + head (row groups start on a token); rows past the
+    // tensor are zero, rows past Mg are masked in the softmax.
+    const int qrows = (128 / a.G) * a.G;
+    mbar_arrive_expect_tx(q_ready, NR * qrows * 128);
+#pragma unroll
+    for (int g = 0; g < NR; ++g)
+      tma_load_3d(qs + g * (128 * 128), &maps.q, q_ready, g * 64, h * a.G, t_first, l2_policy_evict_first());
+  }
   const int sb = a.spec_base ? a.spec_base[0] : 0;
   const int mw = a.mask ? a.mask_words : 0;
   for (int i = threadIdx.x; i < ntok; i += blockDim.x) {
@@ -852,21 +865,6 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   const int nblocks = k_hi > k_lo ? (k_hi - k_lo + KB - 1) / KB : 0;
   const bool two = nblocks >= kTcTwoGroupsMinBlocks;  // CTA-uniform
   const uint32_t qs_s = smem_u32(qs), ring_s = smem_u32(ring), ps_s = smem_u32(ps);
-  if (warp >= 1) {
-    // Q rows (A operand, K-major, 128-byte swizzle; rows past Mg are zero),
-    // staged by warps 1..5 while warp 0 already streams K/V.
-    const bf16* qb = static_cast<const bf16*>(a.q);
-    for (int idx = threadIdx.x - 32; idx < 128 * (HD / 8); idx += kTcAttnThreads - 32) {
-      const int r = idx / (HD / 8), c = idx % (HD / 8);
-      const int qr = q0 + (r < Mg ? r : 0);
-      const bf16* src = qb + (int64_t)(qr / a.G) * a.ldq + (int64_t)(h * a.G + qr % a.G) * HD + c * 8;
-      cp_async16(qs_s + (c >> 3) * (128 * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4), src, r < Mg);
-    }
-    cp_async_wait_all();
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(q_ready);
-  }
   // TMEM columns: S buffers [0, 64) and [64, 128), O accumulators of the
   // even and odd key blocks at [128, 128 + HD) and [256, 256 + HD)
   const uint32_t tm_o = tmem + 128;
@@ -914,46 +912,53 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
         report_error(a.status, kErrWaitTimeout);
         *abort_flag = 1;
       }
-      auto pv = [&](int j) {
-        if (!ok) return;
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1) || *abort_flag) {
+      // S = Q K^T of block b needs its K block and a free S buffer (the
+      // softmax of block b - 2 has loaded its scores); O += P V of block b
+      // needs its P. Neither waits for the other: the thread polls both and
+      // issues whichever is ready, so the scores of the next blocks are
+      // computed while the softmax warps still work on earlier ones. (Each
+      // barrier can be at most one phase ahead of the one tested: its next
+      // phase needs an MMA this thread has not issued yet.)
+      int nS = 0, nP = 0;
+      uint32_t idle = 0;
+      while (ok && nP < nblocks) {
+        bool prog = false;
+        if (nS < nblocks && mbar_test(&kv_full[nS % kTcAttnStages], (nS / kTcAttnStages) & 1) &&
+            (nS < 2 || mbar_test(&s_free[nS & 1], ((nS >> 1) - 1) & 1))) {
+          tc_fence_after();
+          const uint32_t kb = ring_s + (nS % kTcAttnStages) * Lay::STAGE;
+#pragma unroll
+          for (int ks = 0; ks < HD / 16; ++ks) {
+            const uint32_t off = (ks & 3) * 32;
+            umma_bf16(tmem + (nS & 1) * KB, sdesc_k_sw128(qs_s + (ks >> 2) * (128 * 128) + off),
+                      sdesc_k_sw128(kb + (ks >> 2) * Lay::KV_REGION + off), id_s, ks > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[nS & 1]);
+          ++nS;
+          prog = true;
+        }
+        if (nP < nS && mbar_test(&p_full[nP & 1], (nP >> 1) & 1)) {
+          tc_fence_after();
+          const int j = nP;
+          const uint32_t vb = ring_s + (j % kTcAttnStages) * Lay::STAGE + NR * Lay::KV_REGION;
+          const uint32_t pb = ps_s + (j & 1) * Lay::P_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < KB / 16; ++kk)
+            umma_bf16(tm_o + (two ? (j & 1) * 128 : 0), sdesc_k_sw128(pb + kk * 32),
+                      sdesc_mn_sw128(vb + kk * 2048, Lay::KV_REGION, 1024), id_pv,
+                      (j > (two ? 1 : 0) || kk > 0) ? 1u : 0u);
+          umma_commit(&p_free[j & 1]);
+          umma_commit(&kv_empty[j % kTcAttnStages]);
+          ++nP;
+          prog = true;
+        }
+        idle = prog ? 0u : idle + 1u;
+        if (idle > 4u * kWaitLimit || *abort_flag) {
           report_error(a.status, kErrWaitTimeout);
           *abort_flag = 1;
           ok = false;
-          return;
         }
-        tc_fence_after();
-        const uint32_t vb = ring_s + (j % kTcAttnStages) * Lay::STAGE + NR * Lay::KV_REGION;
-        const uint32_t pb = ps_s + (j & 1) * Lay::P_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < KB / 16; ++kk)
-          umma_bf16(tm_o + (two ? (j & 1) * 128 : 0), sdesc_k_sw128(pb + kk * 32),
-                    sdesc_mn_sw128(vb + kk * 2048, Lay::KV_REGION, 1024), id_pv,
-                    (j > (two ? 1 : 0) || kk > 0) ? 1u : 0u);
-        umma_commit(&p_free[j & 1]);
-        umma_commit(&kv_empty[j % kTcAttnStages]);
-      };
-      for (int b = 0; b < nblocks && ok; ++b) {
-        const int st = b % kTcAttnStages;
-        if (!mbar_wait(&kv_full[st], (b / kTcAttnStages) & 1) ||
-            (b >= 2 && !mbar_wait(&s_free[b & 1], ((b >> 1) - 1) & 1)) || *abort_flag) {
-          report_error(a.status, kErrWaitTimeout);
-          *abort_flag = 1;
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t kb = ring_s + st * Lay::STAGE;
-#pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
-          const uint32_t off = (ks & 3) * 32;
-          umma_bf16(tmem + (b & 1) * KB, sdesc_k_sw128(qs_s + (ks >> 2) * (128 * 128) + off),
-                    sdesc_k_sw128(kb + (ks >> 2) * Lay::KV_REGION + off), id_s, ks > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[b & 1]);
-        if (b >= 1) pv(b - 1);
       }
-      if (nblocks > 0) pv(nblocks - 1);
       // Arrives once every MMA above has retired (also after an abort).
       umma_commit(o_full);
     }
@@ -1354,9 +1359,13 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
       attn_use_tcgen05()) {
     // tcgen05 path: up to 128 query rows of a KV head per CTA (one M = 128
     // tile), key slices merged in a cluster or through global memory.
+    // Row groups start on a token (rows_per_group a multiple of G), so one
+    // 3-D TMA box of 128 / G tokens x G heads holds a group's Q rows.
     const int64_t M = T * a.G;
-    a.groups = (int)((M + 127) / 128);
-    a.rows_per_group = (int)((M + a.groups - 1) / a.groups);
+    const int64_t tok_per_tile = 128 / a.G;
+    if (tok_per_tile < 1) return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: more than 128 heads per KV head");
+    a.groups = (int)((T + tok_per_tile - 1) / tok_per_tile);
+    a.rows_per_group = (int)(((T + a.groups - 1) / a.groups) * a.G);
     a.rt = 8;
     a.kw = 1;
     const int64_t blocks = (int64_t)a.n_kv * a.groups;
@@ -1372,6 +1381,20 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
     if (rc) return rc;
     if (cache_head_stride != max_slots * head_dim)
       return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: K/V heads must be contiguous [n_kv, max_slots, hd]");
+    if ((reinterpret_cast<uintptr_t>(q) & 15) || (ldq * 2) % 16)
+      return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: q rows must be 16-byte aligned");
+    {
+      TensorMapEncodeFn encode = tensor_map_encoder();
+      if (!encode) return fail(SSD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+      cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)n_heads, (cuuint64_t)T};
+      cuuint64_t strides[2] = {(cuuint64_t)head_dim * 2, (cuuint64_t)ldq * 2};
+      cuuint32_t box[3] = {64u, (cuuint32_t)a.G, (cuuint32_t)tok_per_tile};
+      cuuint32_t estr[3] = {1u, 1u, 1u};
+      const CUresult r = encode(&maps.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box,
+                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) return fail(SSD_ERR_CUDA, "ssd_tree_attention: Q tensor map (%d)", (int)r);
+    }
     const size_t smem = head_dim == 128 ? TcAttnLayout<128>::SMEM : TcAttnLayout<64>::SMEM;
     void (*kern)(const AttnMaps, const AttnArgs) = head_dim == 128 ? attn_tc_kernel<128> : attn_tc_kernel<64>;
     static bool tset128 = false, tset64 = false;

@@ -1,4 +1,5 @@
 // Mainloops and host launcher of the skinny GEMM family (see gemm.cuh).
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -585,6 +586,415 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ------------------------------------------------------- tcgen05, GEMM chain
+// Up to kChainMax dependent decode-sized GEMMs of one forward (for example
+// o_proj -> gate/up -> down -> the next layer's q/k/v) in one persistent
+// launch, every CTA resident. Each link is cut like the stream-K kernel: the
+// link's tiles_m x kchunks iterations in G equal contiguous ranges, one per
+// CTA; a CTA runs its range of link 0, then its range of link 1, and so on.
+// The weight stream never waits on a dependency: when a CTA moves to the
+// next link its producer fills the free ring stages with that link's weight
+// boxes while the previous link's last tiles are still being reduced, and
+// only the activation boxes (the previous link's output) wait until every
+// CTA has finished the previous link (done[l] counts CTAs; release stores,
+// acquire polls). Split tiles are summed in K order through two partial
+// slots per CTA as in the stream-K kernel, so each result depends only on
+// the weight shapes and the grid, never on the token count.
+constexpr int kChainMax = 6;
+constexpr int kChainThreads = 256;  // warps: 0 activation TMA, 1 MMA, 2-5 epilogue, 6-7 weight TMA
+constexpr int kChainTiles = 1024;                // weight tiles per link (counter slots)
+constexpr int64_t kChainCounterBase = 16384;     // first workspace counter of the chain block
+constexpr int64_t kChainCounters = kChainMax * 2 * kChainTiles + kChainMax + 1;
+
+struct ChainLink {
+  TcMaps maps;
+  GemmShape g;
+  EpiArgs e;
+};
+struct ChainParams {
+  ChainLink link[kChainMax];
+  int n;
+  int BN, stages;
+  // [kChainMax][2][kChainTiles] arrived / finished per tile, then
+  // done[kChainMax] (CTAs that finished link l), then the exit count
+  uint32_t* counters;
+  float* partials;  // [2 G][BN][128] partial slots, shared by the links
+  uint32_t* status;
+};
+
+// A link of W iterations runs on its first min(G, W) CTAs (every one of
+// them then holds at least one iteration, which the split bookkeeping
+// needs); the other CTAs have an empty range for it.
+__device__ __forceinline__ int chain_ctas(int64_t W, int G) { return W < G ? (int)W : G; }
+__device__ __forceinline__ int64_t chain_begin(int c, int64_t W, int Gl) {
+  return c >= Gl ? W : sk_begin(c, W, Gl);
+}
+
+// Bounded poll until *p >= want (acquire at GPU scope).
+__device__ __forceinline__ bool poll_at_least(const uint32_t* p, uint32_t want) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (ld_acquire_u32(p) >= want) return true;
+    if (i > 64) __nanosleep(128);
+  }
+  return false;
+}
+
+__global__ void __launch_bounds__(kChainThreads, 1) tc_chain_kernel(const __grid_constant__ ChainParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int BN = P.BN, stages = P.stages;
+  const int stage_bytes = tc_stage_bytes(BN);
+  float* stage = reinterpret_cast<float*>(smem + stages * stage_bytes);
+  uint8_t* bar_base = smem + stages * stage_bytes + BN * kTileM * 4;
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(bar_base);  // weight boxes of stage s landed
+  uint64_t* full_b = full_a + stages;                          // activation box of stage s landed
+  uint64_t* empty = full_b + stages;
+  uint64_t* accf = empty + stages;  // [2] accumulator buffer b holds a finished segment
+  uint64_t* acce = accf + 2;        // [2] accumulator buffer b drained by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+  volatile int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  // Shapes and epilogue arguments of the links, copied out of the parameter
+  // space once: indexed by a runtime link number they would otherwise be
+  // read through generic loads on every use.
+  __shared__ GemmShape s_g[kChainMax];
+  __shared__ EpiArgs s_e[kChainMax];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x, cta = blockIdx.x;
+  const uint32_t cols = tc_tmem_cols(BN);
+  uint32_t* done = P.counters + kChainMax * 2 * kChainTiles;
+  uint32_t* exit_count = done + kChainMax;
+  if (threadIdx.x < P.n) {
+    s_g[threadIdx.x] = P.link[threadIdx.x].g;
+    s_e[threadIdx.x] = P.link[threadIdx.x].e;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full_a[s], 1);
+      mbar_init(&full_b[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // One thread issues a TMA box stream at ~40-50 GB/s on B200, under the
+  // ~43 GB/s an SM needs for the HBM peak once the activation boxes are
+  // added, so the weight boxes of alternate stages come from two threads
+  // in two warps (6, 7) and the activation boxes from a third (warp 0); each
+  // completes on its own barrier. Only the activation stream waits for
+  // dependencies: the weight streams run ahead into the next link as far
+  // as the ring allows.
+  if (warp >= 6 || warp == 0) {
+    if (lane == 0) {
+      const bool wproducer = warp >= 6;
+      const int k = warp - 6;  // weight stream: positions pos with pos % 2 == k
+      if (wproducer) {
+        for (int l = 0; l < P.n; ++l)
+          for (int i = 0; i < P.link[l].g.n_seg; ++i) tma_prefetch_desc(&P.link[l].maps.w[i]);
+      } else {
+        for (int l = 0; l < P.n; ++l) tma_prefetch_desc(&P.link[l].maps.x);
+      }
+      const uint64_t pol = wproducer ? l2_policy_evict_first() : l2_policy_evict_last();
+      const uint32_t b_tx = BN * kChunkK * 2;
+      int pos = 0;  // ring positions (stages) of all links so far
+      int issued_to = 0;  // positions below this one this thread has issued (or skipped)
+      bool ok = true;
+      for (int l = 0; l < P.n && ok; ++l) {
+        const TcMaps& maps = P.link[l].maps;
+        const GemmShape& g = s_g[l];
+        const int kchunks = g.kchunks, layout = g.layout, a_box = g.a_box, n_seg = g.n_seg;
+        const int seg1 = g.seg_start[1], seg2 = g.seg_start[2];
+        const int64_t W = (int64_t)g.tiles_m * kchunks;
+        const int Gl = chain_ctas(W, G);
+        const int64_t it0 = chain_begin(cta, W, Gl), it1 = chain_begin(cta + 1, W, Gl);
+        const int n = (int)(it1 - it0);
+        if (n == 0) continue;
+        if (!wproducer) {
+          // Activations: link 0 reads the predecessor kernel's output, link
+          // l > 0 the output of link l - 1 from every CTA.
+          pdl_wait();  // returns at once after the first time
+          if (l > 0) {
+            ok = poll_at_least(&done[l - 1], (uint32_t)G);
+            fence_proxy_async_global();
+            if (!ok) break;
+          }
+        }
+        for (int j = 0; j < n; ++j, ++pos) {
+          if (wproducer && (pos & 1) != k) continue;
+          const int s = pos % stages;
+          if ((pos >= stages && !mbar_wait(&empty[s], ((pos / stages) - 1) & 1)) || *abort_flag) {
+            ok = false;
+            break;
+          }
+          const int64_t it = it0 + j;
+          const int tile = (int)(it / kchunks);
+          const int kc = (int)(it - (int64_t)tile * kchunks);
+          uint8_t* st = smem + s * stage_bytes;
+          if (wproducer) {
+            mbar_arrive_expect_tx(&full_a[s], kABytes);
+            for (int box = 0; box < kTileM / a_box; ++box) {
+              int seg, row;
+              if (layout == SSD_SEG_PAIRS) {
+                if (a_box == 64) {
+                  seg = box;
+                  row = tile * 64;
+                } else {
+                  seg = box >> 1;
+                  row = tile * 64 + (box & 1) * 32;
+                }
+              } else {
+                const int nn = tile * kTileM + box * a_box;
+                seg = (n_seg > 2 && nn >= seg2) ? 2 : ((n_seg > 1 && nn >= seg1) ? 1 : 0);
+                row = nn - (seg == 2 ? seg2 : (seg == 1 ? seg1 : 0));  // rows past the end are zero-filled
+              }
+              tma_load_2d(st + box * a_box * 128, &maps.w[seg], &full_a[s], kc * kChunkK, row, pol);
+            }
+          } else {
+            mbar_arrive_expect_tx(&full_b[s], b_tx);
+            tma_load_2d(st + kABytes, &maps.x, &full_b[s], kc * kChunkK, 0, pol);
+          }
+          issued_to = pos + 1;
+        }
+      }
+      if (!ok) {
+        report_error(P.status, kErrWaitTimeout);
+        *abort_flag = 1;
+        // every copy this thread issued must land before the CTA exits
+        for (int i = (issued_to > stages ? issued_to - stages : 0); i < issued_to; ++i)
+          if (!wproducer || (i & 1) == k) (void)mbar_wait(&(wproducer ? full_a : full_b)[i % stages], (i / stages) & 1);
+      }
+      if (!wproducer) {
+        pdl_wait();  // (a CTA without work still triggers only after its wait)
+        pdl_trigger();
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kTileM, BN);
+      bool ok = true;
+      int i = 0, seg = 0;
+      for (int l = 0; l < P.n && ok; ++l) {
+        const int kchunks = s_g[l].kchunks;
+        const int64_t W = (int64_t)s_g[l].tiles_m * kchunks;
+        const int Gl = chain_ctas(W, G);
+      const int64_t it0 = chain_begin(cta, W, Gl), it1 = chain_begin(cta + 1, W, Gl);
+        for (int64_t it = it0; it < it1 && ok; ++seg) {
+          const int tile = (int)(it / kchunks);
+          const int64_t seg_end = min(it1, (int64_t)(tile + 1) * kchunks);
+          const int b = seg & 1;
+          if (seg >= 2 && !mbar_wait(&acce[b], ((seg >> 1) - 1) & 1)) {
+            report_error(P.status, kErrWaitTimeout);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + b * cols;
+          const int64_t seg_begin = it;
+          for (; it < seg_end; ++it, ++i) {
+            const int s = i % stages;
+            if (*abort_flag || !mbar_wait(&full_a[s], (i / stages) & 1) || !mbar_wait(&full_b[s], (i / stages) & 1)) {
+              report_error(P.status, kErrWaitTimeout);
+              *abort_flag = 1;  // before the commit below, so the epilogue sees it
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a = smem_u32(smem + s * stage_bytes);
+            const uint32_t bb = a + kABytes;
+#pragma unroll
+            for (int kk = 0; kk < kChunkK / 16; ++kk)
+              umma_bf16(d, sdesc_k_sw128(a + kk * 32), sdesc_k_sw128(bb + kk * 32), idesc,
+                        (it != seg_begin || kk != 0) ? 1u : 0u);
+            umma_commit(&empty[s]);
+          }
+          // Arrives when every MMA issued so far has retired (also on abort).
+          umma_commit(&accf[b]);
+        }
+      }
+    }
+  } else if (warp >= 2 && warp <= 5) {
+    // Epilogue warps 2..5 (TMEM lanes 32*(w%4)..+31), per link as in the
+    // stream-K kernel, then one count of this CTA into done[l].
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    pdl_wait();  // the epilogues write buffers earlier kernels may still read
+    bool failed = false;
+    int seg = 0;
+    for (int l = 0; l < P.n && !failed; ++l) {
+      const GemmShape& g = s_g[l];
+      const EpiArgs& e = s_e[l];
+      const int ncols = min(BN, g.T);
+      const int64_t W = (int64_t)g.tiles_m * g.kchunks;
+      const int Gl = chain_ctas(W, G);
+      const int64_t it0 = chain_begin(cta, W, Gl), it1 = chain_begin(cta + 1, W, Gl);
+      uint32_t* arrived = P.counters + (int64_t)l * 2 * kChainTiles;
+      uint32_t* finished = arrived + kChainTiles;
+      if (l > 0) {
+        // The epilogue reads what link l - 1 wrote (residual rows, norm sums).
+        bool ok = true;
+        if (r == 0) ok = poll_at_least(&done[l - 1], (uint32_t)G);
+        if (named_bar_or(1, 128, !ok)) {
+          if (r == 0) {
+            report_error(P.status, kErrWaitTimeout);
+            *abort_flag = 1;
+          }
+          failed = true;
+          break;
+        }
+      }
+      int split_tile[2] = {-1, -1};
+      int n_split = 0, lseg = 0;
+      for (int64_t it = it0; it < it1; ++seg, ++lseg) {
+        const int tile = (int)(it / g.kchunks);
+        const int64_t tile_begin = (int64_t)tile * g.kchunks;
+        const int64_t seg_end = min(it1, tile_begin + g.kchunks);
+        const bool whole = (it == tile_begin) && (seg_end == tile_begin + g.kchunks);
+        const int b = seg & 1;
+        bool bad = !mbar_wait(&accf[b], (seg >> 1) & 1);
+        tc_fence_after();
+        bad = named_bar_or(1, 128, bad || *abort_flag != 0);
+        if (bad) {
+          if (r == 0) {
+            report_error(P.status, kErrWaitTimeout);
+            *abort_flag = 1;
+          }
+          failed = true;
+          break;
+        }
+        const uint32_t src = tmem + b * cols + (static_cast<uint32_t>(q * 32) << 16);
+        if (whole) {
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+            tmem_ld16(src + c0, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (c0 + i < ncols) stage[(c0 + i) * kTileM + r] = v[i];
+          }
+          tc_fence_before();
+          named_bar_sync(1, 128);
+          if (r == 0) mbar_arrive(&acce[b]);  // TMEM buffer b may take segment seg + 2
+          run_epilogue<bf16>(stage, tile, 0, ncols, g, e, r, 1);
+          named_bar_sync(1, 128);  // the stage is reused by the next segment
+        } else {
+          float* mine = P.partials + (int64_t)(2 * cta + (lseg == 0 ? 0 : 1)) * kTileM * BN + r;
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+            tmem_ld16(src + c0, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (c0 + i < ncols) __stcg(mine + (c0 + i) * kTileM, v[i]);
+          }
+          tc_fence_before();
+          __threadfence();
+          named_bar_sync(1, 128);
+          if (r == 0) {
+            mbar_arrive(&acce[b]);
+            atomicAdd(&arrived[tile], 1u);
+          }
+          split_tile[n_split++] = tile;
+        }
+        it = seg_end;
+      }
+      // Finish the split tiles: participant j of P owns token columns j,
+      // j + P, ...; it sums the P partials of those columns in K order.
+      for (int k = 0; k < n_split && !failed; ++k) {
+        const int tile = split_tile[k];
+        const int64_t tile_begin = (int64_t)tile * g.kchunks;
+        const int first = sk_cta_of(tile_begin, W, Gl);
+        const int last = sk_cta_of(tile_begin + g.kchunks - 1, W, Gl);
+        const int np = last - first + 1;
+        const int j = cta - first;
+        bool ok = true;
+        if (r == 0) ok = poll_at_least(&arrived[tile], (uint32_t)np);
+        if (named_bar_or(1, 128, !ok)) {
+          if (r == 0) {
+            report_error(P.status, kErrWaitTimeout);
+            *abort_flag = 1;
+          }
+          failed = true;
+          break;
+        }
+        __threadfence();
+        const int first_slot = 2 * first + (sk_begin(first, W, Gl) == tile_begin ? 0 : 1);
+        const int n_own = (ncols - j + np - 1) / np;
+        const int total = n_own * np;
+        for (int m0 = 0; m0 < total; m0 += 32) {
+          float v[32];
+#pragma unroll
+          for (int u = 0; u < 32; ++u) {
+            const int m = m0 + u;
+            v[u] = 0.f;
+            if (m < total) {
+              const int pi = m % np;
+              const int col = j + (m / np) * np;
+              const int slot = pi == 0 ? first_slot : 2 * (first + pi);
+              v[u] = __ldcg(P.partials + (int64_t)slot * kTileM * BN + col * kTileM + r);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 32; ++u) {
+            const int m = m0 + u;
+            if (m < total) {
+              const int pi = m % np;
+              float* dst = stage + (j + (m / np) * np) * kTileM + r;
+              *dst = (pi == 0 ? 0.f : *dst) + v[u];
+            }
+          }
+        }
+        named_bar_sync(1, 128);
+        run_epilogue<bf16>(stage, tile, 0, ncols, g, e, r, 1, j, np);
+        named_bar_sync(1, 128);
+        if (r == 0) {
+          const unsigned t = atomicAdd(&finished[tile], 1u);
+          if ((int)t == np - 1) {  // every participant has read the partials: reset for the next launch
+            arrived[tile] = 0u;
+            finished[tile] = 0u;
+          }
+        }
+      }
+      if (failed) break;
+      // This CTA's share of link l is written: publish it (generic stores
+      // before later TMA reads of them on other CTAs).
+      __threadfence();
+      fence_proxy_async_global();
+      named_bar_sync(1, 128);
+      if (r == 0) atomicAdd(&done[l], 1u);
+    }
+    if (r == 0) {
+      // The last CTA out resets the link counts for the next launch: every
+      // CTA has passed all its polls of them by the time it counts here.
+      __threadfence();
+      const unsigned t = atomicAdd(exit_count, 1u);
+      if ((int)t == G - 1 && !failed) {
+        for (int l = 0; l < kChainMax; ++l) done[l] = 0u;
+        __threadfence();
+        *exit_count = 0u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * cols);
+  }
+}
+
 // ------------------------------------------------------------------ SIMT path
 // CUDA-core mainloop for the fp32 parity tier: 256 threads = 8 warps x 16
 // feature rows; lanes stride K (coalesced weight rows), 4 tokens per tile.
@@ -996,6 +1406,137 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
   }
   return launch_kernel("simt_gemm_kernel", simt_gemm_kernel<float>, grid, dim3(256), 0, stream, 1u, 1u,
                        static_cast<const float*>(x), ldx, segs, g, e);
+}
+
+
+// ------------------------------------------------------- GEMM chain launch
+// One CTA per SM: a chain CTA runs 256 threads at up to 129 registers, so
+// two would not fit the register file.
+static int chain_ctas_per_sm() { return 1; }
+// static shared memory of tc_chain_kernel (link shapes and epilogue
+// arguments, the epilogue's row-norm scales), rounded up
+constexpr int kChainStaticSmem = 4096;
+static_assert(kChainMax * (sizeof(GemmShape) + sizeof(EpiArgs)) + 1024 <= kChainStaticSmem, "chain static smem");
+static int chain_stages(int BN, int per_sm) {
+  // per CTA: 1 KB reserved by the system, 1 KB of static shared memory (the
+  // epilogue's row-norm scales), alignment slack, barriers, the fp32 stage
+  const int budget = (233472 - per_sm * 2048) / per_sm - kChainStaticSmem - kSkBarBytes;
+  const int st = (budget - BN * kTileM * 4) / tc_stage_bytes(BN);
+  return st > 16 ? 16 : st;
+}
+static size_t chain_smem_bytes(int BN, int stages) {
+  return 1024 + (size_t)stages * tc_stage_bytes(BN) + (size_t)BN * kTileM * 4 + kSkBarBytes;
+}
+static_assert(sizeof(ChainParams) <= 32000, "chain parameters exceed the kernel parameter space");
+
+// Grid of the chain kernel on this device: every CTA must be resident at
+// once (CTAs wait on each other's counts), so the grid is what fits.
+// The grid depends on the SM count only (not on T), so
+// the K splits, and with them every row's rounding, are the same for every
+// token count.
+static_assert(kChainCounterBase + kChainCounters <= kMaxCounters / 2, "chain counters overlap the stream-K ones");
+// Residency holds by construction: chain_stages sizes the shared memory so
+// one CTA fits an SM, 256 threads x <= 255 registers fit the register file,
+// and 2 x 128 TMEM columns fit TMEM. (No occupancy
+// query: the first call may come during a stream capture.)
+static int chain_grid(int BN, int* stages_out) {
+  static bool attr = false;
+  if (!attr) {
+    allow_max_dynamic_smem(tc_chain_kernel);
+    attr = true;
+  }
+  const int per_sm = chain_ctas_per_sm();
+  const int stages = chain_stages(BN, per_sm);
+  if (stages < 2) return 0;
+  *stages_out = stages;
+  return per_sm * device_sms();
+}
+
+int64_t chain_workspace_need(int64_t T) {
+  if (T <= 0 || T > 64) return -1;
+  const int BN = round_bn(T);
+  int stages = 0;
+  const int G = chain_grid(BN, &stages);
+  if (G <= 0) return -1;
+  return kCounterBytes + 2LL * G * kTileM * BN * 4;
+}
+
+int launch_chain(int n, const ChainLinkHost* links, int64_t T, void* workspace, int64_t workspace_bytes,
+                 uint32_t* status, cudaStream_t stream) {
+  if (n < 1 || n > kChainMax) return fail(SSD_ERR_INVALID, "ssd_linear_chain: 1..%d links", kChainMax);
+  if (T < 1 || T > 64) return fail(SSD_ERR_UNSUPPORTED, "ssd_linear_chain: T must be 1..64");
+  if (!workspace) return fail(SSD_ERR_WORKSPACE, "ssd_linear_chain needs a workspace");
+  ChainParams P;
+  memset(&P, 0, sizeof(P));
+  P.BN = round_bn(T);
+  const int G = chain_grid(P.BN, &P.stages);
+  if (G <= 0) return fail(SSD_ERR_CUDA, "ssd_linear_chain: no resident grid for BN %d", P.BN);
+  const int64_t need = kCounterBytes + 2LL * G * kTileM * P.BN * 4;
+  if (need > workspace_bytes)
+    return fail(SSD_ERR_WORKSPACE, "workspace too small: need %lld bytes", (long long)need);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  P.n = n;
+  P.counters = reinterpret_cast<uint32_t*>(ws) + kChainCounterBase;
+  P.partials = reinterpret_cast<float*>(ws + kCounterBytes);
+  P.status = status;
+  for (int l = 0; l < n; ++l) {
+    const ChainLinkHost& h = links[l];
+    if (!h.x || h.K <= 0 || h.K % 8 || h.n_seg < 1 || h.n_seg > 3)
+      return fail(SSD_ERR_INVALID, "ssd_linear_chain: link %d: bad operands", l);
+    if (h.K > (1 << 20)) return fail(SSD_ERR_UNSUPPORTED, "ssd_linear_chain: link %d: K too large", l);
+    GemmShape& g = P.link[l].g;
+    g.T = (int)T;
+    g.K = (int)h.K;
+    g.n_seg = h.n_seg;
+    g.layout = h.layout;
+    int64_t N = 0;
+    for (int i = 0; i < h.n_seg; ++i) {
+      if (!h.w[i] || h.rows[i] <= 0) return fail(SSD_ERR_INVALID, "ssd_linear_chain: link %d: empty segment", l);
+      g.seg_start[i] = (int)N;
+      N += h.rows[i];
+    }
+    g.seg_start[h.n_seg] = (int)N;
+    if (h.layout == SSD_SEG_PAIRS) {
+      if (h.n_seg != 2 || h.rows[0] != h.rows[1])
+        return fail(SSD_ERR_INVALID, "ssd_linear_chain: link %d: PAIRS needs two equal segments", l);
+      g.N = (int)(h.rows[0] * 2);
+      g.tiles_m = (int)((h.rows[0] + 63) / 64);
+    } else {
+      for (int i = 0; i + 1 < h.n_seg; ++i)
+        if (h.rows[i] % 32)
+          return fail(SSD_ERR_UNSUPPORTED, "ssd_linear_chain: link %d: segments must be multiples of 32 rows", l);
+      g.N = (int)N;
+      g.tiles_m = (int)((N + kTileM - 1) / kTileM);
+    }
+    if (g.tiles_m > kChainTiles) return fail(SSD_ERR_UNSUPPORTED, "ssd_linear_chain: link %d: too many tiles", l);
+    g.kchunks = (int)((h.K + kChunkK - 1) / kChunkK);
+    g.BN = P.BN;
+    g.tiles_n = 1;
+    g.splits = 1;
+    g.stages = P.stages;
+    g.status = status;
+    if (h.layout == SSD_SEG_PAIRS) {
+      g.a_box = 64;
+    } else {
+      bool aligned = true;
+      for (int i = 1; i < h.n_seg; ++i) aligned = aligned && (g.seg_start[i] % kTileM == 0);
+      g.a_box = aligned ? 128 : 32;
+    }
+    for (int i = 0; i < h.n_seg; ++i)
+      if (h.rows[i] < g.a_box) g.a_box = 32;
+    TcMaps& maps = P.link[l].maps;
+    for (int i = 0; i < h.n_seg; ++i) {
+      const int rc = get_map(h.w[i], (uint64_t)h.K, (uint64_t)h.rows[i], (uint64_t)h.K * 2, (uint32_t)g.a_box,
+                             &maps.w[i]);
+      if (rc) return rc;
+    }
+    for (int i = h.n_seg; i < 3; ++i) maps.w[i] = maps.w[0];
+    const int rc = get_map(h.x, (uint64_t)h.K, (uint64_t)T, (uint64_t)h.ldx * 2, (uint32_t)P.BN, &maps.x);
+    if (rc) return rc;
+    P.link[l].e = h.e;
+  }
+  return launch_kernel("tc_chain_kernel", tc_chain_kernel, dim3((unsigned)G), dim3(kChainThreads),
+                       chain_smem_bytes(P.BN, P.stages), stream, 1u, 1u, P);
 }
 
 }  // namespace ssd

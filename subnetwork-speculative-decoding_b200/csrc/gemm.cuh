@@ -23,7 +23,7 @@ enum EpiKind : int {
   EPI_RESIDUAL = SSD_EPI_RESIDUAL,
   EPI_SWIGLU = SSD_EPI_SWIGLU,
   EPI_STORE_F32 = SSD_EPI_STORE_F32,
-  EPI_QKV = 16,
+  EPI_QKV = SSD_EPI_QKV,
   EPI_ARGMAX = 17,
   EPI_TOPK = 18,
 };
@@ -82,6 +82,22 @@ struct GemmShape {
   float* partials;
   uint32_t* status;
 };
+
+// One link of launch_chain (host side): the operands of launch_gemm.
+struct ChainLinkHost {
+  const void* x;
+  int64_t ldx, K;
+  int n_seg, layout;
+  const void* w[3];
+  int64_t rows[3];
+  EpiArgs e;
+};
+// Up to 6 dependent decode-sized bf16 GEMMs (T <= 64) in one persistent
+// launch (tc_chain_kernel); workspace as for launch_gemm.
+int launch_chain(int n, const ChainLinkHost* links, int64_t T, void* workspace, int64_t workspace_bytes,
+                 uint32_t* status, cudaStream_t stream);
+// Workspace bytes launch_chain needs for T rows on the current device.
+int64_t chain_workspace_need(int64_t T);
 
 __device__ __forceinline__ int seg_of(const GemmShape& g, int n) {
   int s = 0;

@@ -1,6 +1,8 @@
 // Layer-level entry points: embedding gather, RMSNorm, the fused linear
 // family (plain / residual / SwiGLU / QKV+RoPE+KV write) and the lm_head
 // heads (argmax for verification, log-softmax top-k for drafting).
+#include <cstring>
+
 #include "gemm.cuh"
 #include "host.cuh"
 
@@ -413,6 +415,84 @@ int ssd_qkv_rope(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w
   int64_t rows[3] = {n_heads * head_dim, n_kv_heads * head_dim, n_kv_heads * head_dim};
   return launch_gemm(x, ldx, T, K, 3, w, rows, SSD_SEG_CONCAT, e, dtype, workspace, workspace_bytes, status,
                      static_cast<cudaStream_t>(stream), 0);
+}
+
+int ssd_linear_chain(int32_t n, const SsdLinearArgs* links, int64_t T, int dtype, void* workspace,
+                     int64_t workspace_bytes, uint32_t* status, void* stream) {
+  if (dtype != SSD_BF16) return fail(SSD_ERR_UNSUPPORTED, "ssd_linear_chain: bf16 only");
+  if (!links || n < 1 || n > 6) return fail(SSD_ERR_INVALID, "ssd_linear_chain: 1..6 links");
+  ChainLinkHost h[6];
+  for (int l = 0; l < n; ++l) {
+    const SsdLinearArgs& a = links[l];
+    ChainLinkHost& c = h[l];
+    memset(&c, 0, sizeof(c));
+    c.x = a.x;
+    c.ldx = a.ldx;
+    c.K = a.K;
+    EpiArgs& e = c.e;
+    e.kind = a.epilogue;
+    e.act = a.act;
+    e.out = a.out;
+    e.ldo = a.ldo;
+    const SsdRowNorm* rn = a.in_norm.ssq ? &a.in_norm : nullptr;
+    const SsdNormOut* no = a.norm_out.weight ? &a.norm_out : nullptr;
+    if (a.epilogue == SSD_EPI_QKV) {
+      const int64_t hd = a.head_dim;
+      if (hd <= 0 || hd > 128 || (128 % hd) || (hd & 1))
+        return fail(SSD_ERR_UNSUPPORTED, "ssd_linear_chain: link %d: head_dim must divide 128", l);
+      if (!a.positions || !a.slots || !a.k_cache || !a.v_cache || !a.out || !a.rope_cos || !a.rope_sin ||
+          !a.w[0] || !a.w[1] || !a.w[2])
+        return fail(SSD_ERR_INVALID, "ssd_linear_chain: link %d: NULL q/k/v argument", l);
+      e.head_dim = (int)hd;
+      e.n_q = (int)(a.n_heads * hd);
+      e.n_kv = (int)(a.n_kv_heads * hd);
+      e.rope_cos = a.rope_cos;
+      e.rope_sin = a.rope_sin;
+      e.max_pos = (int)a.max_pos;
+      e.positions = a.positions;
+      e.slots = a.slots;
+      e.k_cache = a.k_cache;
+      e.v_cache = a.v_cache;
+      e.head_stride = a.cache_head_stride;
+      e.max_slots = (int)a.max_slots;
+      c.n_seg = 3;
+      c.layout = SSD_SEG_CONCAT;
+      for (int i = 0; i < 3; ++i) c.w[i] = a.w[i];
+      c.rows[0] = a.n_heads * hd;
+      c.rows[1] = c.rows[2] = a.n_kv_heads * hd;
+      if (const int rc = set_norms(e, rn, nullptr, dtype, "ssd_linear_chain")) return rc;
+      continue;
+    }
+    switch (a.epilogue) {
+      case SSD_EPI_STORE:
+      case SSD_EPI_STORE_F32:
+        if (!a.out) return fail(SSD_ERR_INVALID, "ssd_linear_chain: link %d: out is NULL", l);
+        break;
+      case SSD_EPI_RESIDUAL:
+        if (!a.resid) return fail(SSD_ERR_INVALID, "ssd_linear_chain: link %d: resid is NULL", l);
+        break;
+      case SSD_EPI_SWIGLU:
+        if (!a.out || a.seg_layout != SSD_SEG_PAIRS)
+          return fail(SSD_ERR_INVALID, "ssd_linear_chain: link %d: SwiGLU needs PAIRS + out", l);
+        break;
+      default:
+        return fail(SSD_ERR_INVALID, "ssd_linear_chain: link %d: unknown epilogue %d", l, a.epilogue);
+    }
+    if (a.seg_layout == SSD_SEG_PAIRS && a.epilogue != SSD_EPI_SWIGLU)
+      return fail(SSD_ERR_INVALID, "ssd_linear_chain: link %d: PAIRS layout is only for SwiGLU", l);
+    if (a.n_seg < 1 || a.n_seg > 3) return fail(SSD_ERR_INVALID, "ssd_linear_chain: link %d: n_seg", l);
+    c.n_seg = a.n_seg;
+    c.layout = a.seg_layout;
+    for (int i = 0; i < 3; ++i) {
+      c.w[i] = i < a.n_seg ? a.w[i] : nullptr;
+      c.rows[i] = i < a.n_seg ? a.rows[i] : 0;
+      e.bias[i] = i < a.n_seg ? a.bias[i] : nullptr;
+    }
+    e.resid = a.resid;
+    e.ldr = a.ldr;
+    if (const int rc = set_norms(e, rn, no, dtype, "ssd_linear_chain")) return rc;
+  }
+  return launch_chain(n, h, T, workspace, workspace_bytes, status, static_cast<cudaStream_t>(stream));
 }
 
 int ssd_head_argmax(const void* x, int64_t ldx, int64_t T, int64_t K, const void* w, int64_t vocab,

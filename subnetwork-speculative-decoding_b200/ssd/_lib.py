@@ -34,6 +34,19 @@ class SsdRowNorm(C.Structure):
     _fields_ = [("ssq", P), ("ld", I64), ("parts", I64), ("d", I64), ("eps", F32)]
 
 
+class SsdLinearArgs(C.Structure):
+    """include/ssd_b200.h SsdLinearArgs: one GEMM of ssd_linear_chain."""
+    _fields_ = [("x", P), ("ldx", I64), ("K", I64), ("n_seg", C.c_int32), ("seg_layout", C.c_int32),
+                ("w", P * 3), ("rows", I64 * 3), ("bias", P * 3), ("epilogue", C.c_int32), ("act", C.c_int32),
+                ("out", P), ("ldo", I64), ("resid", P), ("ldr", I64), ("in_norm", SsdRowNorm),
+                ("norm_out", SsdNormOut), ("n_heads", I64), ("n_kv_heads", I64), ("head_dim", I64),
+                ("rope_cos", P), ("rope_sin", P), ("max_pos", I64), ("positions", P), ("slots", P),
+                ("k_cache", P), ("v_cache", P), ("cache_head_stride", I64), ("max_slots", I64)]
+
+
+EPI_QKV = 16
+CHAIN_MAX = 6
+
 TP_MAX_RANKS = 8
 
 
@@ -58,6 +71,7 @@ SIGNATURES: dict[str, tuple] = {
                            P, I64, P, P, P]),
     "ssd_tree_attention": (I32, [P, I64, I64, I64, I64, I64, P, P, I64, I64, P, P, P, P, I64, I64, P, I64, I32, P,
                                  I64, P, P]),
+    "ssd_linear_chain": (I32, [C.c_int32, P, I64, I32, P, I64, P, P]),
     "ssd_head_argmax": (I32, [P, I64, I64, I64, P, I64, P, P, P, I32, P, I64, P, P, P]),
     "ssd_head_topk": (I32, [P, I64, I64, I64, P, I64, P, I64, P, P, I32, P, I64, P, P, P]),
     "ssd_level_prune": (I32, [P, P, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, I64, P, I32, I64, P, P, P, P, P,

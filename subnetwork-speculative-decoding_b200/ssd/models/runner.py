@@ -13,6 +13,8 @@ reused, so a forward can be captured in a CUDA graph.
 
 from __future__ import annotations
 
+import os
+
 from dataclasses import dataclass
 from typing import Optional
 
@@ -311,11 +313,21 @@ def _norm_chain(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm_brid
     return out
 
 
+def chain_enabled(w: ModelWeights, T: int) -> bool:
+    """Whether a bf16 forward of T rows runs its GEMMs as ssd_linear_chain
+    launches (decode-sized, single GPU; SSD_CHAIN=1 turns it on, SSD_CHAIN=0
+    off; off by default while the separate launches measure faster)."""
+    return (w.dtype == torch.bfloat16 and w.tp is None and 1 <= T <= 64
+            and os.environ.get("SSD_CHAIN", "0") == "1")
+
+
 def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm_bridge, fwd: ForwardInputs, T: int,
                      cache, scratch: Scratch, ws: ops.Workspace, kv_bound: int) -> None:
     """run_stack with every RMSNorm folded into the neighbouring kernels (bf16).
     Leaves resid (pre-norm hidden state), and xn / ssq holding the final
-    norm's folded input for final_norm_folded."""
+    norm's folded input for final_norm_folded. Decode-sized forwards run the
+    GEMMs between two attention launches (o_proj, gate/up, down, bridges, the
+    next layer's q/k/v) as one chained launch."""
     norms = _norm_chain(w, layer_indices, pre_layer_bridges, pre_norm_bridge)
     parts, d = norm_parts(w), w.d
     xg = scratch.xn(w.dtype, d)[:T, :d]
@@ -323,6 +335,7 @@ def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm
     resid = scratch.resid[:T]
     out_for = lambda k: ops.NormOut(norms[k][0], xg, ssq)
     in_for = lambda k: ops.RowNorm(ssq, parts, d, norms[k][1])
+    chain = ops.GemmChain(ws, T, chain_enabled(w, T))
     ops.embed(fwd.ids[:T], w.embed, resid, ws, norm_out=out_for(0))
     if w.tp is not None:
         w.tp.begin()
@@ -330,40 +343,42 @@ def run_stack_folded(w: ModelWeights, layer_indices, pre_layer_bridges, pre_norm
     for slot, li in enumerate(layer_indices):
         b = pre_layer_bridges[slot]
         if b is not None:
-            _bridge_folded(b, scratch, T, ws, xg, in_for(k), out_for(k + 1))
+            _bridge_folded(b, scratch, T, chain, xg, in_for(k), out_for(k + 1))
             k += 1
         lw = w.layers[li]
         kc, vc = cache.layer(li)
-        ops.qkv_rope(xg, lw.q, lw.k, lw.v, w.H, w.Hkv, w.hd, w.rope_cos, w.rope_sin, fwd.positions, fwd.slots, kc, vc,
-                     scratch.q[:T], ws, T=T, in_norm=in_for(k))
+        chain.qkv(xg, lw.q, lw.k, lw.v, w.H, w.Hkv, w.hd, w.rope_cos, w.rope_sin, fwd.positions, fwd.slots, kc, vc,
+                  scratch.q[:T], in_norm=in_for(k))
+        chain.flush()
         ops.tree_attention(scratch.q[:T], kc, vc, w.H, w.Hkv, w.hd, fwd.prefix_len, scratch.attn[:T], ws,
                            spec_base=fwd.spec_base if fwd.use_mask else None,
                            spec_mask=fwd.mask if fwd.use_mask else None, kv_bound=kv_bound, T=T,
                            prefix_start=fwd.prefix_start)
-        _residual_linear(w, scratch.attn[:T], lw.o, ws, resid, out_for(k + 1), T)
+        _residual_linear(w, scratch.attn[:T], lw.o, chain, resid, out_for(k + 1), T)
         hid = scratch.hid(w.dtype, w.F, 0)[:T, : w.F]
-        ops.linear(xg, [lw.gate, lw.up], ws, epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid, in_norm=in_for(k + 1))
-        _residual_linear(w, hid, lw.down, ws, resid, out_for(k + 2), T)
+        chain.linear(xg, [lw.gate, lw.up], epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid, in_norm=in_for(k + 1))
+        _residual_linear(w, hid, lw.down, chain, resid, out_for(k + 2), T)
         k += 2
     if pre_norm_bridge is not None:
-        _bridge_folded(pre_norm_bridge, scratch, T, ws, xg, in_for(k), out_for(k + 1))
+        _bridge_folded(pre_norm_bridge, scratch, T, chain, xg, in_for(k), out_for(k + 1))
         k += 1
+    chain.flush()
     assert k == len(norms) - 1
     if w.tp is not None:
         w.tp.end()
 
 
-def _residual_linear(w: ModelWeights, x, weight, ws: ops.Workspace, resid, norm_out, T: int) -> None:
+def _residual_linear(w: ModelWeights, x, weight, chain: ops.GemmChain, resid, norm_out, T: int) -> None:
     """resid += x @ weight^T (+ the next folded norm input). Tensor parallel:
     weight is this rank's input-feature slice; its partial goes to the
     group's exchange buffer and ssd_tp_allreduce_residual sums the ranks'."""
     if w.tp is None:
-        ops.linear(x, [weight], ws, epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=norm_out)
+        chain.linear(x, [weight], epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=norm_out)
         return
     w.tp.check_rows(T)
     parity = w.tp.next_parity()
-    ops.linear(x, [weight], ws, epilogue=L.EPI_STORE_F32, out=w.tp.partials[parity][:T])
-    ops.tp_allreduce_residual(w.tp, parity, T, resid, ws, norm_out=norm_out, dtype=w.dtype)
+    ops.linear(x, [weight], chain.ws, epilogue=L.EPI_STORE_F32, out=w.tp.partials[parity][:T])
+    ops.tp_allreduce_residual(w.tp, parity, T, resid, chain.ws, norm_out=norm_out, dtype=w.dtype)
 
 
 def head_argmax(w: ModelWeights, x, weight, out_idx, ws: ops.Workspace, out_max=None, out_gap=None,
@@ -386,24 +401,24 @@ def head_topk(w: ModelWeights, x, weight, k: int, out_tok, out_lp, ws: ops.Works
                          in_norm=in_norm)
 
 
-def _bridge_folded(bridge, scratch: Scratch, T: int, ws: ops.Workspace, xg, rn, nout) -> None:
+def _bridge_folded(bridge, scratch: Scratch, T: int, chain: ops.GemmChain, xg, rn, nout) -> None:
     """TransitionBridge x + MLP(RMSNorm(x)) with its RMSNorm folded: xg / rn
     carry the folded input, the out-projection produces the next norm's."""
     dt = bridge.norm.weight.dtype
     mlp = bridge.mlp
     if bridge.mlp_type == "swiglu":
         h = scratch.hid(dt, bridge.hidden, 0)[:T, : bridge.hidden]
-        ops.linear(xg, [mlp.gate_proj.weight, mlp.up_proj.weight], ws, biases=[mlp.gate_proj.bias, mlp.up_proj.bias],
-                   epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=h, in_norm=rn)
+        chain.linear(xg, [mlp.gate_proj.weight, mlp.up_proj.weight], biases=[mlp.gate_proj.bias, mlp.up_proj.bias],
+                     epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=h, in_norm=rn)
     else:
         h = xg
         for i, lin in enumerate(mlp.linears()):
             nxt = scratch.hid(dt, bridge.hidden, i % 2)[:T, : lin.weight.shape[0]]
-            ops.linear(h, [lin.weight], ws, biases=[lin.bias], act=bridge.activation, out=nxt,
-                       in_norm=rn if i == 0 else None)
+            chain.linear(h, [lin.weight], biases=[lin.bias], act=bridge.activation, out=nxt,
+                         in_norm=rn if i == 0 else None)
             h = nxt
-    ops.linear(h, [mlp.out_proj.weight], ws, biases=[mlp.out_proj.bias], epilogue=L.EPI_RESIDUAL,
-               resid=scratch.resid[:T], norm_out=nout)
+    chain.linear(h, [mlp.out_proj.weight], biases=[mlp.out_proj.bias], epilogue=L.EPI_RESIDUAL,
+                 resid=scratch.resid[:T], norm_out=nout)
 
 
 def final_norm_folded(w: ModelWeights, scratch: Scratch, r0: int, r1: int):

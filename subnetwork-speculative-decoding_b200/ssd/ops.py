@@ -135,6 +135,99 @@ def linear(x: torch.Tensor, weights: Sequence[torch.Tensor], ws: Workspace, *, b
            dtype_code(weights[0].dtype), ws.ptr, ws.nbytes, _c(in_norm), _c(norm_out), _p(ws.status), _stream())
 
 
+def _norm_fields(a, in_norm: Optional[RowNorm], norm_out: Optional[NormOut]) -> None:
+    if in_norm is not None:
+        a.in_norm = L.SsdRowNorm(_p(in_norm.ssq), in_norm.ssq.stride(0), in_norm.parts, in_norm.d, in_norm.eps)
+    if norm_out is not None:
+        a.norm_out = L.SsdNormOut(_p(norm_out.weight), _p(norm_out.out), norm_out.out.stride(0), _p(norm_out.ssq),
+                                  norm_out.ssq.stride(0))
+
+
+def linear_args(x: torch.Tensor, weights: Sequence[torch.Tensor], *, biases: Sequence = (),
+                epilogue: int = L.EPI_STORE, act: str = "none", layout: int = L.SEG_CONCAT,
+                out: Optional[torch.Tensor] = None, resid: Optional[torch.Tensor] = None,
+                in_norm: Optional[RowNorm] = None, norm_out: Optional[NormOut] = None) -> L.SsdLinearArgs:
+    """One ssd_linear_chain link with linear()'s arguments."""
+    K = weights[0].shape[1]
+    for w in weights:
+        if w.shape[1] != K or not w.is_contiguous():
+            raise ValueError("weight segments must be contiguous [rows, K]")
+    a = L.SsdLinearArgs()
+    a.x, a.ldx, a.K, a.n_seg, a.seg_layout = _p(x), x.stride(0), K, len(weights), layout
+    for i, w in enumerate(weights):
+        a.w[i], a.rows[i] = w.data_ptr(), w.shape[0]
+    for i, b in enumerate(list(biases)[:3]):
+        a.bias[i] = b.data_ptr() if b is not None else None
+    a.epilogue, a.act = epilogue, L.ACT[act]
+    if out is not None:
+        a.out, a.ldo = _p(out), out.stride(0)
+    if resid is not None:
+        a.resid, a.ldr = _p(resid), resid.stride(0)
+    _norm_fields(a, in_norm, norm_out)
+    return a
+
+
+def qkv_args(x, wq, wk, wv, n_heads, n_kv, head_dim, cos, sin, positions, slots, k_cache, v_cache, q_out,
+             in_norm: Optional[RowNorm] = None) -> L.SsdLinearArgs:
+    """One ssd_linear_chain link with qkv_rope()'s arguments."""
+    a = L.SsdLinearArgs()
+    a.x, a.ldx, a.K, a.epilogue = _p(x), x.stride(0), wq.shape[1], L.EPI_QKV
+    for i, w in enumerate((wq, wk, wv)):
+        a.w[i] = _p(w)
+    a.out, a.ldo = _p(q_out), q_out.stride(0)
+    a.n_heads, a.n_kv_heads, a.head_dim = n_heads, n_kv, head_dim
+    a.rope_cos, a.rope_sin, a.max_pos = _p(cos), _p(sin), cos.shape[0]
+    a.positions, a.slots = _p(positions), _p(slots)
+    a.k_cache, a.v_cache, a.cache_head_stride, a.max_slots = _p(k_cache), _p(v_cache), k_cache.stride(0), \
+        k_cache.shape[1]
+    _norm_fields(a, in_norm, None)
+    return a
+
+
+def linear_chain(links: Sequence[L.SsdLinearArgs], T: int, ws: Workspace) -> None:
+    """Run up to CHAIN_MAX dependent GEMM links over T <= 64 rows in one
+    persistent launch (ssd_linear_chain)."""
+    n = len(links)
+    arr = (L.SsdLinearArgs * n)(*links)
+    L.call("ssd_linear_chain", n, C.cast(arr, C.c_void_p), T, L.SSD_BF16, ws.ptr, ws.nbytes, _p(ws.status),
+           _stream())
+
+
+class GemmChain:
+    """Collects the GEMMs between two non-GEMM kernels of a bf16 decode
+    forward and launches them as ssd_linear_chain links (at most CHAIN_MAX
+    per launch); with `enabled` False every call launches on its own."""
+
+    def __init__(self, ws: Workspace, T: int, enabled: bool):
+        self.ws, self.T, self.enabled = ws, T, enabled and 1 <= T <= 64
+        self.links: list = []
+
+    def linear(self, x, weights, **kw) -> None:
+        if not self.enabled:
+            linear(x, weights, self.ws, T=self.T, **kw)
+            return
+        self._add(linear_args(x, weights, **kw))
+
+    def qkv(self, x, wq, wk, wv, n_heads, n_kv, head_dim, cos, sin, positions, slots, k_cache, v_cache, q_out,
+            in_norm=None) -> None:
+        if not self.enabled:
+            qkv_rope(x, wq, wk, wv, n_heads, n_kv, head_dim, cos, sin, positions, slots, k_cache, v_cache, q_out,
+                     self.ws, T=self.T, in_norm=in_norm)
+            return
+        self._add(qkv_args(x, wq, wk, wv, n_heads, n_kv, head_dim, cos, sin, positions, slots, k_cache, v_cache,
+                           q_out, in_norm=in_norm))
+
+    def _add(self, a) -> None:
+        self.links.append(a)
+        if len(self.links) == L.CHAIN_MAX:
+            self.flush()
+
+    def flush(self) -> None:
+        if self.links:
+            linear_chain(self.links, self.T, self.ws)
+            self.links = []
+
+
 def qkv_rope(x, wq, wk, wv, n_heads, n_kv, head_dim, cos, sin, positions, slots, k_cache, v_cache, q_out,
              ws: Workspace, T: Optional[int] = None, in_norm: Optional[RowNorm] = None) -> None:
     """k_cache/v_cache: [n_kv, max_slots, head_dim] views of one layer."""

@@ -40,6 +40,14 @@ def test_library_rejects_bad_arguments_without_gpu():
                0, None, 0, None, None)
     with pytest.raises(L.SSDError):
         L.call("ssd_kv_compact", None, 1, 1, 1, 1, 1, 64, None, None, None, 99, 1, None, None)
+    # GEMM chains: link count, dtype and row limits are checked before any CUDA call
+    links = (L.SsdLinearArgs * 1)()
+    with pytest.raises(ValueError):
+        L.call("ssd_linear_chain", 0, ctypes.cast(links, ctypes.c_void_p), 4, L.SSD_BF16, None, 0, None, None)
+    with pytest.raises(L.SSDError):
+        L.call("ssd_linear_chain", 1, ctypes.cast(links, ctypes.c_void_p), 4, L.SSD_F32, None, 0, None, None)
+    with pytest.raises(ValueError):
+        L.call("ssd_linear_chain", 1, ctypes.cast(links, ctypes.c_void_p), 4, L.SSD_BF16, None, 0, None, None)  # no x
 
 
 YAML = """

@@ -403,3 +403,136 @@ def test_greedy_verify_matches_oracle(seed, n):
     want = OT.greedy_verify(ot, logits)
     got = greedy_verify(t, torch.tensor(logits, device=DEV))
     assert got == (want[0], want[1])
+
+
+# ------------------------------------------------------------ GEMM chain
+def _chain_layer(ops, ws, T, d, F, H, Hkv, hd, chained, seed=40, bridge=None, draw_rows=None):
+    """One decoder layer's GEMMs after attention: o_proj (+ residual, next
+    norm input), gate/up SwiGLU (folded norm), down (+ residual, next norm
+    input), optionally a SwiGLU bridge (gate/up, out_proj + residual), then
+    the next layer's q/k/v with RoPE and cache write; either as one
+    ssd_linear_chain launch or as separate launches. Row inputs are drawn
+    for `draw_rows` rows and the first T used, so row t sees the same data
+    whatever T is."""
+    import ssd._lib as L
+
+    R = draw_rows or T
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    rn = lambda *s, scale=1.0: (torch.randn(*s, generator=g, device=DEV) * scale)
+    wo = rn(d, H * hd, scale=0.02).bfloat16()
+    wg, wu = rn(F, d, scale=0.02).bfloat16(), rn(F, d, scale=0.02).bfloat16()
+    wd = rn(d, F, scale=0.02).bfloat16()
+    wq, wk, wv = rn(H * hd, d, scale=0.02).bfloat16(), rn(Hkv * hd, d, scale=0.02).bfloat16(), \
+        rn(Hkv * hd, d, scale=0.02).bfloat16()
+    ln2, ln_mid, ln_next = [(1 + 0.1 * rn(d)).bfloat16() for _ in range(3)]
+    bw = [rn(bridge, d, scale=0.02).bfloat16(), rn(bridge, d, scale=0.02).bfloat16(),
+          rn(d, bridge, scale=0.02).bfloat16()] if bridge else None
+    attn = rn(R, H * hd).bfloat16()[:T].contiguous()
+    resid = rn(R, d)[:T].contiguous()
+    parts = d // 128
+    xg = torch.zeros(T, d, dtype=torch.bfloat16, device=DEV)
+    ssq = torch.zeros(T, parts, device=DEV)
+    hid = torch.zeros(T, F, dtype=torch.bfloat16, device=DEV)
+    cos, sin = rope_tables(hd, 4096)
+    pos = ((torch.arange(T, device=DEV, dtype=torch.int32) * 37 + 5) % 4000).to(torch.int32)
+    slots = torch.arange(T, device=DEV, dtype=torch.int32)
+    kc = torch.zeros(Hkv, T + 8, hd, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    q = torch.zeros(T, H * hd, dtype=torch.bfloat16, device=DEV)
+    c = ops.GemmChain(ws, T, chained)
+    c.linear(attn, [wo], epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=ops.NormOut(ln2, xg, ssq))
+    c.linear(xg, [wg, wu], epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid,
+             in_norm=ops.RowNorm(ssq, parts, d, 1e-5))
+    c.linear(hid, [wd], epilogue=L.EPI_RESIDUAL, resid=resid,
+             norm_out=ops.NormOut(ln_mid if bridge else ln_next, xg, ssq))
+    out = {}
+    if bridge:
+        bh = torch.zeros(T, bridge, dtype=torch.bfloat16, device=DEV)
+        c.linear(xg, bw[:2], epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=bh,
+                 in_norm=ops.RowNorm(ssq, parts, d, 1e-5))
+        c.linear(bh, [bw[2]], epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=ops.NormOut(ln_next, xg, ssq))
+        out["bh"] = bh
+    c.qkv(xg, wq, wk, wv, H, Hkv, hd, cos, sin, pos, slots, kc, vc, q, in_norm=ops.RowNorm(ssq, parts, d, 1e-6))
+    c.flush()
+    torch.cuda.synchronize()
+    ws.check_status()
+    out.update(resid=resid, xg=xg, ssq=ssq, hid=hid, q=q, k=kc[:, :T].transpose(0, 1), v=vc[:, :T].transpose(0, 1))
+    return out
+
+
+CHAIN_SHAPES = [(33, 4096, 14336, 32, 8, 128), (1, 4096, 14336, 32, 8, 128), (7, 256, 512, 4, 2, 64),
+                (64, 1024, 2816, 8, 2, 128)]
+
+
+@pytest.mark.parametrize("T,d,F,H,Hkv,hd", CHAIN_SHAPES)
+@pytest.mark.parametrize("bridge", [None, 1024])
+def test_linear_chain_matches_separate_launches(ops, ws, T, d, F, H, Hkv, hd, bridge):
+    """ssd_linear_chain vs the same GEMMs launched one by one. The K splits
+    differ, so a link's fp32 sums differ in the last bits; where a link's
+    output is rounded to bf16 (norm inputs, SwiGLU) such a difference can
+    move a value by one bf16 step, and the next link carries that on: the
+    fp32 residual agrees to 3e-3 of its scale, bf16 outputs to 3e-2."""
+    a = _chain_layer(ops, ws, T, d, F, H, Hkv, hd, True, bridge=bridge)
+    b = _chain_layer(ops, ws, T, d, F, H, Hkv, hd, False, bridge=bridge)
+    _close(a["resid"], b["resid"], rtol=1e-2, atol_frac=3e-3)
+    _close(a["ssq"], b["ssq"], rtol=1e-2, atol_frac=3e-3)
+    for key in ("xg", "hid", "q", "k", "v") + (("bh",) if bridge else ()):
+        _close(a[key], b[key], rtol=3e-2, atol_frac=3e-2)
+
+
+@pytest.mark.parametrize("T,K,N", [(33, 4096, 4096), (1, 14336, 4096), (7, 256, 384), (64, 4096, 6144)])
+def test_linear_chain_single_link_matches_linear(ops, ws, T, K, N):
+    """One residual link with a folded norm output: the chain and ssd_linear
+    see identical inputs, so the fp32 residual agrees to fp32 summation
+    order (1e-5 of its scale) and the bf16 norm input to one bf16 step."""
+    import ssd._lib as L
+
+    x = _rand(T, K, seed=50)
+    w = _rand(N, K, scale=0.02, seed=51)
+    wn = (1 + 0.1 * _rand(N, dtype=torch.float32, seed=52)).bfloat16()
+    r0 = _rand(T, N, dtype=torch.float32, seed=53)
+    outs = []
+    for chained in (True, False):
+        resid = r0.clone()
+        xg = torch.zeros(T, N, dtype=torch.bfloat16, device=DEV)
+        ssq = torch.zeros(T, (N + 127) // 128, device=DEV)
+        c = ops.GemmChain(ws, T, chained)
+        c.linear(x, [w], epilogue=L.EPI_RESIDUAL, resid=resid, norm_out=ops.NormOut(wn, xg, ssq))
+        c.flush()
+        torch.cuda.synchronize()
+        ws.check_status()
+        outs.append((resid, xg, ssq))
+    ref = r0 + x.float() @ w.float().T
+    _close(outs[0][0], ref, rtol=1e-4, atol_frac=1e-5)
+    _close(outs[0][0], outs[1][0], rtol=1e-5, atol_frac=1e-5)
+    _close(outs[0][1], outs[1][1], rtol=1e-2, atol_frac=1e-2)
+    _close(outs[0][2], outs[1][2], rtol=1e-4, atol_frac=1e-5)
+
+
+@pytest.mark.parametrize("d,F,H,Hkv,hd", [(4096, 14336, 32, 8, 128), (256, 512, 4, 2, 64)])
+def test_linear_chain_batch_invariant(ops, ws, d, F, H, Hkv, hd):
+    """A row's chained results do not depend on how many rows run with it:
+    every link's K split depends only on the weight shapes and the grid."""
+    full = _chain_layer(ops, ws, 64, d, F, H, Hkv, hd, True, seed=41, bridge=512, draw_rows=64)
+    for T in (1, 17, 33):
+        part = _chain_layer(ops, ws, T, d, F, H, Hkv, hd, True, seed=41, bridge=512, draw_rows=64)
+        for key, v in part.items():
+            assert torch.equal(v, full[key][:T]), (T, key)
+
+
+def test_linear_chain_rejects_bad_arguments(ops, ws):
+    import ssd._lib as L
+
+    x = torch.zeros(4, 128, dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros(128, 128, dtype=torch.bfloat16, device=DEV)
+    out = torch.zeros(4, 128, dtype=torch.bfloat16, device=DEV)
+    a = ops.linear_args(x, [w], out=out)
+    with pytest.raises(ValueError):
+        ops.linear_chain([a] * 7, 4, ws)  # more than 6 links
+    big = torch.zeros(65, 128, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(L.SSDError):
+        ops.linear_chain([ops.linear_args(big, [w], out=torch.zeros_like(big))], 65, ws)  # T > 64
+    bad = ops.linear_args(x, [w], out=out)
+    bad.epilogue = 99
+    with pytest.raises(ValueError):
+        ops.linear_chain([bad], 4, ws)
