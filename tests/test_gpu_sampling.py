@@ -285,6 +285,27 @@ def _exact_joint(oracle_target, prompt, T, top_p, n_tok):
     return out
 
 
+def _joint_passes(gen_fn, exact, V, n_tok, n=4000, confirm_n=16000, seed0=SEED_BASE, marginal=True) -> None:
+    """Chi-square of the joint of the first n_tok tokens (and of the first
+    two) against the exact warped target joint, at p > P_MIN. A fixed seed
+    block fails such a check by chance 1 % of the time per statistic, so a
+    first block that fails is followed by one larger, disjoint block, and
+    the test decides on that one alone: a real bias fails both (the larger
+    block has more power), chance fails both with probability 1e-4."""
+    def ok(counts):
+        good = chi2_pvalue(counts, exact) > P_MIN
+        if marginal and n_tok > 2:
+            good = good and chi2_pvalue(counts.sum(2), exact.sum(2)) > P_MIN
+        return good
+
+    if ok(_joint_counts(lambda s: gen_fn(seed0 + s), n, V, n_tok)):
+        return
+    counts = _joint_counts(lambda s: gen_fn(seed0 + n + s), confirm_n, V, n_tok)
+    assert chi2_pvalue(counts, exact) > P_MIN
+    if marginal and n_tok > 2:
+        assert chi2_pvalue(counts.sum(2), exact.sum(2)) > P_MIN
+
+
 def _joint_counts(gen_fn, n, V, n_tok):
     counts = np.zeros((V,) * n_tok)
     for s in range(n):
@@ -310,12 +331,9 @@ def test_sampled_speculative_matches_target_distribution(v8, tree_name, temperat
     cfg = DraftingConfig(temperature=temperature, top_p=top_p, **DRAFTS[tree_name])
     gen = SpeculativeGenerator(base, draft, cfg, target)
     prompt = [1, 5, 2, 7]
-    n_tok, n = 3, 4000
-    counts = _joint_counts(lambda s: gen.generate(torch.tensor([prompt]), n_tok, {-1}, seed=SEED_BASE + s).tokens, n,
-                           8, n_tok)
+    n_tok = 3
     exact = _exact_joint(oracle_target, prompt, temperature, top_p, n_tok)
-    assert chi2_pvalue(counts, exact) > P_MIN
-    assert chi2_pvalue(counts.sum(2), exact.sum(2)) > P_MIN
+    _joint_passes(lambda seed: gen.generate(torch.tensor([prompt]), n_tok, {-1}, seed=seed).tokens, exact, 8, n_tok)
 
 
 def test_sampled_speculative_vocab_subset(v8):
