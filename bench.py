@@ -322,8 +322,9 @@ def gemm_roofline(w, rows: int, dev) -> dict:
     # gate/up -> down -> the next layer's q/k/v, folded norms), timed the same way
     from ssd.models import runner as R
 
+    # measured whenever it applies; it sets the totals only when the engines use it
     chained = R.chain_enabled(w, rows)
-    if chained:
+    if w.dtype == torch.bfloat16 and w.tp is None and 1 <= rows <= 64:
         parts = R.norm_parts(w)
         ssq = torch.zeros(rows, parts, dtype=torch.float32, device=dev)
         xg = x_d.clone()
@@ -357,8 +358,9 @@ def gemm_roofline(w, rows: int, dev) -> dict:
         torch.cuda.synchronize(dev)
         t = e0.elapsed_time(e1) / 1e3 / (5 * w.L)
         nbytes = sum(out[k]["bytes"] for k in ("qkv", "o_proj", "gate_up", "down"))
-        out["layer_chain"] = {"us": t * 1e6, "gbs": nbytes / t / 1e9, "bytes": nbytes}
-        total_b, total_t = nbytes * w.L, t * w.L
+        out["layer_chain"] = {"us": t * 1e6, "gbs": nbytes / t / 1e9, "bytes": nbytes, "used": chained}
+        if chained:
+            total_b, total_t = nbytes * w.L, t * w.L
         del graph
     # non-GEMM kernels of the same forward: RMSNorm and tree attention over a
     # cache of the bench context (their bytes are the activations / the KV)

@@ -831,15 +831,17 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   pdl_wait();  // Q, the new K/V rows and the row metadata come from earlier kernels
   pdl_trigger();
   if (warp == 0 && lane == 0) {
-    // Q rows (A operand, K-major, 128-byte swizzle): one 3-D box per 64
-    // columns lands tokens t_first.. x the head group's G heads as rows
-    // r = token * G + head (row groups start on a token); rows past the
-    // tensor are zero, rows past Mg are masked in the softmax.
-    const int qrows = (128 / a.G) * a.G;
-    mbar_arrive_expect_tx(q_ready, NR * qrows * 128);
+    // Q rows (A operand, K-major, 128-byte swizzle): per head g of the
+    // group and 64 columns, one 3-D box of TPG = 128 / G tokens from t_first
+    // lands at tile rows g * TPG.. (head-major; row groups start on a
+    // token); rows past the tensor are zero, rows past the group masked.
+    const int tpg = 128 / a.G;
+    mbar_arrive_expect_tx(q_ready, NR * a.G * tpg * 128);
+    const uint64_t pol = l2_policy_evict_first();
+    for (int g = 0; g < a.G; ++g)
 #pragma unroll
-    for (int g = 0; g < NR; ++g)
-      tma_load_3d(qs + g * (128 * 128), &maps.q, q_ready, g * 64, h * a.G, t_first, l2_policy_evict_first());
+      for (int c = 0; c < NR; ++c)
+        tma_load_3d(qs + c * (128 * 128) + g * tpg * 128, &maps.q, q_ready, c * 64, h * a.G + g, t_first, pol);
   }
   const int sb = a.spec_base ? a.spec_base[0] : 0;
   const int mw = a.mask ? a.mask_words : 0;
@@ -871,9 +873,16 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
 
   // softmax-side state (warps 2..9): warpgroup wg takes key blocks wg, wg + 2, ...
   const int q = warp & 3;
-  const int r = q * 32 + lane;  // query row of this thread = TMEM lane
+  const int r = q * 32 + lane;  // tile row of this thread = TMEM lane
   const int wg = warp >= 6 ? 1 : 0;
-  const bool row_ok = warp >= 2 && r < Mg;
+  // Tile rows are head-major: rows g * TPG .. g * TPG + TPG - 1 hold head g
+  // of the group for its tokens, so the valid rows of a small group spread
+  // over all four TMEM lane quarters (and SM sub-partitions) instead of
+  // filling the first ones. lr = the row's logical index (token * G + head),
+  // which the metadata, the slice records and the output use.
+  const int TPG = 128 / a.G;
+  const int lr = (r % TPG) * a.G + r / TPG;
+  const bool row_ok = warp >= 2 && lr < Mg;
   float m_ref = -INFINITY, l = 0.f;
 
   if (warp == 0) {
@@ -964,7 +973,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     }
   } else {
     // ---- softmax warps: thread = query row r
-    const int tok = row_ok ? (q0 + r) / a.G - t_first : 0;
+    const int tok = row_ok ? (q0 + lr) / a.G - t_first : 0;
     const int plen = row_ok ? s_plen[tok] : 0;
     const int pstart = row_ok ? s_pstart[tok] : 0;
     const float sc = a.scale * 1.4426950408889634f;  // base 2
@@ -1102,7 +1111,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   if (P == 1) {
     if (row_ok) {
       const float inv = Lrow > 0.f ? 1.f / Lrow : 0.f;
-      const int qr = q0 + r;
+      const int qr = q0 + lr;
       bf16* op = outp + (int64_t)(qr / a.G) * a.ldo + (int64_t)(h * a.G + qr % a.G) * HD + c0;
 #pragma unroll
       for (int d = 0; d < HH; d += 2) *reinterpret_cast<uint32_t*>(op + d) = pack_bf16(ov[d] * inv, ov[d + 1] * inv);
@@ -1153,7 +1162,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     const int owned = (a.rows_per_group + ns - 1) / ns;
     float* recv = reinterpret_cast<float*>(ring);
     if (row_ok) {
-      const int owner = r % ns, j = r / ns;
+      const int owner = lr % ns, j = lr / ns;
       const uint32_t base = dsmem_map(smem_u32(recv), static_cast<uint32_t>(owner)) +
                             (uint32_t)(((split * owned + j) * rec) * 4);
       if (wg == 0) dsmem_st4(base, Mrow, Lrow, 0.f, 0.f);
@@ -1173,7 +1182,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   // slice); attn_merge_kernel combines the slices of every row in parallel.
   float* recs = a.part + ((int64_t)blk * a.n_splits + split) * a.rows_per_group * rec;
   if (row_ok) {
-    float* pr = recs + (int64_t)r * rec;
+    float* pr = recs + (int64_t)lr * rec;
     if (wg == 0) {
       pr[0] = Mrow;
       pr[1] = Lrow;
@@ -1355,15 +1364,17 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
   // More than one 16-row tile of queries per KV head: the tcgen05 kernel
   // (measured faster from 32 rows up); decode-sized row counts stay on the
   // warp-specialised mma.sync kernel, whose key lanes split the slice.
-  if (dtype == SSD_BF16 && (head_dim == 64 || head_dim == 128) && T * (n_heads / n_kv_heads) > 16 &&
+  const int64_t G_heads = n_heads / n_kv_heads;
+  if (dtype == SSD_BF16 && (head_dim == 64 || head_dim == 128) && T * G_heads > 16 && 128 % G_heads == 0 &&
+      128 / G_heads >= 8 &&
       attn_use_tcgen05()) {
     // tcgen05 path: up to 128 query rows of a KV head per CTA (one M = 128
     // tile), key slices merged in a cluster or through global memory.
-    // Row groups start on a token (rows_per_group a multiple of G), so one
-    // 3-D TMA box of 128 / G tokens x G heads holds a group's Q rows.
-    const int64_t M = T * a.G;
+    // Row groups start on a token (rows_per_group a multiple of G); a
+    // group's Q rows land as one 3-D TMA box of 128 / G tokens per head,
+    // head-major in the tile (G divides 128 and each head's rows start on
+    // a 1024-byte swizzle atom: 128 / G >= 8).
     const int64_t tok_per_tile = 128 / a.G;
-    if (tok_per_tile < 1) return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: more than 128 heads per KV head");
     a.groups = (int)((T + tok_per_tile - 1) / tok_per_tile);
     a.rows_per_group = (int)(((T + a.groups - 1) / a.groups) * a.G);
     a.rt = 8;
@@ -1388,7 +1399,7 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
       if (!encode) return fail(SSD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
       cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)n_heads, (cuuint64_t)T};
       cuuint64_t strides[2] = {(cuuint64_t)head_dim * 2, (cuuint64_t)ldq * 2};
-      cuuint32_t box[3] = {64u, (cuuint32_t)a.G, (cuuint32_t)tok_per_tile};
+      cuuint32_t box[3] = {64u, 1u, (cuuint32_t)tok_per_tile};
       cuuint32_t estr[3] = {1u, 1u, 1u};
       const CUresult r = encode(&maps.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box,
                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -630,11 +630,13 @@ __device__ __forceinline__ int64_t chain_begin(int c, int64_t W, int Gl) {
   return c >= Gl ? W : sk_begin(c, W, Gl);
 }
 
-// Bounded poll until *p >= want (acquire at GPU scope).
+// Bounded poll until *p >= want (acquire at GPU scope). Every CTA polls the
+// same word, so after a few tight polls each one backs off 256 ns between
+// polls to keep that word's L2 slice free for other traffic.
 __device__ __forceinline__ bool poll_at_least(const uint32_t* p, uint32_t want) {
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (ld_acquire_u32(p) >= want) return true;
-    if (i > 64) __nanosleep(128);
+    if (i > 8) __nanosleep(256);
   }
   return false;
 }
@@ -828,10 +830,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) tc_chain_kernel(const __grid
       }
     }
   } else if (warp >= 2 && warp <= 5) {
-    // Epilogue warps 2..5 (TMEM lanes 32*(w%4)..+31), per link as in the
-    // stream-K kernel, then one count of this CTA into done[l].
+    // Epilogue warps 2..5 (TMEM lanes 32*(w%4)..+31): a whole tile runs its
+    // epilogue from TMEM; a split segment writes its fp32 partial to this
+    // CTA's slot and counts itself into the tile, and the participant that
+    // arrives last sums the tile's partials in K order and runs the epilogue
+    // (nobody waits for a tile: no polling on the shared counters). Then one
+    // count of this CTA into done[l].
     const int q = warp & 3;
     const int r = q * 32 + lane;
+    volatile int* s_last = abort_flag + 1;
     pdl_wait();  // the epilogues write buffers earlier kernels may still read
     bool failed = false;
     int seg = 0;
@@ -843,7 +850,6 @@ __global__ void __launch_bounds__(kChainThreads, 1) tc_chain_kernel(const __grid
       const int Gl = chain_ctas(W, G);
       const int64_t it0 = chain_begin(cta, W, Gl), it1 = chain_begin(cta + 1, W, Gl);
       uint32_t* arrived = P.counters + (int64_t)l * 2 * kChainTiles;
-      uint32_t* finished = arrived + kChainTiles;
       if (l > 0) {
         // The epilogue reads what link l - 1 wrote (residual rows, norm sums).
         bool ok = true;
@@ -857,8 +863,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) tc_chain_kernel(const __grid
           break;
         }
       }
-      int split_tile[2] = {-1, -1};
-      int n_split = 0, lseg = 0;
+      int lseg = 0;
       for (int64_t it = it0; it < it1; ++seg, ++lseg) {
         const int tile = (int)(it / g.kchunks);
         const int64_t tile_begin = (int64_t)tile * g.kchunks;
@@ -902,70 +907,52 @@ __global__ void __launch_bounds__(kChainThreads, 1) tc_chain_kernel(const __grid
           tc_fence_before();
           __threadfence();
           named_bar_sync(1, 128);
+          const int first = sk_cta_of(tile_begin, W, Gl);
+          const int np = sk_cta_of(tile_begin + g.kchunks - 1, W, Gl) - first + 1;
           if (r == 0) {
             mbar_arrive(&acce[b]);
-            atomicAdd(&arrived[tile], 1u);
+            *s_last = (atomicAdd(&arrived[tile], 1u) == (unsigned)(np - 1)) ? 1 : 0;
           }
-          split_tile[n_split++] = tile;
+          named_bar_sync(1, 128);
+          if (*s_last) {
+            // Last participant: every partial of the tile is visible. Slots:
+            // the first participant's is its first or last segment (its range
+            // may start before the tile), every later one's is its first.
+            __threadfence();
+            const int first_slot = 2 * first + (sk_begin(first, W, Gl) == tile_begin ? 0 : 1);
+            constexpr int kC = 8, kP = 8;  // columns x participants per batch of loads
+            for (int c0 = 0; c0 < ncols; c0 += kC) {
+              float acc[kC];
+#pragma unroll
+              for (int u = 0; u < kC; ++u) acc[u] = 0.f;
+              for (int p0 = 0; p0 < np; p0 += kP) {
+                float v[kP][kC];
+#pragma unroll
+                for (int pi = 0; pi < kP; ++pi) {
+                  const int pp = p0 + pi;
+                  const int slot = pp == 0 ? first_slot : 2 * (first + pp);
+                  const float* base = P.partials + (int64_t)slot * kTileM * BN + r;
+#pragma unroll
+                  for (int u = 0; u < kC; ++u)
+                    v[pi][u] = (pp < np && c0 + u < ncols) ? __ldcg(base + (c0 + u) * kTileM) : 0.f;
+                }
+#pragma unroll
+                for (int pi = 0; pi < kP; ++pi)
+#pragma unroll
+                  for (int u = 0; u < kC; ++u)
+                    if (p0 + pi < np) acc[u] += v[pi][u];  // K order
+              }
+#pragma unroll
+              for (int u = 0; u < kC; ++u)
+                if (c0 + u < ncols) stage[(c0 + u) * kTileM + r] = acc[u];
+            }
+            named_bar_sync(1, 128);
+            run_epilogue<bf16>(stage, tile, 0, ncols, g, e, r, 1);
+            named_bar_sync(1, 128);
+            if (r == 0) arrived[tile] = 0u;  // ready for the next launch
+          }
         }
         it = seg_end;
-      }
-      // Finish the split tiles: participant j of P owns token columns j,
-      // j + P, ...; it sums the P partials of those columns in K order.
-      for (int k = 0; k < n_split && !failed; ++k) {
-        const int tile = split_tile[k];
-        const int64_t tile_begin = (int64_t)tile * g.kchunks;
-        const int first = sk_cta_of(tile_begin, W, Gl);
-        const int last = sk_cta_of(tile_begin + g.kchunks - 1, W, Gl);
-        const int np = last - first + 1;
-        const int j = cta - first;
-        bool ok = true;
-        if (r == 0) ok = poll_at_least(&arrived[tile], (uint32_t)np);
-        if (named_bar_or(1, 128, !ok)) {
-          if (r == 0) {
-            report_error(P.status, kErrWaitTimeout);
-            *abort_flag = 1;
-          }
-          failed = true;
-          break;
-        }
-        __threadfence();
-        const int first_slot = 2 * first + (sk_begin(first, W, Gl) == tile_begin ? 0 : 1);
-        const int n_own = (ncols - j + np - 1) / np;
-        const int total = n_own * np;
-        for (int m0 = 0; m0 < total; m0 += 32) {
-          float v[32];
-#pragma unroll
-          for (int u = 0; u < 32; ++u) {
-            const int m = m0 + u;
-            v[u] = 0.f;
-            if (m < total) {
-              const int pi = m % np;
-              const int col = j + (m / np) * np;
-              const int slot = pi == 0 ? first_slot : 2 * (first + pi);
-              v[u] = __ldcg(P.partials + (int64_t)slot * kTileM * BN + col * kTileM + r);
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < 32; ++u) {
-            const int m = m0 + u;
-            if (m < total) {
-              const int pi = m % np;
-              float* dst = stage + (j + (m / np) * np) * kTileM + r;
-              *dst = (pi == 0 ? 0.f : *dst) + v[u];
-            }
-          }
-        }
-        named_bar_sync(1, 128);
-        run_epilogue<bf16>(stage, tile, 0, ncols, g, e, r, 1, j, np);
-        named_bar_sync(1, 128);
-        if (r == 0) {
-          const unsigned t = atomicAdd(&finished[tile], 1u);
-          if ((int)t == np - 1) {  // every participant has read the partials: reset for the next launch
-            arrived[tile] = 0u;
-            finished[tile] = 0u;
-          }
-        }
       }
       if (failed) break;
       // This CTA's share of link l is written: publish it (generic stores

@@ -103,7 +103,7 @@ __device__ __forceinline__ uint32_t tp_next_epoch(const TpDev& g, int ch, int b)
 __device__ bool tp_meet(const TpDev& g, int ch, int phase, int b, uint32_t epoch, uint32_t* status) {
   __syncthreads();
   int ok = 1;
-  if (threadIdx.x < g.world) {
+  if (threadIdx.x < g.world && threadIdx.x != g.rank) {  // (meeting oneself needs no flag)
     const int p = threadIdx.x;
     st_release_sys(tp_flag(g.region[p], ch, phase, b, g.rank), epoch);
     const uint32_t* f = tp_flag(g.region[g.rank], ch, phase, b, p);

