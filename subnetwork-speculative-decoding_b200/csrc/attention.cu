@@ -753,7 +753,7 @@ struct TcAttnLayout {
   static constexpr int OFF_RING = Q_BYTES;
   static constexpr int OFF_P = Q_BYTES + kTcAttnStages * STAGE;
   static constexpr int OFF_META = OFF_P + 2 * P_BYTES;
-  static constexpr int META = (kTcAttnMaxTok + 1) * 4 + kTcAttnMaxTok * 4 * 8 + 16 + (2 * kTcAttnStages + 10) * 8 + 16 +
+  static constexpr int META = (kTcAttnMaxTok + 1) * 4 + kTcAttnMaxTok * 4 * 8 + 16 + (4 * kTcAttnStages + 10) * 8 + 16 +
                               (kTcAttnMaxTok + 1) * 4;
   static constexpr int SMEM = 1024 + OFF_META + META;
 };
@@ -772,9 +772,13 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   int* s_plen = reinterpret_cast<int*>(sm + Lay::OFF_META);
   uint64_t* s_mask = reinterpret_cast<uint64_t*>(s_plen + kTcAttnMaxTok + 1);  // [tok][4]
   int* s_misc = reinterpret_cast<int*>(s_mask + kTcAttnMaxTok * 4);           // need_end, min_plen, last, abort
-  uint64_t* kv_full = reinterpret_cast<uint64_t*>(s_misc + 4);
-  uint64_t* kv_empty = kv_full + kTcAttnStages;
-  uint64_t* s_full = kv_empty + kTcAttnStages;  // [2]
+  // K and V halves of a ring stage fill and free separately: K(b) frees
+  // once S(b) is computed, V(b) once P.V(b) is, so keys run ahead of values.
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(s_misc + 4);  // K half of stage landed
+  uint64_t* kv_empty = kv_full + kTcAttnStages;                  // K half read by S
+  uint64_t* v_full = kv_empty + kTcAttnStages;
+  uint64_t* v_empty = v_full + kTcAttnStages;
+  uint64_t* s_full = v_empty + kTcAttnStages;  // [2]
   uint64_t* s_free = s_full + 2;                // [2]
   uint64_t* p_full = s_free + 2;                // [2]
   uint64_t* p_free = p_full + 2;                // [2]
@@ -804,6 +808,8 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
     for (int st = 0; st < kTcAttnStages; ++st) {
       mbar_init(&kv_full[st], 1);
       mbar_init(&kv_empty[st], 1);
+      mbar_init(&v_full[st], 1);
+      mbar_init(&v_empty[st], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -887,29 +893,45 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
 
   if (warp == 0) {
     if (lane == 0 && nblocks > 0) {
+      // K of block b as soon as its half-stage is free (S(b - 4) done), V of
+      // block b as soon as its half-stage is (P.V(b - 4) done); polled in
+      // turn so that neither waits for the other.
       const uint64_t pol = l2_policy_evict_first();
-      int issued = 0;
-      for (int b = 0; b < nblocks; ++b) {
-        const int st = b % kTcAttnStages;
-        if (b >= kTcAttnStages && !mbar_wait(&kv_empty[st], ((b / kTcAttnStages) - 1) & 1)) {
+      constexpr int S = kTcAttnStages;
+      int nK = 0, nV = 0;
+      uint32_t idle = 0;
+      while (nV < nblocks && !*abort_flag) {
+        bool prog = false;
+        if (nK < nblocks && (nK < S || mbar_test(&kv_empty[nK % S], ((nK / S) - 1) & 1))) {
+          const int st = nK % S;
+          mbar_arrive_expect_tx(&kv_full[st], NR * Lay::KV_REGION);
+          const int row = h * a.max_slots + k_lo + nK * KB;
+          uint8_t* dst = ring + st * Lay::STAGE;
+#pragma unroll
+          for (int g = 0; g < NR; ++g) tma_load_2d(dst + g * Lay::KV_REGION, &maps.k, &kv_full[st], g * 64, row, pol);
+          ++nK;
+          prog = true;
+        }
+        if (nV < nK && (nV < S || mbar_test(&v_empty[nV % S], ((nV / S) - 1) & 1))) {
+          const int st = nV % S;
+          mbar_arrive_expect_tx(&v_full[st], NR * Lay::KV_REGION);
+          const int row = h * a.max_slots + k_lo + nV * KB;
+          uint8_t* dst = ring + st * Lay::STAGE;
+#pragma unroll
+          for (int g = 0; g < NR; ++g)
+            tma_load_2d(dst + (NR + g) * Lay::KV_REGION, &maps.v, &v_full[st], g * 64, row, pol);
+          ++nV;
+          prog = true;
+        }
+        idle = prog ? 0u : idle + 1u;
+        if (idle > 4u * kWaitLimit) {
           report_error(a.status, kErrWaitTimeout);
           *abort_flag = 1;
-          break;
         }
-        if (*abort_flag) break;
-        mbar_arrive_expect_tx(&kv_full[st], Lay::STAGE);
-        const int row = h * a.max_slots + k_lo + b * KB;
-        uint8_t* dst = ring + st * Lay::STAGE;
-#pragma unroll
-        for (int g = 0; g < NR; ++g) tma_load_2d(dst + g * Lay::KV_REGION, &maps.k, &kv_full[st], g * 64, row, pol);
-#pragma unroll
-        for (int g = 0; g < NR; ++g)
-          tma_load_2d(dst + (NR + g) * Lay::KV_REGION, &maps.v, &kv_full[st], g * 64, row, pol);
-        ++issued;
       }
       if (*abort_flag) {  // let every copy already issued land before the CTA moves on
-        for (int b = (issued > kTcAttnStages ? issued - kTcAttnStages : 0); b < issued; ++b)
-          (void)mbar_wait(&kv_full[b % kTcAttnStages], (b / kTcAttnStages) & 1);
+        for (int b = (nK > S ? nK - S : 0); b < nK; ++b) (void)mbar_wait(&kv_full[b % S], (b / S) & 1);
+        for (int b = (nV > S ? nV - S : 0); b < nV; ++b) (void)mbar_wait(&v_full[b % S], (b / S) & 1);
       }
     }
   } else if (warp == 1) {
@@ -923,7 +945,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
       }
       // S = Q K^T of block b needs its K block and a free S buffer (the
       // softmax of block b - 2 has loaded its scores); O += P V of block b
-      // needs its P. Neither waits for the other: the thread polls both and
+      // needs its P and its V block. Neither waits for the other: the thread polls both and
       // issues whichever is ready, so the scores of the next blocks are
       // computed while the softmax warps still work on earlier ones. (Each
       // barrier can be at most one phase ahead of the one tested: its next
@@ -943,10 +965,12 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
                       sdesc_k_sw128(kb + (ks >> 2) * Lay::KV_REGION + off), id_s, ks > 0 ? 1u : 0u);
           }
           umma_commit(&s_full[nS & 1]);
+          umma_commit(&kv_empty[nS % kTcAttnStages]);  // the K half may take block nS + 4
           ++nS;
           prog = true;
         }
-        if (nP < nS && mbar_test(&p_full[nP & 1], (nP >> 1) & 1)) {
+        if (nP < nS && mbar_test(&p_full[nP & 1], (nP >> 1) & 1) &&
+            mbar_test(&v_full[nP % kTcAttnStages], (nP / kTcAttnStages) & 1)) {
           tc_fence_after();
           const int j = nP;
           const uint32_t vb = ring_s + (j % kTcAttnStages) * Lay::STAGE + NR * Lay::KV_REGION;
@@ -957,7 +981,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
                       sdesc_mn_sw128(vb + kk * 2048, Lay::KV_REGION, 1024), id_pv,
                       (j > (two ? 1 : 0) || kk > 0) ? 1u : 0u);
           umma_commit(&p_free[j & 1]);
-          umma_commit(&kv_empty[j % kTcAttnStages]);
+          umma_commit(&v_empty[j % kTcAttnStages]);
           ++nP;
           prog = true;
         }
