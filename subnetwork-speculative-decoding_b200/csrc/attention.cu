@@ -730,7 +730,8 @@ __device__ __forceinline__ float ex2_fast(float x) {
 }
 constexpr int kTcAttnStages = 4;
 constexpr int kTcAttnMaxTok = 129;  // token rows spanned by 128 query rows (keeps the metadata 8-byte aligned)
-constexpr int kTcAttnThreads = 320;  // TMA warp, MMA warp, two softmax warpgroups
+constexpr int kTcAttnThreads = 352;  // K TMA warp, MMA warp, two softmax warpgroups, V TMA warp
+constexpr int kTcAttnVWarp = 10;
 constexpr float kLazyRescale = 8.f;  // log2 headroom of P before O is rescaled
 // Key blocks per CTA from which the second softmax warpgroup takes the odd
 // blocks (below it warps 2..5 take every block and accumulator 1 stays unused:
@@ -881,6 +882,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   const int q = warp & 3;
   const int r = q * 32 + lane;  // tile row of this thread = TMEM lane
   const int wg = warp >= 6 ? 1 : 0;
+  const bool softmax_warp = warp >= 2 && warp <= 9;
   // Tile rows are head-major: rows g * TPG .. g * TPG + TPG - 1 hold head g
   // of the group for its tokens, so the valid rows of a small group spread
   // over all four TMEM lane quarters (and SM sub-partitions) instead of
@@ -888,50 +890,38 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   // which the metadata, the slice records and the output use.
   const int TPG = 128 / a.G;
   const int lr = (r % TPG) * a.G + r / TPG;
-  const bool row_ok = warp >= 2 && lr < Mg;
+  const bool row_ok = softmax_warp && lr < Mg;
   float m_ref = -INFINITY, l = 0.f;
 
-  if (warp == 0) {
+  if (warp == 0 || warp == kTcAttnVWarp) {
+    // One thread issues a TMA stream at ~35-45 GB/s on B200, below what a
+    // CTA that owns an SM needs, so K and V have a producer each (warp 0
+    // lane 0: K of block b once S(b - 4) freed its half-stage; warp 10 lane
+    // 0: V of block b once P.V(b - 4) freed its half).
     if (lane == 0 && nblocks > 0) {
-      // K of block b as soon as its half-stage is free (S(b - 4) done), V of
-      // block b as soon as its half-stage is (P.V(b - 4) done); polled in
-      // turn so that neither waits for the other.
+      const bool is_v = warp == kTcAttnVWarp;
       const uint64_t pol = l2_policy_evict_first();
       constexpr int S = kTcAttnStages;
-      int nK = 0, nV = 0;
-      uint32_t idle = 0;
-      while (nV < nblocks && !*abort_flag) {
-        bool prog = false;
-        if (nK < nblocks && (nK < S || mbar_test(&kv_empty[nK % S], ((nK / S) - 1) & 1))) {
-          const int st = nK % S;
-          mbar_arrive_expect_tx(&kv_full[st], NR * Lay::KV_REGION);
-          const int row = h * a.max_slots + k_lo + nK * KB;
-          uint8_t* dst = ring + st * Lay::STAGE;
-#pragma unroll
-          for (int g = 0; g < NR; ++g) tma_load_2d(dst + g * Lay::KV_REGION, &maps.k, &kv_full[st], g * 64, row, pol);
-          ++nK;
-          prog = true;
-        }
-        if (nV < nK && (nV < S || mbar_test(&v_empty[nV % S], ((nV / S) - 1) & 1))) {
-          const int st = nV % S;
-          mbar_arrive_expect_tx(&v_full[st], NR * Lay::KV_REGION);
-          const int row = h * a.max_slots + k_lo + nV * KB;
-          uint8_t* dst = ring + st * Lay::STAGE;
-#pragma unroll
-          for (int g = 0; g < NR; ++g)
-            tma_load_2d(dst + (NR + g) * Lay::KV_REGION, &maps.v, &v_full[st], g * 64, row, pol);
-          ++nV;
-          prog = true;
-        }
-        idle = prog ? 0u : idle + 1u;
-        if (idle > 4u * kWaitLimit) {
+      uint64_t* fullb = is_v ? v_full : kv_full;
+      uint64_t* emptyb = is_v ? v_empty : kv_empty;
+      const CUtensorMap* map = is_v ? &maps.v : &maps.k;
+      int issued = 0;
+      for (int b = 0; b < nblocks; ++b) {
+        const int st = b % S;
+        if ((b >= S && !mbar_wait(&emptyb[st], ((b / S) - 1) & 1)) || *abort_flag) {
           report_error(a.status, kErrWaitTimeout);
           *abort_flag = 1;
+          break;
         }
+        mbar_arrive_expect_tx(&fullb[st], NR * Lay::KV_REGION);
+        const int row = h * a.max_slots + k_lo + b * KB;
+        uint8_t* dst = ring + st * Lay::STAGE + (is_v ? NR * Lay::KV_REGION : 0);
+#pragma unroll
+        for (int g = 0; g < NR; ++g) tma_load_2d(dst + g * Lay::KV_REGION, map, &fullb[st], g * 64, row, pol);
+        ++issued;
       }
       if (*abort_flag) {  // let every copy already issued land before the CTA moves on
-        for (int b = (nK > S ? nK - S : 0); b < nK; ++b) (void)mbar_wait(&kv_full[b % S], (b / S) & 1);
-        for (int b = (nV > S ? nV - S : 0); b < nV; ++b) (void)mbar_wait(&v_full[b % S], (b / S) & 1);
+        for (int b = (issued > S ? issued - S : 0); b < issued; ++b) (void)mbar_wait(&fullb[b % S], (b / S) & 1);
       }
     }
   } else if (warp == 1) {
@@ -986,11 +976,12 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
           prog = true;
         }
         idle = prog ? 0u : idle + 1u;
-        if (idle > 4u * kWaitLimit || *abort_flag) {
+        if (idle > kWaitLimit || *abort_flag) {
           report_error(a.status, kErrWaitTimeout);
           *abort_flag = 1;
           ok = false;
         }
+        if (!prog) __nanosleep(32);  // (see the producer)
       }
       // Arrives once every MMA above has retired (also after an abort).
       umma_commit(o_full);
@@ -1093,14 +1084,14 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   for (int i = 0; i < HH; ++i) ov[i] = 0.f;
   float Mrow = -INFINITY, Lrow = 0.f;
   const int c0 = wg * HH;
-  if (warp >= 2) {
+  if (softmax_warp) {
     const bool w_ok = mbar_wait(o_full, 0);
     if (!w_ok) report_error(a.status, kErrWaitTimeout);
     tc_fence_after();
     float* s_ml = reinterpret_cast<float*>(ps);  // the P buffers are free once every P V retired
     s_ml[(wg * 128 + r) * 2] = m_ref;
     s_ml[(wg * 128 + r) * 2 + 1] = l;
-    named_bar_sync(3, kTcAttnThreads - 64);
+    named_bar_sync(3, 256);  // the eight softmax warps
     const float m0 = s_ml[r * 2], l0 = s_ml[r * 2 + 1];
     const float m1 = s_ml[(128 + r) * 2], l1 = s_ml[(128 + r) * 2 + 1];
     Mrow = fmaxf(m0, m1);
