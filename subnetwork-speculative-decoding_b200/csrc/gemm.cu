@@ -601,7 +601,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // slots per CTA as in the stream-K kernel, so each result depends only on
 // the weight shapes and the grid, never on the token count.
 constexpr int kChainMax = 6;
-constexpr int kChainThreads = 256;  // warps: 0 activation TMA, 1 MMA, 2-5 epilogue, 6-7 weight TMA
+constexpr int kChainThreads = 288;  // warps: 0, 8 activation TMA; 1 MMA; 2-5 epilogue; 6, 7 weight TMA
 constexpr int kChainTiles = 1024;                // weight tiles per link (counter slots)
 constexpr int64_t kChainCounterBase = 16384;     // first workspace counter of the chain block
 constexpr int64_t kChainCounters = kChainMax * 2 * kChainTiles + kChainMax + 1;
@@ -696,14 +696,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) tc_chain_kernel(const __grid
   // One thread issues a TMA box stream at ~40-50 GB/s on B200, under the
   // ~43 GB/s an SM needs for the HBM peak once the activation boxes are
   // added, so the weight boxes of alternate stages come from two threads
-  // in two warps (6, 7) and the activation boxes from a third (warp 0); each
-  // completes on its own barrier. Only the activation stream waits for
-  // dependencies: the weight streams run ahead into the next link as far
-  // as the ring allows.
+  // in two warps (6, 7) and the activation boxes of alternate stages from
+  // two more (warps 0, 8); weights and activations complete on separate
+  // barriers. Only the activation streams wait for dependencies: the weight
+  // streams run ahead into the next link as far as the ring allows.
   if (warp >= 6 || warp == 0) {
     if (lane == 0) {
-      const bool wproducer = warp >= 6;
-      const int k = warp - 6;  // weight stream: positions pos with pos % 2 == k
+      const bool wproducer = warp == 6 || warp == 7;
+      const int k = wproducer ? warp - 6 : (warp == 0 ? 0 : 1);  // positions pos with pos % 2 == k
       if (wproducer) {
         for (int l = 0; l < P.n; ++l)
           for (int i = 0; i < P.link[l].g.n_seg; ++i) tma_prefetch_desc(&P.link[l].maps.w[i]);
@@ -736,7 +736,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) tc_chain_kernel(const __grid
           }
         }
         for (int j = 0; j < n; ++j, ++pos) {
-          if (wproducer && (pos & 1) != k) continue;
+          if ((pos & 1) != k) continue;
           const int s = pos % stages;
           if ((pos >= stages && !mbar_wait(&empty[s], ((pos / stages) - 1) & 1)) || *abort_flag) {
             ok = false;
@@ -777,9 +777,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) tc_chain_kernel(const __grid
         *abort_flag = 1;
         // every copy this thread issued must land before the CTA exits
         for (int i = (issued_to > stages ? issued_to - stages : 0); i < issued_to; ++i)
-          if (!wproducer || (i & 1) == k) (void)mbar_wait(&(wproducer ? full_a : full_b)[i % stages], (i / stages) & 1);
+          if ((i & 1) == k) (void)mbar_wait(&(wproducer ? full_a : full_b)[i % stages], (i / stages) & 1);
       }
-      if (!wproducer) {
+      if (warp == 0) {
         pdl_wait();  // (a CTA without work still triggers only after its wait)
         pdl_trigger();
       }
