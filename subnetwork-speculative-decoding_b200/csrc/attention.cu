@@ -40,6 +40,7 @@ struct AttnArgs {
   int groups, rows_per_group;  // tensor-core kernel: query rows (token x GQA head) per CTA
   int rt, kw;                  // tensor-core kernel: 16-row tiles and key lanes per CTA
   int cluster_merge;           // key slices of a row group form a cluster and merge through DSMEM
+  int two_min;                 // tensor-core kernel: key blocks from which two softmax warpgroups split them
   void* out;
   int64_t ldo;
   float* part;
@@ -872,7 +873,7 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
   const int k_lo = split * slice;
   const int k_hi = min(k_lo + slice, need_end);
   const int nblocks = k_hi > k_lo ? (k_hi - k_lo + KB - 1) / KB : 0;
-  const bool two = nblocks >= kTcTwoGroupsMinBlocks;  // CTA-uniform
+  const bool two = nblocks >= a.two_min;  // CTA-uniform
   const uint32_t qs_s = smem_u32(qs), ring_s = smem_u32(ring), ps_s = smem_u32(ps);
   // TMEM columns: S buffers [0, 64) and [64, 128), O accumulators of the
   // even and odd key blocks at [128, 128 + HD) and [256, 256 + HD)
@@ -1327,6 +1328,15 @@ int attn_resident_clusters_tc(void (*kern)(const AttnMaps, const AttnArgs), int 
 
 // bf16 tree attention with more than 16 query rows per KV head runs on the
 // tcgen05 kernel; SSD_ATTN=mma keeps every size on the mma.sync kernel.
+// Key blocks per CTA from which the two softmax warpgroups of the tcgen05
+// kernel split the blocks (SSD_ATTN_TWO_MIN overrides).
+int attn_two_groups_min_blocks() {
+  static const int v = [] {
+    const char* e = getenv("SSD_ATTN_TWO_MIN");
+    return e ? atoi(e) : kTcTwoGroupsMinBlocks;
+  }();
+  return v;
+}
 bool attn_use_tcgen05() {
   static const bool v = [] {
     const char* e = getenv("SSD_ATTN");
@@ -1394,6 +1404,7 @@ extern "C" int ssd_tree_attention(const void* q, int64_t ldq, int64_t T, int64_t
     a.rows_per_group = (int)(((T + a.groups - 1) / a.groups) * a.G);
     a.rt = 8;
     a.kw = 1;
+    a.two_min = attn_two_groups_min_blocks();
     const int64_t blocks = (int64_t)a.n_kv * a.groups;
     if (blocks > 16384) return fail(SSD_ERR_UNSUPPORTED, "ssd_tree_attention: too many row groups");
     if ((int64_t)a.n_kv * max_slots > (int64_t)1 << 31)
