@@ -537,6 +537,15 @@ def reference_arm(args) -> None:
         print(json.dumps({"impl": "reference", "unavailable": "the 70B configuration in fp32 needs ~280 GB of host "
                                                               "memory: infeasible for the CPU port"}), flush=True)
         return
+    import torch
+
+    if spec.dtype != torch.float32 and not torch.cuda.is_available():
+        # the bf16 workloads draw their weights with the GPU arm's CUDA generator
+        # (then widen them for the port), so the two arms time the same model
+        print(json.dumps({"impl": "reference", "unavailable": "the weights of this workload are drawn on a GPU "
+                                                              "(same draws as the GPU arm); no GPU on this host"}),
+              flush=True)
+        return
     if args.sequences is None:
         args.sequences = N_SEQUENCES
     t0 = time.time()
