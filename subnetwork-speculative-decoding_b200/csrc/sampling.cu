@@ -15,6 +15,10 @@
 // Random numbers: Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random
 // numbers: as easy as 1, 2, 3", SC 2011), keyed by the caller's seed, with
 // counter (round, row, index, stream); no state is kept between launches.
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "common.cuh"
 #include "host.cuh"
 
@@ -542,7 +546,6 @@ struct RowExchange {
   float* fslot;               // [2][2] floats: (value, index bits) per bank
   unsigned long long* hslot;  // [2][256] histogram bins per bank
   float* gath;                // [2 * kRowMaxSlices] gathered partials
-  unsigned long long* ghist;  // [256] combined histogram
   unsigned long long* whist;  // [kSampWarps][256] per-warp bins (radix select)
   int S;
   int n;  // exchanges so far
@@ -593,85 +596,185 @@ __device__ void row_allbest(RowExchange& x, float& key, int& idx) {
 }
 
 // Cluster-wide radix select over the order keys of the staged slice: four
-// 8-bit levels; at each level every CTA histograms the keys that share the
-// prefix found so far (weight(l) per key: 1 to select by count, a 2^48
-// fixed-point mass to select by probability mass) into one private
-// histogram per warp (a row's keys crowd into a few top-byte bins, so a
-// shared histogram serialises its updates across warps), sums the warps'
-// bins, then the bins are summed over the cluster (integers, so the sums do
-// not depend on the split or the order) and the
-// selected bin is the lowest whose weight strictly above it stays <= target
-// (by mass) or, counting, the bin holding the target-th largest key. Only
-// keys >= floor_key take part. Returns the selected key.
+// 8-bit levels; at each level every CTA histograms the keys >= floor_key that
+// share the prefix found so far (weight(l) per key: 1 to select by count, a
+// 2^48 fixed-point mass to select by probability mass), the bins are summed
+// over the cluster (integers, so the sums do not depend on the split or the
+// order) and the selected bin is the lowest whose weight strictly above it
+// stays <= target (by mass) or, counting, the bin holding the target-th
+// largest key. Returns the selected key.
+//
+// A row's keys crowd into a few top-byte bins, so the first level avoids
+// shared-memory atomics on them. It first tries a window: top_bin is the top
+// byte of the row maximum's key; each thread adds the weights of bins
+// top_bin .. top_bin-7 in registers and only counts the keys of all lower
+// bins (one lump, in bin top_bin-8), and warp sums reach shared memory. The
+// window bins are exactly the full histogram's and the rule never looks below
+// the bin it selects, so when it selects a window bin the result is the full
+// histogram's; when it selects the lump, the level is histogrammed again in
+// full (a cluster-uniform decision), with one private histogram per warp.
+// Deeper levels see few keys over spread-out bins and add to one shared
+// histogram.
 template <typename Weight>
 __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_key, unsigned long long target,
-                                         bool by_count, Weight weight, RowExchange& x, unsigned long long* sel) {
+                                         bool by_count, Weight weight, RowExchange& x, unsigned long long* sel,
+                                         uint32_t top_bin) {
   uint32_t prefix = 0;
   unsigned long long above = 0;
+  bool window = top_bin >= 8u && top_bin <= 255u;
+  const int lane = threadIdx.x & 31;
   for (int level = 0; level < 4; ++level) {
     const int shift = 24 - 8 * level;
     unsigned long long* hist = x.hslot + (x.n & 1) * 256;
-    unsigned long long* mine = x.whist + (threadIdx.x >> 5) * 256;
-    for (int b = threadIdx.x; b < kSampWarps * 256; b += kSampThreads) x.whist[b] = 0ull;
-    __syncthreads();
-    for (int base = 0; base < n; base += kSampThreads) {
-      const int i = base + threadIdx.x;
-      const float l = i < n ? xs[i] : -INFINITY;
-      const uint32_t k = order_key(l);
-      const bool in = i < n && k >= floor_key && (level == 0 || (k >> (shift + 8)) == prefix);
-      // lanes of a bin add their weights exactly (24-bit halves through
-      // integer reductions) and the bin's lowest lane adds the sum to this
-      // warp's own histogram: no other warp writes it, and the leaders of one
-      // step hold distinct bins, so a plain add suffices
-      const uint32_t bin = (k >> shift) & 255u;
-      const unsigned long long v = in ? weight(l) : 0ull;
-      const unsigned peers = __match_any_sync(0xffffffffu, in ? bin : 0xffffffffu);
-      const unsigned lo = __reduce_add_sync(peers, static_cast<unsigned>(v & 0xffffffull));
-      const unsigned hi = __reduce_add_sync(peers, static_cast<unsigned>(v >> 24));
-      if (in && (threadIdx.x & 31) == static_cast<unsigned>(__ffs(peers) - 1))
-        mine[bin] += (static_cast<unsigned long long>(hi) << 24) + lo;
-      __syncwarp();
+    const bool per_warp = level == 0 && !window;
+    if (per_warp) {
+      for (int b = threadIdx.x; b < kSampWarps * 256; b += kSampThreads) x.whist[b] = 0ull;
+    } else {
+      for (int b = threadIdx.x; b < 256; b += kSampThreads) hist[b] = 0ull;
     }
     __syncthreads();
-    for (int b = threadIdx.x; b < 256; b += kSampThreads) {
-      unsigned long long t = 0ull;
-      for (int w = 0; w < kSampWarps; ++w) t += x.whist[w * 256 + b];
-      hist[b] = t;
+    if (level == 0 && window) {
+      unsigned long long acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0ull;
+      unsigned lump = 0;
+      for (int i = threadIdx.x; i < n; i += kSampThreads) {
+        const float l = xs[i];
+        const uint32_t k = order_key(l);
+        if (k < floor_key) continue;
+        const uint32_t d = top_bin - (k >> 24);  // keys never exceed the maximum's
+        if (d >= 8u) {
+          ++lump;
+          continue;
+        }
+        const unsigned long long v = weight(l);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (d == static_cast<uint32_t>(j)) acc[j] += v;
+      }
+      // exact warp sums from 24/24/16-bit pieces through integer reductions;
+      // lane 0 adds them to the CTA's bins. The lump holds its key count:
+      // the rule only asks whether it is empty (it is never above a selected
+      // bin), and selecting it means the full pass.
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const unsigned lo = __reduce_add_sync(0xffffffffu, static_cast<unsigned>(acc[j] & 0xffffffull));
+        const unsigned mid = __reduce_add_sync(0xffffffffu, static_cast<unsigned>((acc[j] >> 24) & 0xffffffull));
+        const unsigned hi = __reduce_add_sync(0xffffffffu, static_cast<unsigned>(acc[j] >> 48));
+        const unsigned long long t =
+            (static_cast<unsigned long long>(hi) << 48) + (static_cast<unsigned long long>(mid) << 24) + lo;
+        if (lane == 0 && t != 0ull) atomicAdd(&hist[top_bin - j], t);
+      }
+      const unsigned lumped = __reduce_add_sync(0xffffffffu, lump);
+      if (lane == 0 && lumped != 0u) atomicAdd(&hist[top_bin - 8], static_cast<unsigned long long>(lumped));
+    } else if (per_warp) {
+      unsigned long long* mine = x.whist + (threadIdx.x >> 5) * 256;
+      for (int i = threadIdx.x; i < n; i += kSampThreads) {
+        const float l = xs[i];
+        const uint32_t k = order_key(l);
+        // only lanes of one warp ever meet on a bin of its own histogram
+        if (k >= floor_key) atomicAdd(&mine[k >> 24], weight(l));
+      }
+    } else {
+      for (int i = threadIdx.x; i < n; i += kSampThreads) {
+        const float l = xs[i];
+        const uint32_t k = order_key(l);
+        if (k >= floor_key && (k >> (shift + 8)) == prefix) atomicAdd(&hist[(k >> shift) & 255u], weight(l));
+      }
     }
-    cluster_sync_all();  // every CTA's bins are complete
-    for (int b = threadIdx.x; b < 256; b += kSampThreads) {
+    __syncthreads();
+    if (per_warp) {
+      for (int b = threadIdx.x; b < 256; b += kSampThreads) {
+        unsigned long long t = 0ull;
+        for (int w = 0; w < kSampWarps; ++w) t += x.whist[w * 256 + b];
+        hist[b] = t;
+      }
+    }
+    cluster_sync_all();  // every CTA's bins are complete; whist is free again
+    {
+      // four quarters of the block each sum a quarter of the ranks' bins
+      static_assert(kSampThreads == 4 * 256, "bin gather assumes 1024 threads");
+      const int b = threadIdx.x & 255, q = threadIdx.x >> 8;
+      const uint32_t a = smem_u32(hist + b);
       unsigned long long t = 0ull;
-      for (int r = 0; r < x.S; ++r) t += dsmem_ld_u64(dsmem_map(smem_u32(hist + b), r));
-      x.ghist[b] = t;
+      for (int r = q; r < x.S; r += 4) t += dsmem_ld_u64(dsmem_map(a, r));
+      x.whist[q * 256 + b] = t;
     }
     ++x.n;
     __syncthreads();
-    if (threadIdx.x == 0) {
-      unsigned long long S = above, sel_S = above;
-      int sb = -1;
-      for (int b = 255; b >= 0; --b) {
-        const unsigned long long hb = x.ghist[b];
-        if (hb == 0ull) continue;
-        if (by_count) {
-          sb = b;
-          sel_S = S;
-          if (S + hb >= target) break;
-          S += hb;
-        } else {
-          if (S > target) break;
-          sb = b;
-          sel_S = S;
-          S += hb;
+    if (threadIdx.x < 32) {
+      // warp 0 selects the bin: lane j holds bins 255-8j down to 248-8j, a
+      // shuffle scan gives the weight strictly above its first bin, and the
+      // lane walks its bins downward applying the rule
+      unsigned long long h[8], tot = 0ull;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const int b = 255 - 8 * lane - t;
+        h[t] = x.whist[b] + x.whist[256 + b] + x.whist[512 + b] + x.whist[768 + b];
+        tot += h[t];
+      }
+      unsigned long long inc = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += v;
+      }
+      unsigned long long c = above + inc - tot;
+      int cand = -1, low = -1;
+      unsigned long long cand_s = 0ull, low_s = 0ull;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const int b = 255 - 8 * lane - t;
+        if (h[t] != 0ull) {
+          if (by_count) {
+            // counting: the first bin (from the top) that reaches the target
+            if (cand < 0 && c + h[t] >= target) {
+              cand = b;
+              cand_s = c;
+            }
+            low = b;
+            low_s = c;
+          } else if (c <= target) {
+            // by mass: the lowest bin whose weight above stays <= target
+            cand = b;
+            cand_s = c;
+          }
+          c += h[t];
         }
       }
-      if (sb < 0) sb = 255;  // unreachable for a finite row
-      sel[0] = (static_cast<unsigned long long>(prefix) << 8) | static_cast<unsigned>(sb);
-      sel[1] = sel_S;
+      const unsigned has = __ballot_sync(0xffffffffu, cand >= 0);
+      int src;
+      int sb = 255;  // no bin qualifies: unreachable for a finite row
+      unsigned long long ss = above;
+      if (has != 0u) {
+        src = by_count ? __ffs(has) - 1 : 31 - __clz(has);
+        sb = __shfl_sync(0xffffffffu, cand, src);
+        ss = __shfl_sync(0xffffffffu, cand_s, src);
+      } else if (by_count) {
+        // the target lies below every key: the lowest non-empty bin
+        const unsigned nz = __ballot_sync(0xffffffffu, low >= 0);
+        if (nz != 0u) {
+          src = 31 - __clz(nz);
+          sb = __shfl_sync(0xffffffffu, low, src);
+          ss = __shfl_sync(0xffffffffu, low_s, src);
+        }
+      }
+      if (lane == 0) {
+        sel[0] = (static_cast<unsigned long long>(prefix) << 8) | static_cast<unsigned>(sb);
+        sel[1] = ss;
+      }
     }
     __syncthreads();
-    prefix = static_cast<uint32_t>(sel[0]);
-    above = sel[1];
+    const uint32_t got = static_cast<uint32_t>(sel[0]);
+    const unsigned long long got_above = sel[1];
     __syncthreads();
+    if (level == 0 && window && got == top_bin - 8u) {  // the lump: histogram the level in full
+      window = false;
+      --level;
+      continue;
+    }
+    prefix = got;
+    above = got_above;
   }
   return prefix;
 }
@@ -692,7 +795,7 @@ __device__ WarpParams cluster_row_warp(const float* xs, int n, int V, float temp
   float lam_k = -INFINITY;
   if (keep_top > 0 && keep_top < V) {
     floor_key = cluster_radix_select(xs, n, 0u, static_cast<unsigned long long>(keep_top), true,
-                                     [](float) { return 1ull; }, x, sel);
+                                     [](float) { return 1ull; }, x, sel, order_key(P.m) >> 24);
     lam_k = key_float(floor_key);
   }
   float z = 0.f;
@@ -709,7 +812,8 @@ __device__ WarpParams cluster_row_warp(const float* xs, int n, int V, float temp
   const float m = P.m, inv_t = P.inv_t;
   const uint32_t key = cluster_radix_select(
       xs, n, floor_key, target, false,
-      [=](float l) { return static_cast<unsigned long long>((double)expf((l - m) * inv_t) * scale); }, x, sel);
+      [=](float l) { return static_cast<unsigned long long>((double)expf((l - m) * inv_t) * scale); }, x, sel,
+      order_key(m) >> 24);
   P.lambda = key_float(key);
   float zk = 0.f;
   for (int i = threadIdx.x; i < n; i += kSampThreads) {
@@ -725,7 +829,9 @@ __device__ WarpParams cluster_row_warp(const float* xs, int n, int V, float temp
 // draws without replacement, in draw order, to out_tok / out_lp[r * k ...]
 // (k = 0: parameters only). The draws equal gumbel_topk_kernel's for the same
 // parameters: keys lp + Gumbel with RNG counter (round, row_base + r, i,
-// stream), ties to the lower index, tokens through vocab_ids.
+// stream), ties to the lower index, tokens through vocab_ids. KB >= k bounds
+// the per-thread candidate list, which lives in registers.
+template <int KB>
 __global__ void __launch_bounds__(kSampThreads, 1) warp_sample_kernel(
     const float* logits, int64_t ld, int V, float temperature, float top_p, int keep_top, int k,
     const int64_t* vocab_ids,
@@ -735,12 +841,10 @@ __global__ void __launch_bounds__(kSampThreads, 1) warp_sample_kernel(
   __shared__ float red[32];
   __shared__ float fslot[4];
   __shared__ unsigned long long hslot[512];
-  __shared__ unsigned long long ghist[256];
   __shared__ float gath[2 * kRowMaxSlices];
   __shared__ unsigned long long sel[4];
-  __shared__ float s_key[kSampWarps];
-  __shared__ int s_idx[kSampWarps];
-  __shared__ int s_own[kSampWarps];
+  __shared__ float w_key[kSampWarps * kMaxK];  // each warp's k best
+  __shared__ int w_idx[kSampWarps * kMaxK];
   __shared__ float c_key[kRowMaxSlices * kMaxK];  // rank 0: every slice's list
   __shared__ int c_idx[kRowMaxSlices * kMaxK];
   const int S = gridDim.x, s = blockIdx.x, r = blockIdx.y;
@@ -751,7 +855,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) warp_sample_kernel(
   pdl_trigger();
   for (int i = threadIdx.x; i < n; i += kSampThreads) xs[i] = row[i0 + i];
   __syncthreads();
-  RowExchange x{fslot, hslot, gath, ghist, nullptr, S, 0};
+  RowExchange x{fslot, hslot, gath, nullptr, S, 0};
   x.whist = reinterpret_cast<unsigned long long*>(xs + ((len + 1) & ~1));
   const WarpParams P = cluster_row_warp(xs, n, V, temperature, top_p, keep_top, red, x, sel);
   if (s == 0 && threadIdx.x == 0 && params_out) params_out[r] = P;
@@ -762,39 +866,75 @@ __global__ void __launch_bounds__(kSampThreads, 1) warp_sample_kernel(
   const uint64_t sd = seed[0];
   const uint32_t rnd = static_cast<uint32_t>(round ? round[0] : 0);
   const uint32_t row_id = static_cast<uint32_t>(row_base + r);
-  float kk[kMaxK];
-  int ki[kMaxK];
+  static_assert(KB >= 1 && KB <= kMaxK, "candidate list bound");
+  float kk[KB];
+  int ki[KB];
 #pragma unroll
-  for (int j = 0; j < kMaxK; ++j) {
+  for (int j = 0; j < KB; ++j) {
     kk[j] = -INFINITY;
     ki[j] = INT32_MAX;
   }
-  for (int i = threadIdx.x; i < n; i += kSampThreads) {
-    const float lp = warped_lp(P, xs[i]);
-    if (lp == -INFINITY) continue;
+  // the thread's k best stay sorted in registers (static indices only); the
+  // k-th best is mirrored in (tk, ti) for the common reject test
+  float tk = -INFINITY;
+  int ti = INT32_MAX;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto draw = [&](int i) {
     const int gi = i0 + i;
     const float g = -logf(-logf(uniform(sd, rnd, row_id, static_cast<uint32_t>(gi), static_cast<uint32_t>(stream))));
-    const float key = lp + g;
-    if (key > kk[k - 1] || (key == kk[k - 1] && gi < ki[k - 1])) {
-      int j = k - 1;
-      while (j > 0 && (key > kk[j - 1] || (key == kk[j - 1] && gi < ki[j - 1]))) {
-        kk[j] = kk[j - 1];
-        ki[j] = ki[j - 1];
-        --j;
+    float ck = warped_lp(P, xs[i]) + g;
+    int ci = gi;
+    if (ck > tk || (ck == tk && ci < ti)) {
+      // carry the new key down the list, swapping it past every worse one
+#pragma unroll
+      for (int j = 0; j < KB; ++j) {
+        if (j < k && (ck > kk[j] || (ck == kk[j] && ci < ki[j]))) {
+          const float fk = kk[j];
+          const int fi = ki[j];
+          kk[j] = ck;
+          ki[j] = ci;
+          ck = fk;
+          ci = fi;
+        }
       }
-      kk[j] = key;
-      ki[j] = gi;
+#pragma unroll
+      for (int j = 0; j < KB; ++j)
+        if (j == k - 1) {
+          tk = kk[j];
+          ti = ki[j];
+        }
+    }
+  };
+  // Only nucleus members draw. Each warp queues the indices of its kept
+  // logits (the radix select's histograms are free now) and draws 32 at a
+  // time, so a draw pass runs with every lane busy however sparse the
+  // nucleus; lanes hold different subsets than a strided loop would, but the
+  // merges below order by (key, index), so the draws do not change.
+  int* queue = reinterpret_cast<int*>(x.whist) + w * 64;
+  int queued = 0;
+  for (int base = w * 32; base < n; base += kSampThreads) {  // warp-uniform bound
+    const int i = base + lane;
+    const bool kept = i < n && warped_lp(P, xs[i]) != -INFINITY;
+    const unsigned m = __ballot_sync(0xffffffffu, kept);
+    if (kept) queue[queued + __popc(m & ((1u << lane) - 1u))] = i;
+    queued += __popc(m);
+    __syncwarp();
+    if (queued >= 32) {
+      const int mine = queue[lane];
+      __syncwarp();
+      if (lane < queued - 32) queue[lane] = queue[32 + lane];
+      queued -= 32;
+      __syncwarp();
+      draw(mine);
     }
   }
-  // this slice's k best, in order, into rank 0's candidate lists
-  const uint32_t ck0 = dsmem_map(smem_u32(c_key), 0u);
-  const uint32_t ci0 = dsmem_map(smem_u32(c_idx), 0u);
-  int head = 0;
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane < queued) draw(queue[lane]);
+  // this slice's k best, in order, into rank 0's candidate lists: each warp
+  // merges its lanes' sorted lists into its own k best (the winning lane
+  // shifts its list up), then warp 0 merges the warps' lists the same way
   for (int q = 0; q < k; ++q) {
-    float bk = head < k ? kk[head] : -INFINITY;
-    int bi = head < k ? ki[head] : INT32_MAX;
-    int own = threadIdx.x;
+    float bk = kk[0];
+    int bi = ki[0], own = lane;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
@@ -806,27 +946,48 @@ __global__ void __launch_bounds__(kSampThreads, 1) warp_sample_kernel(
         own = oo;
       }
     }
-    if (lane == 0) {
-      s_key[w] = bk;
-      s_idx[w] = bi;
-      s_own[w] = own;
-    }
-    __syncthreads();
-    float gk = -INFINITY;
-    int gi = INT32_MAX, go = -1;
-    for (int j = 0; j < kSampWarps; ++j)
-      if (s_key[j] > gk || (s_key[j] == gk && s_idx[j] < gi)) {
-        gk = s_key[j];
-        gi = s_idx[j];
-        go = s_own[j];
+    if (lane == own) {
+#pragma unroll
+      for (int j = 0; j + 1 < KB; ++j) {
+        kk[j] = kk[j + 1];
+        ki[j] = ki[j + 1];
       }
-    if (threadIdx.x == go) ++head;
-    if (threadIdx.x == 0) {
-      const uint32_t off = static_cast<uint32_t>((s * kMaxK + q) * 4);
-      dsmem_st(ck0 + off, gk);
-      dsmem_st(ci0 + off, __int_as_float(gi));
+      kk[KB - 1] = -INFINITY;
+      ki[KB - 1] = INT32_MAX;
     }
-    __syncthreads();
+    if (lane == 0) {
+      w_key[w * kMaxK + q] = bk;
+      w_idx[w * kMaxK + q] = bi;
+    }
+  }
+  __syncthreads();
+  if (w == 0) {
+    static_assert(kSampWarps == 32, "one lane per warp list");
+    const uint32_t ck0 = dsmem_map(smem_u32(c_key), 0u);
+    const uint32_t ci0 = dsmem_map(smem_u32(c_idx), 0u);
+    int head = 0;
+    for (int q = 0; q < k; ++q) {
+      float bk = head < k ? w_key[lane * kMaxK + head] : -INFINITY;
+      int bi = head < k ? w_idx[lane * kMaxK + head] : INT32_MAX;
+      int own = lane;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        const int oo = __shfl_xor_sync(0xffffffffu, own, o);
+        if (ok > bk || (ok == bk && oi < bi)) {
+          bk = ok;
+          bi = oi;
+          own = oo;
+        }
+      }
+      if (lane == own) ++head;
+      if (lane == 0) {
+        const uint32_t off = static_cast<uint32_t>((s * kMaxK + q) * 4);
+        dsmem_st(ck0 + off, bk);
+        dsmem_st(ci0 + off, __int_as_float(bi));
+      }
+    }
   }
   cluster_sync_all();  // every slice's list is in rank 0's shared memory
   if (s != 0 || threadIdx.x != 0) return;
@@ -882,7 +1043,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_verify_cluster_kernel(
   float* qs = dyn + len;
   pdl_wait();
   pdl_trigger();
-  RowExchange x{fslot, nullptr, gath, nullptr, nullptr, S, 0};
+  RowExchange x{fslot, nullptr, gath, nullptr, S, 0};
   const int n = min(*n_nodes, max_nodes);
   const int c0 = root_pos[0];
   const uint64_t sd = seed[0];
@@ -1069,6 +1230,69 @@ static int row_slices(int64_t V) {
   return (V + S - 1) / S > kRowSliceMax ? 0 : S;
 }
 
+// The warp_sample_kernel instance whose candidate lists hold k draws.
+using WarpSampleKernel = void (*)(const float*, int64_t, int, float, float, int, int, const int64_t*,
+                                  const uint64_t*, const int32_t*, int, int, WarpParams*, int32_t*, float*);
+static WarpSampleKernel warp_sample_instance(int64_t k) {
+  static bool set = false;
+  if (!set) {
+    allow_max_dynamic_smem(warp_sample_kernel<4>);
+    allow_max_dynamic_smem(warp_sample_kernel<8>);
+    allow_max_dynamic_smem(warp_sample_kernel<kMaxK>);
+    set = true;
+  }
+  return k <= 4 ? warp_sample_kernel<4> : k <= 8 ? warp_sample_kernel<8> : warp_sample_kernel<kMaxK>;
+}
+
+// Clusters of S warp_sample_kernel CTAs that can be resident at once, from
+// the occupancy API; cached per instance, size, shared memory and device.
+static int warp_sample_resident(WarpSampleKernel kern, int S, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<void*, int, size_t, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(reinterpret_cast<void*>(kern), S, smem, dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)S, 1);
+  cfg.blockDim = dim3(kSampThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = n;
+  return n;
+}
+
+// Cluster size of warp_sample_kernel for `rows` rows: the largest S up to
+// row_slices(V) whose clusters for all rows are resident at once (slices of
+// up to kSampSliceMax floats), else the fewest CTAs per row. 0 = the row is
+// too long.
+constexpr int kSampSliceMax = 32768;  // 128 KB staged + 64 KB of warp histograms
+static int warp_sample_slices(int64_t V, int64_t rows, WarpSampleKernel kern) {
+  const int most = row_slices(V);
+  if (most == 0) return 0;
+  int least = (int)((V + kSampSliceMax - 1) / kSampSliceMax);
+  if (least > most) least = most;
+  for (int S = most; S > least; --S)
+    if (warp_sample_resident(kern, S, warp_sample_smem(V, S)) >= rows) return S;
+  return least;
+}
+
 }  // namespace ssd
 
 using namespace ssd;
@@ -1121,17 +1345,14 @@ int ssd_warp_sample_topk(const float* logits, int64_t ld, int64_t rows, int64_t 
   if (k < 0 || k > kMaxK) return fail(SSD_ERR_UNSUPPORTED, "ssd_warp_sample_topk: k must be 0..16");
   if (k > 0 && (!seed || !out_tok)) return fail(SSD_ERR_INVALID, "ssd_warp_sample_topk: NULL seed or output");
   if (k == 0 && !params_out) return fail(SSD_ERR_INVALID, "ssd_warp_sample_topk: nothing to compute");
-  const int S = row_slices(V);
+  const WarpSampleKernel kern = warp_sample_instance(k);
+  const int S = warp_sample_slices(V, rows, kern);
   if (S == 0)
     return fail(SSD_ERR_UNSUPPORTED, "ssd_warp_sample_topk: V = %lld exceeds %d", (long long)V,
                 kRowMaxSlices * kRowSliceMax);
   const size_t smem = warp_sample_smem(V, S);
-  static bool set = false;
-  if (!set) {
-    allow_max_dynamic_smem(warp_sample_kernel);
-    set = true;
-  }
-  return launch_kernel("warp_sample_kernel", warp_sample_kernel, dim3((unsigned)S, (unsigned)rows), dim3(kSampThreads),
+  return launch_kernel("warp_sample_kernel", kern, dim3((unsigned)S, (unsigned)rows),
+                       dim3(kSampThreads),
                        smem, static_cast<cudaStream_t>(stream), (unsigned)S, 1u, logits, ld, (int)V, temperature,
                        top_p, (int)(keep_top < V ? keep_top : 0), (int)k, vocab_ids, seed, round, (int)row_base, 0,
                        static_cast<WarpParams*>(params_out), out_tok, out_logprob);
@@ -1150,12 +1371,7 @@ int ssd_sample_token(const float* logits, int64_t V, float temperature, float to
                          (int)row_id, (int)stream_id, scratch, out);
   }
   const size_t smem = warp_sample_smem(V, S);
-  static bool set = false;
-  if (!set) {
-    allow_max_dynamic_smem(warp_sample_kernel);
-    set = true;
-  }
-  return launch_kernel("warp_sample_kernel", warp_sample_kernel, dim3((unsigned)S, 1u), dim3(kSampThreads), smem,
+  return launch_kernel("warp_sample_kernel", warp_sample_instance(1), dim3((unsigned)S, 1u), dim3(kSampThreads), smem,
                        static_cast<cudaStream_t>(stream), (unsigned)S, 1u, logits, (int64_t)V, (int)V, temperature,
                        top_p, 0, 1, static_cast<const int64_t*>(nullptr), seed, round, (int)row_id, (int)stream_id,
                        static_cast<WarpParams*>(nullptr), out, static_cast<float*>(nullptr));

@@ -454,6 +454,65 @@ def test_fused_warp_sample_matches_separate_kernels(V, top_p):
     torch.testing.assert_close(got_l, ref_l, rtol=1e-5, atol=1e-5)
 
 
+def _edge_rows(V):
+    g = torch.Generator().manual_seed(5)
+    rows = torch.empty(6, V)
+    rows[0] = torch.rand(V, generator=g) * 2 - 1  # flat: the nucleus reaches far below the max's bins
+    rows[1] = 0.0  # all tied at zero
+    rows[2] = -100.0 + torch.randn(V, generator=g)  # all negative
+    rows[3] = torch.randn(V, generator=g) * 1e-3  # straddles zero: bins on both sides of the sign
+    rows[4] = torch.randn(V, generator=g) * 2.0
+    rows[4, ::3] = float("-inf")  # masked ids
+    rows[5] = torch.linspace(-30.0, 30.0, V)  # spread over many bins
+    return rows.to(DEV)
+
+
+def _near_nucleus_boundary(row, T, top_p, tol=1e-5):
+    """Whether some prefix mass of the sorted row lies within tol of top_p,
+    where fp32 normalisers of different summation orders may disagree."""
+    x = row[np.isfinite(row)].astype(np.float64)
+    p = np.sort(np.exp((x - x.max()) / T))[::-1]
+    c = np.cumsum(p) / p.sum()
+    return bool(np.abs(c - top_p).min() < tol)
+
+
+@pytest.mark.parametrize("T,top_p", [(1.0, 0.9), (0.7, 0.5), (2.0, 0.99)])
+def test_fused_warp_params_edge_rows(T, top_p):
+    """The fused kernel's first radix level sums the 8 top-byte bins below
+    the row maximum in registers and lumps the rest; when the nucleus reaches
+    into the lump (flat rows, rows across the sign) it histograms the level
+    in full. Either way its max and threshold equal the single-CTA kernel's
+    exactly (rows whose boundary mass is within fp32 reach of top_p aside)."""
+    V = 128256
+    logits = _edge_rows(V)
+    ref = _params(logits, T, top_p).cpu().numpy()
+    got = ops.warp_params_buffer(logits.shape[0], DEV)
+    ops.warp_sample_topk(logits, T, top_p, got)
+    got = got.cpu().numpy()
+    rows = logits.cpu().numpy()
+    np.testing.assert_array_equal(ref[:, 0], got[:, 0])
+    for r in range(rows.shape[0]):
+        if not _near_nucleus_boundary(rows[r], T, top_p):
+            assert ref[r, 2] == got[r, 2], f"row {r}: threshold {got[r, 2]} != {ref[r, 2]}"
+    np.testing.assert_allclose(ref[:, 3], got[:, 3], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("keep_top", [64, 60000])
+def test_fused_keep_top_edge_rows(keep_top):
+    """keep_top selects by count through the same windowed first level: 64
+    lands inside the window, 60000 in the lump. The kept set equals the
+    oracle's keep_top largest logits (ties at the boundary kept)."""
+    V = 128256
+    logits = _edge_rows(V)
+    prm = ops.warp_params_buffer(logits.shape[0], DEV)
+    ops.warp_sample_topk(logits, 1.0, 1.0, prm, keep_top=keep_top)
+    lam = prm.cpu().numpy()[:, 2]
+    rows = logits.cpu().numpy()
+    for r in range(rows.shape[0]):
+        want = np.sort(rows[r])[::-1][keep_top - 1]
+        assert lam[r] == want, f"row {r}: kept threshold {lam[r]} != {want}"
+
+
 def test_clustered_tree_walk_first_token_is_target_distributed():
     """The rejection walk on a cluster (V = 20000: 8 CTAs, vocabulary slices
     of 2500): candidates and mass spread over different slices, so point
