@@ -595,6 +595,34 @@ __device__ void row_allbest(RowExchange& x, float& key, int& idx) {
   idx = bi;
 }
 
+// Row max m and normaliser Z = sum exp((l - m) * inv_t) from every CTA's
+// (max, sum against that max), combined in rank order.
+__device__ void row_max_sum(RowExchange& x, float mc, float zc, float inv_t, float& m, float& Z) {
+  float* slot = x.fslot + (x.n & 1) * 2;
+  if (threadIdx.x == 0) {
+    slot[0] = mc;
+    slot[1] = zc;
+  }
+  cluster_sync_all();
+  if (threadIdx.x < x.S) {
+    const uint32_t a = dsmem_map(smem_u32(slot), threadIdx.x);
+    x.gath[2 * threadIdx.x] = dsmem_ld(a);
+    x.gath[2 * threadIdx.x + 1] = dsmem_ld(a + 4);
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int t = 0; t < x.S; ++t) mx = fmaxf(mx, x.gath[2 * t]);
+  float z = 0.f;
+  for (int t = 0; t < x.S; ++t) {
+    const float mt = x.gath[2 * t];
+    if (mt != -INFINITY) z += x.gath[2 * t + 1] * expf((mt - mx) * inv_t);
+  }
+  __syncthreads();
+  ++x.n;
+  m = mx;
+  Z = z;
+}
+
 // Cluster-wide radix select over the order keys of the staged slice: four
 // 8-bit levels; at each level every CTA histograms the keys >= floor_key that
 // share the prefix found so far (weight(l) per key: 1 to select by count, a
@@ -607,37 +635,41 @@ __device__ void row_allbest(RowExchange& x, float& key, int& idx) {
 // A row's keys crowd into a few top-byte bins, so the first level avoids
 // shared-memory atomics on them. It first tries a window: top_bin is the top
 // byte of the row maximum's key; each thread adds the weights of bins
-// top_bin .. top_bin-7 in registers and only counts the keys of all lower
-// bins (one lump, in bin top_bin-8), and warp sums reach shared memory. The
-// window bins are exactly the full histogram's and the rule never looks below
-// the bin it selects, so when it selects a window bin the result is the full
-// histogram's; when it selects the lump, the level is histogrammed again in
-// full (a cluster-uniform decision), with one private histogram per warp.
-// Deeper levels see few keys over spread-out bins and add to one shared
-// histogram.
+// top_bin .. top_bin-7 into its own slots and only counts the keys of all
+// lower bins (one lump, in bin top_bin-8), and the slots are summed per bin.
+// The window bins are exactly the full histogram's and the rule never looks
+// below the bin it selects, so when it selects a window bin the result is the
+// full histogram's; when it selects the lump, the level is histogrammed again
+// in full (a cluster-uniform decision) through per-thread caches of four bins
+// and one private histogram per warp. Deeper levels see few keys over
+// spread-out bins and add to one shared histogram.
 template <typename Weight>
 __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_key, unsigned long long target,
                                          bool by_count, Weight weight, RowExchange& x, unsigned long long* sel,
-                                         uint32_t top_bin) {
+                                         uint32_t top_bin, unsigned long long* at_or_above = nullptr) {
   uint32_t prefix = 0;
   unsigned long long above = 0;
   bool window = top_bin >= 8u && top_bin <= 255u;
   const int lane = threadIdx.x & 31;
+  // Exchange banks alternate, and a bank's last remote readers finished before
+  // the previous exchange's cluster barrier: the first level zeroes its bank
+  // here, each level zeroes the next one after its own cluster barrier.
+  for (int b = threadIdx.x; b < 256; b += kSampThreads) x.hslot[(x.n & 1) * 256 + b] = 0ull;
   for (int level = 0; level < 4; ++level) {
     const int shift = 24 - 8 * level;
     unsigned long long* hist = x.hslot + (x.n & 1) * 256;
     const bool per_warp = level == 0 && !window;
-    if (per_warp) {
+    if (per_warp)
       for (int b = threadIdx.x; b < kSampWarps * 256; b += kSampThreads) x.whist[b] = 0ull;
-    } else {
-      for (int b = threadIdx.x; b < 256; b += kSampThreads) hist[b] = 0ull;
-    }
-    __syncthreads();
+    if (level == 0) __syncthreads();  // zeroed bins before any add
     if (level == 0 && window) {
-      unsigned long long acc[8];
+      // each thread adds into its own 8 slots (slot j of thread t at
+      // whist[j * kSampThreads + t]): no other thread touches them
+      unsigned long long* slot = x.whist + threadIdx.x;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0ull;
+      for (int j = 0; j < 8; ++j) slot[j * kSampThreads] = 0ull;
       unsigned lump = 0;
+#pragma unroll 2
       for (int i = threadIdx.x; i < n; i += kSampThreads) {
         const float l = xs[i];
         const uint32_t k = order_key(l);
@@ -647,50 +679,91 @@ __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_
           ++lump;
           continue;
         }
-        const unsigned long long v = weight(l);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (d == static_cast<uint32_t>(j)) acc[j] += v;
+        slot[d * kSampThreads] += weight(l);
       }
-      // exact warp sums from 24/24/16-bit pieces through integer reductions;
-      // lane 0 adds them to the CTA's bins. The lump holds its key count:
-      // the rule only asks whether it is empty (it is never above a selected
-      // bin), and selecting it means the full pass.
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const unsigned lo = __reduce_add_sync(0xffffffffu, static_cast<unsigned>(acc[j] & 0xffffffull));
-        const unsigned mid = __reduce_add_sync(0xffffffffu, static_cast<unsigned>((acc[j] >> 24) & 0xffffffull));
-        const unsigned hi = __reduce_add_sync(0xffffffffu, static_cast<unsigned>(acc[j] >> 48));
-        const unsigned long long t =
-            (static_cast<unsigned long long>(hi) << 48) + (static_cast<unsigned long long>(mid) << 24) + lo;
-        if (lane == 0 && t != 0ull) atomicAdd(&hist[top_bin - j], t);
-      }
+      // The lump holds its key count: the rule only asks whether it is empty
+      // (it is never above a selected bin), and selecting it means the full
+      // pass.
       const unsigned lumped = __reduce_add_sync(0xffffffffu, lump);
       if (lane == 0 && lumped != 0u) atomicAdd(&hist[top_bin - 8], static_cast<unsigned long long>(lumped));
+      __syncthreads();
+      {
+        // warp w sums slot w/4 over a quarter of the threads, exactly
+        const int j = (threadIdx.x >> 5) >> 2, q = (threadIdx.x >> 5) & 3;
+        const unsigned long long* src = x.whist + j * kSampThreads + q * 256 + lane;
+        unsigned long long t = 0ull;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) t += src[e * 32];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (lane == 0 && t != 0ull) atomicAdd(&hist[top_bin - j], t);
+      }
     } else if (per_warp) {
+      // Few top-byte bins hold most keys, so each thread keeps four (bin,
+      // sum) pairs in registers and adds an evicted pair to its warp's own
+      // histogram (only lanes of one warp ever meet on those bins).
       unsigned long long* mine = x.whist + (threadIdx.x >> 5) * 256;
+      uint32_t b0 = 256u, b1 = 256u, b2 = 256u, b3 = 256u;  // 256 = empty
+      unsigned long long s0 = 0ull, s1 = 0ull, s2 = 0ull, s3 = 0ull;
+      unsigned victim = 0;
       for (int i = threadIdx.x; i < n; i += kSampThreads) {
         const float l = xs[i];
         const uint32_t k = order_key(l);
-        // only lanes of one warp ever meet on a bin of its own histogram
-        if (k >= floor_key) atomicAdd(&mine[k >> 24], weight(l));
+        if (k < floor_key) continue;
+        const uint32_t bin = k >> 24;
+        const unsigned long long v = weight(l);
+        if (bin == b0) {
+          s0 += v;
+        } else if (bin == b1) {
+          s1 += v;
+        } else if (bin == b2) {
+          s2 += v;
+        } else if (bin == b3) {
+          s3 += v;
+        } else {
+          if (victim == 0u) {
+            if (b0 < 256u) atomicAdd(&mine[b0], s0);
+            b0 = bin;
+            s0 = v;
+          } else if (victim == 1u) {
+            if (b1 < 256u) atomicAdd(&mine[b1], s1);
+            b1 = bin;
+            s1 = v;
+          } else if (victim == 2u) {
+            if (b2 < 256u) atomicAdd(&mine[b2], s2);
+            b2 = bin;
+            s2 = v;
+          } else {
+            if (b3 < 256u) atomicAdd(&mine[b3], s3);
+            b3 = bin;
+            s3 = v;
+          }
+          victim = (victim + 1u) & 3u;
+        }
       }
+      if (b0 < 256u) atomicAdd(&mine[b0], s0);
+      if (b1 < 256u) atomicAdd(&mine[b1], s1);
+      if (b2 < 256u) atomicAdd(&mine[b2], s2);
+      if (b3 < 256u) atomicAdd(&mine[b3], s3);
     } else {
+#pragma unroll 2
       for (int i = threadIdx.x; i < n; i += kSampThreads) {
         const float l = xs[i];
         const uint32_t k = order_key(l);
         if (k >= floor_key && (k >> (shift + 8)) == prefix) atomicAdd(&hist[(k >> shift) & 255u], weight(l));
       }
     }
-    __syncthreads();
     if (per_warp) {
+      __syncthreads();
       for (int b = threadIdx.x; b < 256; b += kSampThreads) {
         unsigned long long t = 0ull;
         for (int w = 0; w < kSampWarps; ++w) t += x.whist[w * 256 + b];
         hist[b] = t;
       }
     }
+    // the cluster barrier also orders this CTA's adds before the reads below
     cluster_sync_all();  // every CTA's bins are complete; whist is free again
+    for (int b = threadIdx.x; b < 256; b += kSampThreads) x.hslot[((x.n + 1) & 1) * 256 + b] = 0ull;
     {
       // four quarters of the block each sum a quarter of the ranks' bins
       static_assert(kSampThreads == 4 * 256, "bin gather assumes 1024 threads");
@@ -721,7 +794,7 @@ __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_
       }
       unsigned long long c = above + inc - tot;
       int cand = -1, low = -1;
-      unsigned long long cand_s = 0ull, low_s = 0ull;
+      unsigned long long cand_s = 0ull, low_s = 0ull, cand_h = 0ull, low_h = 0ull;
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         const int b = 255 - 8 * lane - t;
@@ -731,13 +804,16 @@ __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_
             if (cand < 0 && c + h[t] >= target) {
               cand = b;
               cand_s = c;
+              cand_h = h[t];
             }
             low = b;
             low_s = c;
+            low_h = h[t];
           } else if (c <= target) {
             // by mass: the lowest bin whose weight above stays <= target
             cand = b;
             cand_s = c;
+            cand_h = h[t];
           }
           c += h[t];
         }
@@ -745,11 +821,12 @@ __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_
       const unsigned has = __ballot_sync(0xffffffffu, cand >= 0);
       int src;
       int sb = 255;  // no bin qualifies: unreachable for a finite row
-      unsigned long long ss = above;
+      unsigned long long ss = above, sh = 0ull;
       if (has != 0u) {
         src = by_count ? __ffs(has) - 1 : 31 - __clz(has);
         sb = __shfl_sync(0xffffffffu, cand, src);
         ss = __shfl_sync(0xffffffffu, cand_s, src);
+        sh = __shfl_sync(0xffffffffu, cand_h, src);
       } else if (by_count) {
         // the target lies below every key: the lowest non-empty bin
         const unsigned nz = __ballot_sync(0xffffffffu, low >= 0);
@@ -757,17 +834,20 @@ __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_
           src = 31 - __clz(nz);
           sb = __shfl_sync(0xffffffffu, low, src);
           ss = __shfl_sync(0xffffffffu, low_s, src);
+          sh = __shfl_sync(0xffffffffu, low_h, src);
         }
       }
       if (lane == 0) {
         sel[0] = (static_cast<unsigned long long>(prefix) << 8) | static_cast<unsigned>(sb);
         sel[1] = ss;
+        sel[2] = sh;
       }
     }
+    // sel is next written a level later, after the cluster barrier that every
+    // thread reaches only after reading it here
     __syncthreads();
     const uint32_t got = static_cast<uint32_t>(sel[0]);
     const unsigned long long got_above = sel[1];
-    __syncthreads();
     if (level == 0 && window && got == top_bin - 8u) {  // the lump: histogram the level in full
       window = false;
       --level;
@@ -775,6 +855,7 @@ __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_
     }
     prefix = got;
     above = got_above;
+    if (level == 3 && at_or_above) *at_or_above = got_above + sel[2];
   }
   return prefix;
 }
@@ -783,25 +864,38 @@ __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_
 // kept-mass normaliser and the smallest kept logit. keep_top > 0 first keeps
 // only the keep_top largest logits (ties at the boundary all kept); top_p < 1
 // then keeps the nucleus of what remains, by the same radix select as
-// row_warp with the bins summed over the cluster.
+// row_warp with the bins summed over the cluster. Without keep_top each CTA
+// sums against its own max and one exchange combines (max, sum) pairs. The
+// kept mass of a nucleus is the radix select's integer
+// mass at or above the threshold, scaled back by Z / 2^48 (each of its
+// terms truncates less than 2^-48 of Z).
 __device__ WarpParams cluster_row_warp(const float* xs, int n, int V, float temperature, float top_p, int keep_top,
                                        float* red, RowExchange& x, unsigned long long* sel) {
   WarpParams P;
   P.inv_t = 1.0f / temperature;
-  float mx = -INFINITY;
-  for (int i = threadIdx.x; i < n; i += kSampThreads) mx = fmaxf(mx, xs[i]);
-  P.m = row_allreduce(x, block_max(mx, red), true);
   uint32_t floor_key = 0;
   float lam_k = -INFINITY;
+  float Z;
   if (keep_top > 0 && keep_top < V) {
+    float mx = -INFINITY;
+    for (int i = threadIdx.x; i < n; i += kSampThreads) mx = fmaxf(mx, xs[i]);
+    P.m = row_allreduce(x, block_max(mx, red), true);
     floor_key = cluster_radix_select(xs, n, 0u, static_cast<unsigned long long>(keep_top), true,
                                      [](float) { return 1ull; }, x, sel, order_key(P.m) >> 24);
     lam_k = key_float(floor_key);
+    float z = 0.f;
+    for (int i = threadIdx.x; i < n; i += kSampThreads)
+      if (xs[i] >= lam_k) z += expf((xs[i] - P.m) * P.inv_t);
+    Z = row_allreduce(x, block_sum(z, red), false);
+  } else {
+    float mt = -INFINITY;
+    for (int i = threadIdx.x; i < n; i += kSampThreads) mt = fmaxf(mt, xs[i]);
+    const float mc = block_max(mt, red);
+    float zt = 0.f;
+    if (mc != -INFINITY)
+      for (int i = threadIdx.x; i < n; i += kSampThreads) zt += expf((xs[i] - mc) * P.inv_t);
+    row_max_sum(x, mc, block_sum(zt, red), P.inv_t, P.m, Z);
   }
-  float z = 0.f;
-  for (int i = threadIdx.x; i < n; i += kSampThreads)
-    if (xs[i] >= lam_k) z += expf((xs[i] - P.m) * P.inv_t);
-  const float Z = row_allreduce(x, block_sum(z, red), false);
   if (!(top_p < 1.0f)) {
     P.lambda = lam_k;
     P.log_z = logf(Z);
@@ -810,17 +904,13 @@ __device__ WarpParams cluster_row_warp(const float* xs, int n, int V, float temp
   const double scale = 281474976710656.0 / (double)Z;  // 2^48 / Z
   const unsigned long long target = static_cast<unsigned long long>((double)top_p * 281474976710656.0);
   const float m = P.m, inv_t = P.inv_t;
+  unsigned long long kept = 0ull;
   const uint32_t key = cluster_radix_select(
       xs, n, floor_key, target, false,
       [=](float l) { return static_cast<unsigned long long>((double)expf((l - m) * inv_t) * scale); }, x, sel,
-      order_key(m) >> 24);
+      order_key(m) >> 24, &kept);
   P.lambda = key_float(key);
-  float zk = 0.f;
-  for (int i = threadIdx.x; i < n; i += kSampThreads) {
-    const float l = xs[i];
-    if (l >= P.lambda) zk += expf((l - P.m) * P.inv_t);
-  }
-  P.log_z = logf(row_allreduce(x, block_sum(zk, red), false));
+  P.log_z = (float)log((double)kept * ((double)Z / 281474976710656.0));
   return P;
 }
 
