@@ -49,8 +49,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   volatile int* abort_flag = flag + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile_m = blockIdx.x / g.splits, split = blockIdx.x % g.splits;
-  const int tile_n = blockIdx.y;
+  const int bm = g.n_major ? blockIdx.y : blockIdx.x;
+  const int tile_m = bm / g.splits, split = bm % g.splits;
+  const int tile_n = g.n_major ? blockIdx.x : blockIdx.y;
   const int kc0 = (int)((int64_t)split * g.kchunks / g.splits);
   const int kc1 = (int)((int64_t)(split + 1) * g.kchunks / g.splits);
   const int nk = kc1 - kc0;
@@ -1337,6 +1338,14 @@ int launch_gemm(const void* x, int64_t ldx, int64_t T, int64_t K, int n_seg, con
   }
   if (g.tiles_n > 65535) return fail(SSD_ERR_UNSUPPORTED, "too many token tiles");
   dim3 grid(g.tiles_m * g.splits, g.tiles_n);
+  // Several token tiles (prefill): the CTAs of one weight tile are adjacent in
+  // launch order, so a wave streams each weight tile from HBM once and serves
+  // its other token tiles from L2 (weight-tile-major order re-streams every
+  // weight once per token tile).
+  if (dtype == SSD_BF16 && g.tiles_n > 1 && g.splits == 1 && !head && !plan.sk && g.tiles_m <= 65535) {
+    g.n_major = 1;
+    grid = dim3(g.tiles_n, g.tiles_m);
+  }
 
   if (dtype == SSD_BF16) {
     const bool sk = plan.sk;

@@ -78,6 +78,7 @@ struct GemmShape {
   int stages;
   int tiles_m, tiles_n;
   int a_box;          // weight rows per TMA box (stream-K kernel: 128, 64 or 32)
+  int n_major;        // grid x walks the token tiles (prefill: one weight tile's CTAs run together)
   uint32_t* counters;
   float* partials;
   uint32_t* status;

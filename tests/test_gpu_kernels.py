@@ -84,7 +84,7 @@ def test_linear_bias_act(ops, ws, dtype, act):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("T,N,K", [(1, 4096, 4096), (33, 2048, 8192), (6, 64, 128)])
+@pytest.mark.parametrize("T,N,K", [(1, 4096, 4096), (33, 2048, 8192), (6, 64, 128), (300, 512, 256)])
 def test_linear_residual(ops, ws, dtype, T, N, K):
     x = _rand(T, K, dtype=dtype, seed=8)
     w = _rand(N, K, dtype=dtype, scale=0.02, seed=9)
@@ -96,7 +96,7 @@ def test_linear_residual(ops, ws, dtype, T, N, K):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("T,F,K", [(1, 14336, 4096), (17, 128, 64), (33, 8192, 2048)])
+@pytest.mark.parametrize("T,F,K", [(1, 14336, 4096), (17, 128, 64), (33, 8192, 2048), (300, 256, 128)])
 def test_swiglu(ops, ws, dtype, T, F, K):
     x = _rand(T, K, dtype=dtype, seed=11)
     wg = _rand(F, K, dtype=dtype, scale=0.02, seed=12)
