@@ -72,7 +72,7 @@ def parse():
     ap.add_argument("--no-tp", action="store_true", help="skip the 70B tensor-parallel leg of multi-GPU runs")
     ap.add_argument("--sweep", choices=["c5"], default=None,
                     help="c5: tree-attention and KV-compaction sweep (ctx x tree nodes) on one GPU, then exit")
-    ap.add_argument("--ncu-case", choices=["gemm", "gemm_mix", "attention"], default=None,
+    ap.add_argument("--ncu-case", choices=["gemm", "gemm_mix", "gemm_prefill", "attention"], default=None,
                     help="run one small launch set of a kernel for an ncu capture, then exit")
     ap.add_argument("--rows", type=int, default=None, help="query token rows of the attention ncu case (33)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the time-to-first-token measurement")
@@ -605,6 +605,26 @@ def ncu_case(args, dev) -> None:
         ops.linear(x, [wg, wu], ws, epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid)
         ops.linear(hid, [wd], ws, epilogue=L.EPI_RESIDUAL, resid=resid)
         ops.head_argmax(x, lm, idx, ws)
+    elif args.ncu_case == "gemm_prefill":
+        # the 8B gate/up pair (+SwiGLU) over a 2048-token prompt: 3 warm-up launches, then 10 timed
+        # with CUDA events (capture one with -s 3 -c 1)
+        d, F, T = 4096, 14336, 2048
+        ws = ops.Workspace(dev, 64, 1, 1)
+        x = (torch.randn(T, d, device=dev) * 0.5).bfloat16()
+        wg = (torch.randn(F, d, device=dev) * 0.02).bfloat16()
+        wu = (torch.randn(F, d, device=dev) * 0.02).bfloat16()
+        hid = torch.empty(T, F, device=dev).bfloat16()
+        run = lambda: ops.linear(x, [wg, wu], ws, epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid)
+        for _ in range(3):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            run()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1e3 / 10
+        print(json.dumps({"gemm_prefill_us": us, "tflops": 2 * T * 2 * F * d / us / 1e6}))
     elif args.ncu_case == "gemm":
         # the 8B down_proj shape at verify size: K=14336 -> 4096, 33 rows
         K, N, T = 14336, 4096, 33
