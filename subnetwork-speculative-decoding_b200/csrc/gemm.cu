@@ -1250,7 +1250,20 @@ static SplitPlan plan_splits(int64_t T, int tiles_m, int kchunks, bool head, int
   if (dtype == SSD_BF16) {
     p.BN = round_bn(T);
     p.tiles_n = (int)((T + p.BN - 1) / p.BN);
-    const int per_sm = tc_ctas_per_sm(tiles_m, kchunks, head, sms);
+    // Several token tiles (prefill, T > 256): two or three CTAs per SM. With
+    // three (two stages each) one CTA's epilogue runs under the other two's
+    // main loops: the 8B gate/up pair over 2048 tokens takes 564 us against
+    // 734 us at two per SM (1363 us at one), i.e. a CTA runs ~15 % longer
+    // beside two others than beside one. Whichever needs fewer CTA-times in
+    // whole waves wins (a small grid's last wave would run nearly empty).
+    int per_sm;
+    if (p.tiles_n > 1) {
+      const int64_t ctas = (int64_t)tiles_m * p.tiles_n;
+      const int64_t w2 = (ctas + 2 * sms - 1) / (2 * sms), w3 = (ctas + 3 * sms - 1) / (3 * sms);
+      per_sm = w3 * 115 < w2 * 100 ? 3 : 2;
+    } else {
+      per_sm = tc_ctas_per_sm(tiles_m, kchunks, head, sms);
+    }
     p.splits = (p.tiles_n == 1 && !head) ? choose_cluster_splits(tiles_m, kchunks, per_sm * sms) : 1;
     p.stages = tc_stages(p.BN, per_sm);
     p.sk = p.tiles_n == 1 && p.BN <= 128 && sk_enabled();
