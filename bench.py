@@ -72,7 +72,7 @@ def parse():
     ap.add_argument("--no-tp", action="store_true", help="skip the 70B tensor-parallel leg of multi-GPU runs")
     ap.add_argument("--sweep", choices=["c5"], default=None,
                     help="c5: tree-attention and KV-compaction sweep (ctx x tree nodes) on one GPU, then exit")
-    ap.add_argument("--ncu-case", choices=["gemm", "gemm_mix", "gemm_prefill", "attention"], default=None,
+    ap.add_argument("--ncu-case", choices=["gemm", "gemm_mix", "gemm_prefill", "prefill", "attention"], default=None,
                     help="run one small launch set of a kernel for an ncu capture, then exit")
     ap.add_argument("--rows", type=int, default=None, help="query token rows of the attention ncu case (33)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the time-to-first-token measurement")
@@ -605,6 +605,25 @@ def ncu_case(args, dev) -> None:
         ops.linear(x, [wg, wu], ws, epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid)
         ops.linear(hid, [wd], ws, epilogue=L.EPI_RESIDUAL, resid=resid)
         ops.head_argmax(x, lm, idx, ws)
+    elif args.ncu_case == "prefill":
+        # the C3 target's prefill of a 2048-token prompt: two warm-up prefills, then one inside a
+        # profiler range (capture with ncu --profile-from-start off)
+        from ssd import synthetic as S
+        from ssd.engine.round import TargetStep, TreePlan, cache_capacity
+
+        spec = S.CONFIGS["c3"]
+        _, target, _, cfg = build(spec, dev)
+        P = args.prompt_len or spec.prompt_len
+        ids = S.make_prompt(spec.seed, P, target.weights.V).to(dev)
+        step = TargetStep(target, target.new_cache(cache_capacity(P, spec.max_new_tokens, TreePlan(cfg))),
+                          spec.max_new_tokens)
+        for _ in range(2):
+            step.prefill(ids)
+        torch.cuda.synchronize(dev)
+        torch.cuda.cudart().cudaProfilerStart()
+        step.prefill(ids)
+        torch.cuda.synchronize(dev)
+        torch.cuda.cudart().cudaProfilerStop()
     elif args.ncu_case == "gemm_prefill":
         # the 8B gate/up pair (+SwiGLU) over a 2048-token prompt: 3 warm-up launches, then 10 timed
         # with CUDA events (capture one with -s 3 -c 1)

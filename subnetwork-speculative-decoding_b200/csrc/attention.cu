@@ -706,6 +706,15 @@ __global__ void __launch_bounds__(32 * (kWsMaxConsumers + 1), 1) attn_ws_kernel(
 }
 
 // ------------------------------------------------------------ tcgen05 kernel
+// KV head and row group of tcgen05-kernel CTA column blk (and of its merge):
+// heads vary fastest and the row groups run from the last to the first, so
+// under a causal mask (prefill) the CTAs with the most keys start in the
+// first wave and the short ones fill the tail.
+__device__ __forceinline__ void tc_head_group(const AttnArgs& a, int blk, int& h, int& gr) {
+  h = blk % a.n_kv;
+  gr = a.groups - 1 - blk / a.n_kv;
+}
+
 // bf16, head_dim 64 or 128. A CTA = one KV head x up to 128 query rows (one
 // M = 128 tcgen05 tile; rows past the group are zero) x one key slice.
 // Warp 0 streams the slice's 64-key K and V blocks by TMA (128-byte swizzle,
@@ -794,7 +803,8 @@ __global__ void __launch_bounds__(kTcAttnThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int blk = blockIdx.x;
-  const int h = blk / a.groups, gr = blk % a.groups;
+  int h, gr;
+  tc_head_group(a, blk, h, gr);
   const int split = blockIdx.y;
   const int M = a.T * a.G;
   const int q0 = gr * a.rows_per_group;
@@ -1221,7 +1231,8 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(const AttnArgs a) {
   constexpr int DPL = HD / 32;
   const int blk = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rr = blockIdx.y * 8 + warp;
-  const int h = blk / a.groups, gr = blk % a.groups;
+  int h, gr;
+  tc_head_group(a, blk, h, gr);
   const int M = a.T * a.G;
   const int q0 = gr * a.rows_per_group;
   const int Mg = min(a.rows_per_group, M - q0);
