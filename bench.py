@@ -72,7 +72,8 @@ def parse():
     ap.add_argument("--no-tp", action="store_true", help="skip the 70B tensor-parallel leg of multi-GPU runs")
     ap.add_argument("--sweep", choices=["c5"], default=None,
                     help="c5: tree-attention and KV-compaction sweep (ctx x tree nodes) on one GPU, then exit")
-    ap.add_argument("--ncu-case", choices=["gemm", "gemm_mix", "gemm_prefill", "prefill", "attention"], default=None,
+    ap.add_argument("--ncu-case", choices=["gemm", "gemm_mix", "gemm_prefill", "prefill", "attention", "warp_sample"],
+                    default=None,
                     help="run one small launch set of a kernel for an ncu capture, then exit")
     ap.add_argument("--rows", type=int, default=None, help="query token rows of the attention ncu case (33)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the time-to-first-token measurement")
@@ -605,6 +606,27 @@ def ncu_case(args, dev) -> None:
         ops.linear(x, [wg, wu], ws, epilogue=L.EPI_SWIGLU, layout=L.SEG_PAIRS, out=hid)
         ops.linear(hid, [wd], ws, epilogue=L.EPI_RESIDUAL, resid=resid)
         ops.head_argmax(x, lm, idx, ws)
+    elif args.ncu_case == "warp_sample":
+        # the fused warp + Gumbel top-k kernel on a draft level of the sampled C3 path: `--rows` rows
+        # (8) of 128256 N(0, 2^2) logits, T 0.7, top_p 0.9, k 4; 3 warm-up launches, then 10 timed
+        rows, V, k = args.rows or 8, 128256, 4
+        g = torch.Generator(device=dev).manual_seed(3)
+        logits = torch.randn(rows, V, device=dev, generator=g) * 2.0
+        prm = ops.warp_params_buffer(rows, dev)
+        tok = torch.empty(rows * k, dtype=torch.int32, device=dev)
+        lp = torch.empty(rows * k, dtype=torch.float32, device=dev)
+        seed = torch.tensor([1234], dtype=torch.int64, device=dev)
+        rnd = torch.zeros(1, dtype=torch.int32, device=dev)
+        run = lambda: ops.warp_sample_topk(logits, 0.7, 0.9, prm, k, seed, rnd, 0, tok, lp)
+        for _ in range(3):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            run()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"warp_sample_us": e0.elapsed_time(e1) * 1e3 / 10, "rows": rows}))
     elif args.ncu_case == "prefill":
         # the C3 target's prefill of a 2048-token prompt: two warm-up prefills, then one inside a
         # profiler range (capture with ncu --profile-from-start off)
