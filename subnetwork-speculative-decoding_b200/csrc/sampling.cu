@@ -547,6 +547,8 @@ struct RowExchange {
   unsigned long long* hslot;  // [2][256] histogram bins per bank
   float* gath;                // [2 * kRowMaxSlices] gathered partials
   unsigned long long* whist;  // [kSampWarps][256] per-warp bins (radix select)
+  unsigned* cnt;              // [256] sampled key counts per top byte (radix select)
+  int* slot_of;               // [256 + 8]: slot of a top byte (-1: none), then the byte of each slot
   int S;
   int n;  // exchanges so far
 };
@@ -640,9 +642,9 @@ __device__ void row_max_sum(RowExchange& x, float mc, float zc, float inv_t, flo
 // The window bins are exactly the full histogram's and the rule never looks
 // below the bin it selects, so when it selects a window bin the result is the
 // full histogram's; when it selects the lump, the level is histogrammed again
-// in full (a cluster-uniform decision) through per-thread caches of four bins
-// and one private histogram per warp. Deeper levels see few keys over
-// spread-out bins and add to one shared histogram.
+// in full (a cluster-uniform decision): the 8 top bytes most frequent in a
+// sample of the slice get per-thread slots, the others shared atomics. Deeper
+// levels see few keys over spread-out bins and add to one shared histogram.
 template <typename Weight>
 __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_key, unsigned long long target,
                                          bool by_count, Weight weight, RowExchange& x, unsigned long long* sel,
@@ -659,8 +661,6 @@ __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_
     const int shift = 24 - 8 * level;
     unsigned long long* hist = x.hslot + (x.n & 1) * 256;
     const bool per_warp = level == 0 && !window;
-    if (per_warp)
-      for (int b = threadIdx.x; b < kSampWarps * 256; b += kSampThreads) x.whist[b] = 0ull;
     if (level == 0) __syncthreads();  // zeroed bins before any add
     if (level == 0 && window) {
       // each thread adds into its own 8 slots (slot j of thread t at
@@ -699,66 +699,86 @@ __device__ uint32_t cluster_radix_select(const float* xs, int n, uint32_t floor_
         if (lane == 0 && t != 0ull) atomicAdd(&hist[top_bin - j], t);
       }
     } else if (per_warp) {
-      // Few top-byte bins hold most keys, so each thread keeps four (bin,
-      // sum) pairs in registers and adds an evicted pair to its warp's own
-      // histogram (only lanes of one warp ever meet on those bins).
-      unsigned long long* mine = x.whist + (threadIdx.x >> 5) * 256;
-      uint32_t b0 = 256u, b1 = 256u, b2 = 256u, b3 = 256u;  // 256 = empty
-      unsigned long long s0 = 0ull, s1 = 0ull, s2 = 0ull, s3 = 0ull;
-      unsigned victim = 0;
+      // Full first level: a sample of the slice (each thread's first key)
+      // picks the 8 most populated top bytes; their weights go to per-thread
+      // slots as in the window, every other byte to shared atomics. Every bin
+      // is exact whichever bytes get slots.
+      for (int b = threadIdx.x; b < 256; b += kSampThreads) x.cnt[b] = 0u;
+      __syncthreads();
+      if (threadIdx.x < n) {
+        const uint32_t k = order_key(xs[threadIdx.x]);
+        if (k >= floor_key) atomicAdd(&x.cnt[k >> 24], 1u);
+      }
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        // warp 0: eight rounds of a (count, -byte) maximum; lane j holds bytes 8j .. 8j + 7
+        unsigned c[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) c[t] = x.cnt[8 * lane + t];
+        for (int b = lane; b < 256; b += 32) x.slot_of[b] = -1;
+        __syncwarp();
+        for (int sl = 0; sl < 8; ++sl) {
+          unsigned best = 0u;
+          int bb = 256;
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            if (c[t] > best) {
+              best = c[t];
+              bb = 8 * lane + t;
+            }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const unsigned ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int obb = __shfl_xor_sync(0xffffffffu, bb, o);
+            if (ob > best || (ob == best && obb < bb)) {
+              best = ob;
+              bb = obb;
+            }
+          }
+          if (lane == 0) x.slot_of[256 + sl] = best > 0u ? bb : -1;
+          if (best > 0u) {
+            if (lane == 0) x.slot_of[bb] = sl;
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              if (8 * lane + t == bb) c[t] = 0u;
+          }
+        }
+      }
+      unsigned long long* slot = x.whist + threadIdx.x;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) slot[j * kSampThreads] = 0ull;
+      __syncthreads();
       for (int i = threadIdx.x; i < n; i += kSampThreads) {
         const float l = xs[i];
         const uint32_t k = order_key(l);
         if (k < floor_key) continue;
-        const uint32_t bin = k >> 24;
+        const int sl = x.slot_of[k >> 24];
         const unsigned long long v = weight(l);
-        if (bin == b0) {
-          s0 += v;
-        } else if (bin == b1) {
-          s1 += v;
-        } else if (bin == b2) {
-          s2 += v;
-        } else if (bin == b3) {
-          s3 += v;
+        if (sl >= 0) {
+          slot[sl * kSampThreads] += v;
         } else {
-          if (victim == 0u) {
-            if (b0 < 256u) atomicAdd(&mine[b0], s0);
-            b0 = bin;
-            s0 = v;
-          } else if (victim == 1u) {
-            if (b1 < 256u) atomicAdd(&mine[b1], s1);
-            b1 = bin;
-            s1 = v;
-          } else if (victim == 2u) {
-            if (b2 < 256u) atomicAdd(&mine[b2], s2);
-            b2 = bin;
-            s2 = v;
-          } else {
-            if (b3 < 256u) atomicAdd(&mine[b3], s3);
-            b3 = bin;
-            s3 = v;
-          }
-          victim = (victim + 1u) & 3u;
+          atomicAdd(&hist[k >> 24], v);
         }
       }
-      if (b0 < 256u) atomicAdd(&mine[b0], s0);
-      if (b1 < 256u) atomicAdd(&mine[b1], s1);
-      if (b2 < 256u) atomicAdd(&mine[b2], s2);
-      if (b3 < 256u) atomicAdd(&mine[b3], s3);
+      __syncthreads();
+      {
+        // warp w sums slot w/4 over a quarter of the threads, exactly
+        const int j = (threadIdx.x >> 5) >> 2, q = (threadIdx.x >> 5) & 3;
+        const int byte = x.slot_of[256 + j];
+        const unsigned long long* src = x.whist + j * kSampThreads + q * 256 + lane;
+        unsigned long long t = 0ull;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) t += src[e * 32];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (lane == 0 && byte >= 0 && t != 0ull) atomicAdd(&hist[byte], t);
+      }
     } else {
 #pragma unroll 2
       for (int i = threadIdx.x; i < n; i += kSampThreads) {
         const float l = xs[i];
         const uint32_t k = order_key(l);
         if (k >= floor_key && (k >> (shift + 8)) == prefix) atomicAdd(&hist[(k >> shift) & 255u], weight(l));
-      }
-    }
-    if (per_warp) {
-      __syncthreads();
-      for (int b = threadIdx.x; b < 256; b += kSampThreads) {
-        unsigned long long t = 0ull;
-        for (int w = 0; w < kSampWarps; ++w) t += x.whist[w * 256 + b];
-        hist[b] = t;
       }
     }
     // the cluster barrier also orders this CTA's adds before the reads below
@@ -945,7 +965,9 @@ __global__ void __launch_bounds__(kSampThreads, 1) warp_sample_kernel(
   pdl_trigger();
   for (int i = threadIdx.x; i < n; i += kSampThreads) xs[i] = row[i0 + i];
   __syncthreads();
-  RowExchange x{fslot, hslot, gath, nullptr, S, 0};
+  __shared__ unsigned s_cnt[256];
+  __shared__ int s_slot_of[256 + 8];
+  RowExchange x{fslot, hslot, gath, nullptr, s_cnt, s_slot_of, S, 0};
   x.whist = reinterpret_cast<unsigned long long*>(xs + ((len + 1) & ~1));
   const WarpParams P = cluster_row_warp(xs, n, V, temperature, top_p, keep_top, red, x, sel);
   if (s == 0 && threadIdx.x == 0 && params_out) params_out[r] = P;
@@ -1133,7 +1155,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_verify_cluster_kernel(
   float* qs = dyn + len;
   pdl_wait();
   pdl_trigger();
-  RowExchange x{fslot, nullptr, gath, nullptr, S, 0};
+  RowExchange x{fslot, nullptr, gath, nullptr, nullptr, nullptr, S, 0};
   const int n = min(*n_nodes, max_nodes);
   const int c0 = root_pos[0];
   const uint64_t sd = seed[0];
