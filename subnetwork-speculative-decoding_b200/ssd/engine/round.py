@@ -117,6 +117,18 @@ class _Decoder:
         self.gap = torch.zeros(max(head_rows, 1), dtype=torch.float32, device=self.device)
         self.fwd_root = R.ForwardInputs(1, self.device, mask_words=1)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self._prefill_bufs = None  # (rows, ForwardInputs, Scratch, Workspace) of the longest prompt so far
+
+    def _prefill_buffers(self, P: int):
+        """Inputs, activations and workspace for a prompt of P rows, kept for
+        later prompts of up to the same length (the workspace is zeroed once
+        at allocation; its split counters reset themselves)."""
+        if self._prefill_bufs is None or self._prefill_bufs[0] < P:
+            self._prefill_bufs = None  # release the smaller set first
+            w = self.w
+            self._prefill_bufs = (P, R.ForwardInputs(P, self.device, mask_words=1), R.Scratch(w, P),
+                                  ops.Workspace(self.device, max_rows=P, vocab=w.V, max_head_rows=1))
+        return self._prefill_bufs[1:]
 
     def prefill(self, prompt: torch.Tensor) -> None:
         """Target over the prompt (causal), first token = argmax of its last row
@@ -125,10 +137,8 @@ class _Decoder:
         P = int(prompt.numel())
         self.cache.reset()
         self.cache.check_room(P)
-        fwd = R.ForwardInputs(P, self.device, mask_words=1)
+        fwd, scratch, ws = self._prefill_buffers(P)
         fwd.fill(prompt.reshape(-1), torch.arange(P), 0, None)
-        scratch = R.Scratch(w, P)
-        ws = ops.Workspace(self.device, max_rows=P, vocab=w.V, max_head_rows=1)
         R.run_stack_auto(w, self.target.layer_indices, [None] * len(self.target.layer_indices), None, fwd, P,
                          self.cache, scratch, ws, self.cache.max_length)
         xn, rn = R.head_input(w, scratch, P - 1, P)
