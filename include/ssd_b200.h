@@ -334,7 +334,8 @@ int ssd_gumbel_topk(const float* logits, int64_t ld, int64_t rows, int64_t V, co
 
 /* Fused ssd_warp_params + ssd_gumbel_topk: each row is split over a
  * thread-block cluster of up to 8 CTAs (slices staged in shared memory,
- * reductions combined in rank order). Writes the rows' warp parameters to
+ * reductions combined in rank order; fewer CTAs per row when that keeps all
+ * rows' clusters resident at once). Writes the rows' warp parameters to
  * params_out (may be NULL when k > 0) and, for k >= 1, the same draws as
  * ssd_gumbel_topk with those parameters (RNG counters (round, row_base + r,
  * i, 0)); out_logprob may be NULL. k = 0 computes the parameters only.
