@@ -632,7 +632,8 @@ __device__ void row_max_sum(RowExchange& x, float mc, float zc, float inv_t, flo
 // over the cluster (integers, so the sums do not depend on the split or the
 // order) and the selected bin is the lowest whose weight strictly above it
 // stays <= target (by mass) or, counting, the bin holding the target-th
-// largest key. Returns the selected key.
+// largest key. Returns the selected key; at_or_above (if given) receives the
+// summed weight of the keys >= it.
 //
 // A row's keys crowd into a few top-byte bins, so the first level avoids
 // shared-memory atomics on them. It first tries a window: top_bin is the top
