@@ -198,6 +198,32 @@ def test_bf16_speculative_equals_target_only(tree_name):
         assert set(ar.times) == {"prefill", "decode"}
 
 
+def test_prefill_buffers_reused_across_prompt_lengths():
+    """One engine prefills prompts of 300 rows (three GEMM token tiles), 40 rows
+    and 300 rows again, reusing its prefill inputs, activations and workspace;
+    after each, its state (first token, sequence length) equals a fresh
+    engine's for the same prompt (bf16 tiny model)."""
+    from ssd.engine.round import TargetStep, cache_capacity
+
+    base = tiny_base(torch.bfloat16)
+    target = TargetRunner(base)
+    long_p, short_p = S.make_prompt(7, 300, 128), S.make_prompt(8, 40, 128)
+
+    def fresh(p):
+        e = TargetStep(target, target.new_cache(cache_capacity(p.numel(), 8)), 8)
+        e.prefill(p.to(DEV))
+        return e
+
+    ref = {300: fresh(long_p), 40: fresh(short_p)}
+    eng = TargetStep(target, target.new_cache(cache_capacity(300, 8)), 8)
+    for p in (long_p, short_p, long_p):
+        eng.prefill(p.to(DEV))
+        torch.cuda.synchronize()
+        want = ref[p.numel()]
+        assert torch.equal(eng.state, want.state)
+        assert torch.equal(eng.out_tokens[:1], want.out_tokens[:1])
+
+
 @pytest.mark.slow
 def test_c1_full_size_fp32_matches_reference():
     """BASELINE config 1 at full size: SD output == the reference's own
