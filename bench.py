@@ -1238,7 +1238,13 @@ def main() -> None:
     if world > 1 and not tp_run and not args.no_tp:
         del base, target, draft, w
         torch.cuda.empty_cache()
-        tp_line = tp_leg(args, dev, rank, world)
+        # a failure of this extra leg is reported in its key; the C3 line
+        # measured above is still printed (every rank raises alike for shape or
+        # status errors, so all ranks leave the leg together)
+        try:
+            tp_line = tp_leg(args, dev, rank, world)
+        except (RuntimeError, ValueError, MemoryError) as exc:
+            tp_line = {"error": f"{type(exc).__name__}: {exc}"[:400]}
 
     if rank == 0:
         line = {
