@@ -26,6 +26,11 @@ Outputs (tests/golden/):
                and its logits at the same ids teacher-forced on the fp32
                tokens, i.e. how far the reference's own bf16 arithmetic lands
                from its fp32 decode.
+  sample_next.json - the reference's batched-generation sampler
+               (ssd/data/generate_selfdistill.py:51-61: top-64 cut, then
+               temperature + top-p) on seeded logit rows: per case the row,
+               the settings and the token counts of many seeded draws; greedy
+               rows record the argmax.
 """
 
 from __future__ import annotations
@@ -254,12 +259,38 @@ def make_c2ref(syn, out_path: Path, n_new: int = 48):
     print(f"wrote {out_path}")
 
 
+# (temperature, top_p) per row of sample_next.json: the cut alone, a nucleus
+# inside the 64 kept logits, a sharp and a flat temperature
+SAMPLE_NEXT_CASES = [(1.0, 1.0), (0.7, 0.9), (1.3, 0.5), (0.5, 0.95), (2.0, 0.8)]
+
+
+def make_sample_next(out_path: Path, vocab: int = 300, draws: int = 40000):
+    """The reference's sample_next on seeded rows of `vocab` logits (more than
+    the 64 it keeps): counts of `draws` tokens drawn with a seeded torch
+    generator (one batched call per case), and the greedy argmax."""
+    import torch
+    from ssd.data.generate_selfdistill import sample_next
+
+    g = torch.Generator().manual_seed(11)
+    cases = []
+    for i, (temp, top_p) in enumerate(SAMPLE_NEXT_CASES):
+        row = torch.randn(vocab, generator=g, dtype=torch.float64).float() * (1.0 + i)
+        gen = torch.Generator().manual_seed(100 + i)
+        tok = sample_next(row.expand(draws, vocab).contiguous(), temp, top_p, gen)[:, 0]
+        counts = torch.bincount(tok, minlength=vocab)
+        cases.append(dict(logits=[float(x) for x in row], temperature=temp, top_p=top_p, draws=draws,
+                          counts=[int(c) for c in counts],
+                          greedy=int(sample_next(row[None], 0.0, 1.0)[0, 0])))
+    out_path.write_text(json.dumps(dict(vocab=vocab, keep=64, cases=cases)))
+    print(f"wrote {out_path}")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--ref", default=os.environ.get("SSD_REFERENCE"), required="SSD_REFERENCE" not in os.environ,
                     help="path of the reference checkout (default: $SSD_REFERENCE)")
     ap.add_argument("--skip-1b", action="store_true")
-    ap.add_argument("--only", choices=["tiny", "c1", "c2ref"])
+    ap.add_argument("--only", choices=["tiny", "c1", "c2ref", "sample_next"])
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
     import torch
@@ -272,6 +303,8 @@ def main():
         make_c1(syn, HERE / "c1.json")
     if not a.skip_1b and a.only in (None, "c2ref"):
         make_c2ref(syn, HERE / "c2ref.json")
+    if a.only in (None, "sample_next"):
+        make_sample_next(HERE / "sample_next.json")
 
 
 if __name__ == "__main__":

@@ -187,6 +187,8 @@ def test_gumbel_max_p_values_uniform_over_seed_blocks():
     import numpy as np
     from scipy import stats
 
+    from oracle.tree import top_k_warp
+
     from oracle.philox import gumbel
 
     p = np.array([0.30, 0.22, 0.15, 0.12, 0.09, 0.06, 0.04, 0.02])
@@ -198,3 +200,31 @@ def test_gumbel_max_p_values_uniform_over_seed_blocks():
         counts = np.bincount(draws, minlength=8)
         pvals.append(stats.chisquare(counts, p * counts.sum()).pvalue)
     assert stats.kstest(pvals, "uniform").pvalue > 1e-3
+
+
+def test_top_k_warp_matches_reference_sample_next():
+    """The oracle's top_k_warp is the distribution of the reference's batched
+    sampler (ssd/data/generate_selfdistill.py:51-61: top-64 cut, temperature,
+    top-p): every token the reference drew lies in the oracle's support, and
+    the reference's counts fit the oracle's probabilities (pooled Pearson
+    chi-square, p > 1e-3 on the fixed fixture); greedy rows give the argmax."""
+    from scipy import stats
+
+    from oracle.tree import top_k_warp
+
+    gold = json.loads((GOLD / "sample_next.json").read_text())
+    for case in gold["cases"]:
+        row = np.asarray(case["logits"], dtype=np.float32)
+        counts = np.asarray(case["counts"], dtype=np.float64)
+        p = top_k_warp(row, gold["keep"], case["temperature"], case["top_p"])
+        assert np.count_nonzero(p) <= gold["keep"]
+        assert counts[p <= 0].sum() == 0, "the reference drew a token outside the oracle's support"
+        exp = p * counts.sum()
+        big = exp >= 5.0
+        obs_l, exp_l = list(counts[big]), list(exp[big])
+        small = (~big) & (p > 0)
+        if small.any():
+            obs_l.append(counts[small].sum())
+            exp_l.append(exp[small].sum())
+        assert stats.chisquare(obs_l, exp_l).pvalue > 1e-3, (case["temperature"], case["top_p"])
+        assert int(np.argmax(row)) == case["greedy"]
