@@ -187,8 +187,6 @@ def test_gumbel_max_p_values_uniform_over_seed_blocks():
     import numpy as np
     from scipy import stats
 
-    from oracle.tree import top_k_warp
-
     from oracle.philox import gumbel
 
     p = np.array([0.30, 0.22, 0.15, 0.12, 0.09, 0.06, 0.04, 0.02])
