@@ -31,6 +31,10 @@ Outputs (tests/golden/):
                temperature + top-p) on seeded logit rows: per case the row,
                the settings and the token counts of many seeded draws; greedy
                rows record the argmax.
+  warp_probs.json - the reference's warp_probs (ssd/engine/tree_drafter.py:
+               34-45) on seeded full-vocabulary rows (regenerated from their
+               seeds by the test; a checksum guards the stream): kept-token
+               count and the 16 largest probabilities per case.
 """
 
 from __future__ import annotations
@@ -285,12 +289,41 @@ def make_sample_next(out_path: Path, vocab: int = 300, draws: int = 40000):
     print(f"wrote {out_path}")
 
 
+# (logit scale, temperature, top_p) per row of warp_probs.json
+WARP_CASES = [(1.0, 0.7, 0.9), (3.0, 1.0, 0.5), (8.0, 1.5, 0.99), (2.0, 0.6, 0.95), (0.5, 1.0, 0.8),
+              (4.0, 0.9, 0.3), (2.0, 1.0, 1.0)]
+
+
+def warp_row(seed: int, scale: float, vocab: int = 128256):
+    """Seeded fp32 logit row of warp_probs.json (torch CPU generator)."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(vocab, generator=g, dtype=torch.float64) * scale).float()
+
+
+def make_warp_probs(out_path: Path):
+    from ssd.engine.tree_drafter import warp_probs
+
+    cases = []
+    for i, (scale, temp, top_p) in enumerate(WARP_CASES):
+        row = warp_row(1000 + i, scale)
+        p = warp_probs(row, temp, top_p)
+        top = p.topk(16)
+        cases.append(dict(seed=1000 + i, scale=scale, temperature=temp, top_p=top_p,
+                          row_sum=float(row.double().sum()), row_sq=float(row.double().square().sum()),
+                          n_kept=int((p > 0).sum()), top_ids=[int(x) for x in top.indices],
+                          top_probs=[float(x) for x in top.values]))
+    out_path.write_text(json.dumps(dict(vocab=128256, cases=cases), indent=1))
+    print(f"wrote {out_path}")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--ref", default=os.environ.get("SSD_REFERENCE"), required="SSD_REFERENCE" not in os.environ,
                     help="path of the reference checkout (default: $SSD_REFERENCE)")
     ap.add_argument("--skip-1b", action="store_true")
-    ap.add_argument("--only", choices=["tiny", "c1", "c2ref", "sample_next"])
+    ap.add_argument("--only", choices=["tiny", "c1", "c2ref", "sample_next", "warp_probs"])
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
     import torch
@@ -305,6 +338,8 @@ def main():
         make_c2ref(syn, HERE / "c2ref.json")
     if a.only in (None, "sample_next"):
         make_sample_next(HERE / "sample_next.json")
+    if a.only in (None, "warp_probs"):
+        make_warp_probs(HERE / "warp_probs.json")
 
 
 if __name__ == "__main__":

@@ -226,3 +226,34 @@ def test_top_k_warp_matches_reference_sample_next():
             exp_l.append(exp[small].sum())
         assert stats.chisquare(obs_l, exp_l).pvalue > 1e-3, (case["temperature"], case["top_p"])
         assert int(np.argmax(row)) == case["greedy"]
+
+
+def test_warp_probs_matches_reference_full_vocabulary():
+    """The oracle's warp_probs (fp64) against the reference's (fp32) on
+    seeded 128 256-logit rows: the 16 largest probabilities agree (ids exact,
+    rtol 2e-4), and the kept-token counts agree except where a token's
+    exclusive prefix mass lies within 2e-5 of top_p, where the reference's
+    fp32 cumulative sum over the sorted row cannot decide (the oracle keeps
+    the exact-arithmetic prefix)."""
+    from oracle.tree import warp_probs
+
+    gold = json.loads((GOLD / "warp_probs.json").read_text())
+    for case in gold["cases"]:
+        g = torch.Generator().manual_seed(case["seed"])
+        row = (torch.randn(gold["vocab"], generator=g, dtype=torch.float64) * case["scale"]).float()
+        assert abs(float(row.double().sum()) - case["row_sum"]) < 1e-6 * (1 + abs(case["row_sum"]))
+        assert abs(float(row.double().square().sum()) - case["row_sq"]) < 1e-9 * case["row_sq"]
+        row = row.numpy()
+        T, top_p = case["temperature"], case["top_p"]
+        p = warp_probs(row, T, top_p)
+        m = min(16, case["n_kept"])  # zero-probability ids past the nucleus have no order
+        order = np.argsort(-p, kind="stable")[:m]
+        assert order.tolist() == case["top_ids"][:m]
+        np.testing.assert_allclose(p[order], case["top_probs"][:m], rtol=2e-4)
+        n = int(np.count_nonzero(p))
+        if n != case["n_kept"]:
+            z = row.astype(np.float64) / T
+            sp = np.sort(np.exp(z - z.max()))[::-1]
+            cum_before = np.cumsum(sp / sp.sum()) - sp / sp.sum()
+            lo, hi = sorted((n, case["n_kept"]))
+            assert np.all(np.abs(cum_before[lo:hi] - top_p) < 2e-5), (case, n)
