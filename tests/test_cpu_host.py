@@ -50,6 +50,55 @@ def test_library_rejects_bad_arguments_without_gpu():
         L.call("ssd_linear_chain", 1, ctypes.cast(links, ctypes.c_void_p), 4, L.SSD_BF16, None, 0, None, None)  # no x
 
 
+def _call_with(name: str, **at):
+    """Call entry point `name` with zeros / NULL / 1.0 in every argument
+    except the positions given as a<index>=value."""
+    res, types = L.SIGNATURES[name]
+    args = []
+    for i, t in enumerate(types):
+        if f"a{i}" in at:
+            args.append(at[f"a{i}"])
+        elif t is ctypes.c_void_p:
+            args.append(None)
+        elif t is ctypes.c_float:
+            args.append(1.0)
+        else:
+            args.append(0)
+    L.call(name, *args)
+
+
+# (entry point, arguments that break its first host-side check, exception):
+# each is rejected before any pointer is read or any CUDA call is made
+BAD_CALLS = [
+    ("ssd_warp_params", dict(a2=0, a3=10), ValueError),  # no rows
+    ("ssd_warp_params", dict(a2=1, a3=10, a4=0.0), ValueError),  # temperature 0
+    ("ssd_warp_params", dict(a2=1, a3=10, a5=1.5), ValueError),  # top_p > 1
+    ("ssd_warp_probs", dict(a2=0, a3=10), ValueError),
+    ("ssd_gumbel_topk", dict(a2=1, a3=10, a5=17), L.SSDError),  # k beyond 16
+    ("ssd_warp_sample_topk", dict(a2=1, a3=10, a6=0, a7=-1), ValueError),  # negative keep_top
+    ("ssd_warp_sample_topk", dict(a2=0, a3=10), ValueError),  # no rows
+    ("ssd_sample_token", dict(a1=0), ValueError),  # empty vocabulary
+    ("ssd_tree_walk_sample", dict(a1=5000), ValueError),  # more nodes than a tree holds
+    ("ssd_level_prune", dict(a2=0, a3=2), ValueError),  # empty frontier
+    ("ssd_level_prune", dict(a2=1000, a3=16), ValueError),  # 16 000 candidates
+    ("ssd_tree_prune", dict(a8=0), ValueError),  # no capacity
+    ("ssd_verify_prep", dict(a1=130, a13=2), ValueError),  # 129 nodes over a 128-slot mask
+    ("ssd_tree_walk_greedy", dict(a1=-1), ValueError),
+    ("ssd_causal_prep", dict(a1=0), ValueError),
+    ("ssd_linear_noalloc", dict(a2=65, a3=4096, a4=1), L.SSDError),  # beyond its fixed scratch
+    ("ssd_linear_noalloc", dict(a2=0, a3=4096, a4=1), L.SSDError),
+]
+
+
+@pytest.mark.parametrize("name,bad,exc", BAD_CALLS, ids=[f"{c[0]}-{i}" for i, c in enumerate(BAD_CALLS)])
+def test_entry_points_reject_bad_shapes_before_any_launch(name, bad, exc):
+    """Status codes map to the reference's exception types (invalid argument:
+    ValueError; unsupported size: the library's RuntimeError subclass), with
+    the failing entry point named in the message."""
+    with pytest.raises(exc, match=name):
+        _call_with(name, **bad)
+
+
 YAML = """
 model:
   base_model: meta-llama/Llama-3.2-1B-Instruct
