@@ -77,3 +77,115 @@ def test_allreduce_parity_alternates_and_checks_even_forwards():
     g.next_parity()
     with pytest.raises(RuntimeError):
         g.end()
+
+
+# ------------------------------------------------------------ two gloo ranks
+def _free_port() -> int:
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rms(x, w, eps):
+    import torch
+
+    return x * torch.rsqrt(x.square().mean(-1, keepdim=True) + eps) * w
+
+
+def _sharded_logits(base, rank: int, world: int, ids):
+    """Forward of this rank's shard in plain torch: column-parallel q/k/v and
+    gate/up, row-parallel o_proj and down (partials summed over the ranks
+    before each residual add), vocabulary-parallel lm_head. Returns the
+    rank's logit columns [T, V / world]."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    cfg = base.config
+    shapes = tp.global_shapes(cfg)
+    params = dict(base.named_parameters())
+    sc = tp.shard_config(cfg, world)
+    H, Hkv, hd, eps = sc.num_attention_heads, sc.num_key_value_heads, sc.head_dim, cfg.rms_norm_eps
+
+    def part(name):
+        w = params[name].detach()
+        b = tp.shard_block(name, shapes[name], rank, world)
+        return w if w.dim() == 1 else w[b.row0:b.row0 + b.rows, b.col0:b.col0 + b.cols]
+
+    def rope(t, cos, sin):
+        half = t.shape[-1] // 2
+        rot = torch.cat([-t[..., half:], t[..., :half]], -1)
+        return t * cos[:, None] + rot * sin[:, None]
+
+    T = ids.numel()
+    x = params["model.embed_tokens.weight"].detach()[ids]
+    cos, sin = (c[0] for c in base.model.rotary_emb(x[None], torch.arange(T)[None]))
+    for i in range(cfg.num_hidden_layers):
+        p = f"model.layers.{i}."
+        xn = _rms(x, part(p + "input_layernorm.weight"), eps)
+        q = rope((xn @ part(p + "self_attn.q_proj.weight").T).view(T, H, hd), cos, sin)
+        k = rope((xn @ part(p + "self_attn.k_proj.weight").T).view(T, Hkv, hd), cos, sin)
+        v = (xn @ part(p + "self_attn.v_proj.weight").T).view(T, Hkv, hd)
+        k, v = (t.repeat_interleave(H // Hkv, dim=1) for t in (k, v))
+        a = F.scaled_dot_product_attention(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1), is_causal=True)
+        o = a.transpose(0, 1).reshape(T, H * hd) @ part(p + "self_attn.o_proj.weight").T
+        dist.all_reduce(o)
+        x = x + o
+        xn = _rms(x, part(p + "post_attention_layernorm.weight"), eps)
+        m = (F.silu(xn @ part(p + "mlp.gate_proj.weight").T) * (xn @ part(p + "mlp.up_proj.weight").T))
+        m = m @ part(p + "mlp.down_proj.weight").T
+        dist.all_reduce(m)
+        x = x + m
+    return _rms(x, part("model.norm.weight"), eps) @ part("lm_head.weight").T
+
+
+def _tp_worker(rank: int, world: int, port: int, q) -> None:
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.set_num_threads(1)
+        base = S.build_base_model("tiny", 0, torch.float32, "cpu")
+        ids = S.make_prompt(21, 12, base.config.vocab_size)[0]
+        with torch.no_grad():
+            local = _sharded_logits(base, rank, world, ids)
+        q.put((rank, local.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_sharded_forward_equals_full_model():
+    """The tensor-parallel layout on two gloo ranks: each rank holds the blocks
+    shard_block gives it and the head counts of shard_config; summing the
+    row-parallel partials and concatenating the vocabulary shards (rank r owns
+    ids [r V/2, (r+1) V/2)) gives the unsharded model's logits, so the merged
+    argmax is the full model's."""
+    import numpy as np
+    import torch
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    base = S.build_base_model("tiny", 0, torch.float32, "cpu")
+    ids = S.make_prompt(21, 12, base.config.vocab_size)
+    with torch.no_grad():
+        full = base(ids).logits[0].numpy()
+    merged = np.concatenate([got[r] for r in range(world)], axis=-1)
+    np.testing.assert_allclose(merged, full, rtol=1e-4, atol=1e-5)
+    assert (merged.argmax(-1) == full.argmax(-1)).all()
