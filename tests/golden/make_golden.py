@@ -35,6 +35,9 @@ Outputs (tests/golden/):
                34-45) on seeded full-vocabulary rows (regenerated from their
                seeds by the test; a checksum guards the stream): kept-token
                count and the 16 largest probabilities per case.
+  verify.json - the reference's verify_inputs and greedy_verify
+               (ssd/engine/verify.py:32-57) on seeded random trees with
+               integer logits (exact ties exercise the first-maximum rule).
 """
 
 from __future__ import annotations
@@ -318,12 +321,68 @@ def make_warp_probs(out_path: Path):
     print(f"wrote {out_path}")
 
 
+def random_tree(g, n: int, vocab: int):
+    """Seeded tree in the drafter's order (every parent before its children),
+    distinct sibling tokens, sibling ranks a random permutation."""
+    import torch
+
+    parents, depths, tokens, ranks = [], [], [], []
+    kids: dict = {}
+    for i in range(n):
+        par = -1 if i == 0 or int(torch.randint(0, 4, (1,), generator=g)) == 0 else int(torch.randint(0, i, (1,), generator=g))
+        used = {tokens[c] for c in kids.get(par, [])}
+        free = [t for t in range(vocab) if t not in used]
+        tok = free[int(torch.randint(0, len(free), (1,), generator=g))]
+        kids.setdefault(par, []).append(i)
+        parents.append(par)
+        depths.append(1 if par == -1 else depths[par] + 1)
+        tokens.append(tok)
+        ranks.append(len(kids[par]) - 1)
+    for sib in kids.values():  # proposal order among siblings: a random permutation
+        perm = torch.randperm(len(sib), generator=g).tolist()
+        for c, r in zip(sib, perm):
+            ranks[c] = r
+    return tokens, parents, depths, ranks
+
+
+def make_verify(out_path: Path, vocab: int = 12):
+    import torch
+    from ssd.engine.tree_drafter import DraftTree
+    from ssd.engine.verify import greedy_verify, verify_inputs
+
+    g = torch.Generator().manual_seed(31)
+    cases = []
+    for n in (0, 1, 3, 7, 12, 20, 31, 40):
+        tokens, parents, depths, ranks = random_tree(g, n, vocab)
+        tree = DraftTree(tokens=tokens, parents=parents, depths=depths, scores=[0.0] * n, ranks=ranks,
+                         draft_pos=[-1] * n)
+        root_token, root_pos = int(torch.randint(0, vocab, (1,), generator=g)), int(torch.randint(0, 50, (1,), generator=g))
+        past = root_pos
+        logits = torch.randint(0, 4, (n + 1, vocab), generator=g).float()  # ties everywhere
+        cur = -1  # plant a path: each accepted node's row favours one of its children
+        while True:
+            kids = [c for c in range(n) if parents[c] == cur]
+            if not kids or int(torch.randint(0, 5, (1,), generator=g)) == 0:
+                break
+            c = kids[int(torch.randint(0, len(kids), (1,), generator=g))]
+            logits[cur + 1, tokens[c]] = 4.0
+            cur = c
+        ids, pos, mask = verify_inputs(tree, root_token, root_pos, past, "cpu")
+        acc, bonus = greedy_verify(tree, logits)
+        cases.append(dict(tokens=tokens, parents=parents, depths=depths, ranks=ranks, root_token=root_token,
+                          root_pos=root_pos, past=past, logits=logits.int().tolist(), ids=ids[0].tolist(),
+                          positions=pos[0].tolist(), mask_rows=[[int(j) for j in torch.nonzero(r)[:, 0]] for r in mask],
+                          accepted=acc, bonus=int(bonus)))
+    out_path.write_text(json.dumps(dict(vocab=vocab, cases=cases)))
+    print(f"wrote {out_path}")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--ref", default=os.environ.get("SSD_REFERENCE"), required="SSD_REFERENCE" not in os.environ,
                     help="path of the reference checkout (default: $SSD_REFERENCE)")
     ap.add_argument("--skip-1b", action="store_true")
-    ap.add_argument("--only", choices=["tiny", "c1", "c2ref", "sample_next", "warp_probs"])
+    ap.add_argument("--only", choices=["tiny", "c1", "c2ref", "sample_next", "warp_probs", "verify"])
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
     import torch
@@ -340,6 +399,8 @@ def main():
         make_sample_next(HERE / "sample_next.json")
     if a.only in (None, "warp_probs"):
         make_warp_probs(HERE / "warp_probs.json")
+    if a.only in (None, "verify"):
+        make_verify(HERE / "verify.json")
 
 
 if __name__ == "__main__":

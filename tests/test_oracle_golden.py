@@ -257,3 +257,32 @@ def test_warp_probs_matches_reference_full_vocabulary():
             cum_before = np.cumsum(sp / sp.sum()) - sp / sp.sum()
             lo, hi = sorted((n, case["n_kept"]))
             assert np.all(np.abs(cum_before[lo:hi] - top_p) < 2e-5), (case, n)
+
+
+def test_verify_inputs_and_greedy_verify_match_reference():
+    """verify_inputs and greedy_verify against the reference's own outputs
+    (ssd/engine/verify.py:32-57) on seeded random trees of 0-40 nodes with
+    integer logits full of exact ties (the first maximum wins): the oracle's
+    ids, positions, mask, accepted path and bonus, and the host
+    verify_inputs of this package, equal the recorded ones exactly."""
+    from oracle.tree import DraftTree as OTree
+    from oracle.tree import greedy_verify, verify_inputs
+    from ssd.engine import verify as V
+    from ssd.engine.tree_drafter import DraftTree
+
+    gold = json.loads((GOLD / "verify.json").read_text())
+    for c in gold["cases"]:
+        n = len(c["tokens"])
+        fields = dict(tokens=c["tokens"], parents=c["parents"], depths=c["depths"], scores=[0.0] * n,
+                      ranks=c["ranks"], draft_pos=[-1] * n)
+        want_mask = np.zeros((n + 1, c["past"] + n + 1), dtype=bool)
+        for i, cols in enumerate(c["mask_rows"]):
+            want_mask[i, cols] = True
+        ids, pos, mask = verify_inputs(OTree(**fields), c["root_token"], c["root_pos"], c["past"])
+        assert (ids, pos) == (c["ids"], c["positions"])
+        assert (mask == want_mask).all()
+        ids, pos, mask = V.verify_inputs(DraftTree(**fields), c["root_token"], c["root_pos"], c["past"], "cpu")
+        assert ids[0].tolist() == c["ids"] and pos[0].tolist() == c["positions"]
+        assert (mask.numpy() == want_mask).all()
+        acc, bonus = greedy_verify(OTree(**fields), np.asarray(c["logits"], dtype=np.float32))
+        assert (acc, bonus) == (c["accepted"], c["bonus"])
