@@ -90,3 +90,50 @@ def test_two_gloo_ranks_match_single_process():
         assert slowest == float(world)
         merged = {i: o for part in gathered for i, o in part}
         assert [merged[i] for i in range(len(ref))] == ref
+
+
+def _leaving_worker(rank: int, world: int, port: int, q) -> None:
+    """Step 1 on both ranks; then rank 1 leaves between steps (exits without
+    joining the next collective) and rank 0's next reduction must fail on the
+    host within the short process-group timeout instead of waiting for good."""
+    import time
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    first = dp.all_sum(1.0, world)
+    if rank == 1:
+        q.put((rank, first, None, 0.0))
+        q.close()
+        q.join_thread()  # flush the queue before leaving without any clean-up
+        os._exit(0)
+    t0 = time.time()
+    try:
+        dp.all_sum(1.0, world)
+        err = None
+    except Exception as exc:  # gloo reports the departed peer or the timeout
+        err = type(exc).__name__
+    q.put((rank, first, err, time.time() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_departed_rank_surfaces_as_an_error_on_the_next_collective():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world):
+        rank, first, err, dt = q.get(timeout=120)
+        got[rank] = (first, err, dt)
+    for p in procs:
+        p.join(timeout=60)
+    assert got[0][0] == got[1][0] == 2.0
+    assert got[0][1] is not None, "rank 0's collective returned although its peer had left"
+    assert got[0][2] < 60.0
