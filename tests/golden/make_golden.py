@@ -37,7 +37,9 @@ Outputs (tests/golden/):
                count and the 16 largest probabilities per case.
   verify.json - the reference's verify_inputs and greedy_verify
                (ssd/engine/verify.py:32-57) on seeded random trees with
-               integer logits (exact ties exercise the first-maximum rule).
+               integer logits (exact ties exercise the first-maximum rule),
+               and DraftTree's children / ancestors / subset
+               (ssd/engine/tree_drafter.py:63-95) on the same trees.
 """
 
 from __future__ import annotations
@@ -369,10 +371,18 @@ def make_verify(out_path: Path, vocab: int = 12):
             cur = c
         ids, pos, mask = verify_inputs(tree, root_token, root_pos, past, "cpu")
         acc, bonus = greedy_verify(tree, logits)
+        # DraftTree's own methods: children, ancestors, and the subset of an
+        # ancestor-closed random node set (its remapped arrays)
+        pick = [i for i in range(n) if int(torch.randint(0, 3, (1,), generator=g)) == 0]
+        keep = sorted({a for i in pick for a in tree.ancestors(i)})
+        sub = tree.subset(keep)
         cases.append(dict(tokens=tokens, parents=parents, depths=depths, ranks=ranks, root_token=root_token,
                           root_pos=root_pos, past=past, logits=logits.int().tolist(), ids=ids[0].tolist(),
                           positions=pos[0].tolist(), mask_rows=[[int(j) for j in torch.nonzero(r)[:, 0]] for r in mask],
-                          accepted=acc, bonus=int(bonus)))
+                          accepted=acc, bonus=int(bonus),
+                          children={str(k): v for k, v in tree.children().items()},
+                          ancestors=[tree.ancestors(i) for i in range(n)], keep=keep,
+                          subset=dict(tokens=sub.tokens, parents=sub.parents, depths=sub.depths, ranks=sub.ranks)))
     out_path.write_text(json.dumps(dict(vocab=vocab, cases=cases)))
     print(f"wrote {out_path}")
 

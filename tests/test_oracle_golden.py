@@ -286,3 +286,23 @@ def test_verify_inputs_and_greedy_verify_match_reference():
         assert (mask.numpy() == want_mask).all()
         acc, bonus = greedy_verify(OTree(**fields), np.asarray(c["logits"], dtype=np.float32))
         assert (acc, bonus) == (c["accepted"], c["bonus"])
+
+
+def test_draft_tree_methods_match_reference():
+    """DraftTree (ssd/engine/tree_drafter.py:48-95, the host type the API
+    returns) and the oracle's restatement: children in sibling rank order,
+    ancestors root-first, and subset's remapped arrays equal the reference's
+    on the seeded random trees of verify.json."""
+    from oracle.tree import DraftTree as OTree
+    from ssd.engine.tree_drafter import DraftTree
+
+    gold = json.loads((GOLD / "verify.json").read_text())
+    for c in gold["cases"]:
+        n = len(c["tokens"])
+        fields = dict(tokens=c["tokens"], parents=c["parents"], depths=c["depths"], scores=[0.0] * n,
+                      ranks=c["ranks"], draft_pos=[-1] * n)
+        for tree in (DraftTree(**fields), OTree(**fields)):
+            assert {str(k): v for k, v in tree.children().items()} == c["children"]
+            assert [tree.ancestors(i) for i in range(n)] == c["ancestors"]
+            sub = tree.subset(c["keep"])
+            assert dict(tokens=sub.tokens, parents=sub.parents, depths=sub.depths, ranks=sub.ranks) == c["subset"]
