@@ -237,3 +237,34 @@ def test_verify_inputs_match_oracle(seed, n, past):
     rids, rpos, rmask = OT.verify_inputs(ot, 9, past, past)
     assert ids[0].tolist() == rids and pos[0].tolist() == rpos
     assert np.array_equal(mask.numpy(), rmask)
+
+
+def test_kv_cache_protocol_on_the_host():
+    """KVCache's host protocol (ssd/engine/kv_cache.py:21-73 of the reference):
+    update writes at [len, len + q) and returns the views up to len + q;
+    advance moves the length; crop discards the tail (a longer crop is a
+    ValueError); overflow is a RuntimeError; keep_positions of positions
+    already in place only sets the length (no kernel)."""
+    import torch
+
+    from ssd.engine.kv_cache import KVCache
+
+    c = KVCache(2, 6)
+    k1, v1 = torch.arange(12.0).view(1, 2, 3, 2), -torch.arange(12.0).view(1, 2, 3, 2)
+    k, v = c.update(1, k1, v1)
+    assert k.shape == (1, 2, 3, 2) and torch.equal(k, k1) and torch.equal(v, v1)
+    c.advance(3)
+    assert c.get_seq_length() == 3
+    k, _ = c.update(1, k1[:, :, :2] + 100, v1[:, :, :2])
+    assert k.shape == (1, 2, 5, 2) and torch.equal(k[:, :, :3], k1) and torch.equal(k[:, :, 3:], k1[:, :, :2] + 100)
+    c.advance(2)
+    with pytest.raises(RuntimeError, match="overflow"):
+        c.update(0, k1[:, :, :2], v1[:, :, :2])
+    with pytest.raises(ValueError):
+        c.crop(6)
+    c.crop(4)
+    assert c.get_seq_length() == 4
+    c.keep_positions(2, [2, 3])
+    assert c.get_seq_length() == 4
+    c.reset()
+    assert c.get_seq_length() == 0
